@@ -1,0 +1,201 @@
+"""Headline benchmark: decode tokens/s (max over ranks) on the Qwen3-8B-shaped model, bf16, TP = N GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: tensor parallel over NCCL)
+
+Workload (BASELINE config 5 shape): random-init Qwen3-8B architecture (36 layers, hidden 4096, 32 q / 8 kv heads,
+head_dim 128, SwiGLU 12288, vocab 151936, seed 4); B concurrent requests with prompt lengths uniform in
+[512, 8192] (random ids) are prefilled through the engine (their TTFT is recorded), then W warm-up and K timed
+decode steps run through ``LLM.step()``.
+
+* ``value``: decode tokens / device time.  Device time is measured with CUDA events recorded inside the model
+  runner around each decode step's GPU work (H2D of the step metadata, CUDA-graph replay of the forward + LM
+  head, sampler) and summed over the K steps; max over ranks.
+* ``e2e``: the same tokens / wall-clock of the K ``LLM.step()`` calls (host scheduling, pinned H2D of each step's
+  inputs, D2H read of the sampled tokens included); max over ranks.
+The weights (16 GB) and the KV cache (tens of GB) are far larger than the 126 MB L2, so no explicit L2 flush is
+needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+BASELINE_VALUE = None  # the reference publishes no decode tok/s figure
+
+
+def _clock_sampler_start(path: str):
+    try:
+        return subprocess.Popen(
+            ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+             "--format=csv,noheader,nounits", "-lms", "200"],
+            stdout=open(path, "w"), stderr=subprocess.DEVNULL)
+    except Exception:
+        return None
+
+
+def _clock_summary(path: str, gpu_index: int):
+    sms, maxs, reasons = [], [], set()
+    try:
+        for line in open(path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9 or not parts[0].isdigit() or int(parts[0]) != gpu_index:
+                continue
+            sm, mx = float(parts[1]), float(parts[2])
+            sms.append(sm)
+            maxs.append(mx)
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(n)
+    except Exception:
+        pass
+    if not sms:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons)}
+
+
+def qwen3_8b_config():
+    from nanovllm_b200.config import HfConfig
+    return HfConfig(vocab_size=151936, hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                    num_attention_heads=32, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
+                    rms_norm_eps=1e-6, rope_theta=1_000_000.0, tie_word_embeddings=False, model_type="qwen3",
+                    architectures=["Qwen3ForCausalLM"], torch_dtype="bfloat16")
+
+
+def run_reference(args):
+    line = {"impl": "reference",
+            "unavailable": "the reference is a Java 21 / Maven CPU library: pip cannot install it (no setup.py or "
+                           "pyproject.toml) and this image has no JDK or Maven to build or run it"}
+    print(json.dumps(line))
+
+
+def run_ours(args):
+    from nanovllm_b200 import ops
+    from nanovllm_b200.config import EngineConfig
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel import state as ps
+    from nanovllm_b200.sampling_params import SamplingParams
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        ps.init_tp("nccl", timeout_s=300)
+    rank = ps.tp_rank()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    hf = qwen3_8b_config()
+    weights = init_random_weights(hf, seed=4, device=dev)
+    B = args.batch
+    gen = torch.Generator().manual_seed(1234)
+    lens = torch.randint(args.min_prompt, args.max_prompt + 1, (B,), generator=gen).tolist()
+    prompts = [torch.randint(1, hf.vocab_size - 1, (n,), generator=gen).tolist() for n in lens]
+    max_len = args.max_prompt + args.warmup + args.steps + 64
+    cfg = EngineConfig(max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=args.prefill_chunk,
+                       gpu_memory_utilization=0.92, stop_on_degenerate=False, cuda_graph_max_bs=B)
+    llm = LLM((hf, weights), cfg, device=dev)
+    del weights
+    sp = SamplingParams(max_tokens=args.warmup + args.steps + 8, ignore_eos=True).deterministic()
+    seqs = [llm.add_request(p, sp) for p in prompts]
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter()
+    while any(s.num_completion_tokens == 0 for s in seqs):
+        llm.step()
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t_pf
+    ttfts = sorted(s.t_first_token - s.t_arrival for s in seqs)
+    p50_ttft = ttfts[len(ttfts) // 2]
+    prefill_tokens = sum(lens)
+    running = len(llm.scheduler.running)
+
+    runner = llm.runner
+    step_ms = []
+
+    def timed_step():
+        runner.step_events = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        seqs_, is_prefill, _ = llm.step()
+        assert not is_prefill
+        step_ms.append(runner.step_events[0].elapsed_time(runner.step_events[1]))
+        return len(seqs_)
+
+    for _ in range(args.warmup):
+        timed_step()
+    step_ms.clear()
+    ops.reset_launch_count()
+    clock_path = os.path.join("gpurun_out" if os.path.isdir("gpurun_out") else "/tmp", f"bench_clocks_r{rank}.csv")
+    sampler = _clock_sampler_start(clock_path) if rank == 0 else None
+    ps.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tokens = 0
+    for _ in range(args.steps):
+        tokens += timed_step()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ps.barrier()
+    if sampler is not None:
+        time.sleep(0.3)
+        sampler.terminate()
+    launches = ops.launch_count()
+    dev_ms = sum(step_ms)
+    t = torch.tensor([dev_ms, wall * 1000.0], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, wall_ms = float(t[0]), float(t[1])
+    h2d = runner.last_h2d_bytes
+    llm.close()
+    if rank == 0:
+        value = tokens / (dev_ms / 1000.0)
+        e2e = tokens / (wall_ms / 1000.0)
+        line = {
+            "metric": "decode tok/s (box, max over ranks) Qwen3-8B-shape TP1/2/4/8; p50 TTFT",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
+            "dtype": "bf16", "data": "synthetic: random-init weights (seed 4), random prompt ids",
+            "config": {"model": "Qwen3-8B-shape (36L, H4096, 32/8 heads, hd128, I12288, V151936)",
+                       "global_batch": running, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}]",
+                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (16 GB weights + KV cache)",
+                       "prefill_tokens": prefill_tokens, "prefill_s": round(prefill_s, 3),
+                       "p50_ttft_ms": round(p50_ttft * 1000, 1)},
+            "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 8 * running},
+            "gpu_launches": launches,
+            "clocks": _clock_summary(clock_path, local),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        ps.destroy()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--min-prompt", type=int, default=512)
+    ap.add_argument("--max-prompt", type=int, default=8192)
+    ap.add_argument("--prefill-chunk", type=int, default=16384)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,49 @@
+// Python bindings of the sm_100a kernels (module nanovllm_b200._C).
+#include <torch/extension.h>
+
+void rms_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual,
+                   c10::optional<torch::Tensor> weight, double eps, int64_t mode);
+void layer_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor weight,
+                     torch::Tensor bias, double eps);
+void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
+                             c10::optional<torch::Tensor> q_w, c10::optional<torch::Tensor> k_w, int64_t norm_mode,
+                             bool v_norm, double eps, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
+                             c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slots, int64_t nq,
+                             int64_t nkv, int64_t head_dim, bool apply_rope);
+void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
+                       torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_lse,
+                       double scale, double softcap, int64_t window, int64_t part_tiles, int64_t nsplit,
+                       c10::optional<torch::Tensor> err);
+void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu_q, torch::Tensor cu_k,
+                            int64_t max_q, c10::optional<torch::Tensor> k_cache, c10::optional<torch::Tensor> v_cache,
+                            c10::optional<torch::Tensor> block_tables, c10::optional<torch::Tensor> kv_src,
+                            int64_t nq, int64_t nkv, int64_t hd, double scale, double softcap, int64_t window,
+                            bool causal, c10::optional<torch::Tensor> err);
+void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
+               int64_t force_splits, c10::optional<torch::Tensor> err);
+int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K);
+void embedding_cuda(torch::Tensor out, torch::Tensor table, torch::Tensor ids, double scale, int64_t vstart,
+                    int64_t vend);
+void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interleaved);
+void bias_act_cuda(torch::Tensor x, c10::optional<torch::Tensor> bias, int64_t act);
+void gather_rows_cuda(torch::Tensor out, torch::Tensor src, torch::Tensor idx);
+void mean_pool_l2_cuda(torch::Tensor out, torch::Tensor x, torch::Tensor cu);
+void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
+                 torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nanovllm_b200 sm_100a kernels";
+  m.def("rms_norm", &rms_norm_cuda);
+  m.def("layer_norm", &layer_norm_cuda);
+  m.def("qk_norm_rope_store", &qk_norm_rope_store_cuda);
+  m.def("paged_decode", &paged_decode_cuda);
+  m.def("prefill_attention", &prefill_attention_cuda);
+  m.def("gemm", &gemm_cuda);
+  m.def("gemm_splits_for", &gemm_splits_for);
+  m.def("embedding", &embedding_cuda);
+  m.def("act_mul", &act_mul_cuda);
+  m.def("bias_act", &bias_act_cuda);
+  m.def("gather_rows", &gather_rows_cuda);
+  m.def("mean_pool_l2", &mean_pool_l2_cuda);
+  m.def("sample", &sample_cuda);
+}

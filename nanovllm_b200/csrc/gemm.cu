@@ -1,0 +1,443 @@
+// Blackwell tcgen05 GEMM:  C[i, j] = sum_k A[i, k] * B[j, k]   (A [Ma, K], B [Nb, K], both K-major bf16).
+//
+// Replaces the reference's CPU dense linear (nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/tensor/
+// MatmulRuntime.java:234-309, a column-split gemv in fp32) for every projection of every model.
+//
+// Design (sm_100a):
+//  * persistent kernel, one CTA per SM, 6 warps:
+//      warp 0      TMA producer (one elected lane): A and B tiles of 64 K-elements with the 128-byte swizzle
+//                  into a STAGES-deep shared-memory ring tracked by full/empty mbarriers;
+//      warp 1      TMEM allocator + MMA issuer (one lane): tcgen05.mma.cta_group::1.kind::f16, M=128, N=BN,
+//                  K=16, accumulating in tensor memory; tcgen05.commit frees ring stages and publishes tiles;
+//      warps 2..5  epilogue: tcgen05.ld 32x32b of their TMEM lane quadrant, convert, store.
+//  * two TMEM accumulators (2 x BN columns) so the epilogue of tile t overlaps the main loop of tile t+1.
+//  * prefill-sized M: A = activations, B = weights, bf16 output, optional fused SiLU(gate)*up / GELU(gate)*up
+//    on gate/up rows interleaved in 128-row blocks (one 256-wide tile holds 128 gate + 128 up columns).
+//  * decode-sized M (<= 256 tokens): swap A/B so the weight rows fill the 128-lane MMA M dimension and the
+//    tokens are the N dimension; the K range is split over CTAs so every SM streams weights; partial sums are
+//    written per split in fp32 and reduced in a fixed order (deterministic) by splitk_reduce_kernel, which
+//    also applies the activation.
+// Every mbarrier wait is bounded; on timeout the kernel records an error code and all roles exit, TMEM is
+// freed, and the host sees the code through the error word.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+enum OutMode : int { kOutBf16 = 0, kOutBf16T = 1, kOutPartialT = 2 };
+enum Act : int { kActNone = 0, kActSiluMul = 1, kActGeluMul = 2 };
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+struct GemmArgs {
+  int Ma, Nb, K;
+  int tiles_m, tiles_n, splits, kblocks;
+  int out_mode, act;
+  void* out;
+  long out_ld;
+  int* err;
+};
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
+  uint32_t need = 2u * bn;
+  uint32_t c = 32;
+  while (c < need) c <<= 1;
+  return c;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap amap,
+                                                         const __grid_constant__ CUtensorMap bmap, GemmArgs args) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = tmem_cols_for(BN);
+  constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;  // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;      // [2]
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = args.tiles_m * args.tiles_n * args.splits;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      nvb::mbar_init(&full_bar[s], 1);
+      nvb::mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      nvb::mbar_init(&tfull_bar[a], 1);
+      nvb::mbar_init(&tempty_bar[a], 4);
+    }
+    nvb::fence_mbar_init();
+  }
+  if (warp == 1) {
+    nvb::tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    nvb::tmem_relinquish();
+  }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  // unit -> (tile_m fastest, then tile_n, then split): concurrently running CTAs share B tiles.
+  auto decode_unit = [&](int u, int& tm, int& tn, int& sp) {
+    tm = u % args.tiles_m;
+    const int r = u / args.tiles_m;
+    tn = r % args.tiles_n;
+    sp = r / args.tiles_n;
+  };
+  auto k_range = [&](int sp, int& kb0, int& kb1) {
+    kb0 = (int)((long)args.kblocks * sp / args.splits);
+    kb1 = (int)((long)args.kblocks * (sp + 1) / args.splits);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      nvb::tma_prefetch_desc(&amap);
+      nvb::tma_prefetch_desc(&bmap);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int tm, tn, sp, kb0, kb1;
+        decode_unit(u, tm, tn, sp);
+        k_range(sp, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!nvb::mbar_wait(&empty_bar[s], (round & 1u) ^ 1u, args.err, &abort_flag)) { ok = false; break; }
+          uint8_t* sa = smem + s * STAGE_BYTES;
+          nvb::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+          nvb::tma_load_2d(sa, &amap, &full_bar[s], kb * BK, tm * BM);
+          nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, tn * BN);
+        }
+      }
+      if (!ok) {
+        // bounded drain of copies that may still be landing in the ring
+        for (uint32_t j = (it > STAGES ? it - STAGES : 0); j < it; ++j)
+          nvb::mbar_wait(&full_bar[j % STAGES], (j / STAGES) & 1u, nullptr, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++lt) {
+        int tm, tn, sp, kb0, kb1;
+        decode_unit(u, tm, tn, sp);
+        k_range(sp, kb0, kb1);
+        const uint32_t acc = lt & 1u, use = lt >> 1;
+        if (!nvb::mbar_wait(&tempty_bar[acc], (use & 1u) ^ 1u, args.err, &abort_flag)) { ok = false; break; }
+        nvb::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!nvb::mbar_wait(&full_bar[s], (it / STAGES) & 1u, args.err, &abort_flag)) { ok = false; break; }
+          nvb::tc_fence_after();
+          const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = nvb::sdesc_kmajor_sw128(a_addr + kk * 32);
+            const uint64_t bd = nvb::sdesc_kmajor_sw128(b_addr + kk * 32);
+            nvb::tc_mma_f16(d_tmem, ad, bd, IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          nvb::tc_commit(&empty_bar[s]);
+        }
+        if (!ok) break;
+        nvb::tc_commit(&tfull_bar[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    uint32_t lt = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++lt) {
+      int tm, tn, sp;
+      decode_unit(u, tm, tn, sp);
+      const uint32_t acc = lt & 1u, use = lt >> 1;
+      int ok = 0;
+      if (lane == 0) ok = nvb::mbar_wait(&tfull_bar[acc], use & 1u, args.err, &abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      nvb::tc_fence_after();
+      const int a_row = tm * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + acc * BN + ((uint32_t)(quad * 32) << 16);
+      if (args.out_mode == kOutBf16) {
+        bf16* out = reinterpret_cast<bf16*>(args.out);
+        if (args.act == kActNone) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t r[16];
+            nvb::tmem_ld_32x32b_x16(t_row + c, r);
+            nvb::tmem_ld_wait();
+            const int col = tn * BN + c;
+            if (a_row < args.Ma) {
+              bf16* dst = out + (long)a_row * args.out_ld + col;
+              if (col + 16 <= args.Nb && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                uint4 v0, v1;
+                uint32_t* p0 = reinterpret_cast<uint32_t*>(&v0);
+                uint32_t* p1 = reinterpret_cast<uint32_t*>(&v1);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  p0[j] = nvb::pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+                  p1[j] = nvb::pack_bf16x2(__uint_as_float(r[8 + 2 * j]), __uint_as_float(r[9 + 2 * j]));
+                }
+                reinterpret_cast<uint4*>(dst)[0] = v0;
+                reinterpret_cast<uint4*>(dst)[1] = v1;
+              } else {
+                for (int j = 0; j < 16 && col + j < args.Nb; ++j) dst[j] = __float2bfloat16(__uint_as_float(r[j]));
+              }
+            }
+          }
+        } else {
+          // gate = columns [0,128) of the tile, up = [128,256); output column tn*128 + c
+#pragma unroll 1
+          for (int c = 0; c < BN / 2; c += 16) {
+            uint32_t rg[16], ru[16];
+            nvb::tmem_ld_32x32b_x16(t_row + c, rg);
+            nvb::tmem_ld_32x32b_x16(t_row + BN / 2 + c, ru);
+            nvb::tmem_ld_wait();
+            const int col = tn * (BN / 2) + c;
+            if (a_row < args.Ma && col < args.Nb / 2) {
+              bf16* dst = out + (long)a_row * args.out_ld + col;
+              float v[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float gte = __uint_as_float(rg[j]), up = __uint_as_float(ru[j]);
+                v[j] = (args.act == kActSiluMul ? silu(gte) : gelu_tanh(gte)) * up;
+              }
+              uint4 v0, v1;
+              uint32_t* p0 = reinterpret_cast<uint32_t*>(&v0);
+              uint32_t* p1 = reinterpret_cast<uint32_t*>(&v1);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                p0[j] = nvb::pack_bf16x2(v[2 * j], v[2 * j + 1]);
+                p1[j] = nvb::pack_bf16x2(v[8 + 2 * j], v[9 + 2 * j]);
+              }
+              reinterpret_cast<uint4*>(dst)[0] = v0;
+              reinterpret_cast<uint4*>(dst)[1] = v1;
+            }
+          }
+        }
+      } else {
+        // swapped: C^T, i.e. out[token j][feature a_row]; lanes are consecutive features -> coalesced per j
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          nvb::tmem_ld_32x32b_x16(t_row + c, r);
+          nvb::tmem_ld_wait();
+          if (a_row < args.Ma) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int tok = tn * BN + c + j;
+              if (tok < args.Nb) {
+                if (args.out_mode == kOutBf16T) {
+                  reinterpret_cast<bf16*>(args.out)[(long)tok * args.out_ld + a_row] =
+                      __float2bfloat16(__uint_as_float(r[j]));
+                } else {
+                  reinterpret_cast<float*>(args.out)[((long)sp * args.Nb + tok) * args.Ma + a_row] =
+                      __uint_as_float(r[j]);
+                }
+              }
+            }
+          }
+        }
+      }
+      nvb::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) nvb::mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// partial [splits][M][Ma] fp32 -> out [M][Ma or Ma/2] bf16 (activation on 128-interleaved gate/up rows)
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int Ma, bf16* __restrict__ out,
+                                     long out_ld, int act) {
+  const int ncols = act == kActNone ? Ma : Ma / 2;
+  const long total = (long)M * ncols;
+  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
+    const int tok = idx / ncols, f = idx % ncols;
+    if (act == kActNone) {
+      float s = 0.f;
+      for (int sp = 0; sp < splits; ++sp) s += partial[((long)sp * M + tok) * Ma + f];
+      out[(long)tok * out_ld + f] = __float2bfloat16(s);
+    } else {
+      const int gr = (f >> 7) * 256 + (f & 127);
+      float g = 0.f, u = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        g += partial[((long)sp * M + tok) * Ma + gr];
+        u += partial[((long)sp * M + tok) * Ma + gr + 128];
+      }
+      out[(long)tok * out_ld + f] = __float2bfloat16((act == kActSiluMul ? silu(g) : gelu_tanh(g)) * u);
+    }
+  }
+}
+
+template <int BN, int STAGES>
+constexpr size_t gemm_smem() {
+  return 1024 + STAGES * (size_t)(BM * BK * 2 + BN * BK * 2) + (2 * STAGES + 4) * 8 + 64;
+}
+
+int num_sms() {
+  static int n = -1;
+  if (n < 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, int STAGES>
+void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cudaStream_t stream, int max_ctas) {
+  auto kern = gemm_tc_kernel<BN, STAGES>;
+  constexpr size_t sm = gemm_smem<BN, STAGES>();
+  static_assert(sm <= 227 * 1024, "gemm shared memory budget");
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const int units = a.tiles_m * a.tiles_n * a.splits;
+  int grid = units < max_ctas ? units : max_ctas;
+  kern<<<grid, 192, sm, stream>>>(am, bm, a);
+}
+
+// Decode BN options (the token count rounded up to 16).
+template <int STAGES_HINT>
+void launch_swap(int bn, const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cudaStream_t st, int ctas) {
+  switch (bn) {
+    case 16: launch_gemm<16, 8>(am, bm, a, st, ctas); break;
+    case 32: launch_gemm<32, 8>(am, bm, a, st, ctas); break;
+    case 48: launch_gemm<48, 8>(am, bm, a, st, ctas); break;
+    case 64: launch_gemm<64, 8>(am, bm, a, st, ctas); break;
+    case 80: launch_gemm<80, 7>(am, bm, a, st, ctas); break;
+    case 96: launch_gemm<96, 6>(am, bm, a, st, ctas); break;
+    case 112: launch_gemm<112, 6>(am, bm, a, st, ctas); break;
+    case 128: launch_gemm<128, 6>(am, bm, a, st, ctas); break;
+    case 144: launch_gemm<144, 5>(am, bm, a, st, ctas); break;
+    case 160: launch_gemm<160, 5>(am, bm, a, st, ctas); break;
+    case 176: launch_gemm<176, 5>(am, bm, a, st, ctas); break;
+    case 192: launch_gemm<192, 4>(am, bm, a, st, ctas); break;
+    case 208: launch_gemm<208, 4>(am, bm, a, st, ctas); break;
+    case 224: launch_gemm<224, 4>(am, bm, a, st, ctas); break;
+    case 240: launch_gemm<240, 4>(am, bm, a, st, ctas); break;
+    default: launch_gemm<256, 4>(am, bm, a, st, ctas); break;
+  }
+}
+
+int choose_splits(int tiles, int kblocks, int sms) {
+  if (tiles >= sms) return 1;
+  int best = 1;
+  double best_eff = -1.0;
+  const int max_s = kblocks / 4 < 32 ? (kblocks / 4 > 1 ? kblocks / 4 : 1) : 32;
+  for (int s = 1; s <= max_s; ++s) {
+    const int u = tiles * s;
+    const int waves = (u + sms - 1) / sms;
+    const double eff = (double)u / ((double)waves * sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+// y = x @ w^T (x [M, K] bf16, w [N, K] bf16) with optional activation on 128-interleaved gate/up rows of w.
+// ``workspace`` (fp32, >= splits * M * N elements when M <= 256) holds split-K partials.
+void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
+               int64_t force_splits, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm expects bf16 CUDA tensors");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "shape mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "K must be the contiguous dimension");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(K % 8 == 0, "K must be a multiple of 8 (16-byte TMA rows)");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
+  TORCH_CHECK(out.stride(-1) == 1, "output rows must be contiguous");
+  if (act != kActNone) TORCH_CHECK(N % 256 == 0, "fused gate/up activation needs N % 256 == 0");
+  if (M == 0) return;
+  int* e = err.has_value() ? err->data_ptr<int>() : nullptr;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int sms = num_sms();
+  const int kblocks = (K + BK - 1) / BK;
+  GemmArgs a{};
+  a.K = K;
+  a.kblocks = kblocks;
+  a.act = (int)act;
+  a.err = e;
+  if (M <= 256) {
+    const int bn = ((M + 15) / 16) * 16;
+    a.Ma = N;
+    a.Nb = M;
+    a.tiles_m = (N + BM - 1) / BM;
+    a.tiles_n = 1;
+    a.splits = force_splits > 0 ? (int)force_splits : choose_splits(a.tiles_m, kblocks, sms);
+    if (a.splits > kblocks) a.splits = kblocks;
+    CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
+    CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
+    if (a.splits == 1 && act == kActNone) {
+      a.out_mode = kOutBf16T;
+      a.out = out.data_ptr();
+      a.out_ld = out.stride(0);
+      launch_swap<0>(bn, am, bm, a, stream, sms);
+    } else {
+      TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
+                      workspace->numel() >= (long)a.splits * M * N,
+                  "gemm: fp32 workspace of splits*M*N elements required");
+      a.out_mode = kOutPartialT;
+      a.out = workspace->data_ptr();
+      a.out_ld = N;
+      launch_swap<0>(bn, am, bm, a, stream, sms);
+      C10_CUDA_KERNEL_LAUNCH_CHECK();
+      const long total = (long)M * (act == kActNone ? N : N / 2);
+      int blocks = (int)((total + 255) / 256);
+      if (blocks > sms * 8) blocks = sms * 8;
+      splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(workspace->data_ptr<float>(), a.splits, M, N,
+                                                       reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0), (int)act);
+    }
+  } else {
+    constexpr int BN = 256;
+    a.Ma = M;
+    a.Nb = N;
+    a.tiles_m = (M + BM - 1) / BM;
+    a.tiles_n = (N + BN - 1) / BN;
+    a.splits = 1;
+    a.out_mode = kOutBf16;
+    a.out = out.data_ptr();
+    a.out_ld = out.stride(0);
+    CUtensorMap am = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), BM);
+    CUtensorMap bm = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BN);
+    launch_gemm<BN, 4>(am, bm, a, stream, sms);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Number of K splits the decode path would use (lets the caller size the workspace).
+int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K) {
+  if (M > 256) return 1;
+  return choose_splits((int)((N + BM - 1) / BM), (int)((K + BK - 1) / BK), num_sms());
+}

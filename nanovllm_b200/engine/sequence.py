@@ -1,0 +1,152 @@
+"""Per-request state of the continuous-batching engine.
+
+Behavior follows nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/engine/Sequence.java:
+a process-wide monotonically increasing ``seq_id`` (Sequence.java:28-86), the token list with the prompt
+length, the page table (``block_table``), cached / scheduled token counters, per-request sampling knobs, and a
+WAITING -> RUNNING -> FINISHED status.  Block math (Sequence.java:323-350): ``num_blocks`` is
+ceil(len / block_size) and ``block(i)`` is the i-th page's token slice.
+
+The degenerate-repetition stop (Sequence.java:379-449) is reproduced: after >= 32 completion tokens the
+sequence stops on a >= 32 same-token streak, on two identical trailing halves with period 16..64 (step 8),
+or, after >= 48 completion tokens, on any 12-gram seen 3 times in the last 128 completion tokens.
+
+New: per-request timestamps (arrival, first token, finish) so the engine reports TTFT / TPOT.
+"""
+from __future__ import annotations
+
+import enum
+import itertools
+import time
+from typing import List, Optional
+
+from ..sampling_params import SamplingParams
+
+
+class SequenceStatus(enum.Enum):
+    WAITING = 0
+    RUNNING = 1
+    FINISHED = 2
+
+
+_SEQ_COUNTER = itertools.count()
+
+
+class Sequence:
+    __slots__ = ("seq_id", "token_ids", "num_tokens", "num_prompt_tokens", "last_token", "block_size",
+                 "block_table", "num_cached_tokens", "num_scheduled_tokens", "status", "is_prefill",
+                 "temperature", "top_k", "top_p", "max_tokens", "ignore_eos", "seed", "t_arrival",
+                 "t_first_token", "t_finish", "user_tag")
+
+    def __init__(self, token_ids: List[int], sampling: Optional[SamplingParams] = None, block_size: int = 256,
+                 user_tag=None):
+        if not token_ids:
+            raise ValueError("prompt must contain at least one token")
+        sp = sampling or SamplingParams()
+        self.seq_id = next(_SEQ_COUNTER)
+        self.token_ids = list(token_ids)
+        self.num_tokens = len(self.token_ids)
+        self.num_prompt_tokens = self.num_tokens
+        self.last_token = self.token_ids[-1]
+        self.block_size = block_size
+        self.block_table: List[int] = []
+        self.num_cached_tokens = 0
+        self.num_scheduled_tokens = 0
+        self.status = SequenceStatus.WAITING
+        self.is_prefill = True
+        self.temperature = sp.temperature
+        self.top_k = sp.top_k
+        self.top_p = sp.top_p
+        self.max_tokens = sp.max_tokens
+        self.ignore_eos = sp.ignore_eos
+        self.seed = sp.seed
+        self.t_arrival = time.perf_counter()
+        self.t_first_token: Optional[float] = None
+        self.t_finish: Optional[float] = None
+        self.user_tag = user_tag
+
+    def __len__(self):
+        return self.num_tokens
+
+    @property
+    def is_finished(self) -> bool:
+        return self.status == SequenceStatus.FINISHED
+
+    @property
+    def num_completion_tokens(self) -> int:
+        return self.num_tokens - self.num_prompt_tokens
+
+    @property
+    def prompt_token_ids(self) -> List[int]:
+        return self.token_ids[:self.num_prompt_tokens]
+
+    @property
+    def completion_token_ids(self) -> List[int]:
+        return self.token_ids[self.num_prompt_tokens:]
+
+    @property
+    def num_cached_blocks(self) -> int:
+        return self.num_cached_tokens // self.block_size
+
+    @property
+    def num_blocks(self) -> int:
+        return (self.num_tokens + self.block_size - 1) // self.block_size
+
+    @property
+    def last_block_num_tokens(self) -> int:
+        return self.num_tokens - (self.num_blocks - 1) * self.block_size
+
+    def block(self, i: int) -> List[int]:
+        if not (0 <= i < self.num_blocks):
+            raise IndexError(i)
+        return self.token_ids[i * self.block_size:(i + 1) * self.block_size]
+
+    def append_token(self, token_id: int) -> None:
+        self.token_ids.append(int(token_id))
+        self.last_token = int(token_id)
+        self.num_tokens += 1
+        if self.t_first_token is None:
+            self.t_first_token = time.perf_counter()
+
+    # ----------------------------------------------------------- degenerate-repetition stop
+    def has_degenerate_repetition(self) -> bool:
+        completion = self.num_completion_tokens
+        if completion < 32:
+            return False
+        if self._same_token_streak() >= 32:
+            return True
+        max_period = min(64, completion // 2)
+        for period in range(16, max_period + 1, 8):
+            if self._ends_with_two_identical_blocks(period):
+                return True
+        return completion >= 48 and self._has_overused_ngram()
+
+    def _same_token_streak(self) -> int:
+        streak = 0
+        ids = self.token_ids
+        for i in range(self.num_tokens - 1, self.num_prompt_tokens - 1, -1):
+            if ids[i] != self.last_token:
+                break
+            streak += 1
+        return streak
+
+    def _ends_with_two_identical_blocks(self, period: int) -> bool:
+        start = self.num_tokens - 2 * period
+        if start < self.num_prompt_tokens:
+            return False
+        ids = self.token_ids
+        return ids[start:start + period] == ids[start + period:start + 2 * period]
+
+    def _has_overused_ngram(self, ngram: int = 12, min_hits: int = 3) -> bool:
+        window = min(self.num_completion_tokens, 128)
+        if window < ngram * min_hits:
+            return False
+        start0 = self.num_tokens - window
+        counts = {}
+        ids = self.token_ids
+        for s in range(start0, self.num_tokens - ngram + 1):
+            key = tuple(ids[s:s + ngram])
+            c = counts.get(key, 0) + 1
+            if c >= min_hits:
+                return True
+            counts[key] = c
+        return False

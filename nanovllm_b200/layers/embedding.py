@@ -1,0 +1,64 @@
+"""Vocab-parallel embedding and LM head.
+
+Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/layers/VocabParallelEmbedding.java:32-253.
+The embedding gathers rows (optionally scaled, Gemma's sqrt(H)); the LM head scores only the LAST token of each
+prefill sequence (cu_seqlens_q[i+1] - 1, VocabParallelEmbedding.java:227-252) and every row in decode.
+With TP each rank owns V/TP vocabulary rows: the embedding zeroes ids outside its range and all-reduces; the
+head computes its logit slice and all-gathers it so every rank samples the same token.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..engine.context import get_context
+from ..parallel import state as ps
+
+
+class VocabParallelEmbedding:
+    def __init__(self, weight: torch.Tensor, scale: float = 1.0):
+        r, s = ps.tp_rank(), ps.tp_size()
+        self.vocab = weight.shape[0]
+        if s > 1:
+            per = (self.vocab + s - 1) // s
+            self.vstart = r * per
+            self.vend = min(self.vocab, (r + 1) * per)
+            self.weight = weight[self.vstart:self.vend].contiguous()
+        else:
+            self.vstart, self.vend, self.weight = 0, self.vocab, weight
+        self.scale = scale
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        w = self.weight
+        if hasattr(w, "embedding"):
+            y = w.embedding(ids, self.scale, self.vstart, self.vend)
+        else:
+            y = ops.embedding(w, ids, self.scale, self.vstart, self.vend)
+        return ps.all_reduce(y)
+
+
+class ParallelLMHead:
+    def __init__(self, weight: torch.Tensor, vocab: Optional[int] = None):
+        r, s = ps.tp_rank(), ps.tp_size()
+        self.vocab = vocab or weight.shape[0]
+        if s > 1 and weight.shape[0] == self.vocab:
+            per = (self.vocab + s - 1) // s
+            w = weight[r * per:min(self.vocab, (r + 1) * per)]
+            if w.shape[0] < per:  # pad the last shard so all_gather sees equal shapes
+                w = torch.cat([w, torch.zeros(per - w.shape[0], w.shape[1], dtype=w.dtype, device=w.device)])
+            self.weight = w.contiguous()
+        else:
+            self.weight = weight
+
+    def __call__(self, hidden: torch.Tensor, gather_last: bool = True) -> torch.Tensor:
+        if gather_last:
+            ctx = get_context()
+            if ctx.is_prefill:
+                hidden = ops.gather_rows(hidden, ctx.last_token_idx)
+        w = self.weight
+        logits = w.linear(hidden) if hasattr(w, "linear") else ops.linear(hidden, w)
+        if ps.tp_size() > 1:
+            logits = ps.all_gather_last(logits)[:, :self.vocab]
+        return logits

@@ -1,0 +1,152 @@
+"""Linear layers with real tensor-parallel sharding.
+
+The reference's Linear family (nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/layers/Linear.java:26-405)
+binds a kernel per weight type, applies bias and (Gemma4 QAT) input/output SRQ fake-quant; its Column / Row /
+Merged / Qkv subclasses are TP names that never shard.  Here:
+
+* ``ColumnParallelLinear`` keeps rows [r*N/TP, (r+1)*N/TP) of W (output features);
+* ``MergedColumnParallelLinear`` (gate_up) keeps each rank's gate and up slice and stores them interleaved in
+  128-row blocks so the GEMM epilogue computes act(gate) * up on one tile;
+* ``QKVParallelLinear`` keeps each rank's q heads and kv heads (kv heads are replicated when nkv < TP);
+* ``RowParallelLinear`` keeps columns [r*K/TP, (r+1)*K/TP) of W and all-reduces (or reduce-scatters in the
+  sequence-parallel path) the partial outputs.
+
+Weights may also be packed (GGUF blocks, Gemma QAT ints): ``PackedWeight`` objects expose ``linear(x)`` and are
+dispatched here without densifying when the fused dequant GEMM supports the type.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import ops
+from ..parallel import state as ps
+
+
+def shard_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = w.shape[0]
+    assert n % size == 0, f"dimension {n} not divisible by TP={size}"
+    k = n // size
+    return w[rank * k:(rank + 1) * k]
+
+
+def shard_cols(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
+    n = w.shape[1]
+    assert n % size == 0, f"dimension {n} not divisible by TP={size}"
+    k = n // size
+    return w[:, rank * k:(rank + 1) * k]
+
+
+class LinearBase:
+    weight: torch.Tensor
+    bias: Optional[torch.Tensor]
+
+    def __init__(self):
+        self.bias = None
+        self.act = ops.ACT_NONE
+
+    def _mm(self, x: torch.Tensor, act: int = ops.ACT_NONE) -> torch.Tensor:
+        w = self.weight
+        if hasattr(w, "linear"):  # packed weight (GGUF / QAT): fused dequant path
+            y = w.linear(x)
+            if act != ops.ACT_NONE:
+                y = ops.act_mul(y, act, interleaved=True)
+        else:
+            y = ops.linear(x, w, act)
+        if self.bias is not None:
+            ops.bias_act_(y, self.bias, ops.BIAS_ACT_NONE)
+        return y
+
+
+class ReplicatedLinear(LinearBase):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None):
+        super().__init__()
+        self.weight, self.bias = weight, bias
+
+    def __call__(self, x):
+        return self._mm(x)
+
+
+class ColumnParallelLinear(LinearBase):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, shard: bool = True):
+        super().__init__()
+        r, s = ps.tp_rank(), ps.tp_size()
+        self.weight = shard_rows(weight, r, s) if (shard and s > 1) else weight
+        self.bias = shard_rows(bias, r, s) if (bias is not None and shard and s > 1) else bias
+
+    def __call__(self, x):
+        return self._mm(x)
+
+
+class MergedColumnParallelLinear(LinearBase):
+    """gate_up: per-rank [gate_r; up_r] interleaved in 128-row blocks; __call__ returns act(gate) * up."""
+
+    def __init__(self, gate: torch.Tensor, up: torch.Tensor, act: int, interleave_block: int = 128):
+        super().__init__()
+        r, s = ps.tp_rank(), ps.tp_size()
+        g = shard_rows(gate, r, s) if s > 1 else gate
+        u = shard_rows(up, r, s) if s > 1 else up
+        self.act = act
+        self.intermediate = g.shape[0]
+        if self.intermediate % interleave_block == 0:
+            self.weight = ops.ref.interleave_gate_up(torch.cat([g, u], 0), interleave_block).contiguous()
+            self.interleaved = True
+        else:
+            self.weight = torch.cat([g, u], 0).contiguous()
+            self.interleaved = False
+
+    def __call__(self, x):
+        if self.interleaved and not hasattr(self.weight, "linear"):
+            return ops.linear(x, self.weight, self.act)
+        y = self._mm(x) if hasattr(self.weight, "linear") else ops.linear(x, self.weight)
+        return ops.act_mul(y, self.act, interleaved=self.interleaved)
+
+
+class QKVParallelLinear(LinearBase):
+    def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int, num_kv_heads: int,
+                 head_dim: int, bq=None, bk=None, bv=None):
+        super().__init__()
+        r, s = ps.tp_rank(), ps.tp_size()
+        assert num_heads % s == 0, "num_heads must be divisible by TP"
+        self.nq = num_heads // s
+        if num_kv_heads >= s:
+            assert num_kv_heads % s == 0
+            self.nkv = num_kv_heads // s
+            kv_rank = r
+            kv_parts = s
+        else:  # replicate kv heads: rank r uses kv head r * nkv / s
+            self.nkv = 1
+            kv_parts = num_kv_heads
+            kv_rank = r * num_kv_heads // s
+        self.head_dim = head_dim
+        qs = shard_rows(q, r, s) if s > 1 else q
+        ks = shard_rows(k, kv_rank, kv_parts) if s > 1 else k
+        vs = shard_rows(v, kv_rank, kv_parts) if s > 1 else v
+        self.weight = torch.cat([qs, ks, vs], 0).contiguous()
+        if bq is not None:
+            bqs = shard_rows(bq, r, s) if s > 1 else bq
+            bks = shard_rows(bk, kv_rank, kv_parts) if s > 1 else bk
+            bvs = shard_rows(bv, kv_rank, kv_parts) if s > 1 else bv
+            self.bias = torch.cat([bqs, bks, bvs], 0).contiguous()
+
+    def __call__(self, x):
+        return self._mm(x)
+
+
+class RowParallelLinear(LinearBase):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, reduce: bool = True):
+        super().__init__()
+        r, s = ps.tp_rank(), ps.tp_size()
+        self.weight = shard_cols(weight, r, s).contiguous() if s > 1 else weight
+        self.bias = bias  # added once, after the reduction
+        self.reduce = reduce
+
+    def __call__(self, x):
+        w = self.weight
+        y = w.linear(x) if hasattr(w, "linear") else ops.linear(x, w)
+        if self.reduce:
+            ps.all_reduce(y)
+        if self.bias is not None:
+            ops.bias_act_(y, self.bias, ops.BIAS_ACT_NONE)
+        return y

@@ -1,0 +1,273 @@
+"""``LLM``: the engine front door (builder, generate family, cancel, timeout, stats, listeners).
+
+Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/llm/LLM.java:
+* Builder knobs (1443-1946): sampling defaults, deterministic, stop token ids, max_num_batched_tokens,
+  max_num_seqs, max_model_len, KV block size / count, warmup; embedding models are rejected (1883-1886);
+* one in-flight generate per engine (a lock, 178, 774-822); ``cancel()`` sets a flag that is checked between
+  engine steps (370-372, 910-928) and raises GenerationCancelledException; a wall-clock deadline raises
+  GenerationTimeoutException the same way; an interrupted generate clears the scheduler (826-834);
+* prompts are clamped so max_tokens <= max_model_len - prompt length, and a prompt that fills the context is
+  an error (865-874);
+* warmup = one synthetic 64-token prefill + 16 decode steps (277-301).
+New here: per-request TTFT / TPOT (``GenerationStats``), an online request API (``add_request`` / ``step`` /
+``abort``) for Poisson serving, and TP=1/2/4/8 through torch.distributed (SPMD: every rank runs this engine).
+"""
+from __future__ import annotations
+
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Dict, Iterable, List, Optional, Sequence as Seq, Union
+
+import torch
+
+from .config import EngineConfig, HfConfig
+from .engine.model_runner import ModelRunner
+from .engine.scheduler import Scheduler
+from .engine.sequence import Sequence
+from .exceptions import GenerationCancelledException, GenerationTimeoutException, NanoLlvmException
+from .parallel import state as ps
+from .sampling_params import SamplingParams
+
+
+@dataclass
+class GenerationStats:
+    """Counts and timings of one generate call (GenerationStats.java:23-63) plus TTFT / TPOT."""
+    prompt_tokens: int = 0
+    completion_tokens: int = 0
+    elapsed_s: float = 0.0
+    ttft_s: List[float] = field(default_factory=list)
+    tpot_s: List[float] = field(default_factory=list)
+    prefill_steps: int = 0
+    decode_steps: int = 0
+    preemptions: int = 0
+
+    @property
+    def completion_tokens_per_second(self) -> float:
+        return self.completion_tokens / self.elapsed_s if self.elapsed_s > 0 else 0.0
+
+    @staticmethod
+    def _pct(xs: List[float], q: float) -> float:
+        if not xs:
+            return float("nan")
+        s = sorted(xs)
+        return s[min(len(s) - 1, int(round(q * (len(s) - 1))))]
+
+    def p50_ttft(self) -> float:
+        return self._pct(self.ttft_s, 0.5)
+
+    def p99_ttft(self) -> float:
+        return self._pct(self.ttft_s, 0.99)
+
+    def p50_tpot(self) -> float:
+        return self._pct(self.tpot_s, 0.5)
+
+
+@dataclass
+class GenerationOutput:
+    prompt_token_ids: List[int]
+    token_ids: List[int]
+    text: Optional[str] = None
+    finish_reason: str = "stop"
+    ttft_s: Optional[float] = None
+
+
+class LLM:
+    def __init__(self, model, cfg: Optional[EngineConfig] = None, sampling: Optional[SamplingParams] = None,
+                 device: Optional[Union[str, torch.device]] = None, warmup: bool = False):
+        """``model``: an ``LlmModel`` (from LlmModelFactory) or a (HfConfig, weights-dict) tuple."""
+        from .api.model import LlmModel
+        if isinstance(model, LlmModel):
+            if model.is_embedding():
+                raise ValueError("embedding models cannot back an LLM engine (use LlmModel.embed)")
+            hf, weights, tokenizer = model.hf_config, model.weights, model.tokenizer
+        else:
+            hf, weights = model
+            tokenizer = None
+        self.hf: HfConfig = hf
+        self.tokenizer = tokenizer
+        self.model_handle = model
+        self.cfg = cfg or EngineConfig()
+        self.cfg.clamp_to_model(hf)
+        self.default_sampling = sampling or SamplingParams()
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+        self.device = torch.device(device)
+        from .models.registry import causal_model_class
+        cls = causal_model_class(hf)
+        self.model = cls(hf, weights, self.device, max_pos=self.cfg.max_model_len + 1)
+        stop = list(self.cfg.stop_token_ids)
+        if not stop and tokenizer is not None:
+            stop = list(tokenizer.stop_token_ids())
+        if not stop and self.cfg.eos >= 0:
+            stop = [self.cfg.eos]
+        self.runner = ModelRunner(self.model, hf, self.cfg, self.device)
+        self.scheduler = Scheduler(self.cfg, self.runner.num_blocks, stop, on_release=self.runner.release_state)
+        self._lock = threading.Lock()
+        self._cancel = threading.Event()
+        self._closed = False
+        self.listeners: List[Callable] = []
+        if warmup:
+            self.warmup()
+
+    # ------------------------------------------------------------------ builder
+    class Builder:
+        def __init__(self, model):
+            self._model = model
+            self._cfg = {}
+            self._sampling = SamplingParams()
+            self._device = None
+            self._warmup = False
+
+        def max_num_batched_tokens(self, v): self._cfg["max_num_batched_tokens"] = int(v); return self
+        def max_num_seqs(self, v): self._cfg["max_num_seqs"] = int(v); return self
+        def max_model_len(self, v): self._cfg["max_model_len"] = int(v); return self
+        def kvcache_block_size(self, v): self._cfg["kvcache_block_size"] = int(v); return self
+        def num_kvcache_blocks(self, v): self._cfg["num_kvcache_blocks"] = int(v); return self
+        def gpu_memory_utilization(self, v): self._cfg["gpu_memory_utilization"] = float(v); return self
+        def tensor_parallel_size(self, v): self._cfg["tensor_parallel_size"] = int(v); return self
+        def enforce_eager(self, v=True): self._cfg["enforce_eager"] = bool(v); return self
+        def cuda_graph_max_bs(self, v): self._cfg["cuda_graph_max_bs"] = int(v); return self
+        def stop_token_ids(self, ids): self._cfg["stop_token_ids"] = tuple(int(i) for i in ids); return self
+        def stop_on_degenerate(self, v): self._cfg["stop_on_degenerate"] = bool(v); return self
+        def seed(self, v): self._cfg["seed"] = int(v); return self
+        def sampling(self, sp: SamplingParams): self._sampling = sp; return self
+        def deterministic(self): self._sampling = self._sampling.deterministic(); return self
+        def device(self, d): self._device = d; return self
+        def warmup(self, v=True): self._warmup = bool(v); return self
+
+        def build(self) -> "LLM":
+            return LLM(self._model, EngineConfig(**self._cfg), self._sampling, self._device, self._warmup)
+
+    @staticmethod
+    def builder(model) -> "LLM.Builder":
+        return LLM.Builder(model)
+
+    # ------------------------------------------------------------------ lifecycle
+    def warmup(self) -> None:
+        ids = [[(i * 7919) % max(2, self.hf.vocab_size - 1) + 1 for i in range(64)]]
+        self.generate_token_ids(ids, SamplingParams(max_tokens=16, ignore_eos=True).deterministic())
+
+    def cancel(self) -> None:
+        """Stop the running generate at the next step boundary (thread-safe)."""
+        self._cancel.set()
+
+    def close(self) -> None:
+        if not self._closed:
+            self.scheduler.clear()
+            self.runner.close()
+            self._closed = True
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+    # ------------------------------------------------------------------ online API
+    def add_request(self, prompt_token_ids: List[int], sampling: Optional[SamplingParams] = None,
+                    tag=None) -> Sequence:
+        sp = self._fit_sampling(len(prompt_token_ids), sampling or self.default_sampling)
+        seq = Sequence(prompt_token_ids, sp, self.cfg.kvcache_block_size, user_tag=tag)
+        self.scheduler.add(seq)
+        return seq
+
+    def abort(self, seq: Sequence) -> bool:
+        return self.scheduler.abort(seq.seq_id)
+
+    def has_unfinished(self) -> bool:
+        return not self.scheduler.is_finished()
+
+    def step(self, appended_out: Optional[list] = None):
+        seqs, is_prefill = self.scheduler.schedule()
+        toks = self.runner.run(seqs, is_prefill)
+        finished = self.scheduler.postprocess(seqs, toks, is_prefill, appended_out)
+        for s in finished:
+            s.t_finish = time.perf_counter()
+        return seqs, is_prefill, finished
+
+    def _fit_sampling(self, prompt_len: int, sp: SamplingParams) -> SamplingParams:
+        room = self.cfg.max_model_len - prompt_len
+        if room <= 0:
+            raise ValueError(f"prompt of {prompt_len} tokens leaves no room in max_model_len={self.cfg.max_model_len}")
+        if sp.max_tokens > room:
+            sp = sp.with_(max_tokens=room)
+        return sp
+
+    # ------------------------------------------------------------------ generate family
+    def generate_token_ids(self, prompts: Seq[List[int]], sampling: Optional[Union[SamplingParams, Seq[SamplingParams]]] = None,
+                           on_token: Optional[Callable[[int, int, int], None]] = None,
+                           timeout_s: Optional[float] = None, stats: Optional[GenerationStats] = None
+                           ) -> List[GenerationOutput]:
+        """Generate for a batch of token-id prompts; ``on_token(prompt_index, seq_id, token)`` streams."""
+        if not self._lock.acquire(blocking=False):
+            raise NanoLlvmException("another generate call is already running on this engine")
+        self._cancel.clear()
+        t0 = time.perf_counter()
+        deadline = t0 + timeout_s if timeout_s else None
+        seqs: List[Sequence] = []
+        try:
+            for i, p in enumerate(prompts):
+                sp = sampling[i] if isinstance(sampling, (list, tuple)) else (sampling or self.default_sampling)
+                seqs.append(self.add_request(list(p), sp, tag=i))
+            by_id = {s.seq_id: s for s in seqs}
+            st = stats if stats is not None else GenerationStats()
+            while self.has_unfinished():
+                if self._cancel.is_set():
+                    raise GenerationCancelledException("generation cancelled")
+                if deadline is not None and time.perf_counter() > deadline:
+                    raise GenerationTimeoutException(f"generation exceeded {timeout_s}s")
+                appended = [] if on_token is not None else None
+                _, is_prefill, _ = self.step(appended)
+                if is_prefill:
+                    st.prefill_steps += 1
+                else:
+                    st.decode_steps += 1
+                if appended:
+                    for sid, tok in appended:
+                        s = by_id.get(sid)
+                        if s is not None:
+                            on_token(s.user_tag, sid, tok)
+            st.elapsed_s = time.perf_counter() - t0
+            st.preemptions = self.scheduler.num_preemptions
+            outs = []
+            for s in seqs:
+                st.prompt_tokens += s.num_prompt_tokens
+                st.completion_tokens += s.num_completion_tokens
+                ttft = (s.t_first_token - s.t_arrival) if s.t_first_token else None
+                if ttft is not None:
+                    st.ttft_s.append(ttft)
+                if s.t_first_token and s.t_finish and s.num_completion_tokens > 1:
+                    st.tpot_s.append((s.t_finish - s.t_first_token) / (s.num_completion_tokens - 1))
+                reason = "length" if s.num_completion_tokens >= s.max_tokens else "stop"
+                outs.append(GenerationOutput(s.prompt_token_ids, s.completion_token_ids, None, reason, ttft))
+            self.last_stats = st
+            return outs
+        except BaseException:
+            self.scheduler.clear()
+            raise
+        finally:
+            self._lock.release()
+
+    def generate(self, prompts: Union[str, Seq[str]], sampling: Optional[SamplingParams] = None,
+                 on_token: Optional[Callable] = None, timeout_s: Optional[float] = None) -> List[GenerationOutput]:
+        if self.tokenizer is None:
+            raise NanoLlvmException("this engine has no tokenizer; use generate_token_ids")
+        single = isinstance(prompts, str)
+        texts = [prompts] if single else list(prompts)
+        ids = [self.tokenizer.encode(t) for t in texts]
+        outs = self.generate_token_ids(ids, sampling, on_token, timeout_s)
+        for o in outs:
+            o.text = self.tokenizer.decode(o.token_ids, skip_special=True)
+        return outs
+
+    def complete(self, prompt: str, sampling: Optional[SamplingParams] = None) -> str:
+        return self.generate([prompt], sampling)[0].text
+
+    def chat_once(self, user: str, system: Optional[str] = None, sampling: Optional[SamplingParams] = None) -> str:
+        from .chat.messages import ChatMessage
+        msgs = ([ChatMessage.system(system)] if system else []) + [ChatMessage.user(user)]
+        prompt = self.tokenizer.apply_chat_template(msgs, add_generation_prompt=True)
+        ids = self.tokenizer.encode(prompt, allow_special=True)
+        out = self.generate_token_ids([ids], sampling)[0]
+        return self.tokenizer.decode(out.token_ids, skip_special=True)

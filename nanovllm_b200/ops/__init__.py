@@ -1,0 +1,275 @@
+"""Op layer: CUDA tensors run the sm_100a kernels of ``nanovllm_b200._C``; CPU tensors run the fp32 restatement
+in ``reference_cpu`` (the oracle and the timed CPU baseline).
+
+On a CUDA tensor there is no silent fallback: if the extension did not load, the op raises.  The per-device
+error word (int32) is passed to every kernel that waits on an mbarrier or a peer flag; ``check_device_errors``
+reads it after a synchronisation and raises ``DeviceWaitTimeout`` when a bounded wait gave up.
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from . import reference_cpu as ref
+from ..exceptions import DeviceWaitTimeout
+
+ACT_NONE, ACT_SILU_MUL, ACT_GELU_MUL = ref.ACT_NONE, ref.ACT_SILU_MUL, ref.ACT_GELU_MUL
+BIAS_ACT_NONE, BIAS_ACT_GELU_ERF, BIAS_ACT_GELU_TANH = ref.BIAS_ACT_NONE, ref.BIAS_ACT_GELU_ERF, ref.BIAS_ACT_GELU_TANH
+
+_C = None
+_C_ERROR: Optional[BaseException] = None
+try:  # the extension is built in-tree by setup.py / __graft_entry__.build()
+    from .. import _C as _C  # type: ignore
+except BaseException as e:  # noqa: BLE001 - keep the reason for the loud error below
+    _C_ERROR = e
+
+
+def extension_loaded() -> bool:
+    return _C is not None
+
+
+def _cuda_ext():
+    if _C is None:
+        raise RuntimeError(f"nanovllm_b200._C is not built or failed to load ({_C_ERROR!r}); "
+                           "run `python setup.py build_ext --inplace`")
+    return _C
+
+
+_LAUNCHES = [0]
+
+
+def add_launches(n: int) -> None:
+    """Kernel-launch accounting (CUDA-graph replays add the count recorded at capture)."""
+    _LAUNCHES[0] += int(n)
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]
+
+
+def reset_launch_count() -> None:
+    _LAUNCHES[0] = 0
+
+
+_ERR: Dict[int, torch.Tensor] = {}
+_WS: Dict[int, torch.Tensor] = {}
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _ERR.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=device)
+        _ERR[idx] = t
+    return t
+
+
+def check_device_errors(device: Optional[torch.device] = None) -> None:
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    code = int(error_word(dev).item())
+    if code != 0:
+        error_word(dev).zero_()
+        raise DeviceWaitTimeout(f"device kernel reported error code {code} (1 = mbarrier wait timeout, "
+                                f"2 = peer flag timeout, 3 = bad argument)")
+
+
+def workspace(device: torch.device, numel: int) -> torch.Tensor:
+    """Shared fp32 scratch for split-K partials; grows on demand (pre-size it before CUDA-graph capture)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _WS.get(idx)
+    if t is None or t.numel() < numel:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("gemm workspace must be reserved before CUDA graph capture")
+        t = torch.empty(max(numel, 1 << 20), dtype=torch.float32, device=device)
+        _WS[idx] = t
+    return t
+
+
+def reserve_workspace(device: torch.device, max_m: int, max_n: int, max_k: int) -> None:
+    if _C is None:
+        return
+    splits = max(_C.gemm_splits_for(m, max_n, max_k) for m in (1, 16, 64, 128, 256) if m <= max(1, max_m))
+    workspace(device, splits * min(256, max_m) * max_n)
+
+
+# ------------------------------------------------------------------------------------------------ norms
+def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: int = 0,
+             residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
+             ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+    """Returns (normed, residual).  With ``residual`` the sum x + residual is written back into it."""
+    if not x.is_cuda:
+        y, r = ref.rms_norm(x, weight, eps, mode, residual)
+        if residual is not None:
+            residual.copy_(r)
+            r = residual
+        return y, r
+    if out is None:
+        out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    _cuda_ext().rms_norm(out, x, residual, weight, float(eps), int(mode))
+    add_launches(1)
+    return out, residual
+
+
+def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
+               residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.layer_norm(x, weight, bias, eps, residual)
+    out = torch.empty_like(x)
+    _cuda_ext().layer_norm(out, x.contiguous(), residual, weight, bias, float(eps))
+    add_launches(1)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ rope + kv
+def qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, norm_mode, v_norm, eps, k_cache, v_cache, slots,
+                       nq, nkv, hd, apply_rope=True):
+    """Returns q [T, nq, hd] (normed + rotated); k and v go into the paged caches at ``slots``."""
+    if not qkv.is_cuda:
+        q, _, _ = ref.qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, norm_mode, v_norm, eps, k_cache,
+                                         v_cache, slots, nq, nkv, hd, apply_rope)
+        return q.reshape(qkv.shape[0], nq, hd)
+    q = torch.empty(qkv.shape[0], nq, hd, dtype=qkv.dtype, device=qkv.device)
+    _cuda_ext().qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, int(norm_mode), bool(v_norm), float(eps), q,
+                                   k_cache, v_cache, slots, int(nq), int(nkv), int(hd), bool(apply_rope))
+    add_launches(1)
+    return q
+
+
+# ------------------------------------------------------------------------------------------------ attention
+DECODE_TILE = 64
+
+
+def decode_partition(batch: int, nkv: int, max_len: int, sms: int = 148) -> Tuple[int, int]:
+    """(tiles per split, number of splits) so that batch * nkv * splits covers ~4 CTAs per SM."""
+    tiles = max(1, (max_len + DECODE_TILE - 1) // DECODE_TILE)
+    target = 4 * sms
+    per = max(1, min(16, (batch * nkv * tiles + target - 1) // target))
+    per = max(per, (tiles + 63) // 64)  # at most 64 splits
+    return per, (tiles + per - 1) // per
+
+
+def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap=0.0, window=0, max_len=None,
+                 out=None, scratch=None):
+    if not q.is_cuda:
+        return ref.paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap, window)
+    B, nq, hd = q.shape
+    nkv = k_cache.shape[1]
+    if max_len is None:
+        max_len = block_tables.shape[1] * k_cache.shape[2]
+    per, nsplit = decode_partition(B, nkv, max_len)
+    if out is None:
+        out = torch.empty_like(q)
+    if nsplit > 1:
+        need = B * nq * nsplit * (hd + 1)
+        if scratch is None or scratch.numel() < need:
+            scratch = torch.empty(need, dtype=torch.float32, device=q.device)
+        part_o = scratch[:B * nq * nsplit * hd]
+        part_lse = scratch[B * nq * nsplit * hd:need]
+    else:
+        part_o = part_lse = out  # unused
+    _cuda_ext().paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, part_o, part_lse, float(scale),
+                             float(softcap), int(window), int(per), int(nsplit), error_word(q.device))
+    add_launches(2 if nsplit > 1 else 1)
+    return out
+
+
+def decode_scratch_numel(batch: int, nq: int, nkv: int, hd: int, max_len: int) -> int:
+    _, nsplit = decode_partition(batch, nkv, max_len)
+    return batch * nq * nsplit * (hd + 1) if nsplit > 1 else 0
+
+
+def prefill_attention(q, cu_q, cu_k, max_q, nq, nkv, hd, scale, softcap=0.0, window=0, causal=True,
+                      k_cache=None, v_cache=None, block_tables=None, kv_src=None, out=None):
+    if not q.is_cuda:
+        return ref.prefill_attention(q.reshape(q.shape[0], nq, hd), cu_q, cu_k, nq, nkv, hd, scale, softcap, window,
+                                     causal, k_cache, v_cache, block_tables, kv_src)
+    if out is None:
+        out = torch.empty(q.shape[0], nq, hd, dtype=q.dtype, device=q.device)
+    _cuda_ext().prefill_attention(q, out, cu_q, cu_k, int(max_q), k_cache, v_cache, block_tables, kv_src, int(nq),
+                                  int(nkv), int(hd), float(scale), float(softcap), int(window), bool(causal),
+                                  error_word(q.device))
+    add_launches(1)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ linear
+def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[torch.Tensor] = None,
+           force_splits: int = 0) -> torch.Tensor:
+    """y = x @ w^T on the tcgen05 GEMM.  act != 0 expects gate/up rows interleaved in 128-row blocks."""
+    if not x.is_cuda:
+        return ref.linear(x, w, act)
+    M, K = x.shape
+    N = w.shape[0]
+    ncols = N // 2 if act != ACT_NONE else N
+    if out is None:
+        out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
+    C = _cuda_ext()
+    ws = None
+    launches = 1
+    if M <= 256:
+        splits = force_splits if force_splits > 0 else C.gemm_splits_for(M, N, K)
+        if splits > 1 or act != ACT_NONE:
+            ws = workspace(x.device, splits * M * N)
+            launches = 2
+    C.gemm(x, w, out, int(act), ws, int(force_splits), error_word(x.device))
+    add_launches(launches)
+    return out
+
+
+def act_mul(x: torch.Tensor, act: int, interleaved: bool = False) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.act_mul(x, act, interleaved)
+    out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    _cuda_ext().act_mul(out, x, int(act), bool(interleaved))
+    add_launches(1)
+    return out
+
+
+def bias_act_(x: torch.Tensor, bias: Optional[torch.Tensor], act: int = BIAS_ACT_NONE) -> torch.Tensor:
+    if not x.is_cuda:
+        x.copy_(ref.bias_act(x, bias, act))
+        return x
+    _cuda_ext().bias_act(x, bias, int(act))
+    add_launches(1)
+    return x
+
+
+def embedding(table: torch.Tensor, ids: torch.Tensor, scale: float = 1.0, vstart: int = 0,
+              vend: Optional[int] = None) -> torch.Tensor:
+    vend = table.shape[0] + vstart if vend is None else vend
+    if not table.is_cuda:
+        return ref.embedding(table, ids, scale, vstart, vend)
+    out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    _cuda_ext().embedding(out, table, ids.long(), float(scale), int(vstart), int(vend))
+    add_launches(1)
+    return out
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    if not src.is_cuda:
+        return src[idx.long()]
+    out = torch.empty(idx.numel(), src.shape[1], dtype=src.dtype, device=src.device)
+    _cuda_ext().gather_rows(out, src, idx.long())
+    add_launches(1)
+    return out
+
+
+def mean_pool_l2(x: torch.Tensor, cu: torch.Tensor) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.mean_pool_l2(x, cu)
+    out = torch.empty(cu.numel() - 1, x.shape[1], dtype=torch.float32, device=x.device)
+    _cuda_ext().mean_pool_l2(out, x, cu.int())
+    add_launches(1)
+    return out
+
+
+def sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float = 0.0, out=None) -> torch.Tensor:
+    if not logits.is_cuda:
+        return ref.sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap)
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
+    _cuda_ext().sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, float(softcap), out)
+    add_launches(1)
+    return out

@@ -1,0 +1,193 @@
+"""Scheduler / block manager / sequence semantics (reference: engine/Scheduler.java, BlockManager.java,
+Sequence.java and the corresponding cases of CoreUnitTest: blockManagerPrefixCache, detectsDegenerateTokenRepetition)."""
+import pytest
+
+from nanovllm_b200.config import EngineConfig
+from nanovllm_b200.engine.block_manager import BlockManager, compute_hash
+from nanovllm_b200.engine.scheduler import Scheduler
+from nanovllm_b200.engine.sequence import Sequence, SequenceStatus
+from nanovllm_b200.sampling_params import SamplingParams
+
+
+def seq(n, start=0, bs=256, **kw):
+    return Sequence(list(range(start, start + n)), SamplingParams(**kw) if kw else None, bs)
+
+
+def test_block_math():
+    s = seq(513)
+    assert s.num_blocks == 3 and s.last_block_num_tokens == 1
+    assert s.block(1) == list(range(256, 512))
+
+
+def test_block_size_must_be_multiple_of_256():
+    with pytest.raises(ValueError):
+        EngineConfig(kvcache_block_size=128)
+
+
+def test_prefix_cache_reuses_full_blocks_only():
+    bm = BlockManager(16, 256)
+    a = seq(600)
+    assert bm.can_allocate(a) == 0
+    bm.allocate(a, 0)
+    a.num_scheduled_tokens = 600
+    bm.hash_blocks(a)  # publishes blocks 0 and 1 (full), not the partial third
+    b = seq(600)
+    cached = bm.can_allocate(b)
+    assert cached == 2
+    bm.allocate(b, cached)
+    assert b.block_table[:2] == a.block_table[:2]
+    assert b.block_table[2] != a.block_table[2]
+    assert b.num_cached_tokens == 512
+    assert bm.blocks[a.block_table[0]].ref_count == 2
+    bm.deallocate(a)
+    assert bm.blocks[b.block_table[0]].ref_count == 1
+    bm.deallocate(b)
+    assert bm.num_free_blocks == 16
+
+
+def test_last_block_never_cached():
+    bm = BlockManager(8, 256)
+    a = seq(512)
+    bm.allocate(a, 0)
+    a.num_scheduled_tokens = 512
+    bm.hash_blocks(a)
+    b = seq(512)
+    assert bm.can_allocate(b) == 1  # the second (last) block is not a hit even though it is full
+
+
+def test_hash_chain_depends_on_prefix():
+    assert compute_hash([1, 2, 3]) != compute_hash([1, 2, 3], prefix=5)
+
+
+def test_may_append_allocates_on_new_page():
+    bm = BlockManager(4, 256)
+    s = seq(256)
+    bm.allocate(s, 0)
+    assert len(s.block_table) == 1
+    s.append_token(7)  # len 257 -> 257 % 256 == 1
+    assert bm.can_append(s)
+    bm.may_append(s)
+    assert len(s.block_table) == 2
+
+
+def test_scheduler_prefill_first_then_decode():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=1000, max_model_len=2048)
+    sch = Scheduler(cfg, 32)
+    a, b = seq(100), seq(50)
+    sch.add(a)
+    sch.add(b)
+    batch, pre = sch.schedule()
+    assert pre and batch == [a, b]
+    sch.postprocess(batch, [1, 2], True)
+    assert a.completion_token_ids == [1] and b.completion_token_ids == [2]
+    batch, pre = sch.schedule()
+    assert not pre and batch == [a, b]
+
+
+def test_chunked_prefill_keeps_head_waiting():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=300, max_model_len=4096)
+    sch = Scheduler(cfg, 32)
+    a = seq(700)
+    sch.add(a)
+    batch, pre = sch.schedule()
+    assert pre and a.num_scheduled_tokens == 300 and a.status == SequenceStatus.WAITING
+    sch.postprocess(batch, [9], True)
+    assert a.num_completion_tokens == 0 and a.num_cached_tokens == 300  # mid-prompt token discarded
+    batch, _ = sch.schedule()
+    assert a.num_scheduled_tokens == 300
+    sch.postprocess(batch, [9], True)
+    batch, _ = sch.schedule()
+    assert a.num_scheduled_tokens == 100 and a.status == SequenceStatus.RUNNING
+    sch.postprocess(batch, [5], True)
+    assert a.completion_token_ids == [5]
+
+
+def test_second_prompt_not_chunked_when_budget_short():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=300, max_model_len=4096)
+    sch = Scheduler(cfg, 32)
+    a, b = seq(200), seq(200, start=1000)
+    sch.add(a)
+    sch.add(b)
+    batch, _ = sch.schedule()
+    assert batch == [a]
+
+
+def test_preemption_takes_running_tail():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=4096, max_model_len=4096)
+    sch = Scheduler(cfg, 2)
+    a, b = seq(256), seq(256, start=500)
+    sch.add(a)
+    sch.add(b)
+    batch, pre = sch.schedule()
+    assert pre and len(batch) == 2
+    sch.postprocess(batch, [1, 1], True)  # both now need a second page for the next decode token
+    batch, pre = sch.schedule()
+    assert not pre
+    assert batch == [a] and b.status == SequenceStatus.WAITING and sch.waiting[0] is b
+    assert sch.num_preemptions == 1 and not b.block_table
+
+
+def test_stop_rules():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=4096, max_model_len=4096, eos=3)
+    sch = Scheduler(cfg, 8)
+    a = seq(10, max_tokens=5)
+    b = seq(10, start=50, max_tokens=5, ignore_eos=True)
+    sch.add(a)
+    sch.add(b)
+    batch, pre = sch.schedule()
+    fin = sch.postprocess(batch, [3, 3], True)
+    assert fin == [a] and a.is_finished and not b.is_finished
+    for _ in range(4):
+        batch, _ = sch.schedule()
+        fin = sch.postprocess(batch, [3], False)
+    assert b.is_finished and b.num_completion_tokens == 5
+
+
+def test_degenerate_repetition():
+    s = seq(4)
+    for _ in range(31):
+        s.append_token(7)
+    assert not s.has_degenerate_repetition()
+    s.append_token(7)
+    assert s.has_degenerate_repetition()
+    p = seq(4)
+    for i in range(32):
+        p.append_token(100 + (i % 16))
+    assert p.has_degenerate_repetition()  # two identical halves of period 16
+    r = seq(4)
+    for i in range(40):
+        r.append_token(100 + (i % 20))
+    assert not r.has_degenerate_repetition()  # period 20 is not probed and < 48 tokens for the n-gram rule
+    for i in range(40, 60):
+        r.append_token(100 + (i % 20))
+    assert r.has_degenerate_repetition()  # a 12-gram now occurs 3 times in the window
+    q = seq(4)
+    for i in range(64):
+        q.append_token(i)
+    assert not q.has_degenerate_repetition()
+
+
+def test_sampling_params_validation():
+    with pytest.raises(ValueError):
+        SamplingParams(temperature=0.0)
+    with pytest.raises(ValueError):
+        SamplingParams(top_p=0.0)
+    with pytest.raises(ValueError):
+        SamplingParams(max_tokens=0)
+    sp = SamplingParams.builder().temperature(0.7).top_k(5).seed(3).build()
+    assert sp.deterministic().top_k == 1 and sp.deterministic().top_p == 1.0
+    d = SamplingParams()
+    assert (d.temperature, d.top_p, d.top_k, d.max_tokens) == (0.6, 0.95, 0, 256)
+
+
+def test_abort_and_clear_release_blocks():
+    cfg = EngineConfig(max_num_seqs=4, max_num_batched_tokens=4096, max_model_len=4096)
+    released = []
+    sch = Scheduler(cfg, 8, on_release=released.append)
+    a, b = seq(300), seq(20, start=900)
+    sch.add(a)
+    sch.add(b)
+    sch.schedule()
+    assert sch.abort(a.seq_id) and a in released
+    sch.clear()
+    assert sch.block_manager.num_free_blocks == 8 and sch.is_finished()
