@@ -131,6 +131,15 @@ def run_ours(args):
     for _ in range(args.warmup):
         timed_step()
     step_ms.clear()
+    if args.profile_steps > 0:
+        # a capture window for `ncu --profile-from-start off`: only these decode steps are profiled
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(args.profile_steps):
+            timed_step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        step_ms.clear()
     ops.reset_launch_count()
     clock_path = os.path.join("gpurun_out" if os.path.isdir("gpurun_out") else "/tmp", f"bench_clocks_r{rank}.csv")
     sampler = _clock_sampler_start(clock_path) if rank == 0 else None
@@ -146,6 +155,7 @@ def run_ours(args):
     if sampler is not None:
         time.sleep(0.3)
         sampler.terminate()
+        sampler.wait()
     launches = ops.launch_count()
     dev_ms = sum(step_ms)
     t = torch.tensor([dev_ms, wall * 1000.0], dtype=torch.float64, device=dev)
@@ -187,6 +197,8 @@ def main():
     ap.add_argument("--min-prompt", type=int, default=512)
     ap.add_argument("--max-prompt", type=int, default=8192)
     ap.add_argument("--prefill-chunk", type=int, default=16384)
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="decode steps run between cudaProfilerStart/Stop before the timed region")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -1,0 +1,185 @@
+"""Per-kernel microbenchmarks (CUDA-event timed, L2-defeating operand rotation) with roofline fractions.
+
+    python -m nanovllm_b200.ops.microbench [--only gemm,decode,prefill,norm,rope,sample] [--iters N]
+
+Each case allocates enough copies of its operands that one sweep over them exceeds the 126 MB L2, and cycles
+through the copies between timed launches, so DRAM numbers are not L2 hits.  Bandwidth fractions are against
+MEASURED_PEAKS.json (hbm_gbs, bf16_tflops) when present, else the pool fallback (6650 GB/s, 1590 TFLOP/s).
+GEMM cases also time torch.matmul (cuBLAS) on the same operands for comparison.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+from .. import ops
+
+L2_BYTES = 126 << 20
+
+
+def peaks():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def _copies(bytes_per_copy: int) -> int:
+    return max(1, min(64, (3 * L2_BYTES) // max(1, bytes_per_copy) + 1))
+
+
+def time_fn(fns, iters: int, warmup: int = 3) -> float:
+    """Mean microseconds per call, cycling through ``fns`` (one per operand copy)."""
+    for i in range(warmup):
+        fns[i % len(fns)]()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(iters):
+        fns[i % len(fns)]()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1000.0 / iters
+
+
+def bench_gemm(M, N, K, iters, act=0):
+    dev = "cuda"
+    wbytes = N * K * 2
+    n = _copies(wbytes + M * K * 2)
+    ws = [(torch.randn(N, K, device=dev) * 0.02).bfloat16() for _ in range(n)]
+    xs = [torch.randn(M, K, device=dev).bfloat16() for _ in range(n)]
+    ours = time_fn([lambda w=w, x=x: ops.linear(x, w, act) for w, x in zip(ws, xs)], iters)
+    cublas = time_fn([lambda w=w, x=x: torch.matmul(x, w.t()) for w, x in zip(ws, xs)], iters)
+    out_cols = N // 2 if act else N
+    byts = wbytes + M * K * 2 + M * out_cols * 2
+    flops = 2.0 * M * N * K
+    return {"case": f"gemm M={M} N={N} K={K}" + (" act" if act else ""), "us": round(ours, 2),
+            "cublas_us": round(cublas, 2), "TBps": round(byts / ours / 1e6, 3), "TFLOPs": round(flops / ours / 1e6, 1)}
+
+
+def bench_decode(B, ctx, nq, nkv, hd, iters):
+    dev = "cuda"
+    BS = 256
+    nblk = (ctx + BS - 1) // BS
+    kv_bytes = 2 * B * ctx * nkv * hd * 2
+    n = _copies(kv_bytes)
+    caches = []
+    for _ in range(n):
+        kc = torch.randn(B * nblk, nkv, BS, hd, device=dev).bfloat16()
+        vc = torch.randn(B * nblk, nkv, BS, hd, device=dev).bfloat16()
+        caches.append((kc, vc))
+    bt = torch.arange(B * nblk, device=dev, dtype=torch.int32).view(B, nblk)
+    lens = torch.full((B,), ctx, device=dev, dtype=torch.int32)
+    q = torch.randn(B, nq, hd, device=dev).bfloat16()
+    scratch = torch.empty(ops.decode_scratch_numel(B, nq, nkv, hd, ctx) + 1, device=dev)
+    us = time_fn([lambda c=c: ops.paged_decode(q, c[0], c[1], bt, lens, hd ** -0.5, max_len=ctx, scratch=scratch)
+                  for c in caches], iters)
+    return {"case": f"decode_attn B={B} ctx={ctx} nq={nq} nkv={nkv} hd={hd}", "us": round(us, 2),
+            "TBps": round(kv_bytes / us / 1e6, 3)}
+
+
+def bench_prefill(T, nq, nkv, hd, iters):
+    dev = "cuda"
+    BS = 256
+    nblk = (T + BS - 1) // BS
+    kc = torch.randn(nblk, nkv, BS, hd, device=dev).bfloat16()
+    vc = torch.randn(nblk, nkv, BS, hd, device=dev).bfloat16()
+    bt = torch.arange(nblk, device=dev, dtype=torch.int32).view(1, nblk)
+    q = torch.randn(T, nq, hd, device=dev).bfloat16()
+    cu = torch.tensor([0, T], device=dev, dtype=torch.int32)
+    us = time_fn([lambda: ops.prefill_attention(q, cu, cu, T, nq, nkv, hd, hd ** -0.5, 0.0, 0, True, kc, vc, bt)],
+                 iters)
+    flops = 4.0 * T * T / 2 * hd * nq
+    return {"case": f"prefill_attn T={T} nq={nq} nkv={nkv} hd={hd} causal", "us": round(us, 2),
+            "TFLOPs": round(flops / us / 1e6, 1)}
+
+
+def bench_norm(T, H, iters):
+    dev = "cuda"
+    n = _copies(3 * T * H * 2)
+    xs = [torch.randn(T, H, device=dev).bfloat16() for _ in range(n)]
+    rs = [torch.randn(T, H, device=dev).bfloat16() for _ in range(n)]
+    w = torch.ones(H, device=dev).bfloat16()
+    us = time_fn([lambda x=x, r=r: ops.rms_norm(x, w, 1e-6, 0, r) for x, r in zip(xs, rs)], iters)
+    return {"case": f"add_rms_norm T={T} H={H}", "us": round(us, 2), "TBps": round(4 * T * H * 2 / us / 1e6, 3)}
+
+
+def bench_rope(T, nq, nkv, hd, iters):
+    dev = "cuda"
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=dev).bfloat16()
+    pos = torch.arange(T, device=dev)
+    cs = ops.ref.rope_cos_sin(hd, T + 1, 1e6, device=dev)
+    nb = (T + 255) // 256
+    kc = torch.zeros(nb, nkv, 256, hd, device=dev).bfloat16()
+    vc = torch.zeros_like(kc)
+    slots = torch.arange(T, device=dev, dtype=torch.int32)
+    w = torch.ones(hd, device=dev).bfloat16()
+    us = time_fn([lambda: ops.qk_norm_rope_store(qkv, pos, cs, w, w, 0, False, 1e-6, kc, vc, slots, nq, nkv, hd)],
+                 iters)
+    return {"case": f"qk_norm_rope_store T={T} nq={nq} nkv={nkv} hd={hd}", "us": round(us, 2),
+            "TBps": round(2 * T * (nq + 2 * nkv) * hd * 2 / us / 1e6, 3)}
+
+
+def bench_sample(B, V, iters, greedy):
+    dev = "cuda"
+    logits = torch.randn(B, V, device=dev).bfloat16()
+    f = lambda n, v, dt: torch.full((n,), v, device=dev, dtype=dt)  # noqa: E731
+    args = (f(B, 0.8, torch.float32), f(B, 1 if greedy else 50, torch.int32), f(B, 1.0 if greedy else 0.9, torch.float32),
+            f(B, 1, torch.int64), torch.arange(B, device=dev), f(B, 3, torch.int32))
+    us = time_fn([lambda: ops.sample(logits, *args)], iters)
+    return {"case": f"sample B={B} V={V} {'greedy' if greedy else 'top-k50/top-p0.9'}", "us": round(us, 2)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,decode,prefill,norm,rope,sample")
+    ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args()
+    hbm, tflops, src = peaks()
+    only = set(a.only.split(","))
+    rows = []
+    if "gemm" in only:
+        # Qwen3-8B decode (M = batch) and prefill (M = chunk) shapes
+        for M in (1, 32, 128, 256):
+            for N, K, act in ((6144, 4096, 0), (4096, 4096, 0), (24576, 4096, 1), (4096, 12288, 0)):
+                rows.append(bench_gemm(M, N, K, a.iters, act))
+        rows.append(bench_gemm(128, 151936, 4096, a.iters))
+        for M in (2048, 8192):
+            for N, K, act in ((6144, 4096, 0), (24576, 4096, 1), (4096, 12288, 0)):
+                rows.append(bench_gemm(M, N, K, max(5, a.iters // 5), act))
+    if "decode" in only:
+        for B, ctx in ((1, 4096), (32, 2048), (128, 4352), (128, 8192)):
+            rows.append(bench_decode(B, ctx, 32, 8, 128, a.iters))
+    if "prefill" in only:
+        for T in (2048, 8192):
+            rows.append(bench_prefill(T, 32, 8, 128, max(5, a.iters // 5)))
+    if "norm" in only:
+        rows.append(bench_norm(128, 4096, a.iters))
+        rows.append(bench_norm(8192, 4096, a.iters))
+    if "rope" in only:
+        rows.append(bench_rope(128, 32, 8, 128, a.iters))
+        rows.append(bench_rope(8192, 32, 8, 128, a.iters))
+    if "sample" in only:
+        rows.append(bench_sample(128, 151936, a.iters, True))
+        rows.append(bench_sample(128, 151936, a.iters, False))
+    for r in rows:
+        if "TBps" in r:
+            r["hbm_frac_" + src] = round(r["TBps"] * 1000 / hbm, 3)
+        if "TFLOPs" in r:
+            r["tensor_frac_" + src] = round(r["TFLOPs"] / tflops, 3)
+        print(json.dumps(r), flush=True)
+    if a.out:
+        with open(a.out, "w") as f:
+            for r in rows:
+                f.write(json.dumps(r) + "\n")
+
+
+if __name__ == "__main__":
+    main()
