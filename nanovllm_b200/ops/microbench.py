@@ -141,10 +141,20 @@ def main():
     ap.add_argument("--only", default="gemm,decode,prefill,norm,rope,sample")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--gemm", default=None, help="single GEMM case M,N,K[,act] (e.g. for an ncu capture)")
+    ap.add_argument("--decode", default=None, help="single decode-attention case B,ctx,nq,nkv,hd")
     a = ap.parse_args()
     hbm, tflops, src = peaks()
     only = set(a.only.split(","))
     rows = []
+    if a.gemm or a.decode:
+        only = set()
+        if a.gemm:
+            v = [int(x) for x in a.gemm.split(",")]
+            rows.append(bench_gemm(v[0], v[1], v[2], a.iters, v[3] if len(v) > 3 else 0))
+        if a.decode:
+            v = [int(x) for x in a.decode.split(",")]
+            rows.append(bench_decode(v[0], v[1], v[2], v[3], v[4], a.iters))
     if "gemm" in only:
         # Qwen3-8B decode (M = batch) and prefill (M = chunk) shapes
         for M in (1, 32, 128, 256):
