@@ -2,14 +2,14 @@
 #include <torch/extension.h>
 
 void rms_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual,
-                   c10::optional<torch::Tensor> weight, double eps, int64_t mode);
+                   c10::optional<torch::Tensor> weight, double eps, int64_t mode, c10::optional<torch::Tensor> xpart);
 void layer_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual, torch::Tensor weight,
                      torch::Tensor bias, double eps);
 void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::Tensor cos_sin,
                              c10::optional<torch::Tensor> q_w, c10::optional<torch::Tensor> k_w, int64_t norm_mode,
                              bool v_norm, double eps, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
                              c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slots, int64_t nq,
-                             int64_t nkv, int64_t head_dim, bool apply_rope);
+                             int64_t nkv, int64_t head_dim, bool apply_rope, c10::optional<torch::Tensor> qkv_part);
 void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_lse,
                        double scale, double softcap, int64_t window, int64_t part_tiles, int64_t nsplit,
@@ -19,9 +19,10 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
                             c10::optional<torch::Tensor> block_tables, c10::optional<torch::Tensor> kv_src,
                             int64_t nq, int64_t nkv, int64_t hd, double scale, double softcap, int64_t window,
                             bool causal, c10::optional<torch::Tensor> err);
-void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
-               int64_t force_splits, c10::optional<torch::Tensor> err);
+int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
+                  int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out);
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K);
+void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
 void embedding_cuda(torch::Tensor out, torch::Tensor table, torch::Tensor ids, double scale, int64_t vstart,
                     int64_t vend);
 void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interleaved);
@@ -40,6 +41,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &prefill_attention_cuda);
   m.def("gemm", &gemm_cuda);
   m.def("gemm_splits_for", &gemm_splits_for);
+  m.def("splitk_sum", &splitk_sum_cuda);
   m.def("embedding", &embedding_cuda);
   m.def("act_mul", &act_mul_cuda);
   m.def("bias_act", &bias_act_cuda);

@@ -13,10 +13,10 @@
 //  * two TMEM accumulators (2 x BN columns) so the epilogue of tile t overlaps the main loop of tile t+1.
 //  * prefill-sized M: A = activations, B = weights, bf16 output, optional fused SiLU(gate)*up / GELU(gate)*up
 //    on gate/up rows interleaved in 128-row blocks (one 256-wide tile holds 128 gate + 128 up columns).
-//  * decode-sized M (<= 256 tokens): swap A/B so the weight rows fill the 128-lane MMA M dimension and the
-//    tokens are the N dimension; the K range is split over CTAs so every SM streams weights; partial sums are
-//    written per split in fp32 and reduced in a fixed order (deterministic) by splitk_reduce_kernel, which
-//    also applies the activation.
+//  * decode-sized M (<= 256 tokens): gemm_decode_kernel swaps A/B so the weight rows fill the 128-lane MMA M
+//    dimension and the tokens are the N dimension; the K range is split over the CTAs of a thread-block
+//    cluster so every SM streams weights, and the split partials are reduced through distributed shared memory
+//    in a fixed order (deterministic), with the activation applied there.
 // Every mbarrier wait is bounded; on timeout the kernel records an error code and all roles exit, TMEM is
 // freed, and the host sees the code through the error word.
 #include <torch/extension.h>
@@ -30,7 +30,7 @@ using bf16 = __nv_bfloat16;
 constexpr int BM = 128;
 constexpr int BK = 64;
 
-enum OutMode : int { kOutBf16 = 0, kOutBf16T = 1, kOutPartialT = 2 };
+enum OutMode : int { kOutBf16 = 0 };
 enum Act : int { kActNone = 0, kActSiluMul = 1, kActGeluMul = 2 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
@@ -240,29 +240,6 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
             }
           }
         }
-      } else {
-        // swapped: C^T, i.e. out[token j][feature a_row]; lanes are consecutive features -> coalesced per j
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          nvb::tmem_ld_32x32b_x16(t_row + c, r);
-          nvb::tmem_ld_wait();
-          if (a_row < args.Ma) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int tok = tn * BN + c + j;
-              if (tok < args.Nb) {
-                if (args.out_mode == kOutBf16T) {
-                  reinterpret_cast<bf16*>(args.out)[(long)tok * args.out_ld + a_row] =
-                      __float2bfloat16(__uint_as_float(r[j]));
-                } else {
-                  reinterpret_cast<float*>(args.out)[((long)sp * args.Nb + tok) * args.Ma + a_row] =
-                      __uint_as_float(r[j]);
-                }
-              }
-            }
-          }
-        }
       }
       nvb::tc_fence_before();
       __syncwarp();
@@ -275,27 +252,227 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
   if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
-// partial [splits][M][Ma] fp32 -> out [M][Ma or Ma/2] bf16 (activation on 128-interleaved gate/up rows)
-__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int Ma, bf16* __restrict__ out,
-                                     long out_ld, int act) {
-  const int ncols = act == kActNone ? Ma : Ma / 2;
-  const long total = (long)M * ncols;
-  for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
-    const int tok = idx / ncols, f = idx % ncols;
-    if (act == kActNone) {
-      float s = 0.f;
-      for (int sp = 0; sp < splits; ++sp) s += partial[((long)sp * M + tok) * Ma + f];
-      out[(long)tok * out_ld + f] = __float2bfloat16(s);
-    } else {
-      const int gr = (f >> 7) * 256 + (f & 127);
-      float g = 0.f, u = 0.f;
-      for (int sp = 0; sp < splits; ++sp) {
-        g += partial[((long)sp * M + tok) * Ma + gr];
-        u += partial[((long)sp * M + tok) * Ma + gr + 128];
+// ------------------------------------------------------------------------------------------------ decode GEMM
+// Decode-sized M (<= 256 tokens), swap-AB: the weight rows fill the 128-lane MMA M dimension and the tokens are
+// the MMA N dimension (BN = M rounded up).  Each CTA owns NA (1 or 2) adjacent 128-row weight tiles that share
+// one activation tile per K step, so a stage carries NA x 16 KB of weights for BN x 128 B of activations and a
+// 1-CTA-per-SM ring keeps ~128 KB of weights in flight -- the decode GEMM is a weight-streaming problem and
+// the loaded HBM latency is microseconds.  With the fused activation the two tiles are the gate and up rows of
+// one 128-feature block (128-row interleaved layout) and act(gate) * up is formed in the epilogue.  The K range
+// may be split over S CTAs; split partials are then written as fp32 [S][M][N] and summed, in a fixed order, by
+// the kernel that consumes the output (add+RMSNorm, RoPE) or by splitk_sum_kernel.
+struct DecodeArgs {
+  int N, M, K, kblocks, S, act;
+  bf16* out;
+  long out_ld;
+  float* partial;
+  int* err;
+};
+
+__host__ __device__ constexpr int decode_stages2(int na, int bn) {
+  return (200 * 1024) / (na * BM * BK * 2 + bn * BK * 2) > 8 ? 8 : (200 * 1024) / (na * BM * BK * 2 + bn * BK * 2);
+}
+__host__ __device__ constexpr uint32_t pow2_cols(int n) {
+  uint32_t c = 32;
+  while (c < (uint32_t)n) c <<= 1;
+  return c;
+}
+
+template <int BN, int NA>
+__global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_constant__ CUtensorMap amap,
+                                                             const __grid_constant__ CUtensorMap bmap,
+                                                             DecodeArgs args) {
+  constexpr int STAGES = decode_stages2(NA, BN);
+  constexpr uint32_t A_SUB = BM * BK * 2;
+  constexpr uint32_t A_BYTES = NA * A_SUB;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = pow2_cols(NA * BN);
+  constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int group = blockIdx.x / args.S, split = blockIdx.x % args.S;
+  const int row0 = group * (NA * BM);  // first weight row of this CTA
+  const int kb0 = (int)((long)args.kblocks * split / args.S);
+  const int kb1 = (int)((long)args.kblocks * (split + 1) / args.S);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      nvb::mbar_init(&full_bar[s], 1);
+      nvb::mbar_init(&empty_bar[s], 1);
+    }
+    nvb::mbar_init(tfull_bar, 1);
+    nvb::fence_mbar_init();
+  }
+  if (warp == 1) {
+    nvb::tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    nvb::tmem_relinquish();
+  }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  if (warp == 0 && lane == 0) {
+    nvb::tma_prefetch_desc(&amap);
+    nvb::tma_prefetch_desc(&bmap);
+    uint32_t it = 0;
+    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      const int s = it % STAGES;
+      if (!nvb::mbar_wait(&empty_bar[s], ((it / STAGES) & 1u) ^ 1u, args.err, &abort_flag)) break;
+      uint8_t* sa = smem + s * STAGE_BYTES;
+      nvb::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+#pragma unroll
+      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[s], kb * BK, row0 + j * BM);
+      nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, 0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    uint32_t it = 0;
+    bool ok = true;
+    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      const int s = it % STAGES;
+      if (!nvb::mbar_wait(&full_bar[s], (it / STAGES) & 1u, args.err, &abort_flag)) { ok = false; break; }
+      nvb::tc_fence_after();
+      const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+      for (int j = 0; j < NA; ++j)
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          nvb::tc_mma_f16(tmem_base + j * BN, nvb::sdesc_kmajor_sw128(a_addr + j * A_SUB + kk * 32),
+                          nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+      nvb::tc_commit(&empty_bar[s]);
+    }
+    if (ok) nvb::tc_commit(tfull_bar);
+  }
+  __syncwarp();
+  int ok = 0;
+  if (lane == 0) ok = nvb::mbar_wait(tfull_bar, 0, args.err, &abort_flag) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  nvb::tc_fence_after();
+
+  if (ok) {
+    const int r = threadIdx.x;  // TMEM lane = row inside each tile
+    const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
+    if (args.act != kActNone) {
+      // NA == 2: tile 0 = gate rows, tile 1 = up rows of feature block ``group``
+      const int f = group * BM + r;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t g[16], u[16];
+        nvb::tmem_ld_32x32b_x16(t_row + c, g);
+        nvb::tmem_ld_32x32b_x16(t_row + BN + c, u);
+        nvb::tmem_ld_wait();
+        if (f < args.N / 2)
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = c + j;
+            if (t < args.M) {
+              const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
+              args.out[(long)t * args.out_ld + f] =
+                  __float2bfloat16((args.act == kActSiluMul ? silu(gv) : gelu_tanh(gv)) * uv);
+            }
+          }
       }
-      out[(long)tok * out_ld + f] = __float2bfloat16((act == kActSiluMul ? silu(g) : gelu_tanh(g)) * u);
+    } else {
+#pragma unroll
+      for (int jt = 0; jt < NA; ++jt) {
+        const int f = row0 + jt * BM + r;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          nvb::tmem_ld_32x32b_x16(t_row + jt * BN + c, v);
+          nvb::tmem_ld_wait();
+          if (f < args.N) {
+            if (args.S == 1) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (c + j < args.M) args.out[(long)(c + j) * args.out_ld + f] = __float2bfloat16(__uint_as_float(v[j]));
+            } else {
+              float* dst = args.partial + (long)split * args.M * args.N + f;
+#pragma unroll
+              for (int j = 0; j < 16; ++j)
+                if (c + j < args.M) dst[(long)(c + j) * args.N] = __uint_as_float(v[j]);
+            }
+          }
+        }
+      }
     }
   }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// out[m][n] = sum_s partial[s][m][n], fixed order (float4 over n; N % 4 == 0)
+__global__ void splitk_sum_kernel(const float* __restrict__ partial, int S, long MN, bf16* __restrict__ out, int N,
+                                  long out_ld) {
+  const long total4 = MN / 4;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(partial)[i];
+    for (int s = 1; s < S; ++s) {
+      const float4 v = reinterpret_cast<const float4*>(partial + (long)s * MN)[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    const long e = i * 4;
+    const long m = e / N, n = e % N;
+    bf16* d = out + m * out_ld + n;
+    *reinterpret_cast<uint32_t*>(d) = nvb::pack_bf16x2(acc.x, acc.y);
+    *reinterpret_cast<uint32_t*>(d + 2) = nvb::pack_bf16x2(acc.z, acc.w);
+  }
+}
+
+template <int BN, int NA>
+cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
+                          cudaStream_t stream) {
+  auto kern = gemm_decode_kernel<BN, NA>;
+  constexpr int ST = decode_stages2(NA, BN);
+  constexpr size_t sm = 1024 + (size_t)ST * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
+  static_assert(sm <= 227 * 1024, "decode gemm shared memory");
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  kern<<<groups * a.S, 128, sm, stream>>>(am, bm, a);
+  return cudaGetLastError();
+}
+
+template <int NA>
+cudaError_t launch_decode_bn(int bn, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
+                             cudaStream_t st) {
+  switch (bn) {
+    case 16: return launch_decode<16, NA>(am, bm, a, groups, st);
+    case 32: return launch_decode<32, NA>(am, bm, a, groups, st);
+    case 64: return launch_decode<64, NA>(am, bm, a, groups, st);
+    case 128: return launch_decode<128, NA>(am, bm, a, groups, st);
+    default: return launch_decode<256, NA>(am, bm, a, groups, st);
+  }
+}
+
+// K splits: make groups * S a near-multiple of the SM count (one CTA per SM), >= 4 k-blocks per split.
+int decode_splits(int groups, int kblocks, int sms) {
+  if (groups >= sms) return 1;
+  int best = 1;
+  double best_eff = (double)groups / (double)sms;
+  for (int s = 2; s <= 16 && s * 4 <= kblocks; ++s) {
+    const int u = groups * s;
+    const int waves = (u + sms - 1) / sms;
+    const double eff = (double)u / ((double)waves * sms);
+    if (eff > best_eff + 0.03) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
 }
 
 template <int BN, int STAGES>
@@ -324,52 +501,12 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
   kern<<<grid, 192, sm, stream>>>(am, bm, a);
 }
 
-// Decode BN options (the token count rounded up to 16).
-template <int STAGES_HINT>
-void launch_swap(int bn, const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cudaStream_t st, int ctas) {
-  switch (bn) {
-    case 16: launch_gemm<16, 8>(am, bm, a, st, ctas); break;
-    case 32: launch_gemm<32, 8>(am, bm, a, st, ctas); break;
-    case 48: launch_gemm<48, 8>(am, bm, a, st, ctas); break;
-    case 64: launch_gemm<64, 8>(am, bm, a, st, ctas); break;
-    case 80: launch_gemm<80, 7>(am, bm, a, st, ctas); break;
-    case 96: launch_gemm<96, 6>(am, bm, a, st, ctas); break;
-    case 112: launch_gemm<112, 6>(am, bm, a, st, ctas); break;
-    case 128: launch_gemm<128, 6>(am, bm, a, st, ctas); break;
-    case 144: launch_gemm<144, 5>(am, bm, a, st, ctas); break;
-    case 160: launch_gemm<160, 5>(am, bm, a, st, ctas); break;
-    case 176: launch_gemm<176, 5>(am, bm, a, st, ctas); break;
-    case 192: launch_gemm<192, 4>(am, bm, a, st, ctas); break;
-    case 208: launch_gemm<208, 4>(am, bm, a, st, ctas); break;
-    case 224: launch_gemm<224, 4>(am, bm, a, st, ctas); break;
-    case 240: launch_gemm<240, 4>(am, bm, a, st, ctas); break;
-    default: launch_gemm<256, 4>(am, bm, a, st, ctas); break;
-  }
-}
-
-int choose_splits(int tiles, int kblocks, int sms) {
-  if (tiles >= sms) return 1;
-  int best = 1;
-  double best_eff = -1.0;
-  const int max_s = kblocks / 4 < 32 ? (kblocks / 4 > 1 ? kblocks / 4 : 1) : 32;
-  for (int s = 1; s <= max_s; ++s) {
-    const int u = tiles * s;
-    const int waves = (u + sms - 1) / sms;
-    const double eff = (double)u / ((double)waves * sms);
-    if (eff > best_eff + 0.02) {
-      best_eff = eff;
-      best = s;
-    }
-  }
-  return best;
-}
-
 }  // namespace
 
 // y = x @ w^T (x [M, K] bf16, w [N, K] bf16) with optional activation on 128-interleaved gate/up rows of w.
-// ``workspace`` (fp32, >= splits * M * N elements when M <= 256) holds split-K partials.
-void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
-               int64_t force_splits, c10::optional<torch::Tensor> err) {
+// ``workspace`` is unused (kept for ABI stability): decode split partials are reduced in distributed shared memory.
+int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
+                  int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
               "gemm expects bf16 CUDA tensors");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "shape mismatch");
@@ -379,7 +516,7 @@ void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act,
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
   TORCH_CHECK(out.stride(-1) == 1, "output rows must be contiguous");
   if (act != kActNone) TORCH_CHECK(N % 256 == 0, "fused gate/up activation needs N % 256 == 0");
-  if (M == 0) return;
+  if (M == 0) return 0;
   int* e = err.has_value() ? err->data_ptr<int>() : nullptr;
   auto stream = at::cuda::getCurrentCUDAStream();
   const int sms = num_sms();
@@ -389,35 +526,49 @@ void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act,
   a.kblocks = kblocks;
   a.act = (int)act;
   a.err = e;
+  int64_t splits_used = 1;
   if (M <= 256) {
-    const int bn = ((M + 15) / 16) * 16;
-    a.Ma = N;
-    a.Nb = M;
-    a.tiles_m = (N + BM - 1) / BM;
-    a.tiles_n = 1;
-    a.splits = force_splits > 0 ? (int)force_splits : choose_splits(a.tiles_m, kblocks, sms);
-    if (a.splits > kblocks) a.splits = kblocks;
+    const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    const int NA = (act != kActNone || N % 256 == 0) ? 2 : 1;
+    DecodeArgs d{};
+    d.N = N;
+    d.M = M;
+    d.K = K;
+    d.kblocks = kblocks;
+    d.act = (int)act;
+    const int groups = (N + NA * BM - 1) / (NA * BM);
+    if (act != kActNone) {
+      d.S = 1;  // the activation needs complete sums in the epilogue
+    } else if (force_splits > 0) {
+      d.S = (int)force_splits;
+    } else {
+      d.S = workspace.has_value() ? decode_splits(groups, kblocks, sms) : 1;
+    }
+    if (d.S > kblocks) d.S = kblocks;
+    splits_used = d.S;
+    d.out = reinterpret_cast<bf16*>(out.data_ptr());
+    d.out_ld = out.stride(0);
+    d.err = e;
+    if (d.S > 1) {
+      TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
+                      workspace->numel() >= (long)d.S * M * N,
+                  "decode gemm: fp32 partial buffer of S*M*N elements required");
+      d.partial = workspace->data_ptr<float>();
+    }
+    if (getenv("NVB_GEMM_DEBUG"))
+      printf("[gemm decode] M=%d N=%d K=%d bn=%d NA=%d groups=%d S=%d\n", M, N, K, bn, NA, groups, d.S);
     CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
     CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
-    if (a.splits == 1 && act == kActNone) {
-      a.out_mode = kOutBf16T;
-      a.out = out.data_ptr();
-      a.out_ld = out.stride(0);
-      launch_swap<0>(bn, am, bm, a, stream, sms);
-    } else {
-      TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
-                      workspace->numel() >= (long)a.splits * M * N,
-                  "gemm: fp32 workspace of splits*M*N elements required");
-      a.out_mode = kOutPartialT;
-      a.out = workspace->data_ptr();
-      a.out_ld = N;
-      launch_swap<0>(bn, am, bm, a, stream, sms);
-      C10_CUDA_KERNEL_LAUNCH_CHECK();
-      const long total = (long)M * (act == kActNone ? N : N / 2);
-      int blocks = (int)((total + 255) / 256);
+    cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, am, bm, d, groups, stream)
+                            : launch_decode_bn<1>(bn, am, bm, d, groups, stream);
+    TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
+    if (d.S > 1 && partial_out) {
+      // the caller consumes the partials itself (fused into its next kernel)
+    } else if (d.S > 1) {
+      const long MN = (long)M * N;
+      int blocks = (int)((MN / 4 + 255) / 256);
       if (blocks > sms * 8) blocks = sms * 8;
-      splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(workspace->data_ptr<float>(), a.splits, M, N,
-                                                       reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0), (int)act);
+      splitk_sum_kernel<<<blocks, 256, 0, stream>>>(d.partial, d.S, MN, d.out, N, d.out_ld);
     }
   } else {
     constexpr int BN = 256;
@@ -434,10 +585,31 @@ void gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act,
     launch_gemm<BN, 4>(am, bm, a, stream, sms);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return M <= 256 ? splits_used : 1;
 }
 
-// Number of K splits the decode path would use (lets the caller size the workspace).
+// Workspace splits the decode path needs from the caller (always 1: it reduces on chip).
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K) {
-  if (M > 256) return 1;
-  return choose_splits((int)((N + BM - 1) / BM), (int)((K + BK - 1) / BK), num_sms());
+  // K splits the decode path uses when the caller provides a partial buffer (act == none)
+  if (M > 256 || M <= 0) return 1;
+  const int NA = N % 256 == 0 ? 2 : 1;
+  const int groups = (int)((N + NA * BM - 1) / (NA * BM));
+  const int kblocks = (int)((K + BK - 1) / BK);
+  int s = decode_splits(groups, kblocks, num_sms());
+  return s > kblocks ? kblocks : s;
+}
+
+// out [M, N] bf16 = sum over splits of parts [S, M, N] fp32 (fixed order).
+void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out) {
+  TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.is_contiguous() && parts.dim() == 3, "parts [S, M, N] fp32");
+  const int S = parts.size(0);
+  const long M = parts.size(1), N = parts.size(2);
+  TORCH_CHECK(N % 4 == 0 && out.stride(-1) == 1, "N must be a multiple of 4");
+  const long MN = M * N;
+  if (MN == 0) return;
+  int blocks = (int)((MN / 4 + 255) / 256);
+  if (blocks > num_sms() * 8) blocks = num_sms() * 8;
+  splitk_sum_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      parts.data_ptr<float>(), S, MN, reinterpret_cast<bf16*>(out.data_ptr()), (int)N, out.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -45,12 +45,31 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 template <int NV>
 __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
                                 __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
-                                int H, long x_stride, long out_stride, float eps, int mode) {
+                                int H, long x_stride, long out_stride, float eps, int mode,
+                                const float* __restrict__ xpart, int nsplit, long part_stride) {
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
   float v[NV][8];
-  load_vecs<NV>(x + row * x_stride, H, tid, nt, v);
+  if (xpart == nullptr) {
+    load_vecs<NV>(x + row * x_stride, H, tid, nt, v);
+  } else {
+    // x = sum of split-K partials [nsplit][rows][H] (fp32), summed in split order
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int col = (tid + i * nt) * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
+      if (col < H) {
+        for (int sp = 0; sp < nsplit; ++sp) {
+          const float4* p = reinterpret_cast<const float4*>(xpart + sp * part_stride + row * (long)H + col);
+          const float4 a = p[0], b = p[1];
+          v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;
+          v[i][4] += b.x; v[i][5] += b.y; v[i][6] += b.z; v[i][7] += b.w;
+        }
+      }
+    }
+  }
   if (residual != nullptr) {
     float r[NV][8];
     load_vecs<NV>(residual + row * (long)H, H, tid, nt, r);
@@ -173,7 +192,7 @@ void check_row_tensor(const torch::Tensor& t, const char* name) {
 
 // out = norm(x) or, with residual: residual += x; out = norm(residual).   x may be a row-strided view.
 void rms_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tensor> residual,
-                   c10::optional<torch::Tensor> weight, double eps, int64_t mode) {
+                   c10::optional<torch::Tensor> weight, double eps, int64_t mode, c10::optional<torch::Tensor> xpart) {
   check_row_tensor(x, "x");
   check_row_tensor(out, "out");
   const int H = x.size(-1);
@@ -201,7 +220,18 @@ void rms_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tens
   auto stream = at::cuda::getCurrentCUDAStream();
   auto* o = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   auto* xi = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
-#define LAUNCH(NVV) rms_norm_kernel<NVV><<<rows, threads, 0, stream>>>(o, xi, res, w, H, xs, os, (float)eps, (int)mode)
+  const float* xp = nullptr;
+  int nsplit = 0;
+  long pstride = 0;
+  if (xpart.has_value()) {
+    TORCH_CHECK(xpart->scalar_type() == at::kFloat && xpart->is_contiguous() && xpart->dim() == 3 &&
+                    xpart->size(1) == rows && xpart->size(2) == H,
+                "xpart must be contiguous fp32 [splits, rows, H]");
+    xp = xpart->data_ptr<float>();
+    nsplit = xpart->size(0);
+    pstride = rows * (long)H;
+  }
+#define LAUNCH(NVV) rms_norm_kernel<NVV><<<rows, threads, 0, stream>>>(o, xi, res, w, H, xs, os, (float)eps, (int)mode, xp, nsplit, pstride)
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

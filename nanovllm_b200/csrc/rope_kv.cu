@@ -19,7 +19,7 @@ __global__ void qk_norm_rope_store_kernel(
     const float* __restrict__ cos_sin, int rot_stride, const __nv_bfloat16* __restrict__ q_w,
     const __nv_bfloat16* __restrict__ k_w, int norm_mode, int v_norm, float eps, __nv_bfloat16* __restrict__ q_out,
     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ slots,
-    int nq, int nkv, int block_size, int apply_rope) {
+    int nq, int nkv, int block_size, int apply_rope, const float* __restrict__ qkv_part, int nsplit, long part_stride) {
   constexpr int HD = PAIRS * 64;
   constexpr int HALF = HD / 2;
   const long t = blockIdx.x;
@@ -31,12 +31,26 @@ __global__ void qk_norm_rope_store_kernel(
   const int total = nq + 2 * nkv;
   for (int h = warp; h < total; h += nwarps) {
     const bool is_q = h < nq, is_k = (h >= nq && h < nq + nkv), is_v = h >= nq + nkv;
-    const __nv_bfloat16* src = row + (long)h * HD;
     float lo[PAIRS], hi[PAIRS];
+    if (qkv_part == nullptr) {
+      const __nv_bfloat16* src = row + (long)h * HD;
 #pragma unroll
-    for (int p = 0; p < PAIRS; ++p) {
-      lo[p] = __bfloat162float(src[lane + 32 * p]);
-      hi[p] = __bfloat162float(src[lane + 32 * p + HALF]);
+      for (int p = 0; p < PAIRS; ++p) {
+        lo[p] = __bfloat162float(src[lane + 32 * p]);
+        hi[p] = __bfloat162float(src[lane + 32 * p + HALF]);
+      }
+    } else {
+      // sum of split-K partials [nsplit][T][width] (fp32), in split order
+      const float* src = qkv_part + t * (long)total * HD + (long)h * HD;
+#pragma unroll
+      for (int p = 0; p < PAIRS; ++p) lo[p] = hi[p] = 0.f;
+      for (int sp = 0; sp < nsplit; ++sp) {
+#pragma unroll
+        for (int p = 0; p < PAIRS; ++p) {
+          lo[p] += src[sp * part_stride + lane + 32 * p];
+          hi[p] += src[sp * part_stride + lane + 32 * p + HALF];
+        }
+      }
     }
     const int mode = is_v ? (v_norm ? 2 : -1) : norm_mode;
     if (mode >= 0) {
@@ -91,7 +105,7 @@ void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::
                              c10::optional<torch::Tensor> q_w, c10::optional<torch::Tensor> k_w, int64_t norm_mode,
                              bool v_norm, double eps, torch::Tensor q_out, c10::optional<torch::Tensor> k_cache,
                              c10::optional<torch::Tensor> v_cache, c10::optional<torch::Tensor> slots, int64_t nq,
-                             int64_t nkv, int64_t head_dim, bool apply_rope) {
+                             int64_t nkv, int64_t head_dim, bool apply_rope, c10::optional<torch::Tensor> qkv_part) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == at::kBFloat16, "qkv must be bf16 CUDA");
   TORCH_CHECK(qkv.stride(-1) == 1, "qkv rows must be contiguous");
   TORCH_CHECK(positions.scalar_type() == at::kLong, "positions must be int64");
@@ -116,12 +130,24 @@ void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::
   }
   const int total = nq + 2 * nkv;
   int warps = total < 8 ? total : 8;
+  const float* qp = nullptr;
+  int nsplit = 0;
+  long pstride = 0;
+  if (qkv_part.has_value()) {
+    TORCH_CHECK(qkv_part->scalar_type() == at::kFloat && qkv_part->is_contiguous() && qkv_part->dim() == 3 &&
+                    qkv_part->size(1) == T && qkv_part->size(2) == (long)total * head_dim,
+                "qkv_part must be contiguous fp32 [splits, T, (nq + 2 nkv) * hd]");
+    qp = qkv_part->data_ptr<float>();
+    nsplit = qkv_part->size(0);
+    pstride = T * (long)total * head_dim;
+  }
   auto stream = at::cuda::getCurrentCUDAStream();
 #define LAUNCH(P)                                                                                                  \
   qk_norm_rope_store_kernel<P><<<T, warps * 32, 0, stream>>>(                                                      \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),        \
       cos_sin.data_ptr<float>(), (int)cos_sin.size(-1), qw, kw, (int)norm_mode, v_norm ? 1 : 0, (float)eps,         \
-      reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), kc, vc, sl, (int)nq, (int)nkv, block_size, apply_rope ? 1 : 0)
+      reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), kc, vc, sl, (int)nq, (int)nkv, block_size, apply_rope ? 1 : 0, \
+      qp, nsplit, pstride)
   switch (head_dim / 64) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

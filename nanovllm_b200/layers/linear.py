@@ -104,6 +104,7 @@ class MergedColumnParallelLinear(LinearBase):
 
 
 class QKVParallelLinear(LinearBase):
+    """q/k/v merged; without a bias the decode output may stay split-K (the RoPE kernel sums it)."""
     def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int, num_kv_heads: int,
                  head_dim: int, bq=None, bk=None, bv=None):
         super().__init__()
@@ -131,6 +132,8 @@ class QKVParallelLinear(LinearBase):
             self.bias = torch.cat([bqs, bks, bvs], 0).contiguous()
 
     def __call__(self, x):
+        if self.bias is None and not hasattr(self.weight, "linear"):
+            return ops.linear(x, self.weight, partial_ok=True)
         return self._mm(x)
 
 
@@ -144,7 +147,12 @@ class RowParallelLinear(LinearBase):
 
     def __call__(self, x):
         w = self.weight
-        y = w.linear(x) if hasattr(w, "linear") else ops.linear(x, w)
+        if hasattr(w, "linear"):
+            y = w.linear(x)
+        elif ps.tp_size() == 1 and self.bias is None:
+            return ops.linear(x, w, partial_ok=True)  # the following add+RMSNorm sums the split partials
+        else:
+            y = ops.linear(x, w)
         if self.reduce:
             ps.all_reduce(y)
         if self.bias is not None:

@@ -37,6 +37,46 @@ def _cuda_ext():
     return _C
 
 
+class SplitK:
+    """Unreduced output of a split-K decode GEMM: fp32 partials [S, M, N] whose sum is the result.
+
+    Consumers that can fuse the sum (add+RMSNorm, the RoPE/KV-store kernel) take it directly; anything else
+    calls ``materialize``.  The partials are summed in split order, so the result is deterministic."""
+    __slots__ = ("parts",)
+
+    def __init__(self, parts: torch.Tensor):
+        self.parts = parts
+
+    @property
+    def shape(self):
+        return tuple(self.parts.shape[1:])
+
+    @property
+    def dtype(self):
+        return torch.bfloat16
+
+    @property
+    def device(self):
+        return self.parts.device
+
+    @property
+    def is_cuda(self):
+        return True
+
+    def reshape(self, *shape):
+        return materialize(self).reshape(*shape)
+
+
+def materialize(x):
+    """bf16 tensor from a SplitK (one fused sum kernel), identity for tensors."""
+    if isinstance(x, SplitK):
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        _cuda_ext().splitk_sum(x.parts, out)
+        add_launches(1)
+        return out
+    return x
+
+
 _LAUNCHES = [0]
 
 
@@ -105,15 +145,22 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: 
             residual.copy_(r)
             r = residual
         return y, r
+    if isinstance(x, SplitK):
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+        _cuda_ext().rms_norm(out, out, residual, weight, float(eps), int(mode), x.parts)
+        add_launches(1)
+        return out, residual
     if out is None:
         out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
-    _cuda_ext().rms_norm(out, x, residual, weight, float(eps), int(mode))
+    _cuda_ext().rms_norm(out, x, residual, weight, float(eps), int(mode), None)
     add_launches(1)
     return out, residual
 
 
 def layer_norm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, eps: float,
                residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    x = materialize(x)
     if not x.is_cuda:
         return ref.layer_norm(x, weight, bias, eps, residual)
     out = torch.empty_like(x)
@@ -130,9 +177,13 @@ def qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, norm_mode, v_norm, eps
         q, _, _ = ref.qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, norm_mode, v_norm, eps, k_cache,
                                          v_cache, slots, nq, nkv, hd, apply_rope)
         return q.reshape(qkv.shape[0], nq, hd)
-    q = torch.empty(qkv.shape[0], nq, hd, dtype=qkv.dtype, device=qkv.device)
+    part = None
+    if isinstance(qkv, SplitK):
+        part = qkv.parts
+        qkv = torch.empty(1, part.shape[2], dtype=torch.bfloat16, device=part.device).expand(part.shape[1], -1)
+    q = torch.empty(qkv.shape[0], nq, hd, dtype=torch.bfloat16, device=qkv.device)
     _cuda_ext().qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, int(norm_mode), bool(v_norm), float(eps), q,
-                                   k_cache, v_cache, slots, int(nq), int(nkv), int(hd), bool(apply_rope))
+                                   k_cache, v_cache, slots, int(nq), int(nkv), int(hd), bool(apply_rope), part)
     add_launches(1)
     return q
 
@@ -196,29 +247,40 @@ def prefill_attention(q, cu_q, cu_k, max_q, nq, nkv, hd, scale, softcap=0.0, win
 
 # ------------------------------------------------------------------------------------------------ linear
 def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[torch.Tensor] = None,
-           force_splits: int = 0) -> torch.Tensor:
-    """y = x @ w^T on the tcgen05 GEMM.  act != 0 expects gate/up rows interleaved in 128-row blocks."""
+           force_splits: int = 0, partial_ok: bool = False):
+    """y = x @ w^T on the tcgen05 GEMM.  act != 0 expects gate/up rows interleaved in 128-row blocks.
+
+    For decode-sized M the K range may be split over CTAs; with ``partial_ok`` the unreduced fp32 partials are
+    returned as a ``SplitK`` for a consumer that fuses the sum, otherwise a sum kernel produces bf16."""
     if not x.is_cuda:
         return ref.linear(x, w, act)
+    x = materialize(x)
     M, K = x.shape
     N = w.shape[0]
     ncols = N // 2 if act != ACT_NONE else N
+    C = _cuda_ext()
+    parts = None
+    splits = 1
+    if M <= 256 and act == ACT_NONE:
+        splits = force_splits if force_splits > 0 else C.gemm_splits_for(M, N, K)
+        if splits > 1:
+            parts = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
     if out is None:
         out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
-    C = _cuda_ext()
-    ws = None
-    launches = 1
-    if M <= 256:
-        splits = force_splits if force_splits > 0 else C.gemm_splits_for(M, N, K)
-        if splits > 1 or act != ACT_NONE:
-            ws = workspace(x.device, splits * M * N)
-            launches = 2
-    C.gemm(x, w, out, int(act), ws, int(force_splits), error_word(x.device))
-    add_launches(launches)
+    C.gemm(x, w, out, int(act), parts, int(splits if parts is not None else (force_splits or 0)),
+           error_word(x.device), bool(partial_ok and parts is not None))
+    if parts is not None:
+        if partial_ok:
+            add_launches(1)
+            return SplitK(parts)
+        add_launches(2)
+        return out
+    add_launches(1)
     return out
 
 
 def act_mul(x: torch.Tensor, act: int, interleaved: bool = False) -> torch.Tensor:
+    x = materialize(x)
     if not x.is_cuda:
         return ref.act_mul(x, act, interleaved)
     out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
@@ -228,6 +290,8 @@ def act_mul(x: torch.Tensor, act: int, interleaved: bool = False) -> torch.Tenso
 
 
 def bias_act_(x: torch.Tensor, bias: Optional[torch.Tensor], act: int = BIAS_ACT_NONE) -> torch.Tensor:
+    if isinstance(x, SplitK):
+        x = materialize(x)
     if not x.is_cuda:
         x.copy_(ref.bias_act(x, bias, act))
         return x
@@ -248,6 +312,7 @@ def embedding(table: torch.Tensor, ids: torch.Tensor, scale: float = 1.0, vstart
 
 
 def gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    src = materialize(src)
     if not src.is_cuda:
         return src[idx.long()]
     out = torch.empty(idx.numel(), src.shape[1], dtype=src.dtype, device=src.device)

@@ -155,12 +155,13 @@ def main():
         if a.decode:
             v = [int(x) for x in a.decode.split(",")]
             rows.append(bench_decode(v[0], v[1], v[2], v[3], v[4], a.iters))
-    if "gemm" in only:
+    if "gemm" in only or "gemmd" in only:
         # Qwen3-8B decode (M = batch) and prefill (M = chunk) shapes
         for M in (1, 32, 128, 256):
             for N, K, act in ((6144, 4096, 0), (4096, 4096, 0), (24576, 4096, 1), (4096, 12288, 0)):
                 rows.append(bench_gemm(M, N, K, a.iters, act))
         rows.append(bench_gemm(128, 151936, 4096, a.iters))
+    if "gemm" in only:
         for M in (2048, 8192):
             for N, K, act in ((6144, 4096, 0), (24576, 4096, 1), (4096, 12288, 0)):
                 rows.append(bench_gemm(M, N, K, max(5, a.iters // 5), act))

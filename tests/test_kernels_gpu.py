@@ -191,6 +191,49 @@ def test_gemm_fused_gate_up(M, act):
     close(y, y_ref, 5e-3, 0.03)
 
 
+@pytest.mark.parametrize("M,N,K", [(5, 4096, 4096), (128, 6144, 4096), (200, 4096, 12288)])
+def test_gemm_split_partials_fused_into_consumers(M, N, K):
+    """Split-K partials summed by add+RMSNorm / RoPE match the materialised GEMM result."""
+    g = torch.Generator().manual_seed(M * 7 + N)
+    x = (torch.randn(M, K, generator=g) * 0.5).bfloat16().to(DEV)
+    w = (torch.randn(N, K, generator=g) * 0.02).bfloat16().to(DEV)
+    y = ops.linear(x, w, partial_ok=True)
+    dense = ops.linear(x, w)
+    if isinstance(y, ops.SplitK):
+        close(ops.materialize(y), dense, 2e-3, 0.02)
+        res = torch.randn(M, N, generator=g).bfloat16().to(DEV)
+        wn = torch.ones(N).bfloat16().to(DEV)
+        r1 = res.clone()
+        a, _ = ops.rms_norm(y, wn, 1e-6, 0, r1)
+        r2 = res.clone()
+        b, _ = ops.rms_norm(dense, wn, 1e-6, 0, r2)
+        close(a, b, 3e-2)
+        close(r1, r2, 2e-2)
+    close(ops.materialize(y), ref.linear(x.cpu(), w.cpu()), 2e-3, 0.02)
+
+
+def test_rope_consumes_split_partials():
+    g = torch.Generator().manual_seed(77)
+    nq, nkv, hd, T, K = 8, 2, 128, 9, 4096
+    x = (torch.randn(T, K, generator=g) * 0.5).bfloat16().to(DEV)
+    w = (torch.randn((nq + 2 * nkv) * hd, K, generator=g) * 0.02).bfloat16().to(DEV)
+    y = ops.linear(x, w, partial_ok=True, force_splits=4)
+    assert isinstance(y, ops.SplitK)
+    dense = ops.materialize(y)
+    cs = ref.rope_cos_sin(hd, 64, 1e6).to(DEV)
+    pos = torch.arange(T, device=DEV)
+    nw = torch.ones(hd).bfloat16().to(DEV)
+    kc = torch.zeros(2, nkv, 256, hd).bfloat16().to(DEV)
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    slots = torch.arange(T, device=DEV, dtype=torch.int32)
+    q1 = ops.qk_norm_rope_store(y, pos, cs, nw, nw, 0, False, 1e-6, kc, vc, slots, nq, nkv, hd)
+    q2 = ops.qk_norm_rope_store(dense, pos, cs, nw, nw, 0, False, 1e-6, kc2, vc2, slots, nq, nkv, hd)
+    close(q1, q2, 3e-2)
+    close(kc, kc2, 3e-2)
+    close(vc, vc2, 3e-2)
+
+
 def test_gemm_forced_splits_deterministic():
     g = torch.Generator().manual_seed(9)
     x = torch.randn(64, 4096, generator=g).bfloat16().to(DEV)
