@@ -66,9 +66,15 @@ def all_gather_last(x: torch.Tensor) -> torch.Tensor:
     """Concatenate per-rank shards along the last dimension."""
     if _TP_SIZE == 1:
         return x
-    parts = torch.empty((_TP_SIZE,) + tuple(x.shape), dtype=x.dtype, device=x.device)
-    dist.all_gather_into_tensor(parts, x.contiguous(), group=_GROUP)
-    return torch.cat(list(parts.unbind(0)), dim=-1)
+    x = x.contiguous()
+    if x.is_cuda:
+        parts = torch.empty((_TP_SIZE,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+        dist.all_gather_into_tensor(parts, x, group=_GROUP)
+        chunks = list(parts.unbind(0))
+    else:
+        chunks = [torch.empty_like(x) for _ in range(_TP_SIZE)]
+        dist.all_gather(chunks, x, group=_GROUP)
+    return torch.cat(chunks, dim=-1)
 
 
 def reduce_scatter_rows(x: torch.Tensor) -> torch.Tensor:
