@@ -1,0 +1,135 @@
+"""``LlmModelFactory``: path -> ``LlmModel`` over the three checkpoint containers.
+
+Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/models/LlmModelFactory.java:94-895 (load
+dispatch: a ``.gguf`` file -> GGUF causal (qwen3, lfm2) or embedding (bert); a Hugging Face folder ->
+safetensors when present, else ONNX; tokenizer from tokenizer.json -> tokenizer.model -> GGUF metadata;
+``ModelSupport.require`` before any payload is read; options map; Builder) and the architecture processors'
+bind / fill steps (llmarch/*).  Weights are returned as a name -> tensor map in the names each model graph
+consumes: Hugging Face names for qwen3 / llama / gemma3 / gemma4 (GGUF qwen3 tensors renamed), GGUF names for lfm2
+and bert (ONNX BERT names mapped onto them).  GGUF blocks are dequantised at load (on the GPU when one is present).
+"""
+from __future__ import annotations
+
+import os
+from typing import Dict, Optional
+
+import torch
+
+from ..config import HfConfig
+from ..exceptions import ModelLoadException, UnsupportedModelException
+from ..loaders import model_support as MS
+from ..loaders.gguf import GgufFile
+from ..loaders.gguf_configs import hf_config_from_gguf, hf_name_for_qwen3
+from ..tokenizer.tokenizer import Tokenizer
+from .model import LlmModel
+
+OPTION_THINK_TAGS = "think_tags"
+OPTION_CHAT_SPECIALS = "chat_specials"
+
+
+def _is_gguf(path: str) -> bool:
+    if not os.path.isfile(path):
+        return False
+    with open(path, "rb") as f:
+        return f.read(4) == b"GGUF"
+
+
+def _load_device(device) -> torch.device:
+    if device is not None:
+        return torch.device(device)
+    return torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+
+
+class LlmModelFactory:
+    @staticmethod
+    def make(path: str, options: Optional[dict] = None, device=None, dtype=torch.bfloat16) -> LlmModel:
+        path = os.fspath(path)
+        if _is_gguf(path) or path.lower().endswith(".gguf"):
+            return _load_gguf(path, options, _load_device(device), dtype)
+        if os.path.isdir(path):
+            return _load_hf_folder(path, options, _load_device(device), dtype)
+        raise ModelLoadException(f"model path not found or not a GGUF file / model folder: {path}")
+
+    class Builder:
+        def __init__(self):
+            self._path = None
+            self._options = {}
+            self._device = None
+
+        def path(self, p):
+            self._path = p
+            return self
+
+        def option(self, k, v):
+            self._options[k] = v
+            return self
+
+        def think_tags(self, tags):
+            self._options[OPTION_THINK_TAGS] = tags
+            return self
+
+        def device(self, d):
+            self._device = d
+            return self
+
+        def build(self) -> LlmModel:
+            if self._path is None:
+                raise ValueError("path is required")
+            return LlmModelFactory.make(self._path, self._options, self._device)
+
+    @staticmethod
+    def builder() -> "LlmModelFactory.Builder":
+        return LlmModelFactory.Builder()
+
+
+def _load_gguf(path: str, options, device, dtype) -> LlmModel:
+    g = GgufFile(path)
+    sel = MS.resolve_gguf(g.architecture)
+    MS.check_source(sel, MS.SRC_GGUF, g.architecture, [])
+    hf = hf_config_from_gguf(g.metadata, sel.architecture)
+    tok = Tokenizer.from_gguf(g.metadata)
+    weights: Dict[str, torch.Tensor] = {}
+    packed = False
+    for name, info in g.tensors.items():
+        if sel.architecture == MS.QWEN3:
+            target = hf_name_for_qwen3(name)
+            if target is None:
+                continue
+        else:
+            target = name
+        packed = packed or info.ggml_type not in (0, 1, 30)
+        weights[target] = g.get(name, dtype=torch.float32, device=device).to(dtype)
+    if sel.architecture == MS.QWEN3 and "lm_head.weight" not in weights:
+        hf.tie_word_embeddings = True
+    g.close()
+    return LlmModel(hf, weights, tok, options, source=path, container="gguf", packed=packed)
+
+
+def _load_hf_folder(d: str, options, device, dtype) -> LlmModel:
+    cfg_path = os.path.join(d, "config.json")
+    if not os.path.isfile(cfg_path):
+        raise ModelLoadException(f"{d}: no config.json")
+    hf = HfConfig.load(cfg_path)
+    from ..loaders.onnx import normalize_bert_name, normalize_chat_name, read_initializers, select_file
+    has_st = any(f.endswith(".safetensors") for f in os.listdir(d))
+    onnx_file = None if has_st else select_file(d)
+    source = MS.SRC_HF_SAFETENSORS if has_st else (MS.SRC_ONNX if onnx_file else None)
+    if source is None:
+        raise ModelLoadException(f"{d}: no *.safetensors or loadable *.onnx weights")
+    sel = MS.require(hf, source)
+    tok = Tokenizer.from_pretrained(d)
+    if source == MS.SRC_HF_SAFETENSORS:
+        if sel.architecture == MS.GEMMA4:
+            from ..loaders.gemma4_qat import load_gemma4_qat
+            weights = load_gemma4_qat(d, hf)
+        else:
+            from ..loaders.safetensors import SafetensorsCheckpoint
+            ck = SafetensorsCheckpoint(d)
+            weights = {k: ck.get(k) for k in ck.keys()}
+    else:
+        raw = read_initializers(onnx_file)
+        norm = normalize_bert_name if sel.architecture == MS.BERT else normalize_chat_name
+        weights = {norm(k): v for k, v in raw.items()}
+    if hf.tie_word_embeddings is False and "lm_head.weight" not in weights and sel.architecture != MS.BERT:
+        hf.tie_word_embeddings = True
+    return LlmModel(hf, weights, tok, options, source=d, container=source, packed=False)

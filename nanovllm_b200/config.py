@@ -325,6 +325,7 @@ class EngineConfig:
     eos: int = -1
     stop_token_ids: tuple = ()
     stop_on_degenerate: bool = True
+    enable_prefix_caching: bool = True
     fused_comm: bool = True
     seed: int = 0
 

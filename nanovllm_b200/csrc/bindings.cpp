@@ -29,6 +29,8 @@ void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interlea
 void bias_act_cuda(torch::Tensor x, c10::optional<torch::Tensor> bias, int64_t act);
 void gather_rows_cuda(torch::Tensor out, torch::Tensor src, torch::Tensor idx);
 void mean_pool_l2_cuda(torch::Tensor out, torch::Tensor x, torch::Tensor cu);
+void shortconv_cuda(torch::Tensor proj, torch::Tensor weight, torch::Tensor cu, torch::Tensor rows, torch::Tensor fresh,
+                    torch::Tensor state, int64_t state_off, torch::Tensor out);
 void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
                  torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out);
 
@@ -48,4 +50,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_rows", &gather_rows_cuda);
   m.def("mean_pool_l2", &mean_pool_l2_cuda);
   m.def("sample", &sample_cuda);
+  m.def("shortconv", &shortconv_cuda);
 }

@@ -50,10 +50,12 @@ class Block:
 
 
 class BlockManager:
-    def __init__(self, num_blocks: int, block_size: int):
+    def __init__(self, num_blocks: int, block_size: int, prefix_caching: bool = True):
         if num_blocks <= 0:
             raise ValueError("num_blocks must be > 0")
         self.block_size = block_size
+        # models with recurrent per-sequence state (LFM2 conv) cannot skip a cached prefix
+        self.prefix_caching = prefix_caching
         self.blocks = [Block(i) for i in range(num_blocks)]
         self.hash_to_block_id: Dict[int, int] = {}
         self.free_block_ids = deque(range(num_blocks))
@@ -99,7 +101,7 @@ class BlockManager:
         h = -1
         cached = 0
         new_blocks = seq.num_blocks
-        for i in range(seq.num_blocks - 1):
+        for i in range(seq.num_blocks - 1 if self.prefix_caching else 0):
             toks = seq.block(i)
             h = compute_hash(toks, h)
             bid = self.hash_to_block_id.get(h, -1)

@@ -37,7 +37,7 @@ class Scheduler:
         self.stop_on_degenerate = cfg.stop_on_degenerate
         ids = list(stop_token_ids) if stop_token_ids else ([cfg.eos] if cfg.eos >= 0 else [])
         self.stop_token_ids = frozenset(int(x) for x in ids)
-        self.block_manager = BlockManager(num_blocks, cfg.kvcache_block_size)
+        self.block_manager = BlockManager(num_blocks, cfg.kvcache_block_size, cfg.enable_prefix_caching)
         self.waiting: deque = deque()
         self.running: deque = deque()
         self.on_release = on_release

@@ -101,6 +101,8 @@ class LLM:
             stop = list(tokenizer.stop_token_ids())
         if not stop and self.cfg.eos >= 0:
             stop = [self.cfg.eos]
+        if self.model.state_specs():
+            self.cfg.enable_prefix_caching = False
         self.runner = ModelRunner(self.model, hf, self.cfg, self.device)
         self.scheduler = Scheduler(self.cfg, self.runner.num_blocks, stop, on_release=self.runner.release_state)
         self._lock = threading.Lock()

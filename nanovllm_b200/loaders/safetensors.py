@@ -16,6 +16,8 @@ import struct
 from typing import Dict, Iterator, List, Optional, Tuple
 
 import numpy as np
+import warnings
+
 import torch
 
 from ..exceptions import ModelLoadException
@@ -75,7 +77,9 @@ class SafetensorsFile:
         shape = tuple(e["shape"])
         if len(buf) == 0:
             return torch.empty(shape, dtype=_DTYPES[dt])
-        t = torch.frombuffer(buf, dtype=_DTYPES[dt])
+        with warnings.catch_warnings():
+            warnings.simplefilter("ignore")  # read-only mapping: tensors are never written
+            t = torch.frombuffer(buf, dtype=_DTYPES[dt])
         return t.reshape(shape)
 
     def close(self):

@@ -53,7 +53,7 @@ class WeightBag:
     def dense(self, name: str) -> torch.Tensor:
         """Dense bf16 tensor even when the source is packed (for norms, embeddings on CPU, tests)."""
         t = self.require(name)
-        if hasattr(t, "dequantize"):
+        if not isinstance(t, torch.Tensor) and hasattr(t, "dequantize"):
             return t.dequantize(self.dtype)
         return t
 

@@ -338,3 +338,14 @@ def sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float 
     _cuda_ext().sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, float(softcap), out)
     add_launches(1)
     return out
+
+
+def shortconv(proj, weight, cu, rows, fresh, state, state_off: int):
+    """LFM2 gated short conv over [B | C | x] projections with the per-sequence recurrent state."""
+    proj = materialize(proj)
+    if not proj.is_cuda:
+        return ref.shortconv(proj, weight, cu, rows, fresh, state, state_off)
+    out = torch.empty(proj.shape[0], weight.shape[0], dtype=proj.dtype, device=proj.device)
+    _cuda_ext().shortconv(proj, weight, cu, rows, fresh, state, int(state_off), out)
+    add_launches(1)
+    return out

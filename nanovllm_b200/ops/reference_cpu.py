@@ -305,3 +305,27 @@ def sample(logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, s
         score = p[idxs].double().numpy() / np.maximum(1e-10, g)
         out[r] = int(idxs[int(np.argmax(score))])
     return out
+
+
+def shortconv(proj: torch.Tensor, weight: torch.Tensor, cu: torch.Tensor, rows: torch.Tensor, fresh: torch.Tensor,
+              state: torch.Tensor, state_off: int) -> torch.Tensor:
+    """LFM2 gated short conv (ShortConv.java:102-243): y = C * causal_conv(B * x), per-sequence state of the last
+    L-1 B*x rows (zeros when ``fresh``), updated in place."""
+    H, L = weight.shape
+    p = proj.float()
+    b, c, x = p[:, :H], p[:, H:2 * H], p[:, 2 * H:]
+    bx = b * x
+    out = torch.empty(proj.shape[0], H, dtype=torch.float32)
+    w = weight.float()
+    for s in range(len(cu) - 1):
+        t0, t1 = int(cu[s]), int(cu[s + 1])
+        if t1 <= t0:
+            continue
+        row = int(rows[s])
+        sl = state[row, state_off:state_off + (L - 1) * H].view(L - 1, H)
+        prev = torch.zeros(L - 1, H) if bool(fresh[s]) else sl.clone()
+        window = torch.cat([prev, bx[t0:t1]], 0)
+        for t in range(t1 - t0):
+            out[t0 + t] = (window[t:t + L] * w.t()).sum(0)
+        sl.copy_(window[-(L - 1):] if L > 1 else sl)
+    return (c * out).to(proj.dtype)

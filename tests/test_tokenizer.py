@@ -1,0 +1,146 @@
+"""Tokenizer codecs vs the HF ``tokenizers`` library (oracle) on tokenizers trained in-test, GGUF vocabularies,
+special-token atomicity, streaming decode, stop ids and the hand-coded chat templates (reference analogues:
+TokenizerCodecTest and the chat/template cases of CoreUnitTest)."""
+import json
+import os
+
+import pytest
+
+from nanovllm_b200.tokenizer.tokenizer import CHATML, PLAIN, TURN_BASED, Tokenizer
+
+tk = pytest.importorskip("tokenizers")
+
+CORPUS = [
+    "The quick brown fox jumps over the lazy dog. Über naïve café! 東京タワー 123 4567.",
+    "Hello, world! It's a test's test; we'll see: x=1+2*3 (ok?) \n\n  indented\tTabs",
+    "Emoji 🙂🚀 and accents àéîõü, numbers 3.14159 and 2026, CAPS and MiXeD case.",
+] * 20
+SAMPLES = ["The quick brown fox", "Hello,  world!\n\nNew para", "naïve café 東京 🙂", "x=1+2*3 (ok?)",
+           "  leading and trailing  ", "It's 2026; we'll see."]
+
+
+def _save(t, tmp_path, name="tokenizer.json", config=None):
+    d = tmp_path / name.replace(".json", "")
+    d.mkdir()
+    t.save(str(d / "tokenizer.json"))
+    if config is not None:
+        (d / "tokenizer_config.json").write_text(json.dumps(config))
+    return str(d)
+
+
+def _train_bytelevel(tmp_path):
+    from tokenizers import Tokenizer as T, decoders, models, pre_tokenizers, trainers
+    t = T(models.BPE())
+    t.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    t.decoder = decoders.ByteLevel()
+    t.train_from_iterator(CORPUS, trainers.BpeTrainer(vocab_size=400, special_tokens=["<|endoftext|>", "<|im_start|>",
+                                                                                       "<|im_end|>", "<think>",
+                                                                                       "</think>"],
+                                                      initial_alphabet=pre_tokenizers.ByteLevel.alphabet()))
+    return t
+
+
+def test_byte_level_bpe_matches_oracle(tmp_path):
+    t = _train_bytelevel(tmp_path)
+    ours = Tokenizer.from_pretrained(_save(t, tmp_path, config={"eos_token": "<|endoftext|>"}))
+    for s in SAMPLES:
+        assert ours.encode(s) == t.encode(s).ids, s
+        assert ours.decode(ours.encode(s)) == s
+
+
+def test_special_tokens_are_atomic_and_chatml(tmp_path):
+    t = _train_bytelevel(tmp_path)
+    ours = Tokenizer.from_pretrained(_save(t, tmp_path, config={"eos_token": "<|endoftext|>"}))
+    ids = ours.encode("<|im_start|>user\nhi<|im_end|>")
+    assert ids[0] == ours.token_id("<|im_start|>") and ours.token_id("<|im_end|>") in ids
+    assert ours.chat_format == CHATML
+    p = ours.apply_chat_template([{"role": "user", "content": "hi"}], add_generation_prompt=True)
+    assert p == "<|im_start|>user\nhi<|im_end|>\n<|im_start|>assistant\n<think>\n\n</think>\n\n"
+    p2 = ours.apply_chat_template([{"role": "user", "content": "hi"}], enable_thinking=True)
+    assert p2.endswith("<|im_start|>assistant\n")
+    assert ours.stop_token_ids()[:2] == [ours.token_id("<|endoftext|>"), ours.token_id("<|im_end|>")]
+    assert ours.decode(ids, skip_special=True) == "user\nhi"
+
+
+def test_wordpiece_matches_oracle(tmp_path):
+    from tokenizers import Tokenizer as T, decoders, models, normalizers, pre_tokenizers, trainers
+    t = T(models.WordPiece(unk_token="[UNK]"))
+    t.normalizer = normalizers.BertNormalizer(lowercase=True)
+    t.pre_tokenizer = pre_tokenizers.BertPreTokenizer()
+    t.decoder = decoders.WordPiece()
+    t.train_from_iterator(CORPUS, trainers.WordPieceTrainer(vocab_size=300, special_tokens=["[UNK]", "[CLS]", "[SEP]",
+                                                                                            "[PAD]", "[MASK]"]))
+    ours = Tokenizer.from_pretrained(_save(t, tmp_path))
+    for s in SAMPLES:
+        assert ours.encode(s) == t.encode(s, add_special_tokens=False).ids, s
+    assert ours.cls_sep_ids() == (t.token_to_id("[CLS]"), t.token_to_id("[SEP]"))
+
+
+def test_unigram_and_metaspace_bpe_match_oracle(tmp_path):
+    from tokenizers import Tokenizer as T, decoders, models, pre_tokenizers, trainers
+    u = T(models.Unigram())
+    u.pre_tokenizer = pre_tokenizers.Metaspace()
+    u.decoder = decoders.Metaspace()
+    u.train_from_iterator(CORPUS, trainers.UnigramTrainer(vocab_size=200, special_tokens=["<unk>"], unk_token="<unk>"))
+    ours = Tokenizer.from_pretrained(_save(u, tmp_path, "uni.json"))
+    for s in ["The quick brown fox", "lazy dog jumps", "Hello world"]:
+        assert ours.encode(s) == u.encode(s).ids, s
+        assert ours.decode(ours.encode(s)) == u.decode(u.encode(s).ids)
+    b = T(models.BPE(byte_fallback=True, unk_token="<unk>"))
+    b.pre_tokenizer = pre_tokenizers.Metaspace()
+    b.decoder = decoders.Metaspace()
+    b.train_from_iterator(CORPUS, trainers.BpeTrainer(vocab_size=300, special_tokens=["<unk>"] +
+                                                      [f"<0x{i:02X}>" for i in range(256)]))
+    ours_b = Tokenizer.from_pretrained(_save(b, tmp_path, "msp.json"))
+    for s in ["The quick brown fox", "jumps over", "Hello, world!"]:
+        assert ours_b.encode(s) == b.encode(s).ids, s
+
+
+def test_gguf_gpt2_vocab_matches_json(tmp_path):
+    t = _train_bytelevel(tmp_path)
+    tj = json.loads(t.to_str())
+    vocab = tj["model"]["vocab"]
+    tokens = [None] * (max(vocab.values()) + 1)
+    for k, v in vocab.items():
+        tokens[v] = k
+    for a in tj["added_tokens"]:
+        tokens[a["id"]] = a["content"]
+    types = [3 if a in ("<|endoftext|>", "<|im_start|>", "<|im_end|>", "<think>", "</think>") else 1 for a in tokens]
+    merges = [m if isinstance(m, str) else " ".join(m) for m in tj["model"]["merges"]]
+    meta = {"tokenizer.ggml.model": "gpt2", "tokenizer.ggml.pre": "default", "tokenizer.ggml.tokens": tokens,
+            "tokenizer.ggml.token_type": types, "tokenizer.ggml.merges": merges,
+            "tokenizer.ggml.eos_token_id": vocab.get("<|endoftext|>", 0)}
+    g = Tokenizer.from_gguf(meta)
+    for s in SAMPLES:
+        assert g.encode(s) == t.encode(s).ids
+
+
+def test_turn_based_and_plain_templates():
+    from nanovllm_b200.tokenizer.codecs import Char
+    vocab = {c: i for i, c in enumerate(["<bos>", "<start_of_turn>", "<end_of_turn>", "a", "b"])}
+    tok = Tokenizer(Char(vocab), list(vocab.keys()), added={"<bos>": 0, "<start_of_turn>": 1, "<end_of_turn>": 2},
+                    special_ids=[0, 1, 2], eos_id=2)
+    assert tok.chat_format == TURN_BASED
+    p = tok.apply_chat_template([{"role": "system", "content": "S"}, {"role": "user", "content": "U"},
+                                 {"role": "assistant", "content": "A"}, {"role": "user", "content": "V"}])
+    assert p == ("<bos><start_of_turn>user\nS\n\nU<end_of_turn>\n<start_of_turn>model\nA<end_of_turn>\n"
+                 "<start_of_turn>user\nV<end_of_turn>\n<start_of_turn>model\n")
+    angle = {c: i for i, c in enumerate(["<bos>", "<|turn>", "<turn|>"])}
+    t4 = Tokenizer(Char(angle), list(angle.keys()), added=dict(angle), eos_id=2)
+    p4 = t4.apply_chat_template([{"role": "system", "content": " sys "}, {"role": "user", "content": "q"}],
+                                enable_thinking=True)
+    assert p4 == "<bos><|turn>system\n<|think|>\nsys<turn|>\n<|turn>user\nq<turn|>\n<|turn>model\n"
+    plain = Tokenizer(Char({"a": 0}), ["a"], eos_id=0)
+    assert plain.chat_format == PLAIN
+    assert plain.apply_chat_template([{"role": "user", "content": "hi"}]) == "user: hi\nassistant: "
+
+
+def test_stream_decoder_emits_complete_characters(tmp_path):
+    t = _train_bytelevel(tmp_path)
+    ours = Tokenizer.from_pretrained(_save(t, tmp_path))
+    text = "café 東京 🙂 ok"
+    ids = ours.encode(text)
+    sd = ours.stream_decoder()
+    out = "".join(sd.push(i) for i in ids) + sd.flush()
+    assert out == text
+    assert "�" not in out
