@@ -478,9 +478,10 @@ __global__ void attn_generic_kernel(const bf16* __restrict__ q, long q_tok_strid
   const int key_end = causal ? pos + 1 : klen;
   const int key_begin = (causal && window > 0) ? max(0, pos - window + 1) : 0;
   float qv[16], acc[16];
-  const int per = HD / 32;
+  const int per = (HD + 31) / 32;  // dims per lane; lanes past HD idle when HD < 32
   for (int i = 0; i < per; ++i) {
-    qv[i] = __bfloat162float(q[(long)tq * q_tok_stride + h * HD + lane + 32 * i]);
+    const int dim = lane + 32 * i;
+    qv[i] = dim < HD ? __bfloat162float(q[(long)tq * q_tok_stride + h * HD + dim]) : 0.f;
     acc[i] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
@@ -496,17 +497,20 @@ __global__ void attn_generic_kernel(const bf16* __restrict__ q, long q_tok_strid
       vr = vc + (long)(k0 + key) * kv_tok_stride + kvh * HD;
     }
     float d = 0.f;
-    for (int i = 0; i < per; ++i) d += qv[i] * __bfloat162float(kr[lane + 32 * i]);
+    for (int i = 0; i < per; ++i)
+      if (lane + 32 * i < HD) d += qv[i] * __bfloat162float(kr[lane + 32 * i]);
     d = nvb::warp_sum(d);
     const float x = apply_cap(d * scale, softcap);
     const float nm = fmaxf(m, x);
     const float corr = expf(m - nm), p = expf(x - nm);
     l = l * corr + p;
-    for (int i = 0; i < per; ++i) acc[i] = acc[i] * corr + p * __bfloat162float(vr[lane + 32 * i]);
+    for (int i = 0; i < per; ++i)
+      if (lane + 32 * i < HD) acc[i] = acc[i] * corr + p * __bfloat162float(vr[lane + 32 * i]);
     m = nm;
   }
   for (int i = 0; i < per; ++i)
-    out[(long)tq * o_tok_stride + h * HD + lane + 32 * i] = __float2bfloat16(l > 0.f ? acc[i] / l : 0.f);
+    if (lane + 32 * i < HD)
+      out[(long)tq * o_tok_stride + h * HD + lane + 32 * i] = __float2bfloat16(l > 0.f ? acc[i] / l : 0.f);
 }
 
 template <int HD, int STAGES>

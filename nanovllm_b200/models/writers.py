@@ -37,7 +37,8 @@ def byte_level_tokenizer_json(vocab_size: int, specials=("<|endoftext|>", "<|im_
     while nxt < vocab_size - len(specials):
         vocab[f"<filler{nxt}>"] = nxt
         nxt += 1
-    added = [{"id": nxt + i, "content": s, "special": True} for i, s in enumerate(specials)]
+    # think tags are plain added tokens (special=False) as in Qwen3's tokenizer.json: they survive skip-special decode
+    added = [{"id": nxt + i, "content": s, "special": s not in ("<think>", "</think>")} for i, s in enumerate(specials)]
     return {"version": "1.0", "added_tokens": added, "normalizer": None,
             "pre_tokenizer": {"type": "ByteLevel", "add_prefix_space": False, "use_regex": True},
             "decoder": {"type": "ByteLevel"},
