@@ -109,8 +109,18 @@ class LlmModel:
             return enc.embed_ids([self._wrap(list(text))])[0]
         return enc.embed_ids([self._wrap(self.tokenizer.encode(t)) for t in text])
 
-    def embed_ids(self, batches: List[List[int]], device=None) -> torch.Tensor:
-        return self._get_encoder(device).embed_ids(batches)
+    def embed_ids(self, batches: List[List[int]], device=None, keep_device: bool = False) -> torch.Tensor:
+        return self._get_encoder(device).embed_ids(batches, keep_device=keep_device)
+
+    def embed_batch(self, texts: Sequence[str], device=None) -> torch.Tensor:
+        """[N, H] embeddings left on the encoder's device (one packed encoder pass per 64k tokens)."""
+        if not self.is_embedding():
+            raise ValueError("embed_batch() needs an embedding model")
+        ids = [self._wrap(self.tokenizer.encode(t)) for t in texts]
+        return self._get_encoder(device).embed_ids(ids, keep_device=True)
+
+    def is_closed(self) -> bool:
+        return self._closed
 
     def _wrap(self, ids: List[int]) -> List[int]:
         tok = self.tokenizer

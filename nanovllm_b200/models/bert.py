@@ -101,8 +101,9 @@ class BertEncoder:
             return pos
         return (pos.float() + self.type0.float()).to(pos.dtype)
 
-    def embed_ids(self, batch: List[List[int]], max_tokens: int = 65536) -> torch.Tensor:
-        """Mean-pooled, L2-normalised embeddings [N, H] (fp32) for token-id sequences, packed in chunks."""
+    def embed_ids(self, batch: List[List[int]], max_tokens: int = 65536, keep_device: bool = False) -> torch.Tensor:
+        """Mean-pooled, L2-normalised embeddings [N, H] (fp32) for token-id sequences, packed in chunks
+        (returned on the encoder's device with ``keep_device``, else on the host)."""
         outs = []
         i = 0
         while i < len(batch):
@@ -118,6 +119,7 @@ class BertEncoder:
             for s in chunk:
                 cu_l.append(cu_l[-1] + len(s))
             cu = torch.tensor(cu_l, dtype=torch.int32, device=self.device)
-            outs.append(self.encode_packed(ids, pos, cu, max(len(s) for s in chunk)).float().cpu())
+            e = self.encode_packed(ids, pos, cu, max(len(s) for s in chunk)).float()
+            outs.append(e if keep_device else e.cpu())
             i = j
         return torch.cat(outs, 0)

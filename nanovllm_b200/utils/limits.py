@@ -30,6 +30,23 @@ class ResourceLimits:
     MAX_DIMS = _env_int("MAX_DIMS", 8)
     MAX_HISTORY_MESSAGES = _env_int("MAX_HISTORY_MESSAGES", 200)
 
+    def __init__(self, max_file_bytes: int = None, max_total_corpus_bytes: int = None, max_corpus_files: int = None):
+        """An instance carries the corpus budgets of one loader (class attributes are the process defaults)."""
+        self.max_file_bytes = self.MAX_FILE_BYTES if max_file_bytes is None else int(max_file_bytes)
+        self.max_total_corpus_bytes = self.MAX_CORPUS_BYTES if max_total_corpus_bytes is None \
+            else int(max_total_corpus_bytes)
+        self.max_corpus_files = self.MAX_CORPUS_FILES if max_corpus_files is None else int(max_corpus_files)
+        if min(self.max_file_bytes, self.max_total_corpus_bytes, self.max_corpus_files) <= 0:
+            raise ValueError("resource limits must be positive")
+
+    @classmethod
+    def current(cls) -> "ResourceLimits":
+        return cls()
+
+    def __repr__(self) -> str:
+        return (f"ResourceLimits(file={self.max_file_bytes}, corpus={self.max_total_corpus_bytes}, "
+                f"files={self.max_corpus_files})")
+
 
 class Props:
     """NANOVLLM_* properties (model path, models dir, rag dir, arch confirmation, threads, color)."""
