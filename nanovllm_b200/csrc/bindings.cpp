@@ -33,6 +33,12 @@ void shortconv_cuda(torch::Tensor proj, torch::Tensor weight, torch::Tensor cu, 
                     torch::Tensor state, int64_t state_off, torch::Tensor out);
 void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
                  torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out);
+void rms_norm_post_add_cuda(torch::Tensor x, torch::Tensor residual, c10::optional<torch::Tensor> weight, double eps,
+                            int64_t mode, double post_scale);
+void ple_combine_cuda(torch::Tensor out, torch::Tensor proj, torch::Tensor tok, torch::Tensor weight, double eps,
+                      double proj_scale, double out_scale);
+void gate_act_mul_cuda(torch::Tensor out, torch::Tensor gate, torch::Tensor other);
+void srq_cuda(torch::Tensor x, double scale);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";
@@ -51,4 +57,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mean_pool_l2", &mean_pool_l2_cuda);
   m.def("sample", &sample_cuda);
   m.def("shortconv", &shortconv_cuda);
+  m.def("rms_norm_post_add", &rms_norm_post_add_cuda);
+  m.def("ple_combine", &ple_combine_cuda);
+  m.def("gate_act_mul", &gate_act_mul_cuda);
+  m.def("srq", &srq_cuda);
 }

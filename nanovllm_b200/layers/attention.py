@@ -19,7 +19,8 @@ class Attention:
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, scale: float, rope: torch.Tensor,
                  q_norm: Optional[torch.Tensor] = None, k_norm: Optional[torch.Tensor] = None, norm_mode: int = -1,
                  eps: float = 1e-6, v_norm: bool = False, window: int = 0, softcap: float = 0.0,
-                 apply_rope: bool = True, write_kv: bool = True):
+                 apply_rope: bool = True, write_kv: bool = True, q_only: bool = False):
+        """``q_only``: the input holds only the q heads (a KV-shared layer reading another layer's cache)."""
         self.nq, self.nkv, self.hd = num_heads, num_kv_heads, head_dim
         self.scale = scale
         self.rope = rope
@@ -30,6 +31,7 @@ class Attention:
         self.softcap = softcap
         self.apply_rope = apply_rope
         self.write_kv = write_kv
+        self.q_only = q_only
         self.k_cache: Optional[torch.Tensor] = None
         self.v_cache: Optional[torch.Tensor] = None
 
@@ -42,8 +44,8 @@ class Attention:
         kc = self.k_cache if self.write_kv else None
         vc = self.v_cache if self.write_kv else None
         q = ops.qk_norm_rope_store(qkv, positions, self.rope, self.q_norm, self.k_norm, self.norm_mode, self.v_norm,
-                                   self.eps, kc, vc, ctx.slot_mapping if kc is not None else None, self.nq, self.nkv,
-                                   self.hd, self.apply_rope)
+                                   self.eps, kc, vc, ctx.slot_mapping if kc is not None else None, self.nq,
+                                   0 if self.q_only else self.nkv, self.hd, self.apply_rope)
         if ctx.is_prefill:
             o = ops.prefill_attention(q, ctx.cu_seqlens_q, ctx.cu_seqlens_k, ctx.max_seqlen_q, self.nq, self.nkv,
                                       self.hd, self.scale, self.softcap, self.window, True, self.k_cache,

@@ -349,3 +349,49 @@ def shortconv(proj, weight, cu, rows, fresh, state, state_off: int):
     _cuda_ext().shortconv(proj, weight, cu, rows, fresh, state, int(state_off), out)
     add_launches(1)
     return out
+
+
+# ----------------------------------------------------------------------------------------------- Gemma4
+def rms_norm_post_add_(x, residual: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: int = 0,
+                       post_scale: float = 1.0) -> torch.Tensor:
+    """residual = (residual + rmsnorm(x) * w) * post_scale, in place."""
+    x = materialize(x)
+    if not residual.is_cuda:
+        return ref.rms_norm_post_add(x, residual, weight, eps, mode, post_scale)
+    _cuda_ext().rms_norm_post_add(x, residual, weight, float(eps), int(mode), float(post_scale))
+    add_launches(1)
+    return residual
+
+
+def ple_combine(proj, tok: torch.Tensor, weight: torch.Tensor, eps: float, proj_scale: float,
+                out_scale: float) -> torch.Tensor:
+    proj = materialize(proj)
+    if not proj.is_cuda:
+        return ref.ple_combine(proj, tok, weight, eps, proj_scale, out_scale)
+    out = torch.empty_like(tok)
+    _cuda_ext().ple_combine(out, proj.contiguous(), tok, weight, float(eps), float(proj_scale), float(out_scale))
+    add_launches(1)
+    return out
+
+
+def gate_act_mul(gate, other: torch.Tensor) -> torch.Tensor:
+    """gelu_tanh(gate) * other; ``other`` may be a column slice."""
+    gate = materialize(gate)
+    if not gate.is_cuda:
+        return ref.gate_act_mul(gate, other)
+    out = torch.empty(gate.shape, dtype=gate.dtype, device=gate.device)
+    _cuda_ext().gate_act_mul(out, gate, other)
+    add_launches(1)
+    return out
+
+
+def srq_(x: torch.Tensor, scale: float) -> torch.Tensor:
+    """In-place static-range activation fake-quant (no-op for scale 0)."""
+    if scale == 0.0:
+        return x
+    if not x.is_cuda:
+        x.copy_(ref.srq(x, scale))
+        return x
+    _cuda_ext().srq(x, float(scale))
+    add_launches(1)
+    return x

@@ -329,3 +329,36 @@ def shortconv(proj: torch.Tensor, weight: torch.Tensor, cu: torch.Tensor, rows: 
             out[t0 + t] = (window[t:t + L] * w.t()).sum(0)
         sl.copy_(window[-(L - 1):] if L > 1 else sl)
     return (c * out).to(proj.dtype)
+
+
+# ----------------------------------------------------------------------------------------------- Gemma4
+def _gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    return 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x * x * x)))
+
+
+def rms_norm_post_add(x, residual, weight, eps, mode=0, post_scale=1.0):
+    """residual = (residual + rmsnorm(x) * w) * post_scale, in place (Gemma4 sandwich norm + layer_scalar)."""
+    n, _ = rms_norm(x, weight, eps, mode)
+    residual.copy_(((residual.float() + n.float()) * post_scale).to(residual.dtype))
+    return residual
+
+
+def ple_combine(proj, tok, weight, eps, proj_scale, out_scale):
+    """(rmsnorm(proj * proj_scale) * w + tok) * out_scale over rows of width P = weight.numel()."""
+    P = weight.numel()
+    p = (proj.float() * proj_scale).to(proj.dtype).reshape(-1, P)
+    n, _ = rms_norm(p, weight, eps, 0)
+    out = (n.float() + tok.reshape(-1, P).float()) * out_scale
+    return out.to(proj.dtype).reshape(proj.shape)
+
+
+def gate_act_mul(gate, other):
+    return (_gelu_tanh(gate.float()) * other.float()).to(gate.dtype)
+
+
+def srq(x: torch.Tensor, scale: float) -> torch.Tensor:
+    """Static-range activation fake-quant: clamp(floor(x / s + 0.5), -128, 127) * s (GemmaQat.applySrq)."""
+    if scale == 0.0:
+        return x
+    q = torch.floor(x.float() / scale + 0.5).clamp(-128.0, 127.0)
+    return (q * scale).to(x.dtype)

@@ -9,6 +9,7 @@ from nanovllm_b200.models.registry import init_random_weights
 from nanovllm_b200.ops import reference_cpu as ref
 from nanovllm_b200.sampling_params import SamplingParams
 
+from test_gemma4 import gemma4_tiny
 from test_models_cpu import _prefill_logits, bert_tiny, gemma3_tiny, lfm2_tiny
 
 pytestmark = pytest.mark.gpu
@@ -39,7 +40,7 @@ def test_shortconv_kernel_matches_oracle():
     assert torch.allclose(st_gpu.cpu(), st_cpu, atol=1e-5)
 
 
-@pytest.mark.parametrize("make", [gemma3_tiny, lfm2_tiny])
+@pytest.mark.parametrize("make", [gemma3_tiny, lfm2_tiny, gemma4_tiny])
 def test_causal_family_gpu_matches_cpu(make):
     hf = make()
     w = init_random_weights(hf, 7)
@@ -70,3 +71,31 @@ def test_bert_gpu_matches_cpu():
     a = BertEncoder(hf, w, torch.device("cpu")).embed_ids(ids)
     b = BertEncoder(hf, w, torch.device("cuda")).embed_ids(ids)
     assert torch.nn.functional.cosine_similarity(a, b, dim=1).min() > 0.999
+
+
+def test_gemma4_elementwise_kernels_match_oracle():
+    g = torch.Generator().manual_seed(3)
+    T, H, L, P = 37, 256, 5, 64
+    x = torch.randn(T, H, generator=g).bfloat16()
+    res = torch.randn(T, H, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16()
+    want = ref.rms_norm_post_add(x, res.clone(), w, 1e-6, 0, 0.75)
+    got = ops.rms_norm_post_add_(x.cuda(), res.cuda(), w.cuda(), 1e-6, 0, 0.75)
+    assert torch.allclose(got.float().cpu(), want.float(), atol=3e-2, rtol=2e-2)
+    proj = torch.randn(T, L * P, generator=g).bfloat16()
+    tok = torch.randn(T, L * P, generator=g).bfloat16()
+    pw = (1 + 0.1 * torch.randn(P, generator=g)).bfloat16()
+    want = ref.ple_combine(proj, tok, pw, 1e-6, 0.0625, 0.7071)
+    got = ops.ple_combine(proj.cuda(), tok.cuda(), pw.cuda(), 1e-6, 0.0625, 0.7071)
+    assert torch.allclose(got.float().cpu(), want.float(), atol=3e-2, rtol=2e-2)
+    wide = torch.randn(T, 3 * P, generator=g).bfloat16()
+    gate = torch.randn(T, P, generator=g).bfloat16()
+    want = ref.gate_act_mul(gate, wide[:, P:2 * P])
+    got = ops.gate_act_mul(gate.cuda(), wide.cuda()[:, P:2 * P])
+    assert torch.allclose(got.float().cpu(), want.float(), atol=2e-2, rtol=2e-2)
+    y = (4 * torch.randn(T, 2 * P, generator=g)).bfloat16()
+    want = y.clone()
+    want[:, :P] = ref.srq(y[:, :P], 0.05)
+    yc = y.cuda()
+    ops.srq_(yc[:, :P], 0.05)
+    assert torch.equal(yc.cpu(), want)
