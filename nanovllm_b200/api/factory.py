@@ -25,6 +25,7 @@ from .model import LlmModel
 
 OPTION_THINK_TAGS = "think_tags"
 OPTION_CHAT_SPECIALS = "chat_specials"
+OPTION_LISTENER = "listener"  # an LlmListener that receives load progress events
 
 
 def _is_gguf(path: str) -> bool:
@@ -42,7 +43,15 @@ def _load_device(device) -> torch.device:
 
 class LlmModelFactory:
     @staticmethod
-    def make(path: str, options: Optional[dict] = None, device=None, dtype=torch.bfloat16) -> LlmModel:
+    def make(path, options: Optional[dict] = None, device=None, dtype=torch.bfloat16) -> LlmModel:
+        """``path``: a model folder, a .gguf file, or a ``ModelFileSource`` (api.sources)."""
+        from .sources import ModelFileSource
+        if isinstance(path, ModelFileSource):
+            src = path
+            try:
+                return LlmModelFactory.make(src.local_path(), options, device, dtype)
+            finally:
+                src.close()
         path = os.fspath(path)
         if _is_gguf(path) or path.lower().endswith(".gguf"):
             return _load_gguf(path, options, _load_device(device), dtype)
@@ -90,7 +99,10 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
     tok = Tokenizer.from_gguf(g.metadata)
     weights: Dict[str, torch.Tensor] = {}
     packed = False
+    from ..utils.progress import LoadProgress
+    prog = LoadProgress(f"GGUF {os.path.basename(path)}", len(g.tensors), (options or {}).get(OPTION_LISTENER))
     for name, info in g.tensors.items():
+        prog.step(name)
         if sel.architecture == MS.QWEN3:
             target = hf_name_for_qwen3(name)
             if target is None:
@@ -102,6 +114,7 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
     if sel.architecture == MS.QWEN3 and "lm_head.weight" not in weights:
         hf.tie_word_embeddings = True
     g.close()
+    prog.finish(f"{len(weights)} tensors")
     return LlmModel(hf, weights, tok, options, source=path, container="gguf", packed=packed)
 
 
@@ -124,8 +137,15 @@ def _load_hf_folder(d: str, options, device, dtype) -> LlmModel:
             weights = load_gemma4_qat(d, hf)
         else:
             from ..loaders.safetensors import SafetensorsCheckpoint
+            from ..utils.progress import LoadProgress
             ck = SafetensorsCheckpoint(d)
-            weights = {k: ck.get(k) for k in ck.keys()}
+            keys = ck.keys()
+            prog = LoadProgress(f"safetensors {os.path.basename(d)}", len(keys), (options or {}).get(OPTION_LISTENER))
+            weights = {}
+            for k in keys:
+                weights[k] = ck.get(k)
+                prog.step(k)
+            prog.finish(f"{len(keys)} tensors")
     else:
         raw = read_initializers(onnx_file)
         norm = normalize_bert_name if sel.architecture == MS.BERT else normalize_chat_name

@@ -170,10 +170,10 @@ def _engine_think_tags(llm) -> ThinkTags:
 
 # ----------------------------------------------------------------------------------------------- session
 class ChatSession:
-    def __init__(self, llm, system_prompt: str = "", sampling: Optional[SamplingParams] = None,
+    def __init__(self, llm, system_prompt: Optional[str] = None, sampling: Optional[SamplingParams] = None,
                  think_tags: Optional[ThinkTags] = None, enable_thinking: bool = False,
                  max_history_messages: int = ResourceLimits.MAX_HISTORY_MESSAGES,
-                 timeout_s: Optional[float] = None, advisors: Sequence[LlmAdvisor] = (), mixer=None,
+                 timeout_s: Optional[float] = None, advisors: Optional[Sequence[LlmAdvisor]] = None, mixer=None,
                  listener: Optional[LlmListener] = None, emit_debug_prompts: bool = False,
                  seed_messages: Sequence[ChatMessage] = (), recover_unusable_answers: bool = False,
                  unusable_answer: Optional[Callable[[str], bool]] = None,
@@ -185,13 +185,15 @@ class ChatSession:
         self.llm = llm
         self.tok = llm.tokenizer
         self.sampling = sampling or llm.default_sampling
-        self.tags = think_tags or _engine_think_tags(llm)
+        self.tags = think_tags or getattr(llm, "think_tags", None) or _engine_think_tags(llm)
         self.enable_thinking = enable_thinking
         self.max_history = max_history_messages
         self.timeout_s = timeout_s
-        self.advisors = list(advisors)
-        self.mixer = mixer or DefaultAdvisorMixer()
-        self.listener = listener
+        self.advisors = list(advisors if advisors is not None else (getattr(llm, "advisors", None) or []))
+        self.mixer = mixer or getattr(llm, "advisor_mixer", None) or DefaultAdvisorMixer()
+        self.listener = listener if listener is not None else getattr(llm, "listener", None)
+        if system_prompt is None:
+            system_prompt = getattr(llm, "system_prompt", "") or ""
         self.debug = emit_debug_prompts
         self.recover = recover_unusable_answers
         self.unusable = unusable_answer or (lambda s: not s.strip())

@@ -86,7 +86,11 @@ class HfConfig:
 
     @staticmethod
     def parse(text_or_dict) -> "HfConfig":
-        root = json.loads(text_or_dict) if isinstance(text_or_dict, str) else dict(text_or_dict)
+        if isinstance(text_or_dict, (str, bytes)):
+            from .utils.json_limits import loads
+            root = loads(text_or_dict, "config.json")
+        else:
+            root = dict(text_or_dict)
         model_type = root.get("model_type")
         nested = isinstance(root.get("text_config"), dict)
         image = "vision_config" in root or "image_token_id" in root

@@ -39,6 +39,13 @@ void ple_combine_cuda(torch::Tensor out, torch::Tensor proj, torch::Tensor tok, 
                       double proj_scale, double out_scale);
 void gate_act_mul_cuda(torch::Tensor out, torch::Tensor gate, torch::Tensor other);
 void srq_cuda(torch::Tensor x, double scale);
+std::vector<torch::Tensor> symm_alloc_cuda(int64_t nbytes);
+int64_t ipc_open_cuda(torch::Tensor handle);
+void ipc_close_cuda(int64_t ptr);
+void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, std::vector<int64_t> out,
+                            std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
+                            c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
+                            c10::optional<torch::Tensor> err, int64_t max_blocks);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";
@@ -61,4 +68,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ple_combine", &ple_combine_cuda);
   m.def("gate_act_mul", &gate_act_mul_cuda);
   m.def("srq", &srq_cuda);
+  m.def("symm_alloc", &symm_alloc_cuda);
+  m.def("ipc_open", &ipc_open_cuda);
+  m.def("ipc_close", &ipc_close_cuda);
+  m.def("tp_allreduce_norm", &tp_allreduce_norm_cuda);
 }

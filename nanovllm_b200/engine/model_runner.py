@@ -56,6 +56,10 @@ class ModelRunner:
         self.state_rows: Dict[int, int] = {}
         self.free_state_rows: List[int] = []
         self.final_softcap = getattr(model, "final_softcap", 0.0)
+        if self.is_cuda and ps.tp_size() > 1:
+            # symmetric buffers for the fused all-reduce + RMSNorm kernels (collective: same point on all ranks)
+            from ..parallel import symm
+            symm.init_workspace(max(cfg.max_num_batched_tokens, cfg.max_num_seqs), hf.hidden_size, device)
         self._allocate_kv()
         self._allocate_state()
         self._attn_scratch = None
@@ -84,6 +88,11 @@ class ModelRunner:
             cap = max(32, budget // bpb)
             per_seq = self.max_blocks_per_seq
             nb = int(min(max(self.cfg.max_num_seqs * per_seq, 128), cap))
+            if ps.tp_size() > 1:
+                # every rank must schedule with the same pool size (ranks run the scheduler in lock-step)
+                t = torch.tensor([nb], dtype=torch.int64, device=self.device)
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN, group=ps.tp_group())
+                nb = int(t.item())
         else:
             nb = int(min(max(self.cfg.max_num_seqs * self.max_blocks_per_seq, 128), max(32, (2 << 30) // bpb)))
         self.num_blocks = nb

@@ -22,6 +22,7 @@ import torch
 
 from .. import ops
 from ..parallel import state as ps
+from ..parallel import symm
 
 
 def shard_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
@@ -151,6 +152,14 @@ class RowParallelLinear(LinearBase):
             y = w.linear(x)
         elif ps.tp_size() == 1 and self.bias is None:
             return ops.linear(x, w, partial_ok=True)  # the following add+RMSNorm sums the split partials
+        elif self.reduce and self.bias is None and getattr(x, "is_cuda", False):
+            ws = symm.workspace()
+            T = x.shape[0]
+            if ws is not None and ws.fits(T, w.shape[0]):
+                # partial sum straight into the symmetric buffer; the consumer fuses all-reduce + norm
+                ops.linear(x, w, out=ws.in_view(T))
+                return ops.TPPartial(ws, T)
+            y = ops.linear(x, w)
         else:
             y = ops.linear(x, w)
         if self.reduce:

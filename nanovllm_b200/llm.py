@@ -109,6 +109,11 @@ class LLM:
         self._cancel = threading.Event()
         self._closed = False
         self.listeners: List[Callable] = []
+        self.listener = None          # default LlmListener for chat sessions on this engine
+        self.system_prompt = ""       # default system prompt for chat sessions (empty, as in the reference)
+        self.advisors: List = []      # LlmAdvisor list run before every chat turn
+        self.advisor_mixer = None
+        self.think_tags = None
         if warmup:
             self.warmup()
 
@@ -120,6 +125,7 @@ class LLM:
             self._sampling = SamplingParams()
             self._device = None
             self._warmup = False
+            self._extra = {}
 
         def max_num_batched_tokens(self, v): self._cfg["max_num_batched_tokens"] = int(v); return self
         def max_num_seqs(self, v): self._cfg["max_num_seqs"] = int(v); return self
@@ -137,9 +143,18 @@ class LLM:
         def deterministic(self): self._sampling = self._sampling.deterministic(); return self
         def device(self, d): self._device = d; return self
         def warmup(self, v=True): self._warmup = bool(v); return self
+        # chat-level defaults picked up by ChatSession / RagSession (LLM.java builder knobs)
+        def listen(self, listener): self._extra["listener"] = listener; return self
+        def system_prompt(self, text: str): self._extra["system_prompt"] = text or ""; return self
+        def advisors(self, *advisors): self._extra["advisors"] = list(advisors); return self
+        def advisor_mixer(self, mixer): self._extra["advisor_mixer"] = mixer; return self
+        def think_tags(self, tags): self._extra["think_tags"] = tags; return self
 
         def build(self) -> "LLM":
-            return LLM(self._model, EngineConfig(**self._cfg), self._sampling, self._device, self._warmup)
+            llm = LLM(self._model, EngineConfig(**self._cfg), self._sampling, self._device, self._warmup)
+            for k, v in self._extra.items():
+                setattr(llm, k, v)
+            return llm
 
     @staticmethod
     def builder(model) -> "LLM.Builder":

@@ -67,8 +67,40 @@ class SplitK:
         return materialize(self).reshape(*shape)
 
 
+class TPPartial:
+    """This rank's row-parallel partial sum [T, H], already in the symmetric workspace's ``in`` slot.
+
+    A following RMSNorm (with or without residual) runs the fused all-reduce + residual + RMSNorm kernel over
+    peer memory; anything else calls ``materialize`` (a plain fused all-reduce)."""
+    __slots__ = ("ws", "T")
+
+    def __init__(self, ws, T: int):
+        self.ws, self.T = ws, T
+
+    @property
+    def shape(self):
+        return (self.T, self.ws.hidden)
+
+    @property
+    def dtype(self):
+        return torch.bfloat16
+
+    @property
+    def device(self):
+        return self.ws.buf.device
+
+    @property
+    def is_cuda(self):
+        return True
+
+    def reshape(self, *shape):
+        return materialize(self).reshape(*shape)
+
+
 def materialize(x):
-    """bf16 tensor from a SplitK (one fused sum kernel), identity for tensors."""
+    """bf16 tensor from a SplitK (one fused sum kernel) or a TPPartial (fused all-reduce), identity otherwise."""
+    if isinstance(x, TPPartial):
+        return x.ws.allreduce_norm(x.T, None, 0.0, 3, None)[0]
     if isinstance(x, SplitK):
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
         _cuda_ext().splitk_sum(x.parts, out)
@@ -139,6 +171,8 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: 
              residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None
              ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Returns (normed, residual).  With ``residual`` the sum x + residual is written back into it."""
+    if isinstance(x, TPPartial):
+        return x.ws.allreduce_norm(x.T, weight, eps, mode, residual)
     if not x.is_cuda:
         y, r = ref.rms_norm(x, weight, eps, mode, residual)
         if residual is not None:

@@ -312,10 +312,8 @@ def utf8_complete_prefix(data: bytes) -> Tuple[str, bytes]:
 def _read_json(path: str) -> Optional[dict]:
     if not os.path.isfile(path):
         return None
-    if os.path.getsize(path) > ResourceLimits.JSON_MAX_BYTES:
-        raise ModelLoadException(f"{path} exceeds the JSON size limit")
-    with open(path, "r", encoding="utf-8") as f:
-        return json.load(f)
+    from ..utils.json_limits import load_file
+    return load_file(path)
 
 
 def _token_content(v):
