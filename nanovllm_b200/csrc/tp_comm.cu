@@ -44,11 +44,16 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Thread t < nranks publishes this block's arrival to rank t and waits (bounded) for rank t's arrival.
-__device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase, uint32_t epoch, int* err) {
+// Thread t < nranks publishes this block's arrival to rank t and waits (bounded) for rank t's arrival.  With
+// ``publish_writes`` the block's earlier global stores (peer stores included) are made visible at system scope
+// before the flag: bar.sync orders them before the signalling thread's fence + release store.
+__device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase, uint32_t epoch, int* err,
+                              bool publish_writes) {
   const int t = threadIdx.x;
   int ok = 1;
+  if (publish_writes) __syncthreads();
   if (t < nranks) {
+    if (publish_writes) __threadfence_system();
     st_release_sys(P.sig[t] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + rank), epoch);
     const uint32_t* mine = P.sig[rank] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + t);
     const uint64_t t0 = nvb::global_timer_ns();
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
   if (threadIdx.x == 0) s_epoch = counters[blockIdx.x] + 1;
   __syncthreads();
   const uint32_t epoch = s_epoch;
-  if (!block_barrier(P, rank, nranks, 0, epoch, err)) {
+  if (!block_barrier(P, rank, nranks, 0, epoch, err, false)) {
     if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
     return;
   }
@@ -114,11 +119,19 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
       if (col < H) {
-        for (int p = 0; p < nranks; ++p) {  // fixed rank order: every owner sums identically
-          float f[8];
-          unpack8(*reinterpret_cast<const uint4*>(P.in[p] + base + col), f);
+        // issue every rank's load before the first use so the NVLink latencies overlap
+        uint4 raw[kMaxRanks];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < nranks) raw[p] = *reinterpret_cast<const uint4*>(P.in[p] + base + col);
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p) {  // fixed rank order: every owner sums identically
+          if (p < nranks) {
+            float f[8];
+            unpack8(raw[p], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] += f[j];
+          }
         }
         if (has_res) {
           float r[8];
@@ -126,7 +139,9 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
 #pragma unroll
           for (int j = 0; j < 8; ++j) v[i][j] += r[j];
           const uint4 packed = pack8(v[i]);
-          for (int p = 0; p < nranks; ++p) *reinterpret_cast<uint4*>(P.res[p] + base + col) = packed;
+#pragma unroll
+          for (int p = 0; p < kMaxRanks; ++p)
+            if (p < nranks) *reinterpret_cast<uint4*>(P.res[p] + base + col) = packed;
           unpack8(packed, v[i]);  // continue from the rounded value every rank stores
         }
       }
@@ -137,7 +152,9 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
         const int col = (tid + i * nt) * 8;
         if (col >= H) continue;
         const uint4 packed = pack8(v[i]);
-        for (int p = 0; p < nranks; ++p) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
+#pragma unroll
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < nranks) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
       }
       continue;
     }
@@ -166,11 +183,12 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
 #pragma unroll
       for (int j = 0; j < 8; ++j) o[j] = v[i][j] * inv * g[j];
       const uint4 packed = pack8(o);
-      for (int p = 0; p < nranks; ++p) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < nranks) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
     }
   }
-  __threadfence_system();
-  block_barrier(P, rank, nranks, 1, epoch, err);
+  block_barrier(P, rank, nranks, 1, epoch, err, true);
   if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
 }
 

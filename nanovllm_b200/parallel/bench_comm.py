@@ -4,7 +4,7 @@ by the RMSNorm kernel, on the residual-stream shapes of a TP decode / prefill st
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \
         -m nanovllm_b200.parallel.bench_comm [--hidden 4096] [--tokens 1,128,2048,16384] [--iters 50]
 
-Timing: CUDA events on the launching stream around ``iters`` back-to-back launches (after a warm-up and a
+Timing: ``iters`` calls captured in one CUDA graph, CUDA events around one replay (after a warm-up replay and a
 barrier), max over ranks, microseconds per call.  The roofline of the fused path is its NVLink traffic per
 rank -- reduce-scatter reads (R-1)/R * T*H*2 bytes and the all-gather writes 2 * (R-1)/R * T*H*2 bytes (new
 residual and normalised rows) -- over the measured 770 GB/s per direction.
@@ -26,17 +26,29 @@ LINK_GBS = 770.0
 
 
 def _time(fn, iters: int) -> float:
+    """GPU time per call: ``iters`` calls captured in one CUDA graph (the decode path replays graphs, so host
+    launch overhead is not part of the cost being compared)."""
     for _ in range(3):
         fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
     torch.cuda.synchronize()
     dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(iters):
-        fn()
+    g.replay()
     b.record()
     torch.cuda.synchronize()
     us = torch.tensor([a.elapsed_time(b) * 1000.0 / iters], device="cuda")
+    del g
     dist.all_reduce(us, op=dist.ReduceOp.MAX)
     return float(us.item())
 
