@@ -21,7 +21,7 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
                             bool causal, c10::optional<torch::Tensor> err);
 int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out);
-int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K);
+int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act);
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
 void embedding_cuda(torch::Tensor out, torch::Tensor table, torch::Tensor ids, double scale, int64_t vstart,
                     int64_t vend);

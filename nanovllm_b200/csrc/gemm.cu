@@ -413,6 +413,39 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// Split-K finish of the fused gate/up GEMM: partials [S][M][N] in the 128-row interleaved weight order
+// (block b = rows [256b, 256b + 128) gate, [256b + 128, 256b + 256) up); out[m][f] = act(sum gate) * sum up for
+// f = 128 b + j, sums in split order.  One thread per 4 consecutive features of one row.
+__global__ void splitk_act_kernel(const float* __restrict__ partial, int S, int M, int N, bf16* __restrict__ out,
+                                  long out_ld, int act) {
+  const int I = N / 2;
+  const long total4 = (long)M * I / 4;
+  const long MN = (long)M * N;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {
+    const long e = i * 4;
+    const int m = (int)(e / I), f = (int)(e % I);
+    const int g = (f >> 7) * 256 + (f & 127);
+    const float* pg = partial + (long)m * N + g;
+    float4 a = *reinterpret_cast<const float4*>(pg);
+    float4 u = *reinterpret_cast<const float4*>(pg + 128);
+    for (int s = 1; s < S; ++s) {
+      const float4 va = *reinterpret_cast<const float4*>(pg + s * MN);
+      const float4 vu = *reinterpret_cast<const float4*>(pg + s * MN + 128);
+      a.x += va.x; a.y += va.y; a.z += va.z; a.w += va.w;
+      u.x += vu.x; u.y += vu.y; u.z += vu.z; u.w += vu.w;
+    }
+    const float ga[4] = {a.x, a.y, a.z, a.w}, ua[4] = {u.x, u.y, u.z, u.w};
+    uint32_t packed[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float o0 = (act == kActSiluMul ? silu(ga[2 * j]) : gelu_tanh(ga[2 * j])) * ua[2 * j];
+      const float o1 = (act == kActSiluMul ? silu(ga[2 * j + 1]) : gelu_tanh(ga[2 * j + 1])) * ua[2 * j + 1];
+      packed[j] = nvb::pack_bf16x2(o0, o1);
+    }
+    *reinterpret_cast<uint2*>(out + (long)m * out_ld + f) = make_uint2(packed[0], packed[1]);
+  }
+}
+
 // out[m][n] = sum_s partial[s][m][n], fixed order (float4 over n; N % 4 == 0)
 __global__ void splitk_sum_kernel(const float* __restrict__ partial, int S, long MN, bf16* __restrict__ out, int N,
                                   long out_ld) {
@@ -537,14 +570,18 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
     d.kblocks = kblocks;
     d.act = (int)act;
     const int groups = (N + NA * BM - 1) / (NA * BM);
-    if (act != kActNone) {
-      d.S = 1;  // the activation needs complete sums in the epilogue
-    } else if (force_splits > 0) {
+    if (force_splits > 0) {
       d.S = (int)force_splits;
     } else {
       d.S = workspace.has_value() ? decode_splits(groups, kblocks, sms) : 1;
     }
     if (d.S > kblocks) d.S = kblocks;
+    // with split K the activation runs after the split sum (splitk_act_kernel), not in the GEMM epilogue
+    if (d.S > 1 && act != kActNone) {
+      TORCH_CHECK(!partial_out, "partial output is not offered for the fused-activation GEMM");
+      TORCH_CHECK(out.stride(0) % 4 == 0, "activation output rows must be 8-byte aligned");
+      d.act = kActNone;
+    }
     splits_used = d.S;
     d.out = reinterpret_cast<bf16*>(out.data_ptr());
     d.out_ld = out.stride(0);
@@ -562,7 +599,12 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
     cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, am, bm, d, groups, stream)
                             : launch_decode_bn<1>(bn, am, bm, d, groups, stream);
     TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
-    if (d.S > 1 && partial_out) {
+    if (d.S > 1 && act != kActNone) {
+      const long work = (long)M * (N / 2) / 4;
+      int blocks = (int)((work + 255) / 256);
+      if (blocks > sms * 8) blocks = sms * 8;
+      splitk_act_kernel<<<blocks, 256, 0, stream>>>(d.partial, d.S, M, N, d.out, d.out_ld, (int)act);
+    } else if (d.S > 1 && partial_out) {
       // the caller consumes the partials itself (fused into its next kernel)
     } else if (d.S > 1) {
       const long MN = (long)M * N;
@@ -589,12 +631,15 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 }
 
 // Workspace splits the decode path needs from the caller (always 1: it reduces on chip).
-int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K) {
-  // K splits the decode path uses when the caller provides a partial buffer (act == none)
+int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
+  // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;
   const int NA = N % 256 == 0 ? 2 : 1;
   const int groups = (int)((N + NA * BM - 1) / (NA * BM));
   const int kblocks = (int)((K + BK - 1) / BK);
+  // a split fused-activation GEMM pays an extra fp32 round trip and a finishing kernel: only worth it when
+  // at most half the SMs would otherwise hold work
+  if (act != 0 && groups * 2 > num_sms()) return 1;
   int s = decode_splits(groups, kblocks, num_sms());
   return s > kblocks ? kblocks : s;
 }

@@ -61,7 +61,22 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[i][j] = 0.f;
       if (col < H) {
-        for (int sp = 0; sp < nsplit; ++sp) {
+        int sp = 0;
+        for (; sp + 4 <= nsplit; sp += 4) {  // four splits' loads in flight, still added in split order
+          float4 a[4], b[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float4* p = reinterpret_cast<const float4*>(xpart + (sp + u) * part_stride + row * (long)H + col);
+            a[u] = p[0];
+            b[u] = p[1];
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            v[i][0] += a[u].x; v[i][1] += a[u].y; v[i][2] += a[u].z; v[i][3] += a[u].w;
+            v[i][4] += b[u].x; v[i][5] += b[u].y; v[i][6] += b[u].z; v[i][7] += b[u].w;
+          }
+        }
+        for (; sp < nsplit; ++sp) {
           const float4* p = reinterpret_cast<const float4*>(xpart + sp * part_stride + row * (long)H + col);
           const float4 a = p[0], b = p[1];
           v[i][0] += a.x; v[i][1] += a.y; v[i][2] += a.z; v[i][3] += a.w;

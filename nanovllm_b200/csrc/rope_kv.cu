@@ -29,7 +29,9 @@ __global__ void qk_norm_rope_store_kernel(
   const int32_t slot = slots != nullptr ? slots[t] : -1;
   const __nv_bfloat16* row = qkv + t * qkv_stride;
   const int total = nq + 2 * nkv;
-  for (int h = warp; h < total; h += nwarps) {
+  // blockIdx.y picks a chunk of nwarps heads: more CTAs in flight when the input is split-K partials
+  const int h_end = min(total, (int)(blockIdx.y + 1) * nwarps);
+  for (int h = blockIdx.y * nwarps + warp; h < h_end; h += nwarps) {
     const bool is_q = h < nq, is_k = (h >= nq && h < nq + nkv), is_v = h >= nq + nkv;
     float lo[PAIRS], hi[PAIRS];
     if (qkv_part == nullptr) {
@@ -44,7 +46,24 @@ __global__ void qk_norm_rope_store_kernel(
       const float* src = qkv_part + t * (long)total * HD + (long)h * HD;
 #pragma unroll
       for (int p = 0; p < PAIRS; ++p) lo[p] = hi[p] = 0.f;
-      for (int sp = 0; sp < nsplit; ++sp) {
+      int sp = 0;
+      for (; sp + 4 <= nsplit; sp += 4) {  // four splits' loads in flight, still added in split order
+#pragma unroll
+        for (int p = 0; p < PAIRS; ++p) {
+          float a[4], b[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            a[u] = src[(sp + u) * part_stride + lane + 32 * p];
+            b[u] = src[(sp + u) * part_stride + lane + 32 * p + HALF];
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            lo[p] += a[u];
+            hi[p] += b[u];
+          }
+        }
+      }
+      for (; sp < nsplit; ++sp) {
 #pragma unroll
         for (int p = 0; p < PAIRS; ++p) {
           lo[p] += src[sp * part_stride + lane + 32 * p];
@@ -143,7 +162,7 @@ void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::
   }
   auto stream = at::cuda::getCurrentCUDAStream();
 #define LAUNCH(P)                                                                                                  \
-  qk_norm_rope_store_kernel<P><<<T, warps * 32, 0, stream>>>(                                                      \
+  qk_norm_rope_store_kernel<P><<<dim3((unsigned)T, (unsigned)((total + warps - 1) / warps)), warps * 32, 0, stream>>>(                                                      \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),        \
       cos_sin.data_ptr<float>(), (int)cos_sin.size(-1), qw, kw, (int)norm_mode, v_norm ? 1 : 0, (float)eps,         \
       reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), kc, vc, sl, (int)nq, (int)nkv, block_size, apply_rope ? 1 : 0, \

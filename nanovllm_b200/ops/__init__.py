@@ -162,7 +162,7 @@ def workspace(device: torch.device, numel: int) -> torch.Tensor:
 def reserve_workspace(device: torch.device, max_m: int, max_n: int, max_k: int) -> None:
     if _C is None:
         return
-    splits = max(_C.gemm_splits_for(m, max_n, max_k) for m in (1, 16, 64, 128, 256) if m <= max(1, max_m))
+    splits = max(_C.gemm_splits_for(m, max_n, max_k, 0) for m in (1, 16, 64, 128, 256) if m <= max(1, max_m))
     workspace(device, splits * min(256, max_m) * max_n)
 
 
@@ -295,16 +295,16 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
     C = _cuda_ext()
     parts = None
     splits = 1
-    if M <= 256 and act == ACT_NONE:
-        splits = force_splits if force_splits > 0 else C.gemm_splits_for(M, N, K)
+    if M <= 256:
+        splits = force_splits if force_splits > 0 else C.gemm_splits_for(M, N, K, int(act))
         if splits > 1:
             parts = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
     if out is None:
         out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
     C.gemm(x, w, out, int(act), parts, int(splits if parts is not None else (force_splits or 0)),
-           error_word(x.device), bool(partial_ok and parts is not None))
+           error_word(x.device), bool(partial_ok and parts is not None and act == ACT_NONE))
     if parts is not None:
-        if partial_ok:
+        if partial_ok and act == ACT_NONE:
             add_launches(1)
             return SplitK(parts)
         add_launches(2)

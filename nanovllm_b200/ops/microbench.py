@@ -35,31 +35,44 @@ def _copies(bytes_per_copy: int) -> int:
 
 
 def time_fn(fns, iters: int, warmup: int = 3) -> float:
-    """Mean microseconds per call, cycling through ``fns`` (one per operand copy)."""
+    """Mean GPU microseconds per call, cycling through ``fns`` (one per operand copy).  The ``iters`` calls are
+    captured in one CUDA graph and replayed, so host launch overhead (Python, argument marshalling) is not
+    counted -- the engine's decode path replays graphs the same way."""
     for i in range(warmup):
         fns[i % len(fns)]()
     torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g):
+            for i in range(iters):
+                fns[i % len(fns)]()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for i in range(iters):
-        fns[i % len(fns)]()
+    g.replay()
     b.record()
     torch.cuda.synchronize()
+    del g
     return a.elapsed_time(b) * 1000.0 / iters
 
 
-def bench_gemm(M, N, K, iters, act=0):
+def bench_gemm(M, N, K, iters, act=0, splits=0):
     dev = "cuda"
     wbytes = N * K * 2
     n = _copies(wbytes + M * K * 2)
     ws = [(torch.randn(N, K, device=dev) * 0.02).bfloat16() for _ in range(n)]
     xs = [torch.randn(M, K, device=dev).bfloat16() for _ in range(n)]
-    ours = time_fn([lambda w=w, x=x: ops.linear(x, w, act) for w, x in zip(ws, xs)], iters)
+    ours = time_fn([lambda w=w, x=x: ops.linear(x, w, act, force_splits=splits) for w, x in zip(ws, xs)], iters)
     cublas = time_fn([lambda w=w, x=x: torch.matmul(x, w.t()) for w, x in zip(ws, xs)], iters)
     out_cols = N // 2 if act else N
     byts = wbytes + M * K * 2 + M * out_cols * 2
     flops = 2.0 * M * N * K
-    return {"case": f"gemm M={M} N={N} K={K}" + (" act" if act else ""), "us": round(ours, 2),
+    return {"case": f"gemm M={M} N={N} K={K}" + (" act" if act else "") + (f" S={splits}" if splits else ""),
+            "us": round(ours, 2),
             "cublas_us": round(cublas, 2), "TBps": round(byts / ours / 1e6, 3), "TFLOPs": round(flops / ours / 1e6, 1)}
 
 
@@ -141,7 +154,7 @@ def main():
     ap.add_argument("--only", default="gemm,decode,prefill,norm,rope,sample")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--out", default=None)
-    ap.add_argument("--gemm", default=None, help="single GEMM case M,N,K[,act] (e.g. for an ncu capture)")
+    ap.add_argument("--gemm", default=None, help="GEMM cases M,N,K[,act[,splits]] separated by ';' (e.g. for an ncu capture)")
     ap.add_argument("--decode", default=None, help="single decode-attention case B,ctx,nq,nkv,hd")
     a = ap.parse_args()
     hbm, tflops, src = peaks()
@@ -150,8 +163,9 @@ def main():
     if a.gemm or a.decode:
         only = set()
         if a.gemm:
-            v = [int(x) for x in a.gemm.split(",")]
-            rows.append(bench_gemm(v[0], v[1], v[2], a.iters, v[3] if len(v) > 3 else 0))
+            for case in a.gemm.split(";"):
+                v = [int(x) for x in case.split(",")]
+                rows.append(bench_gemm(v[0], v[1], v[2], a.iters, v[3] if len(v) > 3 else 0, v[4] if len(v) > 4 else 0))
         if a.decode:
             v = [int(x) for x in a.decode.split(",")]
             rows.append(bench_decode(v[0], v[1], v[2], v[3], v[4], a.iters))

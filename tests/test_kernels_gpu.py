@@ -191,6 +191,23 @@ def test_gemm_fused_gate_up(M, act):
     close(y, y_ref, 5e-3, 0.03)
 
 
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_gemm_fused_gate_up_split_k(splits):
+    """Decode-sized fused gate/up GEMM with the K range split over CTAs (activation after the split sum)."""
+    g = torch.Generator().manual_seed(11 + splits)
+    M, K, I = 96, 2048, 2048
+    x = (torch.randn(M, K, generator=g) * 0.5).bfloat16()
+    gate = (torch.randn(I, K, generator=g) * 0.05).bfloat16()
+    up = (torch.randn(I, K, generator=g) * 0.05).bfloat16()
+    w = ref.interleave_gate_up(torch.cat([gate, up]), 128).contiguous()
+    yg, yu = ref.linear(x, gate).float(), ref.linear(x, up).float()
+    y_ref = (ref.silu(yg) * yu).bfloat16()
+    y = ops.linear(x.to(DEV), w.to(DEV), ops.ACT_SILU_MUL, force_splits=splits)
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    close(y, y_ref, 5e-3, 0.03)
+
+
 @pytest.mark.parametrize("M,N,K", [(5, 4096, 4096), (128, 6144, 4096), (200, 4096, 12288)])
 def test_gemm_split_partials_fused_into_consumers(M, N, K):
     """Split-K partials summed by add+RMSNorm / RoPE match the materialised GEMM result."""
