@@ -47,11 +47,13 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 // Thread t < nranks publishes this block's arrival to rank t and waits (bounded) for rank t's arrival.  With
 // ``publish_writes`` the block's earlier global stores (peer stores included) are made visible at system scope
 // before the flag: bar.sync orders them before the signalling thread's fence + release store.
+// ``sync_first`` alone (no fence) publishes "this block is done reading": the loads' values were consumed
+// before bar.sync, and the release store orders them before the flag.
 __device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase, uint32_t epoch, int* err,
-                              bool publish_writes) {
+                              bool publish_writes, bool sync_first = false) {
   const int t = threadIdx.x;
   int ok = 1;
-  if (publish_writes) __syncthreads();
+  if (publish_writes || sync_first) __syncthreads();
   if (t < nranks) {
     if (publish_writes) __threadfence_system();
     st_release_sys(P.sig[t] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + rank), epoch);
@@ -94,10 +96,14 @@ __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
 }
 
 // mode: 0 x*w, 1 x*(1+w), 2 weightless, 3 no norm (plain all-reduce; out = sum (+ residual))
+// oneshot: every rank reads ALL rows from every peer and writes only its own residual / output (no peer stores,
+// no system fence); the closing barrier then only says "done reading your partials".  Two-shot (oneshot = 0)
+// moves (R-1)/R of the bytes instead of R-1 times them and wins once the message is large.
 template <int NV>
 __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int rank, int nranks, int T, int H,
                                                                  const bf16* __restrict__ w, float eps, int mode,
-                                                                 int has_res, uint32_t* counters, int* err) {
+                                                                 int has_res, uint32_t* counters, int* err,
+                                                                 int oneshot) {
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) s_epoch = counters[blockIdx.x] + 1;
@@ -107,8 +113,9 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
     if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
     return;
   }
-  const int per = (T + nranks - 1) / nranks;
-  const int r0 = rank * per, r1 = min(T, r0 + per);
+  const int per = oneshot ? T : (T + nranks - 1) / nranks;
+  const int r0 = oneshot ? 0 : rank * per, r1 = min(T, r0 + per);
+  const int p_lo = oneshot ? rank : 0, p_hi = oneshot ? rank + 1 : nranks;  // ranks whose buffers get the result
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int row = r0 + blockIdx.x; row < r1; row += gridDim.x) {
     const size_t base = (size_t)row * H;
@@ -141,7 +148,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
           const uint4 packed = pack8(v[i]);
 #pragma unroll
           for (int p = 0; p < kMaxRanks; ++p)
-            if (p < nranks) *reinterpret_cast<uint4*>(P.res[p] + base + col) = packed;
+            if (p >= p_lo && p < p_hi) *reinterpret_cast<uint4*>(P.res[p] + base + col) = packed;
           unpack8(packed, v[i]);  // continue from the rounded value every rank stores
         }
       }
@@ -154,7 +161,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
         const uint4 packed = pack8(v[i]);
 #pragma unroll
         for (int p = 0; p < kMaxRanks; ++p)
-          if (p < nranks) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
+          if (p >= p_lo && p < p_hi) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
       }
       continue;
     }
@@ -185,10 +192,10 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
       const uint4 packed = pack8(o);
 #pragma unroll
       for (int p = 0; p < kMaxRanks; ++p)
-        if (p < nranks) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
+        if (p >= p_lo && p < p_hi) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
     }
   }
-  block_barrier(P, rank, nranks, 1, epoch, err, true);
+  block_barrier(P, rank, nranks, 1, epoch, err, !oneshot, true);
   if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
 }
 
@@ -228,7 +235,7 @@ void ipc_close_cuda(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>
 void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, std::vector<int64_t> out,
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
-                            c10::optional<torch::Tensor> err, int64_t max_blocks) {
+                            c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot) {
   const int R = (int)in.size();
   TORCH_CHECK(R >= 1 && R <= kMaxRanks && (int)out.size() == R && (int)sig.size() == R && (int)res.size() == R,
               "one pointer per rank (at most 8 ranks)");
@@ -253,7 +260,8 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
   int threads = ((H / 8 + 31) / 32) * 32;
   if (threads > 1024) threads = 1024;
   const int nv = (H / 8 + threads - 1) / threads;
-  const int per = (int)((T + R - 1) / R);
+  if (oneshot < 0) oneshot = ((long)(R - 1) * T * H * 2 <= (2l << 20)) ? 1 : 0;  // auto: one-shot up to 2 MiB
+  const int per = oneshot ? (int)T : (int)((T + R - 1) / R);
   int grid = per < max_blocks ? per : (int)max_blocks;
   if (grid > kMaxBlocks) grid = kMaxBlocks;
   if (grid < 1) grid = 1;
@@ -262,7 +270,7 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
   uint32_t* cnt = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
 #define LAUNCH(NV_)                                                                                              \
   tp_allreduce_norm_kernel<NV_><<<grid, threads, 0, stream>>>(P, (int)rank, R, (int)T, (int)H, w, (float)eps, \
-                                                              (int)mode, has_res ? 1 : 0, cnt, e)
+                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot)
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;
