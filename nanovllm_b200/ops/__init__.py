@@ -280,6 +280,12 @@ def prefill_attention(q, cu_q, cu_k, max_q, nq, nkv, hd, scale, softcap=0.0, win
 
 
 # ------------------------------------------------------------------------------------------------ linear
+def library_gemm() -> bool:
+    """``NVB_BASELINE=1``: every projection runs as a cuBLAS GEMM (torch.matmul) with the activation as a
+    separate kernel -- the unfused library baseline this engine is compared against."""
+    return os.environ.get("NVB_BASELINE", "0") not in ("0", "", "false", "no")
+
+
 def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[torch.Tensor] = None,
            force_splits: int = 0, partial_ok: bool = False):
     """y = x @ w^T on the tcgen05 GEMM.  act != 0 expects gate/up rows interleaved in 128-row blocks.
@@ -289,6 +295,12 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
     if not x.is_cuda:
         return ref.linear(x, w, act)
     x = materialize(x)
+    if library_gemm():
+        if act != ACT_NONE:
+            return act_mul(torch.matmul(x, w.t()), act, interleaved=True)
+        if out is not None:
+            return torch.matmul(x, w.t(), out=out)
+        return torch.matmul(x, w.t())
     M, K = x.shape
     N = w.shape[0]
     ncols = N // 2 if act != ACT_NONE else N

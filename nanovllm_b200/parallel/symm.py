@@ -33,6 +33,8 @@ _WS: Optional["TPWorkspace"] = None
 
 
 def fused_enabled() -> bool:
+    if os.environ.get("NVB_BASELINE", "0") not in ("0", "", "false", "no"):
+        return False  # the library baseline all-reduces through NCCL
     return os.environ.get("NVB_TP_FUSED", "1") not in ("0", "false", "no")
 
 
