@@ -1,6 +1,6 @@
 """Headline benchmark: decode tokens/s (max over ranks) on the Qwen3-8B-shaped model, bf16, TP = N GPUs.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference|baseline]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: tensor parallel over NCCL)
 
 Workload (BASELINE config 5 shape): random-init Qwen3-8B architecture (36 layers, hidden 4096, 32 q / 8 kv heads,
@@ -13,6 +13,10 @@ decode steps run through ``LLM.step()``.
   head, sampler) and summed over the K steps; max over ranks.
 * ``e2e``: the same tokens / wall-clock of the K ``LLM.step()`` calls (host scheduling, pinned H2D of each step's
   inputs, D2H read of the sampled tokens included); max over ranks.
+* ``p50_ttft_ms``: after the timed region, ``--ttft-probe`` new requests join the running batch one at a time;
+  TTFT is add_request -> first sampled token (the prefill-first scheduler runs the newcomer's prefill next).
+* ``--impl baseline``: the same engine with every projection as a cuBLAS GEMM (activation as its own kernel)
+  and NCCL all-reduces -- the unfused library baseline.
 The weights (16 GB) and the KV cache (tens of GB) are far larger than the 126 MB L2, so no explicit L2 flush is
 needed between steps.
 """
@@ -100,12 +104,13 @@ def run_ours(args):
     gen = torch.Generator().manual_seed(1234)
     lens = torch.randint(args.min_prompt, args.max_prompt + 1, (B,), generator=gen).tolist()
     prompts = [torch.randint(1, hf.vocab_size - 1, (n,), generator=gen).tolist() for n in lens]
-    max_len = args.max_prompt + args.warmup + args.steps + 64
+    extra = 4 * args.ttft_probe + args.profile_steps
+    max_len = args.max_prompt + args.warmup + args.steps + extra + 64
     cfg = EngineConfig(max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=args.prefill_chunk,
                        gpu_memory_utilization=0.92, stop_on_degenerate=False, cuda_graph_max_bs=B)
     llm = LLM((hf, weights), cfg, device=dev)
     del weights
-    sp = SamplingParams(max_tokens=args.warmup + args.steps + 8, ignore_eos=True).deterministic()
+    sp = SamplingParams(max_tokens=args.warmup + args.steps + extra + 8, ignore_eos=True).deterministic()
     seqs = [llm.add_request(p, sp) for p in prompts]
     torch.cuda.synchronize()
     t_pf = time.perf_counter()
@@ -114,7 +119,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t_pf
     ttfts = sorted(s.t_first_token - s.t_arrival for s in seqs)
-    p50_ttft = ttfts[len(ttfts) // 2]
+    p50_ttft_burst = ttfts[len(ttfts) // 2]
     prefill_tokens = sum(lens)
     running = len(llm.scheduler.running)
 
@@ -158,16 +163,32 @@ def run_ours(args):
         sampler.wait()
     launches = ops.launch_count()
     dev_ms = sum(step_ms)
+    h2d = runner.last_h2d_bytes
+    runner.step_events = None
+    # TTFT under load: new requests (prompt lengths from the same distribution) join the running batch one at a
+    # time, two decode steps apart; TTFT = add_request -> first sampled token on the host
+    probe = []
+    for _ in range(args.ttft_probe):
+        n = int(torch.randint(args.min_prompt, args.max_prompt + 1, (1,), generator=gen))
+        req = llm.add_request(torch.randint(1, hf.vocab_size - 1, (n,), generator=gen).tolist(),
+                              SamplingParams(max_tokens=2, ignore_eos=True).deterministic())
+        while req.num_completion_tokens == 0:
+            llm.step()
+        probe.append(req.t_first_token - req.t_arrival)
+        for _ in range(2):
+            llm.step()
+    probe.sort()
+    p50_ttft = probe[len(probe) // 2] if probe else p50_ttft_burst
     t = torch.tensor([dev_ms, wall * 1000.0], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     dev_ms, wall_ms = float(t[0]), float(t[1])
-    h2d = runner.last_h2d_bytes
     llm.close()
     if rank == 0:
         value = tokens / (dev_ms / 1000.0)
         e2e = tokens / (wall_ms / 1000.0)
         line = {
+            "impl": args.impl,
             "metric": "decode tok/s (box, max over ranks) Qwen3-8B-shape TP1/2/4/8; p50 TTFT",
             "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
@@ -177,7 +198,9 @@ def run_ours(args):
                        "global_batch": running, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}]",
                        "parallelism": f"tp{world}", "l2": "inputs larger than L2 (16 GB weights + KV cache)",
                        "prefill_tokens": prefill_tokens, "prefill_s": round(prefill_s, 3),
-                       "p50_ttft_ms": round(p50_ttft * 1000, 1)},
+                       "p50_ttft_ms": round(p50_ttft * 1000, 1),
+                       "ttft_note": f"p50 over {len(probe)} requests joining a running batch of {running}; "
+                                    f"the initial burst of {B} prompts had p50 {round(p50_ttft_burst * 1000, 1)} ms"},
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8 * running},
             "gpu_launches": launches,
@@ -199,13 +222,18 @@ def main():
     ap.add_argument("--prefill-chunk", type=int, default=16384)
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="decode steps run between cudaProfilerStart/Stop before the timed region")
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "baseline"], default="ours",
+                    help="baseline: this engine with cuBLAS GEMMs (separate activation kernel) and NCCL all-reduce")
+    ap.add_argument("--ttft-probe", type=int, default=8,
+                    help="requests that join the running batch one at a time after the timed region (p50 TTFT)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
         return
+    if args.impl == "baseline":
+        os.environ["NVB_BASELINE"] = "1"  # cuBLAS GEMMs + separate activation + NCCL all-reduce
     run_ours(args)
 
 
