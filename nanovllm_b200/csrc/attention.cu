@@ -21,6 +21,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 #include "tma_host.h"
 
 #include "attention_kernels.cuh"
@@ -58,12 +59,12 @@ void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
     auto cu_k = torch::zeros({B + 1}, ctx_lens.options());
     cu_k.slice(0, 1).copy_(torch::cumsum(ctx_lens, 0));
     const int total = B * nq;
-    attn_generic_kernel<<<(total * 32 + 127) / 128, 128, 0, stream>>>(
+    C10_CUDA_CHECK(nvb::launch(attn_generic_kernel, dim3((total * 32 + 127) / 128), dim3(128), 0, stream, 
         reinterpret_cast<const bf16*>(q.data_ptr()), (long)nq * hd, reinterpret_cast<bf16*>(out.data_ptr()),
         (long)nq * hd, reinterpret_cast<const bf16*>(k_cache.data_ptr()),
         reinterpret_cast<const bf16*>(v_cache.data_ptr()), 0, cu_q.data_ptr<int>(), cu_k.data_ptr<int>(),
         block_tables.data_ptr<int>(), block_tables.size(1), 1, B, nq, nkv, hd, block_size, (float)scale,
-        (float)softcap, (int)window, 1, B);
+        (float)softcap, (int)window, 1, B));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
@@ -81,9 +82,9 @@ void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
     auto kern = paged_decode_kernel<HD_, ST_>;                                                                   \
     size_t sm = decode_smem<HD_, ST_>();                                                                         \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                            \
-    kern<<<grid, 128, sm, stream>>>(km, vm, qp, block_tables.data_ptr<int>(), block_tables.size(1),              \
+    C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(128), sm, stream, km, vm, qp, block_tables.data_ptr<int>(), block_tables.size(1),              \
                                     ctx_lens.data_ptr<int>(), op, po, pl, nq, nkv, block_size, (float)scale,     \
-                                    (float)softcap, (int)window, (int)part_tiles, e);                            \
+                                    (float)softcap, (int)window, (int)part_tiles, e));                            \
   }
   if (hd == 64) LAUNCH_DEC(64, 4)
   else if (hd == 128) LAUNCH_DEC(128, 3)
@@ -91,8 +92,8 @@ void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
 #undef LAUNCH_DEC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (nsplit > 1) {
-    attn_combine_kernel<<<dim3(nq, B), hd < 128 ? hd : 128, 0, stream>>>(
-        po, pl, ctx_lens.data_ptr<int>(), op, nq, (int)nsplit, hd, (int)part_tiles, (int)window);
+    C10_CUDA_CHECK(nvb::launch(attn_combine_kernel, dim3(dim3(nq, B)), dim3(hd < 128 ? hd : 128), 0, stream, 
+        po, pl, ctx_lens.data_ptr<int>(), op, nq, (int)nsplit, hd, (int)part_tiles, (int)window));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }
@@ -135,10 +136,10 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
     const bf16* vc = paged ? reinterpret_cast<const bf16*>(v_cache->data_ptr())
                            : reinterpret_cast<const bf16*>(kv_src->data_ptr()) + (nq + nkv) * hd;
     const long kvs = paged ? 0 : kv_src->stride(0);
-    attn_generic_kernel<<<((long)total_q * nq * 32 + 127) / 128, 128, 0, stream>>>(
+    C10_CUDA_CHECK(nvb::launch(attn_generic_kernel, dim3(((long)total_q * nq * 32 + 127) / 128), dim3(128), 0, stream, 
         reinterpret_cast<const bf16*>(q.data_ptr()), q_stride, reinterpret_cast<bf16*>(out.data_ptr()), o_stride, kc,
         vc, kvs, cu_q.data_ptr<int>(), cu_k.data_ptr<int>(), bt, bt_stride, paged ? 1 : 0, nseq, nq, nkv, hd,
-        block_size, (float)scale, (float)softcap, (int)window, causal ? 1 : 0, total_q);
+        block_size, (float)scale, (float)softcap, (int)window, causal ? 1 : 0, total_q));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
@@ -165,9 +166,9 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
     auto kern = prefill_attn_kernel<HD_, ST_>;                                                                   \
     size_t sm = prefill_smem<HD_, ST_>();                                                                        \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                            \
-    kern<<<grid, 128, sm, stream>>>(km, vm, qp, q_stride, op, o_stride, cu_q.data_ptr<int>(),                    \
+    C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(128), sm, stream, km, vm, qp, q_stride, op, o_stride, cu_q.data_ptr<int>(),                    \
                                     cu_k.data_ptr<int>(), bt, bt_stride, paged ? 1 : 0, nq, nkv, block_size,     \
-                                    (float)scale, (float)softcap, (int)window, causal ? 1 : 0, e);               \
+                                    (float)scale, (float)softcap, (int)window, causal ? 1 : 0, e));               \
   }
   if (hd == 64) LAUNCH_PF(64, 4)
   else if (hd == 128) LAUNCH_PF(128, 2)

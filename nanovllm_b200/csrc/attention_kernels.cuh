@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ ctx_lens, bf16* __restrict__ out,
     float* __restrict__ part_o, float* __restrict__ part_lse, int nq, int nkv, int block_size, float scale,
     float softcap, int window, int part_tiles, int* err) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   constexpr int TILE = KT * HD * 2;
   constexpr int QP = HD + 8;  // padded Q row (elements)
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -249,6 +251,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                     const int* __restrict__ ctx_lens, bf16* __restrict__ out, int nq, int nsplit,
                                     int HD, int part_tiles, int window) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const int qh = blockIdx.x, b = blockIdx.y;
   const int ctx = ctx_lens[b];
   const int ntiles = (ctx + KT - 1) / KT;
@@ -277,6 +281,8 @@ __global__ void __launch_bounds__(128) prefill_attn_kernel(
     long q_tok_stride, bf16* __restrict__ out, long o_tok_stride, const int* __restrict__ cu_q,
     const int* __restrict__ cu_k, const int* __restrict__ block_tables, int bt_stride, int paged, int nq, int nkv,
     int block_size, float scale, float softcap, int window, int causal, int* err) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   constexpr int TILE = KT * HD * 2;
   constexpr int QP = HD + 8;
   const int qtile = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
@@ -464,6 +470,8 @@ __global__ void attn_generic_kernel(const bf16* __restrict__ q, long q_tok_strid
                                     const int* __restrict__ block_tables, int bt_stride, int paged, int nseq, int nq,
                                     int nkv, int HD, int block_size, float scale, float softcap, int window,
                                     int causal, int total_q) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp_global >= total_q * nq) return;

@@ -35,6 +35,15 @@ NV_DEVICE uint64_t global_timer_ns() {
   return t;
 }
 
+// ------------------------------------------------------------------------------------------ programmatic launch
+// Every kernel starts with pdl_wait(): it returns once the preceding kernel on the stream has completed and its
+// memory is visible (immediately when the kernel was launched without the programmatic-serialization
+// attribute).  pdl_trigger() lets the next kernel's CTAs be scheduled while this one is still running, so their
+// prologue (barrier set-up, TMEM allocation, weight prefetch) overlaps this kernel's tail.  Nothing before
+// pdl_wait() may read data an earlier kernel writes or write data an earlier kernel reads.
+NV_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+NV_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 NV_DEVICE void record_error(int* err, int code) {
   if (err != nullptr) atomicCAS(err, 0, code);
 }

@@ -22,6 +22,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 #include "tma_host.h"
 
 namespace {
@@ -58,6 +59,8 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int bn) {
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap amap,
                                                          const __grid_constant__ CUtensorMap bmap, GemmArgs args) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   constexpr uint32_t A_BYTES = BM * BK * 2;
   constexpr uint32_t B_BYTES = BN * BK * 2;
   constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
@@ -320,12 +323,26 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   __syncthreads();
   nvb::tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  nvb::pdl_trigger();
 
   if (warp == 0 && lane == 0) {
     nvb::tma_prefetch_desc(&amap);
     nvb::tma_prefetch_desc(&bmap);
-    uint32_t it = 0;
-    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+    // The weights are never written by earlier kernels: the first ring's weight tiles stream in before the
+    // dependency wait, overlapping the previous kernel's tail; the activation tiles follow after it.
+    const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+    for (int it = 0; it < pre; ++it) {
+      uint8_t* sa = smem + it * STAGE_BYTES;
+      nvb::mbar_arrive_expect_tx(&full_bar[it], STAGE_BYTES);
+#pragma unroll
+      for (int j = 0; j < NA; ++j)
+        nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[it], (kb0 + it) * BK, row0 + j * BM);
+    }
+    nvb::pdl_wait();
+    for (int it = 0; it < pre; ++it)
+      nvb::tma_load_2d(smem + it * STAGE_BYTES + A_BYTES, &bmap, &full_bar[it], (kb0 + it) * BK, 0);
+    uint32_t it = pre;
+    for (int kb = kb0 + pre; kb < kb1; ++kb, ++it) {
       const int s = it % STAGES;
       if (!nvb::mbar_wait(&empty_bar[s], ((it / STAGES) & 1u) ^ 1u, args.err, &abort_flag)) break;
       uint8_t* sa = smem + s * STAGE_BYTES;
@@ -334,7 +351,10 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
       for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[s], kb * BK, row0 + j * BM);
       nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, 0);
     }
-  } else if (warp == 1 && lane == 0) {
+  } else {
+    nvb::pdl_wait();  // the epilogue writes outputs a previous kernel may still read
+  }
+  if (warp == 1 && lane == 0) {
     uint32_t it = 0;
     bool ok = true;
     for (int kb = kb0; kb < kb1; ++kb, ++it) {
@@ -418,6 +438,8 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
 // f = 128 b + j, sums in split order.  One thread per 4 consecutive features of one row.
 __global__ void splitk_act_kernel(const float* __restrict__ partial, int S, int M, int N, bf16* __restrict__ out,
                                   long out_ld, int act) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const int I = N / 2;
   const long total4 = (long)M * I / 4;
   const long MN = (long)M * N;
@@ -449,6 +471,8 @@ __global__ void splitk_act_kernel(const float* __restrict__ partial, int S, int 
 // out[m][n] = sum_s partial[s][m][n], fixed order (float4 over n; N % 4 == 0)
 __global__ void splitk_sum_kernel(const float* __restrict__ partial, int S, long MN, bf16* __restrict__ out, int N,
                                   long out_ld) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long total4 = MN / 4;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total4; i += (long)gridDim.x * blockDim.x) {
     float4 acc = reinterpret_cast<const float4*>(partial)[i];
@@ -475,7 +499,7 @@ cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const De
   constexpr size_t sm = 1024 + (size_t)ST * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
   static_assert(sm <= 227 * 1024, "decode gemm shared memory");
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  kern<<<groups * a.S, 128, sm, stream>>>(am, bm, a);
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a));
   return cudaGetLastError();
 }
 
@@ -531,7 +555,7 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   const int units = a.tiles_m * a.tiles_n * a.splits;
   int grid = units < max_ctas ? units : max_ctas;
-  kern<<<grid, 192, sm, stream>>>(am, bm, a);
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(192), sm, stream, am, bm, a));
 }
 
 }  // namespace
@@ -603,14 +627,14 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
       const long work = (long)M * (N / 2) / 4;
       int blocks = (int)((work + 255) / 256);
       if (blocks > sms * 8) blocks = sms * 8;
-      splitk_act_kernel<<<blocks, 256, 0, stream>>>(d.partial, d.S, M, N, d.out, d.out_ld, (int)act);
+      C10_CUDA_CHECK(nvb::launch(splitk_act_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, M, N, d.out, d.out_ld, (int)act));
     } else if (d.S > 1 && partial_out) {
       // the caller consumes the partials itself (fused into its next kernel)
     } else if (d.S > 1) {
       const long MN = (long)M * N;
       int blocks = (int)((MN / 4 + 255) / 256);
       if (blocks > sms * 8) blocks = sms * 8;
-      splitk_sum_kernel<<<blocks, 256, 0, stream>>>(d.partial, d.S, MN, d.out, N, d.out_ld);
+      C10_CUDA_CHECK(nvb::launch(splitk_sum_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, MN, d.out, N, d.out_ld));
     }
   } else {
     constexpr int BN = 256;
@@ -654,7 +678,7 @@ void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out) {
   if (MN == 0) return;
   int blocks = (int)((MN / 4 + 255) / 256);
   if (blocks > num_sms() * 8) blocks = num_sms() * 8;
-  splitk_sum_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      parts.data_ptr<float>(), S, MN, reinterpret_cast<bf16*>(out.data_ptr()), (int)N, out.stride(0));
+  C10_CUDA_CHECK(nvb::launch(splitk_sum_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+      parts.data_ptr<float>(), S, MN, reinterpret_cast<bf16*>(out.data_ptr()), (int)N, out.stride(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 
@@ -37,6 +38,8 @@ __device__ __forceinline__ float block_sum32(float v, float* red) {
 // Each thread owns up to 4 vectors of 8 elements (H <= 32768 with 1024 threads).
 __global__ void rms_norm_post_add_kernel(const bf16* __restrict__ x, long x_stride, bf16* __restrict__ residual,
                                          const bf16* __restrict__ w, int H, float eps, int mode, float post_scale) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -94,6 +97,8 @@ __global__ void rms_norm_post_add_kernel(const bf16* __restrict__ x, long x_stri
 __global__ void ple_combine_kernel(bf16* __restrict__ out, const bf16* __restrict__ proj, const bf16* __restrict__ tok,
                                    const bf16* __restrict__ w, long rows, int P, float eps, float proj_scale,
                                    float out_scale) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -117,6 +122,8 @@ __global__ void ple_combine_kernel(bf16* __restrict__ out, const bf16* __restric
 
 __global__ void gate_act_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ gate, long g_ld,
                                     const bf16* __restrict__ other, long o_ld, long rows, int cols) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * cols) return;
   const long r = i / cols;
@@ -126,6 +133,8 @@ __global__ void gate_act_mul_kernel(bf16* __restrict__ out, const bf16* __restri
 }
 
 __global__ void srq_kernel(bf16* __restrict__ x, long ld, long rows, int cols, float scale) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * cols) return;
   const long r = i / cols;
@@ -163,9 +172,9 @@ void rms_norm_post_add_cuda(torch::Tensor x, torch::Tensor residual, c10::option
   int threads = ((H / 8 + 31) / 32) * 32;
   if (threads > 1024) threads = 1024;
   TORCH_CHECK((H / 8 + threads - 1) / threads <= 4, "hidden size too large");
-  rms_norm_post_add_kernel<<<rows, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(rms_norm_post_add_kernel, dim3(rows), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const bf16*>(x.data_ptr()), x.dim() > 1 ? x.stride(-2) : H,
-      reinterpret_cast<bf16*>(residual.data_ptr()), w, H, (float)eps, (int)mode, (float)post_scale);
+      reinterpret_cast<bf16*>(residual.data_ptr()), w, H, (float)eps, (int)mode, (float)post_scale));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -181,10 +190,10 @@ void ple_combine_cuda(torch::Tensor out, torch::Tensor proj, torch::Tensor tok, 
   TORCH_CHECK(proj.numel() == tok.numel() && out.numel() == tok.numel() && tok.numel() % P == 0, "shape mismatch");
   const long rows = tok.numel() / P;
   if (rows == 0) return;
-  ple_combine_kernel<<<blocks_for(rows, 8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(ple_combine_kernel, dim3(blocks_for(rows, 8)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(proj.data_ptr()),
       reinterpret_cast<const bf16*>(tok.data_ptr()), reinterpret_cast<const bf16*>(weight.data_ptr()), rows, P,
-      (float)eps, (float)proj_scale, (float)out_scale);
+      (float)eps, (float)proj_scale, (float)out_scale));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -197,9 +206,9 @@ void gate_act_mul_cuda(torch::Tensor out, torch::Tensor gate, torch::Tensor othe
   const long rows = gate.size(0);
   const int cols = gate.size(1);
   if (rows * cols == 0) return;
-  gate_act_mul_kernel<<<blocks_for(rows * cols, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(gate_act_mul_kernel, dim3(blocks_for(rows * cols, 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0),
-      reinterpret_cast<const bf16*>(other.data_ptr()), other.stride(0), rows, cols);
+      reinterpret_cast<const bf16*>(other.data_ptr()), other.stride(0), rows, cols));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -209,7 +218,7 @@ void srq_cuda(torch::Tensor x, double scale) {
   if (scale == 0.0 || x.numel() == 0) return;
   const long rows = x.size(0);
   const int cols = x.size(1);
-  srq_kernel<<<blocks_for(rows * cols, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<bf16*>(x.data_ptr()), x.stride(0), rows, cols, (float)scale);
+  C10_CUDA_CHECK(nvb::launch(srq_kernel, dim3(blocks_for(rows * cols, 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
+      reinterpret_cast<bf16*>(x.data_ptr()), x.stride(0), rows, cols, (float)scale));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -8,6 +8,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 using bf16 = __nv_bfloat16;
@@ -21,6 +22,8 @@ __device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.f + er
 
 __global__ void embedding_kernel(bf16* __restrict__ out, const bf16* __restrict__ table, const int64_t* __restrict__ ids,
                                  int H, float scale, long vstart, long vend) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long t = blockIdx.x;
   const long id = ids[t];
   const bool inside = id >= vstart && id < vend;
@@ -43,6 +46,8 @@ __global__ void embedding_kernel(bf16* __restrict__ out, const bf16* __restrict_
 // act: 1 silu(g)*u, 2 gelu_tanh(g)*u.  layout: 0 = [gate | up] halves, 1 = 128-row interleaved blocks
 __global__ void act_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ x, long rows, int I, long x_ld, int act,
                                int interleaved) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long total = rows * (long)I;
   for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
     const long r = idx / I;
@@ -62,6 +67,8 @@ __global__ void act_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ 
 
 // y = act(x + bias) in place; act: 0 none, 3 gelu(erf), 4 gelu(tanh)
 __global__ void bias_act_kernel(bf16* __restrict__ x, const bf16* __restrict__ bias, long rows, int N, long ld, int act) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long total = rows * (long)N;
   for (long idx = blockIdx.x * (long)blockDim.x + threadIdx.x; idx < total; idx += (long)gridDim.x * blockDim.x) {
     const long r = idx / N;
@@ -76,6 +83,8 @@ __global__ void bias_act_kernel(bf16* __restrict__ x, const bf16* __restrict__ b
 
 __global__ void gather_rows_kernel(bf16* __restrict__ out, const bf16* __restrict__ src, const int64_t* __restrict__ idx,
                                    int H, long src_ld) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const long r = blockIdx.x;
   const bf16* s = src + idx[r] * src_ld;
   bf16* d = out + r * (long)H;
@@ -85,6 +94,8 @@ __global__ void gather_rows_kernel(bf16* __restrict__ out, const bf16* __restric
 
 __global__ void mean_pool_l2_kernel(float* __restrict__ out, const bf16* __restrict__ x, const int* __restrict__ cu,
                                     int H) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   extern __shared__ float acc[];
   __shared__ float red[32];
   const int s = blockIdx.x;
@@ -122,9 +133,9 @@ void embedding_cuda(torch::Tensor out, torch::Tensor table, torch::Tensor ids, d
   TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
   if (T == 0) return;
   int threads = H / 8 < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
-  embedding_kernel<<<T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(embedding_kernel, dim3(T), dim3(threads), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(table.data_ptr()), ids.data_ptr<int64_t>(),
-      H, (float)scale, vstart, vend);
+      H, (float)scale, vstart, vend));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -132,9 +143,9 @@ void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interlea
   const long rows = x.size(0);
   const int I = x.size(1) / 2;
   if (rows == 0) return;
-  act_mul_kernel<<<grid_for(rows * I, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(act_mul_kernel, dim3(grid_for(rows * I, 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()), rows, I, x.stride(0),
-      (int)act, interleaved ? 1 : 0);
+      (int)act, interleaved ? 1 : 0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -142,9 +153,9 @@ void bias_act_cuda(torch::Tensor x, c10::optional<torch::Tensor> bias, int64_t a
   const long rows = x.size(0);
   const int N = x.size(1);
   if (rows == 0) return;
-  bias_act_kernel<<<grid_for(rows * N, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(bias_act_kernel, dim3(grid_for(rows * N, 256)), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(x.data_ptr()), bias.has_value() ? reinterpret_cast<const bf16*>(bias->data_ptr()) : nullptr,
-      rows, N, x.stride(0), (int)act);
+      rows, N, x.stride(0), (int)act));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -153,9 +164,9 @@ void gather_rows_cuda(torch::Tensor out, torch::Tensor src, torch::Tensor idx) {
   const int H = src.size(1);
   TORCH_CHECK(H % 8 == 0 && src.stride(1) == 1, "gather_rows needs 16-byte rows");
   if (R == 0) return;
-  gather_rows_kernel<<<R, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(gather_rows_kernel, dim3(R), dim3(128), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<bf16*>(out.data_ptr()), reinterpret_cast<const bf16*>(src.data_ptr()), idx.data_ptr<int64_t>(), H,
-      src.stride(0));
+      src.stride(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -163,7 +174,7 @@ void mean_pool_l2_cuda(torch::Tensor out, torch::Tensor x, torch::Tensor cu) {
   const int S = cu.numel() - 1;
   const int H = x.size(1);
   if (S <= 0) return;
-  mean_pool_l2_kernel<<<S, 256, H * sizeof(float), at::cuda::getCurrentCUDAStream()>>>(
-      out.data_ptr<float>(), reinterpret_cast<const bf16*>(x.data_ptr()), cu.data_ptr<int>(), H);
+  C10_CUDA_CHECK(nvb::launch(mean_pool_l2_kernel, dim3(S), dim3(256), H * sizeof(float), at::cuda::getCurrentCUDAStream(), 
+      out.data_ptr<float>(), reinterpret_cast<const bf16*>(x.data_ptr()), cu.data_ptr<int>(), H));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -7,6 +7,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 
@@ -47,6 +48,8 @@ __global__ void rms_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bflo
                                 __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
                                 int H, long x_stride, long out_stride, float eps, int mode,
                                 const float* __restrict__ xpart, int nsplit, long part_stride) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -141,6 +144,8 @@ template <int NV>
 __global__ void layer_norm_kernel(__nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
                                   const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w,
                                   const __nv_bfloat16* __restrict__ b, int H, float eps) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   __shared__ float red[32];
   const long row = blockIdx.x;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -246,7 +251,7 @@ void rms_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Tens
     nsplit = xpart->size(0);
     pstride = rows * (long)H;
   }
-#define LAUNCH(NVV) rms_norm_kernel<NVV><<<rows, threads, 0, stream>>>(o, xi, res, w, H, xs, os, (float)eps, (int)mode, xp, nsplit, pstride)
+#define LAUNCH(NVV) C10_CUDA_CHECK(nvb::launch(rms_norm_kernel<NVV>, dim3(rows), dim3(threads), 0, stream, o, xi, res, w, H, xs, os, (float)eps, (int)mode, xp, nsplit, pstride))
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;
@@ -274,7 +279,7 @@ void layer_norm_cuda(torch::Tensor out, torch::Tensor x, c10::optional<torch::Te
   auto* xi = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
   auto* w = reinterpret_cast<const __nv_bfloat16*>(weight.data_ptr());
   auto* b = reinterpret_cast<const __nv_bfloat16*>(bias.data_ptr());
-#define LAUNCH(NVV) layer_norm_kernel<NVV><<<rows, threads, 0, stream>>>(o, xi, res, w, b, H, (float)eps)
+#define LAUNCH(NVV) C10_CUDA_CHECK(nvb::launch(layer_norm_kernel<NVV>, dim3(rows), dim3(threads), 0, stream, o, xi, res, w, b, H, (float)eps))
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

@@ -9,6 +9,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 
@@ -20,6 +21,8 @@ __global__ void qk_norm_rope_store_kernel(
     const __nv_bfloat16* __restrict__ k_w, int norm_mode, int v_norm, float eps, __nv_bfloat16* __restrict__ q_out,
     __nv_bfloat16* __restrict__ k_cache, __nv_bfloat16* __restrict__ v_cache, const int32_t* __restrict__ slots,
     int nq, int nkv, int block_size, int apply_rope, const float* __restrict__ qkv_part, int nsplit, long part_stride) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   constexpr int HD = PAIRS * 64;
   constexpr int HALF = HD / 2;
   const long t = blockIdx.x;
@@ -162,11 +165,11 @@ void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::
   }
   auto stream = at::cuda::getCurrentCUDAStream();
 #define LAUNCH(P)                                                                                                  \
-  qk_norm_rope_store_kernel<P><<<dim3((unsigned)T, (unsigned)((total + warps - 1) / warps)), warps * 32, 0, stream>>>(                                                      \
+  C10_CUDA_CHECK(nvb::launch(qk_norm_rope_store_kernel<P>, dim3(dim3((unsigned)T, (unsigned)((total + warps - 1) / warps))), dim3(warps * 32), 0, stream,                                                       \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), positions.data_ptr<int64_t>(),        \
       cos_sin.data_ptr<float>(), (int)cos_sin.size(-1), qw, kw, (int)norm_mode, v_norm ? 1 : 0, (float)eps,         \
       reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), kc, vc, sl, (int)nq, (int)nkv, block_size, apply_rope ? 1 : 0, \
-      qp, nsplit, pstride)
+      qp, nsplit, pstride))
   switch (head_dim / 64) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

@@ -13,6 +13,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 using bf16 = __nv_bfloat16;
@@ -109,6 +110,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ 
                                                           const int64_t* __restrict__ seq_ids,
                                                           const int* __restrict__ steps, float softcap,
                                                           int64_t* __restrict__ out) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   __shared__ ArgMax sh_am[32];
   __shared__ float sh_f[32];
   __shared__ int sh_i[32];
@@ -303,9 +306,9 @@ void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, 
       seeds.data_ptr<int64_t>(), seq_ids.data_ptr<int64_t>(), steps.data_ptr<int>(), (float)softcap,            \
       out.data_ptr<int64_t>()
   if (logits.scalar_type() == at::kFloat)
-    sample_kernel<float><<<B, kThreads, 0, stream>>>(logits.data_ptr<float>(), ARGS);
+    C10_CUDA_CHECK(nvb::launch(sample_kernel<float>, dim3(B), dim3(kThreads), 0, stream, logits.data_ptr<float>(), ARGS));
   else
-    sample_kernel<bf16><<<B, kThreads, 0, stream>>>(reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS);
+    C10_CUDA_CHECK(nvb::launch(sample_kernel<bf16>, dim3(B), dim3(kThreads), 0, stream, reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS));
 #undef ARGS
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -10,6 +10,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 using bf16 = __nv_bfloat16;
@@ -19,6 +20,8 @@ __global__ void shortconv_kernel(const bf16* __restrict__ proj, long proj_ld, co
                                  int H, const int* __restrict__ cu, const int64_t* __restrict__ rows,
                                  const bool* __restrict__ fresh, float* __restrict__ state, long state_ld,
                                  long state_off, bf16* __restrict__ out) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   const int h = blockIdx.x * blockDim.x + threadIdx.x;
   const int s = blockIdx.y;
   if (h >= H) return;
@@ -67,9 +70,9 @@ void shortconv_cuda(torch::Tensor proj, torch::Tensor weight, torch::Tensor cu, 
   const int S = cu.numel() - 1;
   if (S <= 0) return;
   dim3 grid((H + 127) / 128, S);
-  shortconv_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  C10_CUDA_CHECK(nvb::launch(shortconv_kernel, dim3(grid), dim3(128), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const bf16*>(proj.data_ptr()), proj.stride(0), weight.data_ptr<float>(), L, H,
       cu.data_ptr<int>(), rows.data_ptr<int64_t>(), fresh.data_ptr<bool>(), state.data_ptr<float>(), state.size(1),
-      state_off, reinterpret_cast<bf16*>(out.data_ptr()));
+      state_off, reinterpret_cast<bf16*>(out.data_ptr())));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -20,6 +20,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <vector>
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 
@@ -104,6 +105,8 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
                                                                  const bf16* __restrict__ w, float eps, int mode,
                                                                  int has_res, uint32_t* counters, int* err,
                                                                  int oneshot) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
   __shared__ float red[32];
   __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) s_epoch = counters[blockIdx.x] + 1;
@@ -269,8 +272,8 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
   auto stream = at::cuda::getCurrentCUDAStream();
   uint32_t* cnt = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
 #define LAUNCH(NV_)                                                                                              \
-  tp_allreduce_norm_kernel<NV_><<<grid, threads, 0, stream>>>(P, (int)rank, R, (int)T, (int)H, w, (float)eps, \
-                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot)
+  C10_CUDA_CHECK(nvb::launch(tp_allreduce_norm_kernel<NV_>, dim3(grid), dim3(threads), 0, stream, P, (int)rank, R, (int)T, (int)H, w, (float)eps, \
+                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot))
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;
