@@ -515,6 +515,21 @@ cudaError_t launch_decode_bn(int bn, const CUtensorMap& am, const CUtensorMap& b
   }
 }
 
+// Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
+// one tile per CTA doubles the number of tile groups, which halves the K splits -- and the fp32 split partials
+// -- a small-N projection needs to fill the SMs.  The fused activation needs the gate/up pair (2).  Projections
+// with N <= NVB_DECODE_NA1_MAXN (default 0: off) use one tile.
+int decode_na(int N, int act) {
+  static int maxn = -1;
+  if (maxn < 0) {
+    const char* e = getenv("NVB_DECODE_NA1_MAXN");
+    maxn = e ? atoi(e) : 0;
+  }
+  if (act != kActNone) return 2;
+  if (N % 256 != 0) return 1;
+  return N <= maxn ? 1 : 2;
+}
+
 // K splits: make groups * S a near-multiple of the SM count (one CTA per SM), >= 4 k-blocks per split.
 int decode_splits(int groups, int kblocks, int sms) {
   if (groups >= sms) return 1;
@@ -586,7 +601,7 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
   int64_t splits_used = 1;
   if (M <= 256) {
     const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-    const int NA = (act != kActNone || N % 256 == 0) ? 2 : 1;
+    const int NA = decode_na(N, (int)act);
     DecodeArgs d{};
     d.N = N;
     d.M = M;
@@ -658,7 +673,7 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
   // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;
-  const int NA = N % 256 == 0 ? 2 : 1;
+  const int NA = decode_na((int)N, (int)act);
   const int groups = (int)((N + NA * BM - 1) / (NA * BM));
   const int kblocks = (int)((K + BK - 1) / BK);
   // a split fused-activation GEMM pays an extra fp32 round trip and a finishing kernel: only worth it when
