@@ -518,12 +518,12 @@ cudaError_t launch_decode_bn(int bn, const CUtensorMap& am, const CUtensorMap& b
 // Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
 // one tile per CTA doubles the number of tile groups, which halves the K splits -- and the fp32 split partials
 // -- a small-N projection needs to fill the SMs.  The fused activation needs the gate/up pair (2).  Projections
-// with N <= NVB_DECODE_NA1_MAXN (default 0: off) use one tile.
+// with N <= NVB_DECODE_NA1_MAXN (default 8192) use one tile.
 int decode_na(int N, int act) {
   static int maxn = -1;
   if (maxn < 0) {
     const char* e = getenv("NVB_DECODE_NA1_MAXN");
-    maxn = e ? atoi(e) : 0;
+    maxn = e ? atoi(e) : 8192;
   }
   if (act != kActNone) return 2;
   if (N % 256 != 0) return 1;
@@ -535,10 +535,10 @@ int decode_splits(int groups, int kblocks, int sms) {
   if (groups >= sms) return 1;
   int best = 1;
   double best_eff = (double)groups / (double)sms;
-  for (int s = 2; s <= 16 && s * 4 <= kblocks; ++s) {
+  // one wave only: a second wave repeats the pipeline fill and doubles the fp32 partials for little gain
+  for (int s = 2; s <= 16 && s * 4 <= kblocks && groups * s <= sms; ++s) {
     const int u = groups * s;
-    const int waves = (u + sms - 1) / sms;
-    const double eff = (double)u / ((double)waves * sms);
+    const double eff = (double)u / (double)sms;
     if (eff > best_eff + 0.03) {
       best_eff = eff;
       best = s;

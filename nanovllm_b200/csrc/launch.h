@@ -1,6 +1,6 @@
 // Kernel launch with programmatic dependent launch (PDL): the kernel may be scheduled before its predecessor on
 // the stream finishes and synchronises with it through griddepcontrol.wait (nvb::pdl_wait); stream capture
-// turns it into a programmatic graph edge.  NVB_PDL=1 turns the attribute on (plain stream order otherwise).
+// turns it into a programmatic graph edge.  NVB_PDL=0 turns the attribute off (plain stream order).
 #pragma once
 #include <cuda_runtime.h>
 #include <cstdlib>
@@ -12,7 +12,7 @@ inline bool pdl_enabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = std::getenv("NVB_PDL");
-    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
 }
