@@ -197,6 +197,13 @@ NV_DEVICE void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 NV_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Registers written by asynchronous tcgen05.ld become valid at tcgen05.wait::ld; routing them through an empty
+// volatile asm after the wait keeps the compiler from moving their first use above it.
+template <int N>
+NV_DEVICE void reg_fence(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the 128-byte swizzle that TMA
 // SWIZZLE_128B produces: rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked along M/N.

@@ -385,15 +385,21 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
     if (args.act != kActNone) {
       // NA == 2: tile 0 = gate rows, tile 1 = up rows of feature block ``group``
       const int f = group * BM + r;
+      constexpr int CH = BN < 32 ? BN : 32;  // columns per TMEM round trip (2 x CH registers)
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t g[16], u[16];
-        nvb::tmem_ld_32x32b_x16(t_row + c, g);
-        nvb::tmem_ld_32x32b_x16(t_row + BN + c, u);
+      for (int c = 0; c < BN; c += CH) {
+        uint32_t g[CH], u[CH];
+#pragma unroll
+        for (int q = 0; q < CH; q += 16) {
+          nvb::tmem_ld_32x32b_x16(t_row + c + q, g + q);
+          nvb::tmem_ld_32x32b_x16(t_row + BN + c + q, u + q);
+        }
         nvb::tmem_ld_wait();
+        nvb::reg_fence<CH>(g);
+        nvb::reg_fence<CH>(u);
         if (f < args.N / 2)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < CH; ++j) {
             const int t = c + j;
             if (t < args.M) {
               const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
@@ -406,20 +412,23 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
 #pragma unroll
       for (int jt = 0; jt < NA; ++jt) {
         const int f = row0 + jt * BM + r;
+        constexpr int CH = BN < 64 ? BN : 64;  // columns per TMEM round trip
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t v[16];
-          nvb::tmem_ld_32x32b_x16(t_row + jt * BN + c, v);
+        for (int c = 0; c < BN; c += CH) {
+          uint32_t v[CH];
+#pragma unroll
+          for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + jt * BN + c + q, v + q);
           nvb::tmem_ld_wait();
+          nvb::reg_fence<CH>(v);
           if (f < args.N) {
             if (args.S == 1) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
+              for (int j = 0; j < CH; ++j)
                 if (c + j < args.M) args.out[(long)(c + j) * args.out_ld + f] = __float2bfloat16(__uint_as_float(v[j]));
             } else {
               float* dst = args.partial + (long)split * args.M * args.N + f;
 #pragma unroll
-              for (int j = 0; j < 16; ++j)
+              for (int j = 0; j < CH; ++j)
                 if (c + j < args.M) dst[(long)(c + j) * args.N] = __uint_as_float(v[j]);
             }
           }
