@@ -272,8 +272,10 @@ struct DecodeArgs {
   int* err;
 };
 
-__host__ __device__ constexpr int decode_stages2(int na, int bn) {
-  return (200 * 1024) / (na * BM * BK * 2 + bn * BK * 2) > 8 ? 8 : (200 * 1024) / (na * BM * BK * 2 + bn * BK * 2);
+__host__ __device__ constexpr int decode_stages2(int na, int bn, int ksub = 1) {
+  return (200 * 1024) / (ksub * (na * BM * BK * 2 + bn * BK * 2)) > 8
+             ? 8
+             : (200 * 1024) / (ksub * (na * BM * BK * 2 + bn * BK * 2));
 }
 __host__ __device__ constexpr uint32_t pow2_cols(int n) {
   uint32_t c = 32;
@@ -281,14 +283,17 @@ __host__ __device__ constexpr uint32_t pow2_cols(int n) {
   return c;
 }
 
-template <int BN, int NA>
+// KSUB: 64-wide K boxes per pipeline stage.  Loading KSUB adjacent boxes of the same weight rows back to back
+// turns each weight row's 128-byte reads into KSUB * 128 contiguous bytes per stage (better DRAM page use).
+template <int BN, int NA, int KSUB>
 __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_constant__ CUtensorMap amap,
                                                              const __grid_constant__ CUtensorMap bmap,
                                                              DecodeArgs args) {
-  constexpr int STAGES = decode_stages2(NA, BN);
+  constexpr int STAGES = decode_stages2(NA, BN, KSUB);
   constexpr uint32_t A_SUB = BM * BK * 2;
   constexpr uint32_t A_BYTES = NA * A_SUB;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + BN * BK * 2;
+  constexpr uint32_t SUB_BYTES = A_BYTES + BN * BK * 2;  // one 64-wide K box set: NA weight tiles + activations
+  constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
   constexpr uint32_t TMEM_COLS = pow2_cols(NA * BN);
   constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
 
@@ -303,8 +308,9 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = blockIdx.x / args.S, split = blockIdx.x % args.S;
   const int row0 = group * (NA * BM);  // first weight row of this CTA
-  const int kb0 = (int)((long)args.kblocks * split / args.S);
-  const int kb1 = (int)((long)args.kblocks * (split + 1) / args.S);
+  const int nsuper = args.kblocks / KSUB;  // the host picks KSUB > 1 only when it divides kblocks
+  const int kb0 = (int)((long)nsuper * split / args.S);   // in stage (super-block) units
+  const int kb1 = (int)((long)nsuper * (split + 1) / args.S);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -335,12 +341,18 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
       uint8_t* sa = smem + it * STAGE_BYTES;
       nvb::mbar_arrive_expect_tx(&full_bar[it], STAGE_BYTES);
 #pragma unroll
-      for (int j = 0; j < NA; ++j)
-        nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[it], (kb0 + it) * BK, row0 + j * BM);
+      for (int ks = 0; ks < KSUB; ++ks)
+#pragma unroll
+        for (int j = 0; j < NA; ++j)
+          nvb::tma_load_2d(sa + ks * SUB_BYTES + j * A_SUB, &amap, &full_bar[it], ((kb0 + it) * KSUB + ks) * BK,
+                           row0 + j * BM);
     }
     nvb::pdl_wait();
     for (int it = 0; it < pre; ++it)
-      nvb::tma_load_2d(smem + it * STAGE_BYTES + A_BYTES, &bmap, &full_bar[it], (kb0 + it) * BK, 0);
+#pragma unroll
+      for (int ks = 0; ks < KSUB; ++ks)
+        nvb::tma_load_2d(smem + it * STAGE_BYTES + ks * SUB_BYTES + A_BYTES, &bmap, &full_bar[it],
+                         ((kb0 + it) * KSUB + ks) * BK, 0);
     uint32_t it = pre;
     for (int kb = kb0 + pre; kb < kb1; ++kb, ++it) {
       const int s = it % STAGES;
@@ -348,8 +360,12 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
       uint8_t* sa = smem + s * STAGE_BYTES;
       nvb::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
 #pragma unroll
-      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[s], kb * BK, row0 + j * BM);
-      nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, 0);
+      for (int ks = 0; ks < KSUB; ++ks) {
+#pragma unroll
+        for (int j = 0; j < NA; ++j)
+          nvb::tma_load_2d(sa + ks * SUB_BYTES + j * A_SUB, &amap, &full_bar[s], (kb * KSUB + ks) * BK, row0 + j * BM);
+        nvb::tma_load_2d(sa + ks * SUB_BYTES + A_BYTES, &bmap, &full_bar[s], (kb * KSUB + ks) * BK, 0);
+      }
     }
   } else {
     nvb::pdl_wait();  // the epilogue writes outputs a previous kernel may still read
@@ -361,14 +377,18 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
       const int s = it % STAGES;
       if (!nvb::mbar_wait(&full_bar[s], (it / STAGES) & 1u, args.err, &abort_flag)) { ok = false; break; }
       nvb::tc_fence_after();
-      const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-      for (int j = 0; j < NA; ++j)
+      for (int ks = 0; ks < KSUB; ++ks) {
+        const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES + ks * SUB_BYTES);
+        const uint32_t b_addr = a_addr + A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          nvb::tc_mma_f16(tmem_base + j * BN, nvb::sdesc_kmajor_sw128(a_addr + j * A_SUB + kk * 32),
-                          nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC, (kb > kb0 || kk > 0) ? 1u : 0u);
+        for (int j = 0; j < NA; ++j)
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            nvb::tc_mma_f16(tmem_base + j * BN, nvb::sdesc_kmajor_sw128(a_addr + j * A_SUB + kk * 32),
+                            nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
+                            (kb > kb0 || ks > 0 || kk > 0) ? 1u : 0u);
+      }
       nvb::tc_commit(&empty_bar[s]);
     }
     if (ok) nvb::tc_commit(tfull_bar);
@@ -500,28 +520,45 @@ __global__ void splitk_sum_kernel(const float* __restrict__ partial, int S, long
   }
 }
 
-template <int BN, int NA>
+template <int BN, int NA, int KSUB>
 cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
                           cudaStream_t stream) {
-  auto kern = gemm_decode_kernel<BN, NA>;
-  constexpr int ST = decode_stages2(NA, BN);
-  constexpr size_t sm = 1024 + (size_t)ST * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
-  static_assert(sm <= 227 * 1024, "decode gemm shared memory");
+  auto kern = gemm_decode_kernel<BN, NA, KSUB>;
+  constexpr int ST = decode_stages2(NA, BN, KSUB);
+  constexpr size_t sm = 1024 + (size_t)ST * KSUB * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
+  static_assert(ST >= 1 && sm <= 227 * 1024, "decode gemm shared memory");
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a));
   return cudaGetLastError();
 }
 
-template <int NA>
-cudaError_t launch_decode_bn(int bn, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
-                             cudaStream_t st) {
+template <int NA, int KSUB>
+cudaError_t launch_decode_bn_k(int bn, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
+                               cudaStream_t st) {
   switch (bn) {
-    case 16: return launch_decode<16, NA>(am, bm, a, groups, st);
-    case 32: return launch_decode<32, NA>(am, bm, a, groups, st);
-    case 64: return launch_decode<64, NA>(am, bm, a, groups, st);
-    case 128: return launch_decode<128, NA>(am, bm, a, groups, st);
-    default: return launch_decode<256, NA>(am, bm, a, groups, st);
+    case 16: return launch_decode<16, NA, KSUB>(am, bm, a, groups, st);
+    case 32: return launch_decode<32, NA, KSUB>(am, bm, a, groups, st);
+    case 64: return launch_decode<64, NA, KSUB>(am, bm, a, groups, st);
+    case 128: return launch_decode<128, NA, KSUB>(am, bm, a, groups, st);
+    default: return launch_decode<256, NA, 1>(am, bm, a, groups, st);  // 256-token tiles keep one box per stage
   }
+}
+
+template <int NA>
+cudaError_t launch_decode_bn(int bn, int ksub, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a,
+                             int groups, cudaStream_t st) {
+  return ksub == 2 ? launch_decode_bn_k<NA, 2>(bn, am, bm, a, groups, st)
+                   : launch_decode_bn_k<NA, 1>(bn, am, bm, a, groups, st);
+}
+
+// 64-wide K boxes per decode pipeline stage (NVB_DECODE_KSUB, 1 or 2; default 1).
+int decode_ksub() {
+  static int k = -1;
+  if (k < 0) {
+    const char* e = getenv("NVB_DECODE_KSUB");
+    k = (e && atoi(e) == 2) ? 2 : 1;
+  }
+  return k;
 }
 
 // Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
@@ -644,8 +681,10 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
       printf("[gemm decode] M=%d N=%d K=%d bn=%d NA=%d groups=%d S=%d\n", M, N, K, bn, NA, groups, d.S);
     CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
     CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
-    cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, am, bm, d, groups, stream)
-                            : launch_decode_bn<1>(bn, am, bm, d, groups, stream);
+    int ksub = decode_ksub();
+    if (bn > 128 || kblocks % ksub != 0 || d.S > kblocks / ksub) ksub = 1;
+    cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, ksub, am, bm, d, groups, stream)
+                            : launch_decode_bn<1>(bn, ksub, am, bm, d, groups, stream);
     TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
     if (d.S > 1 && act != kActNone) {
       const long work = (long)M * (N / 2) / 4;
