@@ -43,7 +43,7 @@ void check_kv(const torch::Tensor& c, int64_t nkv, int64_t hd) {
 void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_lse,
                        double scale, double softcap, int64_t window, int64_t part_tiles, int64_t nsplit,
-                       c10::optional<torch::Tensor> err) {
+                       c10::optional<torch::Tensor> err, c10::optional<torch::Tensor> combine_counters) {
   const int B = q.size(0), nq = q.size(1), hd = q.size(2);
   const int nkv = k_cache.size(1), block_size = k_cache.size(2);
   TORCH_CHECK(q.is_contiguous() && out.is_contiguous(), "q/out must be contiguous");
@@ -84,14 +84,23 @@ void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_c
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);                            \
     C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(128), sm, stream, km, vm, qp, block_tables.data_ptr<int>(), block_tables.size(1),              \
                                     ctx_lens.data_ptr<int>(), op, po, pl, nq, nkv, block_size, (float)scale,     \
-                                    (float)softcap, (int)window, (int)part_tiles, e));                            \
+                                    (float)softcap, (int)window, (int)part_tiles, e, cnt));                       \
+  }
+  // the split merge runs inside the decode kernel (last split CTA per (sequence, kv head)) when the caller
+  // provides a zeroed int32 counter array of at least B * nkv entries; otherwise as a separate kernel
+  int* cnt = nullptr;
+  if (nsplit > 1 && combine_counters.has_value()) {
+    TORCH_CHECK(combine_counters->is_cuda() && combine_counters->scalar_type() == at::kInt &&
+                    combine_counters->numel() >= (long)B * nkv,
+                "combine counters must be int32 with at least B * nkv entries");
+    cnt = combine_counters->data_ptr<int>();
   }
   if (hd == 64) LAUNCH_DEC(64, 4)
   else if (hd == 128) LAUNCH_DEC(128, 3)
   else LAUNCH_DEC(256, 2)
 #undef LAUNCH_DEC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  if (nsplit > 1) {
+  if (nsplit > 1 && cnt == nullptr) {
     C10_CUDA_CHECK(nvb::launch(attn_combine_kernel, dim3(dim3(nq, B)), dim3(hd < 128 ? hd : 128), 0, stream, 
         po, pl, ctx_lens.data_ptr<int>(), op, nq, (int)nsplit, hd, (int)part_tiles, (int)window));
     C10_CUDA_KERNEL_LAUNCH_CHECK();

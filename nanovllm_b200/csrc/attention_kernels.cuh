@@ -49,12 +49,52 @@ __device__ __forceinline__ void issue_tile(uint8_t* k_dst, uint8_t* v_dst, const
 }
 
 // ============================================================================================ decode
+// Split-KV finish inside the decode kernel: every split CTA of (sequence b, kv head) announces itself on a
+// per-(b, kv head) counter once its partials are written; the last one to arrive merges the splits (fixed
+// split order, so the result does not depend on which CTA finishes last) and resets the counter for the next
+// launch.  Without a counter array (nullptr) the separate attn_combine_kernel does the merge.
+template <int HD>
+__device__ __forceinline__ void decode_arrive_and_combine(int* counters, const float* part_o, const float* part_lse,
+                                                          bf16* out, int b, int kvh, int nq, int nkv, int G,
+                                                          int nsplit, int ctx, int window, int part_tiles) {
+  __shared__ int s_last;
+  __threadfence();  // this CTA's partials are visible device-wide before it is counted
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int old = atomicAdd(&counters[b * nkv + kvh], 1);
+    s_last = old == nsplit - 1;
+    if (s_last) counters[b * nkv + kvh] = 0;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int ntiles = (ctx + KT - 1) / KT;
+  const int win_start = window > 0 ? max(0, ctx - window) : 0;
+  const int s_lo = (win_start / KT) / part_tiles;
+  const int s_hi = min(nsplit, (ntiles + part_tiles - 1) / part_tiles);
+  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+    const int row = idx / HD, d = idx % HD;
+    const int qh = kvh * G + row;
+    const long base = ((long)b * nq + qh) * nsplit;
+    float M = -INFINITY;
+    for (int sp = s_lo; sp < s_hi; ++sp) M = fmaxf(M, __ldcg(part_lse + base + sp));
+    float num = 0.f, den = 0.f;
+    if (M != -INFINITY)
+      for (int sp = s_lo; sp < s_hi; ++sp) {
+        const float w = exp2f(__ldcg(part_lse + base + sp) - M);
+        num += w * __ldcg(part_o + (base + sp) * HD + d);
+        den += w;
+      }
+    out[((long)b * nq + qh) * HD + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+  }
+}
+
 template <int HD, int STAGES>
 __global__ void __launch_bounds__(128) paged_decode_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
     const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ ctx_lens, bf16* __restrict__ out,
     float* __restrict__ part_o, float* __restrict__ part_lse, int nq, int nkv, int block_size, float scale,
-    float softcap, int window, int part_tiles, int* err) {
+    float softcap, int window, int part_tiles, int* err, int* combine_counters = nullptr) {
   nvb::pdl_wait();
   nvb::pdl_trigger();
   constexpr int TILE = KT * HD * 2;
@@ -68,7 +108,13 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
   const int win_start = window > 0 ? max(0, ctx - window) : 0;
   const int t_begin = max(split * part_tiles, win_start / KT);
   const int t_end = min((split + 1) * part_tiles, ntiles);
-  if (t_begin >= t_end) return;  // the combine step skips splits without keys
+  const bool fused_combine = combine_counters != nullptr && nsplit > 1;
+  if (t_begin >= t_end) {  // the combine step skips splits without keys
+    if (fused_combine)
+      decode_arrive_and_combine<HD>(combine_counters, part_o, part_lse, out, b, kvh, nq, nkv, G, nsplit, ctx, window,
+                                    part_tiles);
+    return;
+  }
   const int nt = t_end - t_begin;
 
   extern __shared__ uint8_t smem_raw[];
@@ -197,6 +243,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
     // drain copies still in flight (bounded) before the CTA exits
     if (tid == 0)
       for (int s = 0; s < STAGES; ++s) nvb::mbar_wait(&bars[s], 0, nullptr, nullptr);
+    if (fused_combine)  // keep the counters consistent; the error word already reports the failure
+      decode_arrive_and_combine<HD>(combine_counters, part_o, part_lse, out, b, kvh, nq, nkv, G, nsplit, ctx, window,
+                                    part_tiles);
     return;
   }
   // merge the four warps' partial softmax states through shared memory (the ring is free now)
@@ -246,6 +295,9 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
       if (dim == 0) part_lse[slot] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
+  if (fused_combine)
+    decode_arrive_and_combine<HD>(combine_counters, part_o, part_lse, out, b, kvh, nq, nkv, G, nsplit, ctx, window,
+                                  part_tiles);
 }
 
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,

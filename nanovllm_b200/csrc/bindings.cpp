@@ -13,7 +13,7 @@ void qk_norm_rope_store_cuda(torch::Tensor qkv, torch::Tensor positions, torch::
 void paged_decode_cuda(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_tables,
                        torch::Tensor ctx_lens, torch::Tensor out, torch::Tensor part_o, torch::Tensor part_lse,
                        double scale, double softcap, int64_t window, int64_t part_tiles, int64_t nsplit,
-                       c10::optional<torch::Tensor> err);
+                       c10::optional<torch::Tensor> err, c10::optional<torch::Tensor> combine_counters);
 void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu_q, torch::Tensor cu_k,
                             int64_t max_q, c10::optional<torch::Tensor> k_cache, c10::optional<torch::Tensor> v_cache,
                             c10::optional<torch::Tensor> block_tables, c10::optional<torch::Tensor> kv_src,

@@ -99,7 +99,7 @@ cudaError_t launch(const CUtensorMap& km, const CUtensorMap& vm, dim3 grid, cuda
   cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (r != cudaSuccess) return r;
   kern<<<grid, 128, sm, st>>>(km, vm, q, bt, bt_stride, ctx, out, po, pl, nq, nkv, block_size, scale, softcap, window,
-                              part_tiles, err);
+                              part_tiles, err, nullptr);  // split merge by the separate combine kernel below
   return cudaGetLastError();
 }
 

@@ -254,10 +254,27 @@ def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap=0.0
         part_lse = scratch[B * nq * nsplit * hd:need]
     else:
         part_o = part_lse = out  # unused
+    cnt = _combine_counters(q.device, B * nkv) if nsplit > 1 else None
     _cuda_ext().paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, out, part_o, part_lse, float(scale),
-                             float(softcap), int(window), int(per), int(nsplit), error_word(q.device))
-    add_launches(2 if nsplit > 1 else 1)
+                             float(softcap), int(window), int(per), int(nsplit), error_word(q.device), cnt)
+    add_launches(2 if nsplit > 1 and cnt is None else 1)
     return out
+
+
+_CNT: Dict[int, torch.Tensor] = {}
+
+
+def _combine_counters(device: torch.device, need: int) -> Optional[torch.Tensor]:
+    """Zeroed int32 arrival counters for the in-kernel split-KV merge (the kernel leaves them zeroed).  They are
+    created outside stream capture; a capture that finds none uses the separate merge kernel instead."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _CNT.get(idx)
+    if t is None or t.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        t = torch.zeros(max(need, 1 << 16), dtype=torch.int32, device=device)
+        _CNT[idx] = t
+    return t
 
 
 def decode_scratch_numel(batch: int, nq: int, nkv: int, hd: int, max_len: int) -> int:
