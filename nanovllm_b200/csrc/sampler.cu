@@ -319,6 +319,326 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const T* __restrict__ 
   if (tid == 0) out[row] = best.i == 0x7fffffff ? 0 : best.i;
 }
 
+
+// ------------------------------------------------------------------------------------------------ fast path
+// bf16 rows with V % 8 == 0 starting on a 16-byte boundary: every pass streams the row with coalesced 16-byte
+// loads.  Index order (needed for the "first k of equal keys" ties) comes from warp-contiguous segments: warp w
+// owns elements [w * SEG, (w + 1) * SEG), lanes cover 8 consecutive elements each per 256-element step, and a
+// tie's rank is (ties in earlier warps) + (ties earlier in this warp's segment) -- the same ranks the chunked
+// slow path computes, so both paths pick the same token.
+constexpr int kWarps = kThreads / 32;
+
+struct WarpSeg {
+  int lo, hi;
+};
+__device__ __forceinline__ WarpSeg warp_seg(int V) {
+  const int per = ((V + 255) / 256 + kWarps - 1) / kWarps * 256;
+  const int lo = min(V, (int)(threadIdx.x >> 5) * per);
+  return {lo, min(V, lo + per)};
+}
+
+struct Row8 {
+  float v[8];
+  uint32_t k[8];  // 0 marks "no element" (no real logit maps to key 0)
+};
+__device__ __forceinline__ Row8 load8(const bf16* x, int i0, int hi, float softcap) {
+  Row8 r;
+  if (i0 < hi) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + i0);
+    const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      r.v[j] = capped(__bfloat162float(e[j]), softcap);
+      r.k[j] = okey(r.v[j]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      r.v[j] = -INFINITY;
+      r.k[j] = 0;
+    }
+  }
+  return r;
+}
+
+__device__ __forceinline__ int warp_excl(int v, int* total) {
+  const int lane = threadIdx.x & 31;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  *total = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - v;
+}
+
+// Per-element ranks among elements equal to key1 / key2 (index order), advancing the warp's running counts.
+__device__ __forceinline__ void step_ranks(const Row8& r, uint32_t key1, uint32_t key2, int& run1, int& run2,
+                                           int (&r1)[8], int (&r2)[8]) {
+  int c1 = 0, c2 = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c1 += (key1 != 0 && r.k[j] == key1);
+    c2 += (key2 != 0 && r.k[j] == key2);
+  }
+  int t1, t2;
+  int a1 = run1 + warp_excl(c1, &t1), a2 = run2 + warp_excl(c2, &t2);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    r1[j] = a1;
+    r2[j] = a2;
+    a1 += (key1 != 0 && r.k[j] == key1);
+    a2 += (key2 != 0 && r.k[j] == key2);
+  }
+  run1 += t1;
+  run2 += t2;
+}
+
+// Ties in earlier warps: every warp counts its own, then each thread sums the counts of the warps before it.
+__device__ __forceinline__ void warp_tie_bases(const bf16* x, int V, float softcap, uint32_t key1, uint32_t key2,
+                                               int* sh1, int* sh2, int& base1, int& base2) {
+  const WarpSeg sg = warp_seg(V);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int c1 = 0, c2 = 0;
+  for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
+    const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      c1 += (key1 != 0 && r.k[j] == key1);
+      c2 += (key2 != 0 && r.k[j] == key2);
+    }
+  }
+  c1 = __reduce_add_sync(0xffffffffu, c1);
+  c2 = __reduce_add_sync(0xffffffffu, c2);
+  __syncthreads();
+  if (lane == 0) {
+    sh1[w] = c1;
+    sh2[w] = c2;
+  }
+  __syncthreads();
+  base1 = base2 = 0;
+  for (int i = 0; i < w; ++i) {
+    base1 += sh1[i];
+    base2 += sh2[i];
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __restrict__ logits, long ld, int V,
+                                                               const float* __restrict__ temps,
+                                                               const int* __restrict__ topk,
+                                                               const float* __restrict__ topp,
+                                                               const int64_t* __restrict__ seeds,
+                                                               const int64_t* __restrict__ seq_ids,
+                                                               const int* __restrict__ steps, float softcap,
+                                                               int64_t* __restrict__ out) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
+  __shared__ ArgMax sh_am[32];
+  __shared__ float sh_f[32];
+  __shared__ int sh_a[32], sh_b[32];
+  __shared__ unsigned int hist_c[256];
+  __shared__ unsigned long long hist_m[256];
+  __shared__ uint32_t sel_key;
+  __shared__ long long sel_before;
+  __shared__ unsigned long long sel_mass_before;
+  const int row = blockIdx.x;
+  const bf16* x = logits + row * ld;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int k = topk[row];
+  const WarpSeg sg = warp_seg(V);
+  const uint4* x4 = reinterpret_cast<const uint4*>(x);
+  const int n4 = V >> 3;
+  if (k == 1) {
+    ArgMax a{-INFINITY, 0x7fffffff};
+#pragma unroll 4
+    for (int i = tid; i < n4; i += blockDim.x) {
+      const uint4 raw = x4[i];
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a = better(a, ArgMax{capped(__bfloat162float(e[j]), softcap), i * 8 + j});
+    }
+    a = block_argmax(a, sh_am);
+    if (tid == 0) out[row] = a.i == 0x7fffffff ? 0 : a.i;
+    return;
+  }
+  const float invT = 1.f / temps[row];
+  const float p = topp[row];
+  float mx = -INFINITY;
+#pragma unroll 4
+  for (int i = tid; i < n4; i += blockDim.x) {
+    const uint4 raw = x4[i];
+    const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) mx = fmaxf(mx, capped(__bfloat162float(e[j]), softcap) * invT);
+  }
+  mx = block_max(mx, sh_f);
+  auto mass = [&](float xv) -> unsigned long long {
+    const float e = __expf(xv * invT - mx);  // in (0, 1]
+    return (unsigned long long)(e * 1099511627776.0f);  // 2^40 fixed point
+  };
+
+  // ---------------- top-k cut-off: key Kk with count(>Kk) < k <= count(>=Kk)
+  uint32_t kk_key = 0;
+  int kk_eq_keep = 0x7fffffff;
+  if (k > 0 && k < V) {
+    uint32_t prefix = 0, mask = 0;
+    long long before = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += blockDim.x) hist_c[b] = 0;
+      __syncthreads();
+      for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
+        const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (r.k[j] != 0 && (r.k[j] & mask) == prefix) atomicAdd(&hist_c[(r.k[j] >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        long long cum = before;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (cum + hist_c[b] >= k) break;
+          cum += hist_c[b];
+        }
+        sel_key = prefix | ((uint32_t)b << shift);
+        sel_before = cum;
+      }
+      __syncthreads();
+      prefix = sel_key;
+      before = sel_before;
+      mask |= 255u << shift;
+    }
+    kk_key = prefix;
+    kk_eq_keep = (int)(k - before);
+  }
+
+  // ---------------- mass of the top-k set (fixed point, order independent sum)
+  int kb1, kb2;
+  warp_tie_bases(x, V, softcap, kk_key, 0, sh_a, sh_b, kb1, kb2);
+  unsigned long long zk = 0;
+  {
+    int run1 = kb1, run2 = 0;
+    for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
+      const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
+      int r1[8], r2[8];
+      step_ranks(r, kk_key, 0, run1, run2, r1, r2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (r.k[j] == 0) continue;
+        bool keep = kk_key == 0 || r.k[j] > kk_key;
+        if (!keep && r.k[j] == kk_key) keep = r1[j] < kk_eq_keep;
+        if (keep) zk += mass(r.v[j]);
+      }
+    }
+  }
+  __syncthreads();
+  for (int b = tid; b < 256; b += blockDim.x) hist_m[b] = 0;
+  __syncthreads();
+  atomicAdd(&hist_m[0], zk);
+  __syncthreads();
+  zk = hist_m[0];
+  __syncthreads();
+
+  // ---------------- top-p cut-off over the top-k set: key Kp with mass(>Kp) < P <= mass(>=Kp)
+  uint32_t kp_key = 0;
+  long long kp_eq_keep = 0x7fffffffffffLL;
+  if (p < 1.f) {
+    const unsigned long long P = (unsigned long long)((double)zk * (double)p);
+    uint32_t prefix = 0, mask = 0;
+    unsigned long long mbefore = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int b = tid; b < 256; b += blockDim.x) hist_m[b] = 0;
+      __syncthreads();
+      int run1 = kb1, run2 = 0;
+      for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
+        const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
+        int r1[8], r2[8];
+        step_ranks(r, kk_key, 0, run1, run2, r1, r2);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (r.k[j] == 0) continue;
+          bool keep = kk_key == 0 || r.k[j] > kk_key;
+          if (!keep && r.k[j] == kk_key) keep = r1[j] < kk_eq_keep;
+          if (keep && (r.k[j] & mask) == prefix) atomicAdd(&hist_m[(r.k[j] >> shift) & 255u], mass(r.v[j]));
+        }
+      }
+      __syncthreads();
+      if (tid == 0) {
+        unsigned long long cum = mbefore;
+        int b = 255;
+        for (; b > 0; --b) {
+          if (hist_m[b] > 0 && cum + hist_m[b] >= P) break;
+          cum += hist_m[b];
+        }
+        sel_key = prefix | ((uint32_t)b << shift);
+        sel_mass_before = cum;
+      }
+      __syncthreads();
+      prefix = sel_key;
+      mbefore = sel_mass_before;
+      mask |= 255u << shift;
+    }
+    kp_key = prefix;
+    // equal keys have equal mass m_eq: keep while mbefore + r * m_eq < P (at least one kept)
+    unsigned long long m_eq = 0;
+#pragma unroll 4
+    for (int i = tid; i < n4; i += blockDim.x) {
+      const uint4 raw = x4[i];
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xv = capped(__bfloat162float(e[j]), softcap);
+        if (okey(xv) == kp_key) m_eq = mass(xv);
+      }
+    }
+    __syncthreads();
+    if (tid == 0) hist_m[0] = 0;
+    __syncthreads();
+    if (m_eq) atomicMax(&hist_m[0], m_eq);
+    __syncthreads();
+    m_eq = hist_m[0];
+    if (m_eq > 0 && P > mbefore) kp_eq_keep = (long long)((P - mbefore + m_eq - 1) / m_eq);
+    else kp_eq_keep = 1;
+    if (kp_eq_keep < 1) kp_eq_keep = 1;
+  }
+
+  // ---------------- draw: argmax mass_i / E_i over the kept set
+  const uint2 key2 = make_uint2((uint32_t)seeds[row], (uint32_t)((uint64_t)seeds[row] >> 32));
+  const uint32_t step = (uint32_t)steps[row];
+  const uint32_t sid = (uint32_t)seq_ids[row];
+  int db1, db2;
+  warp_tie_bases(x, V, softcap, kk_key, kp_key, sh_a, sh_b, db1, db2);
+  ArgMax best{-INFINITY, 0x7fffffff};
+  {
+    int run1 = db1, run2 = db2;
+    for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
+      const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
+      int r1[8], r2[8];
+      step_ranks(r, kk_key, kp_key, run1, run2, r1, r2);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t key = r.k[j];
+        if (key == 0) continue;
+        bool keep = kk_key == 0 || key > kk_key;
+        if (!keep && key == kk_key) keep = r1[j] < kk_eq_keep;
+        if (keep && kp_key != 0) {
+          if (key < kp_key) keep = false;
+          else if (key == kp_key) keep = r2[j] < kp_eq_keep;
+        }
+        if (!keep) continue;
+        const int i = b0 + lane * 8 + j;
+        const uint4 r4 = Philox::gen(make_uint4((uint32_t)i, step, sid, 0x6e76u), key2);
+        const float u = (float)(r4.x >> 8) * (1.0f / 16777216.0f);
+        const float g = -__logf(fmaxf(1e-10f, u));
+        const float pr = __expf(r.v[j] * invT - mx);
+        best = better(best, ArgMax{pr / fmaxf(1e-10f, g), i});
+      }
+    }
+  }
+  best = block_argmax(best, sh_am);
+  if (tid == 0) out[row] = best.i == 0x7fffffff ? 0 : best.i;
+}
 }  // namespace
 
 void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
@@ -331,8 +651,13 @@ void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, 
   logits.stride(0), V, temps.data_ptr<float>(), topk.data_ptr<int>(), topp.data_ptr<float>(),                   \
       seeds.data_ptr<int64_t>(), seq_ids.data_ptr<int64_t>(), steps.data_ptr<int>(), (float)softcap,            \
       out.data_ptr<int64_t>()
+  const bool fast = logits.scalar_type() == at::kBFloat16 && V % 8 == 0 && logits.stride(0) % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 15) == 0 && std::getenv("NVB_SAMPLER_SLOW") == nullptr;
   if (logits.scalar_type() == at::kFloat)
     C10_CUDA_CHECK(nvb::launch(sample_kernel<float>, dim3(B), dim3(kThreads), 0, stream, logits.data_ptr<float>(), ARGS));
+  else if (fast)
+    C10_CUDA_CHECK(nvb::launch(sample_fast_kernel, dim3(B), dim3(kThreads), 0, stream,
+                               reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS));
   else
     C10_CUDA_CHECK(nvb::launch(sample_kernel<bf16>, dim3(B), dim3(kThreads), 0, stream, reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS));
 #undef ARGS

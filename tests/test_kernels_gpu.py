@@ -300,3 +300,22 @@ def test_sampler_matches_oracle():
     got = ops.sample(lb.to(DEV), temps.to(DEV), torch.ones(B, dtype=torch.int32, device=DEV), topp.to(DEV),
                      seeds.to(DEV), sids.to(DEV), steps.to(DEV))
     assert got.cpu().tolist() == torch.argmax(lb.float(), dim=1).tolist()
+
+
+@pytest.mark.parametrize("V", [5000, 5003])
+def test_sampler_bf16_paths_with_ties_match_oracle(V):
+    """bf16 logits with many exact ties: the coalesced fast path (V % 8 == 0) and the generic path (V = 5003)
+    keep the same "first k of equal values" ties as the oracle and draw the same tokens."""
+    g = torch.Generator().manual_seed(7)
+    B = 8
+    lb = (torch.round(torch.randn(B, V, generator=g) * 2) / 2).bfloat16()  # coarse values: lots of ties
+    temps = torch.tensor([1.0, 0.7, 1.3, 0.5, 1.0, 0.9, 0.8, 1.1])
+    topk = torch.tensor([0, 0, 50, 3, 5, 20, 1, 7], dtype=torch.int32)
+    topp = torch.tensor([0.9, 0.5, 0.95, 1.0, 1.0, 0.3, 1.0, 0.8])
+    seeds = torch.arange(1, B + 1, dtype=torch.int64)
+    sids = torch.arange(20, 20 + B, dtype=torch.int64)
+    steps = torch.arange(3, 3 + B, dtype=torch.int32)
+    want = ref.sample(lb.float(), temps, topk, topp, seeds, sids, steps)
+    got = ops.sample(lb.to(DEV), temps.to(DEV), topk.to(DEV), topp.to(DEV), seeds.to(DEV), sids.to(DEV),
+                     steps.to(DEV))
+    assert got.cpu().tolist() == want.tolist()
