@@ -45,7 +45,8 @@ void ipc_close_cuda(int64_t ptr);
 void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, std::vector<int64_t> out,
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
-                            c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot);
+                            c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot,
+                            c10::optional<torch::Tensor> parts);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";

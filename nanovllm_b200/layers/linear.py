@@ -156,9 +156,10 @@ class RowParallelLinear(LinearBase):
             ws = symm.workspace()
             T = x.shape[0]
             if ws is not None and ws.fits(T, w.shape[0]):
-                # partial sum straight into the symmetric buffer; the consumer fuses all-reduce + norm
-                ops.linear(x, w, out=ws.in_view(T))
-                return ops.TPPartial(ws, T)
+                # partial sum straight into the symmetric buffer (or left split over K for the all-reduce
+                # kernel to sum); the consumer fuses all-reduce + norm
+                y = ops.linear(x, w, out=ws.in_view(T), partial_ok=True)
+                return ops.TPPartial(ws, T, y.parts if isinstance(y, ops.SplitK) else None)
             y = ops.linear(x, w)
         else:
             y = ops.linear(x, w)

@@ -71,11 +71,12 @@ class TPPartial:
     """This rank's row-parallel partial sum [T, H], already in the symmetric workspace's ``in`` slot.
 
     A following RMSNorm (with or without residual) runs the fused all-reduce + residual + RMSNorm kernel over
-    peer memory; anything else calls ``materialize`` (a plain fused all-reduce)."""
-    __slots__ = ("ws", "T")
+    peer memory; anything else calls ``materialize`` (a plain fused all-reduce).  ``parts``: the partial is
+    still split over K (fp32 [splits, T, H]); the all-reduce kernel sums the slices into ``in`` first."""
+    __slots__ = ("ws", "T", "parts")
 
-    def __init__(self, ws, T: int):
-        self.ws, self.T = ws, T
+    def __init__(self, ws, T: int, parts: Optional[torch.Tensor] = None):
+        self.ws, self.T, self.parts = ws, T, parts
 
     @property
     def shape(self):
@@ -100,7 +101,7 @@ class TPPartial:
 def materialize(x):
     """bf16 tensor from a SplitK (one fused sum kernel) or a TPPartial (fused all-reduce), identity otherwise."""
     if isinstance(x, TPPartial):
-        return x.ws.allreduce_norm(x.T, None, 0.0, 3, None)[0]
+        return x.ws.allreduce_norm(x.T, None, 0.0, 3, None, parts=x.parts)[0]
     if isinstance(x, SplitK):
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
         _cuda_ext().splitk_sum(x.parts, out)
@@ -172,7 +173,7 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: 
              ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Returns (normed, residual).  With ``residual`` the sum x + residual is written back into it."""
     if isinstance(x, TPPartial):
-        return x.ws.allreduce_norm(x.T, weight, eps, mode, residual)
+        return x.ws.allreduce_norm(x.T, weight, eps, mode, residual, parts=x.parts)
     if not x.is_cuda:
         y, r = ref.rms_norm(x, weight, eps, mode, residual)
         if residual is not None:

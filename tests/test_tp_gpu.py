@@ -118,6 +118,19 @@ def _ar_run(rank, world, port, q):
     ws.in_view(T).copy_(parts[rank].to(dev))
     plain = ops.materialize(ops.TPPartial(ws, T)).float().cpu()
     errs.append(float((plain - total.bfloat16().float()).abs().max()))
+    # partials still split over K (fp32 slices): the kernel sums them locally before the exchange
+    S = 3
+    sl = [torch.randn(S, T, H, generator=torch.Generator().manual_seed(40 + r)) for r in range(world)]
+    tot2 = torch.zeros(T, H)
+    for t in sl:
+        tot2 += t.sum(0).bfloat16().float()
+    want2, _ = ref.rms_norm(tot2.bfloat16(), w, 1e-6, 0)
+    for shot in (1, 0):
+        o2, _ = ws.allreduce_norm(T, w.to(dev), 1e-6, 0, None, oneshot=shot, parts=sl[rank].to(dev))
+        torch.cuda.synchronize()
+        errs.append(float((o2.float().cpu() - want2.float()).abs().max()))
+    plain2 = ops.materialize(ops.TPPartial(ws, T, sl[rank].to(dev))).float().cpu()
+    errs.append(float(((plain2 - tot2) / (1.0 + tot2.abs())).abs().max()))
     # captured in a CUDA graph and replayed twice
     x_in = parts[rank].to(dev)
     w_dev = w.to(dev)
