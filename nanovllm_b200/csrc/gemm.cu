@@ -272,10 +272,14 @@ struct DecodeArgs {
   int* err;
 };
 
+// Ring depth: as many stages as fit in 224 KB of shared memory (at most 16).  Under full load the HBM latency
+// is several microseconds and a CTA's weight bandwidth is its weight bytes in flight over that latency, so the
+// ring is sized by capacity, not by a fixed count.
+constexpr int kDecodeRingBytes = 224 * 1024;
 __host__ __device__ constexpr int decode_stages2(int na, int bn, int ksub = 1) {
-  return (200 * 1024) / (ksub * (na * BM * BK * 2 + bn * BK * 2)) > 8
-             ? 8
-             : (200 * 1024) / (ksub * (na * BM * BK * 2 + bn * BK * 2));
+  return kDecodeRingBytes / (ksub * (na * BM * BK * 2 + bn * BK * 2)) > 16
+             ? 16
+             : kDecodeRingBytes / (ksub * (na * BM * BK * 2 + bn * BK * 2));
 }
 __host__ __device__ constexpr uint32_t pow2_cols(int n) {
   uint32_t c = 32;
@@ -622,7 +626,8 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
 }  // namespace
 
 // y = x @ w^T (x [M, K] bf16, w [N, K] bf16) with optional activation on 128-interleaved gate/up rows of w.
-// ``workspace`` is unused (kept for ABI stability): decode split partials are reduced in distributed shared memory.
+// ``workspace``: fp32 [S, M, N] split-K partials for decode-sized M (S from gemm_splits_for); with ``partial_out``
+// the partials are left for the consumer to sum, otherwise a sum (or split-K activation) kernel follows.
 int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
@@ -717,7 +722,7 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
   return M <= 256 ? splits_used : 1;
 }
 
-// Workspace splits the decode path needs from the caller (always 1: it reduces on chip).
+// K splits (and so the fp32 partial slices of the workspace) the decode path uses for this shape.
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
   // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;

@@ -68,11 +68,19 @@ def bench_gemm(M, N, K, iters, act=0, splits=0):
     xs = [torch.randn(M, K, device=dev).bfloat16() for _ in range(n)]
     ours = time_fn([lambda w=w, x=x: ops.linear(x, w, act, force_splits=splits) for w, x in zip(ws, xs)], iters)
     cublas = time_fn([lambda w=w, x=x: torch.matmul(x, w.t()) for w, x in zip(ws, xs)], iters)
+    # the model's consumers (add+RMSNorm, RoPE, the TP all-reduce) sum split-K slices themselves: time the
+    # GEMM kernel alone as well when it splits
+    sp = splits or (ops._cuda_ext().gemm_splits_for(M, N, K, act) if M <= 256 else 1)
+    gemm_only = None
+    if sp > 1 and not act:
+        gemm_only = time_fn([lambda w=w, x=x: ops.linear(x, w, act, force_splits=splits, partial_ok=True)
+                             for w, x in zip(ws, xs)], iters)
     out_cols = N // 2 if act else N
     byts = wbytes + M * K * 2 + M * out_cols * 2
     flops = 2.0 * M * N * K
     return {"case": f"gemm M={M} N={N} K={K}" + (" act" if act else "") + (f" S={splits}" if splits else ""),
-            "us": round(ours, 2),
+            "us": round(ours, 2), "splits": sp,
+            "gemm_only_us": None if gemm_only is None else round(gemm_only, 2),
             "cublas_us": round(cublas, 2), "TBps": round(byts / ours / 1e6, 3), "TFLOPs": round(flops / ours / 1e6, 1)}
 
 
