@@ -11,12 +11,14 @@ and bert (ONNX BERT names mapped onto them).  GGUF blocks are dequantised at loa
 from __future__ import annotations
 
 import os
+import re
 from typing import Dict, Optional
 
 import torch
 
 from ..config import HfConfig
 from ..exceptions import ModelLoadException, UnsupportedModelException
+from ..ops.quant import GgufPacked, fused_supported
 from ..loaders import model_support as MS
 from ..loaders.gguf import GgufFile
 from ..loaders.gguf_configs import hf_config_from_gguf, hf_name_for_qwen3
@@ -91,14 +93,23 @@ class LlmModelFactory:
         return LlmModelFactory.Builder()
 
 
+# linear projections built by the layer classes (layers/linear.py), HF and GGUF tensor names
+_PROJECTION = re.compile(r"(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj|attn_q|attn_k|attn_v|"
+                         r"attn_output|ffn_gate|ffn_up|ffn_down)\.weight$")
+
+
 def _load_gguf(path: str, options, device, dtype) -> LlmModel:
     g = GgufFile(path)
     sel = MS.resolve_gguf(g.architecture)
     MS.check_source(sel, MS.SRC_GGUF, g.architecture, [])
     hf = hf_config_from_gguf(g.metadata, sel.architecture)
     tok = Tokenizer.from_gguf(g.metadata)
-    weights: Dict[str, torch.Tensor] = {}
+    weights: Dict[str, object] = {}
     packed = False
+    # NVB_GGUF_PACKED=0 dequantizes every tensor at load time (the bf16 path); "force" keeps projections packed
+    # on the CPU too (there they are dequantized per multiply -- for tests)
+    mode = os.environ.get("NVB_GGUF_PACKED", "1")
+    keep_packed = mode == "force" or (device.type == "cuda" and mode not in ("0", "false", "no"))
     from ..utils.progress import LoadProgress
     prog = LoadProgress(f"GGUF {os.path.basename(path)}", len(g.tensors), (options or {}).get(OPTION_LISTENER))
     for name, info in g.tensors.items():
@@ -110,6 +121,12 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
         else:
             target = name
         packed = packed or info.ggml_type not in (0, 1, 30)
+        if keep_packed and _PROJECTION.search(target) and fused_supported(info.ggml_type, info.shape):
+            # projection weights stay in GGUF block format on the GPU (dequant-fused GEMM); the bytes are
+            # copied out of the file mapping, which closes after loading
+            raw = g.packed(name).to(device)
+            weights[target] = GgufPacked(raw, info.ggml_type, info.shape[0], info.shape[1])
+            continue
         weights[target] = g.get(name, dtype=torch.float32, device=device).to(dtype)
     if sel.architecture == MS.QWEN3 and "lm_head.weight" not in weights:
         hf.tie_word_embeddings = True

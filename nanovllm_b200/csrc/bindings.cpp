@@ -23,6 +23,11 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out);
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act);
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
+int64_t qgemm_splits_cuda(int64_t M, int64_t N, int64_t K, int64_t type);
+int64_t qgemm_row_step_bytes(int64_t type);
+int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, int64_t K, torch::Tensor out,
+                   c10::optional<torch::Tensor> parts, c10::optional<torch::Tensor> err, bool partial_out);
+void qdequant_cuda(torch::Tensor w, int64_t type, int64_t N, int64_t K, torch::Tensor out);
 void embedding_cuda(torch::Tensor out, torch::Tensor table, torch::Tensor ids, double scale, int64_t vstart,
                     int64_t vend);
 void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interleaved);
@@ -58,6 +63,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm_cuda);
   m.def("gemm_splits_for", &gemm_splits_for);
   m.def("splitk_sum", &splitk_sum_cuda);
+  m.def("qgemm_splits", &qgemm_splits_cuda);
+  m.def("qgemm_row_step_bytes", &qgemm_row_step_bytes);
+  m.def("qgemm", &qgemm_cuda);
+  m.def("qdequant", &qdequant_cuda);
   m.def("embedding", &embedding_cuda);
   m.def("act_mul", &act_mul_cuda);
   m.def("bias_act", &bias_act_cuda);

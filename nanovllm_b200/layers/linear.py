@@ -11,8 +11,9 @@ Merged / Qkv subclasses are TP names that never shard.  Here:
 * ``RowParallelLinear`` keeps columns [r*K/TP, (r+1)*K/TP) of W and all-reduces (or reduce-scatters in the
   sequence-parallel path) the partial outputs.
 
-Weights may also be packed (GGUF blocks, Gemma QAT ints): ``PackedWeight`` objects expose ``linear(x)`` and are
-dispatched here without densifying when the fused dequant GEMM supports the type.
+Weights may also be packed (GGUF blocks kept in block format, ``ops.quant.GgufPacked``): they expose
+``linear(x, out, partial_ok)`` and the same row / K sharding, concatenation and row permutation as a dense
+tensor, so every class here takes either.
 """
 from __future__ import annotations
 
@@ -25,18 +26,7 @@ from ..parallel import state as ps
 from ..parallel import symm
 
 
-def shard_rows(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
-    n = w.shape[0]
-    assert n % size == 0, f"dimension {n} not divisible by TP={size}"
-    k = n // size
-    return w[rank * k:(rank + 1) * k]
-
-
-def shard_cols(w: torch.Tensor, rank: int, size: int) -> torch.Tensor:
-    n = w.shape[1]
-    assert n % size == 0, f"dimension {n} not divisible by TP={size}"
-    k = n // size
-    return w[:, rank * k:(rank + 1) * k]
+from ..ops.quant import cat_rows, is_packed, shard_cols, shard_rows  # dense tensors and GgufPacked alike
 
 
 class LinearBase:
@@ -49,7 +39,7 @@ class LinearBase:
 
     def _mm(self, x: torch.Tensor, act: int = ops.ACT_NONE) -> torch.Tensor:
         w = self.weight
-        if hasattr(w, "linear"):  # packed weight (GGUF / QAT): fused dequant path
+        if hasattr(w, "linear"):  # packed weight (GGUF blocks): fused dequant path
             y = w.linear(x)
             if act != ops.ACT_NONE:
                 y = ops.act_mul(y, act, interleaved=True)
@@ -90,11 +80,16 @@ class MergedColumnParallelLinear(LinearBase):
         u = shard_rows(up, r, s) if s > 1 else up
         self.act = act
         self.intermediate = g.shape[0]
+        gu = cat_rows([g, u])
         if self.intermediate % interleave_block == 0:
-            self.weight = ops.ref.interleave_gate_up(torch.cat([g, u], 0), interleave_block).contiguous()
+            if is_packed(gu):
+                order = ops.ref.interleave_gate_up(torch.arange(gu.shape[0]).unsqueeze(1), interleave_block)
+                self.weight = gu.permute_rows(order.squeeze(1))
+            else:
+                self.weight = ops.ref.interleave_gate_up(gu, interleave_block).contiguous()
             self.interleaved = True
         else:
-            self.weight = torch.cat([g, u], 0).contiguous()
+            self.weight = gu.contiguous()
             self.interleaved = False
 
     def __call__(self, x):
@@ -125,7 +120,7 @@ class QKVParallelLinear(LinearBase):
         qs = shard_rows(q, r, s) if s > 1 else q
         ks = shard_rows(k, kv_rank, kv_parts) if s > 1 else k
         vs = shard_rows(v, kv_rank, kv_parts) if s > 1 else v
-        self.weight = torch.cat([qs, ks, vs], 0).contiguous()
+        self.weight = cat_rows([qs, ks, vs]).contiguous()
         if bq is not None:
             bqs = shard_rows(bq, r, s) if s > 1 else bq
             bks = shard_rows(bk, kv_rank, kv_parts) if s > 1 else bk
@@ -133,7 +128,9 @@ class QKVParallelLinear(LinearBase):
             self.bias = torch.cat([bqs, bks, bvs], 0).contiguous()
 
     def __call__(self, x):
-        if self.bias is None and not hasattr(self.weight, "linear"):
+        if self.bias is None:
+            if is_packed(self.weight):
+                return self.weight.linear(x, partial_ok=True)
             return ops.linear(x, self.weight, partial_ok=True)
         return self._mm(x)
 
@@ -148,21 +145,24 @@ class RowParallelLinear(LinearBase):
 
     def __call__(self, x):
         w = self.weight
-        if hasattr(w, "linear"):
-            y = w.linear(x)
-        elif ps.tp_size() == 1 and self.bias is None:
-            return ops.linear(x, w, partial_ok=True)  # the following add+RMSNorm sums the split partials
-        elif self.reduce and self.bias is None and getattr(x, "is_cuda", False):
+        packed = is_packed(w)
+
+        def mm(out=None, partial_ok=False):
+            if packed:
+                return w.linear(x, out=out, partial_ok=partial_ok)
+            return ops.linear(x, w, out=out, partial_ok=partial_ok)
+
+        if ps.tp_size() == 1 and self.bias is None:
+            return mm(partial_ok=True)  # the following add+RMSNorm sums the split partials
+        if self.reduce and self.bias is None and getattr(x, "is_cuda", False):
             ws = symm.workspace()
             T = x.shape[0]
             if ws is not None and ws.fits(T, w.shape[0]):
                 # partial sum straight into the symmetric buffer (or left split over K for the all-reduce
                 # kernel to sum); the consumer fuses all-reduce + norm
-                y = ops.linear(x, w, out=ws.in_view(T), partial_ok=True)
+                y = mm(out=ws.in_view(T), partial_ok=True)
                 return ops.TPPartial(ws, T, y.parts if isinstance(y, ops.SplitK) else None)
-            y = ops.linear(x, w)
-        else:
-            y = ops.linear(x, w)
+        y = ops.materialize(mm())
         if self.reduce:
             ps.all_reduce(y)
         if self.bias is not None:

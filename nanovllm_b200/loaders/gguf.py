@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import mmap
 import os
+import math
 import struct
 from dataclasses import dataclass
 from typing import Any, Dict, List, Optional, Tuple
@@ -262,6 +263,19 @@ def pack_random_blocks(ggml_type: int, shape: Tuple[int, ...], seed: int, std: f
         raw[:, 0:2] = f16(std / 74.0)
     elif name == "Q4_0":  # codes -8..7 (std 4.6)
         raw[:, 0:2] = f16(std / 4.6)
+    elif name == "Q4_1":  # d * code + m, codes 0..15 centred by m
+        raw[:, 0:2] = f16(std / 4.6)
+        raw[:, 2:4] = f16(-7.5 * std / 4.6)
+    elif name == "IQ4_NL":  # non-linear grid, spread ~66
+        raw[:, 0:2] = f16(std / 66.0)
+    elif name == "IQ4_XS":  # every 6-bit sub-block scale = 1 (stored +32): low nibbles 1, high bits 2
+        raw[:, 0:2] = f16(std / 66.0)
+        raw[:, 2:4] = 0xAA
+        raw[:, 4:8] = 0x11
+    elif name == "MXFP4":  # doubled e2m1 grid (spread ~5.7) times 2^(e - 128)
+        raw[:, 0] = 128 + int(round(math.log2(std / 5.7)))
+    elif name == "NVFP4":  # four ue4m3 sub-scales of 4 * 2^-10
+        raw[:, 0:4] = 0x04
     else:
         raise ValueError(f"random packing not provided for {name}")
     return raw.tobytes()

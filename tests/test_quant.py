@@ -1,0 +1,107 @@
+"""GGUF weights kept packed (ops/quant.py): sharding / concatenation / permutation of the block bytes match the
+same operations on the dequantized tensor, the tile-major repack is a lossless byte permutation, and a model
+built from packed projections matches the dense-dequantized one (CPU; the fused GEMM itself is in
+test_quant_gpu.py)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from nanovllm_b200.loaders import dequant as DQ
+from nanovllm_b200.loaders.gguf import pack_random_blocks
+from nanovllm_b200.ops.quant import FUSED_TYPES, GgufPacked, cat_rows, repack_tiles, shard_cols, shard_rows
+
+TYPES = sorted(FUSED_TYPES)
+
+
+def _packed(t, N=200, K=512, seed=0):
+    raw = torch.from_numpy(np.frombuffer(pack_random_blocks(t, (N, K), seed), dtype=np.uint8).copy())
+    return GgufPacked(raw, t, N, K)
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_packed_dequantize_matches_decoder(t):
+    w = _packed(t)
+    want = DQ.dequantize(w.raw.reshape(-1), t, w.N * w.K).reshape(w.N, w.K)
+    got = w.dequantize(torch.float32)
+    assert torch.equal(got, want)
+    assert torch.isfinite(got).all() and 0.005 < float(got.std()) < 0.08  # random blocks with a sane spread
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_packed_shard_cat_permute_match_dense(t):
+    w = _packed(t, N=256, K=1024, seed=3)
+    d = w.dequantize(torch.float32)
+    assert torch.equal(shard_rows(w, 1, 4).dequantize(torch.float32), shard_rows(d, 1, 4))
+    assert torch.equal(shard_cols(w, 1, 2).dequantize(torch.float32), shard_cols(d, 1, 2))
+    v = _packed(t, N=64, K=1024, seed=4)
+    assert torch.equal(cat_rows([w, v]).dequantize(torch.float32), torch.cat([d, v.dequantize(torch.float32)], 0))
+    perm = torch.randperm(256, generator=torch.Generator().manual_seed(0))
+    assert torch.equal(w.permute_rows(perm).dequantize(torch.float32), d[perm])
+    with pytest.raises(ValueError):
+        w.cols(128, 640)  # K slices must fall on 256-element boundaries
+
+
+@pytest.mark.parametrize("t", TYPES)
+def test_repack_is_a_lossless_byte_permutation(t):
+    N, K = 300, 768  # N not a multiple of the 128-row tile
+    w = _packed(t, N=N, K=K, seed=5)
+    tiles = repack_tiles(w.raw, t, N, K)
+    bprs = FUSED_TYPES[t]
+    assert tiles.numel() == 3 * (K // 256) * 128 * bprs
+    # every raw byte value survives with its multiplicity (padding adds zeros only)
+    raw_hist = torch.bincount(w.raw.reshape(-1).long(), minlength=256)
+    tile_hist = torch.bincount(tiles.long(), minlength=256)
+    pad = tiles.numel() - w.raw.numel()
+    assert torch.equal(tile_hist[1:], raw_hist[1:]) and int(tile_hist[0] - raw_hist[0]) == pad
+    # row r, step s of the tile-major layout starts at ((r // 128) * S + s) * 128 + r % 128
+    S = K // 256
+    t4 = tiles.reshape(3, S, 128, bprs)
+    row, step = 131, 2
+    if t in (12, 13):  # K-quants keep their block bytes in order
+        be, bb = DQ.block_info(t)
+        assert torch.equal(t4[1, step, 3, :bb], w.raw[row, step * bb:(step + 1) * bb])
+
+
+def test_packed_linear_cpu_matches_dense():
+    w = _packed(12, N=256, K=512, seed=7)
+    x = torch.randn(5, 512).bfloat16()
+    y = w.linear(x).float()
+    want = x.float() @ w.dequantize(torch.float32).bfloat16().float().t()
+    assert torch.allclose(y, want, atol=1e-2, rtol=1e-2)
+
+
+def test_gguf_model_with_packed_projections_matches_dequantized(tmp_path, monkeypatch):
+    from nanovllm_b200.api.factory import LlmModelFactory
+    from nanovllm_b200.config import EngineConfig, HfConfig
+    from nanovllm_b200.engine.sequence import Sequence
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.models.writers import write_gguf_model
+    from nanovllm_b200.sampling_params import SamplingParams
+
+    hf = HfConfig(vocab_size=300, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=64, max_position_embeddings=2048, model_type="qwen3",
+                  architectures=["Qwen3ForCausalLM"], tie_word_embeddings=False)
+    p = write_gguf_model(str(tmp_path / "q.gguf"), hf, init_random_weights(hf, 0), "Q4_K", big_type="Q6_K",
+                         random_packed=True)
+
+    def logits(mode):
+        monkeypatch.setenv("NVB_GGUF_PACKED", mode)
+        m = LlmModelFactory.make(p, device="cpu")
+        kinds = {type(v).__name__ for v in m.weights.values()}
+        llm = LLM(m, EngineConfig(max_num_seqs=2, max_model_len=512, num_kvcache_blocks=4,
+                                  max_num_batched_tokens=256, stop_on_degenerate=False), device="cpu")
+        s = Sequence(list(range(3, 40)), SamplingParams(max_tokens=1), 256)
+        bm = llm.scheduler.block_manager
+        bm.allocate(s, 0)
+        s.num_scheduled_tokens = len(s.token_ids)
+        out = llm.runner.forward_logits([s], True)[0].float()
+        bm.deallocate(s)
+        return out, kinds
+
+    a, ka = logits("force")
+    b, kb = logits("0")
+    assert "GgufPacked" in ka and "GgufPacked" not in kb
+    assert torch.allclose(a, b, atol=2e-2, rtol=2e-2), (a - b).abs().max()
