@@ -1,6 +1,7 @@
 """Headline benchmark: decode tokens/s (max over ranks) on the Qwen3-8B-shaped model, bf16, TP = N GPUs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference|baseline]
+                    [--weights bf16|nvfp4|q4_k|q8_0|mxfp4]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1: tensor parallel over NCCL)
 
 Workload (BASELINE config 5 shape): random-init Qwen3-8B architecture (36 layers, hidden 4096, 32 q / 8 kv heads,
@@ -100,6 +101,17 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     hf = qwen3_8b_config()
     weights = init_random_weights(hf, seed=4, device=dev)
+    if args.weights != "bf16":
+        # the GGUF copy of config 5: every projection as random packed blocks, multiplied packed
+        import re
+        from nanovllm_b200.loaders.dequant import TYPE_BY_NAME
+        from nanovllm_b200.ops.quant import random_packed
+        proj = re.compile(r"(q_proj|k_proj|v_proj|o_proj|gate_proj|up_proj|down_proj)\.weight$")
+        for i, name in enumerate(sorted(weights)):
+            if proj.search(name):
+                N, K = weights[name].shape
+                weights[name] = random_packed(TYPE_BY_NAME[args.weights.upper()], N, K, 4000 + i, dev)
+        torch.cuda.empty_cache()
     B = args.batch
     gen = torch.Generator().manual_seed(1234)
     lens = torch.randint(args.min_prompt, args.max_prompt + 1, (B,), generator=gen).tolist()
@@ -195,8 +207,11 @@ def run_ours(args):
             "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16", "data": "synthetic: random-init weights (seed 4), random prompt ids",
             "config": {"model": "Qwen3-8B-shape (36L, H4096, 32/8 heads, hd128, I12288, V151936)",
+                       "weights": "bf16" if args.weights == "bf16" else
+                                  f"projections GGUF {args.weights.upper()} (packed, dequant-fused GEMM); "
+                                  f"embeddings / LM head bf16",
                        "global_batch": running, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}]",
-                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (16 GB weights + KV cache)",
+                       "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights of several GB + KV cache)",
                        "prefill_tokens": prefill_tokens, "prefill_s": round(prefill_s, 3),
                        "p50_ttft_ms": round(p50_ttft * 1000, 1),
                        "ttft_note": f"p50 over {len(probe)} requests joining a running batch of {running}; "
@@ -224,6 +239,8 @@ def main():
                     help="decode steps run between cudaProfilerStart/Stop before the timed region")
     ap.add_argument("--impl", choices=["ours", "reference", "baseline"], default="ours",
                     help="baseline: this engine with cuBLAS GEMMs (separate activation kernel) and NCCL all-reduce")
+    ap.add_argument("--weights", choices=["bf16", "nvfp4", "q4_k", "q8_0", "mxfp4"], default="bf16",
+                    help="projection weights: bf16, or random GGUF blocks kept packed (the NVFP4 copy of config 5)")
     ap.add_argument("--ttft-probe", type=int, default=8,
                     help="requests that join the running batch one at a time after the timed region (p50 TTFT)")
     args = ap.parse_args()

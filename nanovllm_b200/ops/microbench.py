@@ -84,6 +84,35 @@ def bench_gemm(M, N, K, iters, act=0, splits=0):
             "cublas_us": round(cublas, 2), "TBps": round(byts / ours / 1e6, 3), "TFLOPs": round(flops / ours / 1e6, 1)}
 
 
+def bench_qgemm(ggml_type, M, N, K, iters):
+    """Dequant-fused GEMM on packed GGUF weights vs cuBLAS on the same weights in bf16; bandwidth counts the
+    packed bytes actually streamed (tile-major repack) plus activations and output."""
+    import numpy as np
+    from ..loaders import dequant as DQ
+    from ..loaders.gguf import pack_random_blocks
+    from .quant import FUSED_TYPES, GgufPacked
+    dev = "cuda"
+    raw = torch.from_numpy(np.frombuffer(pack_random_blocks(ggml_type, (N, K), 0), dtype=np.uint8).copy()).to(dev)
+    base = GgufPacked(raw, ggml_type, N, K)
+    pbytes = base.tiles().numel()
+    n = _copies(pbytes + M * K * 2)
+    ws = [GgufPacked(raw, ggml_type, N, K) for _ in range(n)]
+    for w in ws:
+        w._tiles = base.tiles().clone()
+    xs = [torch.randn(M, K, device=dev).bfloat16() for _ in range(n)]
+    ours = time_fn([lambda w=w, x=x: w.linear(x) for w, x in zip(ws, xs)], iters)
+    ours_p = time_fn([lambda w=w, x=x: w.linear(x, partial_ok=True) for w, x in zip(ws, xs)], iters)
+    dense = base.dense_cuda()
+    nd = _copies(N * K * 2 + M * K * 2)
+    ds = [dense.clone() for _ in range(nd)]
+    cublas = time_fn([lambda w=w, x=x: torch.matmul(x, w.t()) for w, x in zip(ds, [xs[i % n] for i in range(nd)])], iters)
+    byts = pbytes + M * K * 2 + M * N * 2
+    return {"case": f"qgemm {DQ.type_name(ggml_type)} M={M} N={N} K={K}", "us": round(ours, 2),
+            "gemm_only_us": round(ours_p, 2), "cublas_bf16_us": round(cublas, 2),
+            "speedup_vs_bf16_cublas": round(cublas / ours, 2), "packed_MB": round(pbytes / 1e6, 2),
+            "TBps": round(byts / ours_p / 1e6, 3)}
+
+
 def bench_decode(B, ctx, nq, nkv, hd, iters):
     dev = "cuda"
     BS = 256
@@ -164,10 +193,17 @@ def main():
     ap.add_argument("--out", default=None)
     ap.add_argument("--gemm", default=None, help="GEMM cases M,N,K[,act[,splits]] separated by ';' (e.g. for an ncu capture)")
     ap.add_argument("--decode", default=None, help="single decode-attention case B,ctx,nq,nkv,hd")
+    ap.add_argument("--qgemm", default=None, help="packed GGUF GEMM cases TYPE,M,N,K separated by ';' (TYPE e.g. Q4_K)")
     a = ap.parse_args()
     hbm, tflops, src = peaks()
     only = set(a.only.split(","))
     rows = []
+    if a.qgemm:
+        from ..loaders.dequant import TYPE_BY_NAME
+        for case in a.qgemm.split(";"):
+            f = case.split(",")
+            rows.append(bench_qgemm(TYPE_BY_NAME[f[0]], int(f[1]), int(f[2]), int(f[3]), a.iters))
+        only = set()
     if a.gemm or a.decode:
         only = set()
         if a.gemm:

@@ -10,6 +10,7 @@ dequantize into a bf16 scratch and use the tensor-core GEMM; CPU tensors fall ba
 """
 from __future__ import annotations
 
+import math
 from typing import List, Optional, Sequence
 
 import torch
@@ -93,7 +94,7 @@ class GgufPacked:
 
     @property
     def device(self):
-        return self.raw.device
+        return (self.raw if self.raw is not None else self._tiles).device
 
     def dim(self) -> int:
         return 2
@@ -102,46 +103,58 @@ class GgufPacked:
         return self
 
     def to_device(self, device) -> "GgufPacked":
-        if self.raw.device == torch.device(device):
+        if self.device == torch.device(device):
             return self
-        return GgufPacked(self.raw.to(device), self.ggml_type, self.N, self.K)
+        return GgufPacked(self._need_raw().to(device), self.ggml_type, self.N, self.K)
 
     def dequantize(self, dtype=torch.bfloat16) -> torch.Tensor:
+        if self.raw is None:
+            return self.dense_cuda().to(dtype)
         flat = self.raw.reshape(-1)
         return DQ.dequantize(flat, self.ggml_type, self.N * self.K, device=flat.device,
                              dtype=torch.float32).reshape(self.N, self.K).to(dtype)
 
     # ---------------------------------------------------------------- sharding (row-parallel splits K)
     def rows(self, a: int, b: int) -> "GgufPacked":
-        return GgufPacked(self.raw[a:b], self.ggml_type, b - a, self.K)
+        return GgufPacked(self._need_raw()[a:b], self.ggml_type, b - a, self.K)
 
     def cols(self, a: int, b: int) -> "GgufPacked":
         be, bb = DQ.block_info(self.ggml_type)
         if a % STEP or b % STEP:
             raise ValueError(f"packed K slice [{a}, {b}) must fall on 256-element boundaries")
-        return GgufPacked(self.raw[:, a // be * bb:b // be * bb].contiguous(), self.ggml_type, self.N, b - a)
+        return GgufPacked(self._need_raw()[:, a // be * bb:b // be * bb].contiguous(), self.ggml_type, self.N, b - a)
 
     def permute_rows(self, index: torch.Tensor) -> "GgufPacked":
-        return GgufPacked(self.raw[index.to(self.raw.device)], self.ggml_type, self.N, self.K)
+        raw = self._need_raw()
+        return GgufPacked(raw[index.to(raw.device)], self.ggml_type, self.N, self.K)
 
     @staticmethod
     def cat_rows(parts: List["GgufPacked"]) -> "GgufPacked":
         t = parts[0].ggml_type
         if any(p.ggml_type != t or p.K != parts[0].K for p in parts):
             raise ValueError("cannot concatenate packed weights of different types / widths")
-        return GgufPacked(torch.cat([p.raw for p in parts], 0), t, sum(p.N for p in parts), parts[0].K)
+        return GgufPacked(torch.cat([p._need_raw() for p in parts], 0), t, sum(p.N for p in parts), parts[0].K)
 
     # ---------------------------------------------------------------- multiply
     def tiles(self) -> torch.Tensor:
+        """The tile-major copy the kernels read.  On the GPU the raw rows are dropped once it exists (sharding
+        and concatenation happen at layer construction, before the first multiply)."""
         if self._tiles is None:
             if torch.cuda.is_available() and torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("packed weight must be repacked before CUDA graph capture")
             self._tiles = repack_tiles(self.raw, self.ggml_type, self.N, self.K)
+            if self._tiles.is_cuda:
+                self.raw = None
         return self._tiles
+
+    def _need_raw(self) -> torch.Tensor:
+        if self.raw is None:
+            raise RuntimeError("packed weight was already repacked for the GPU kernels; shard it before use")
+        return self.raw
 
     def dense_cuda(self) -> torch.Tensor:
         from . import _cuda_ext, add_launches
-        out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.raw.device)
+        out = torch.empty(self.N, self.K, dtype=torch.bfloat16, device=self.device)
         _cuda_ext().qdequant(self.tiles(), self.ggml_type, self.N, self.K, out)
         add_launches(1)
         return out
@@ -176,7 +189,7 @@ class GgufPacked:
         return out
 
     def __repr__(self) -> str:
-        return f"GgufPacked({DQ.type_name(self.ggml_type)}, [{self.N}, {self.K}], {self.raw.device})"
+        return f"GgufPacked({DQ.type_name(self.ggml_type)}, [{self.N}, {self.K}], {self.device})"
 
 
 def is_packed(w) -> bool:
@@ -203,3 +216,38 @@ def cat_rows(parts):
             raise ValueError("cannot mix packed and dense weights in one projection")
         return GgufPacked.cat_rows(list(parts))
     return torch.cat(list(parts), 0)
+
+
+def _f16_bytes(v: float, device) -> torch.Tensor:
+    return torch.tensor([v], dtype=torch.float16).view(torch.uint8).to(device)
+
+
+def random_packed(ggml_type: int, N: int, K: int, seed: int, device, std: float = 0.02) -> GgufPacked:
+    """Random blocks generated on ``device`` whose dequantized values spread like N(0, std) (random codes, block
+    scales chosen for that spread): the random-init stand-in for a quantized checkpoint, without a file."""
+    be, bb = DQ.block_info(ggml_type)
+    nblk = N * K // be
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    raw = torch.randint(0, 256, (nblk, bb), dtype=torch.uint8, device=device, generator=g)
+    t = ggml_type
+    if t == 40:                                      # NVFP4: ue4m3 sub-scales 4 * 2^-10
+        raw[:, 0:4] = 4
+    elif t == 39:                                    # MXFP4: 2^(e - 128) times the doubled e2m1 grid
+        raw[:, 0] = 128 + int(round(math.log2(std / 5.7)))
+    elif t == 12:                                    # Q4_K: 6-bit scales / mins of 32, codes centred by dmin
+        d = std / (32 * 4.6)
+        raw[:, 0:2] = _f16_bytes(d, device)
+        raw[:, 2:4] = _f16_bytes(d * 7.5, device)
+        raw[:, 4:12] = 0xA0
+        raw[:, 12:16] = 0
+    elif t == 14:                                    # Q6_K: int8 scales 16, codes -32..31
+        raw[:, 192:208] = 16
+        raw[:, 208:210] = _f16_bytes(std / (16 * 18.5), device)
+    elif t == 8:                                     # Q8_0
+        raw[:, 0:2] = _f16_bytes(std / 74.0, device)
+    elif t == 2:                                     # Q4_0
+        raw[:, 0:2] = _f16_bytes(std / 4.6, device)
+    else:
+        raise ValueError(f"random packing not provided for {DQ.type_name(t)}")
+    return GgufPacked(raw.reshape(-1), t, N, K)
