@@ -7,7 +7,8 @@
 //
 // Layout (written once at load time by ops/quant.py, a lossless byte permutation of the GGUF blocks): the
 // weight is cut into tiles of 128 rows x 256 K elements ("row steps"); within a row step the block fields are
-// stored structure-of-arrays (all scales first, then all quant bytes) so every field is 2/4/16-byte aligned,
+// stored structure-of-arrays (all scales first, then all quant bytes) so every field is 2/4/16-byte aligned
+// (FP4 codes are regrouped pair-adjacent: byte t of a block holds elements 2t and 2t+1),
 // and the row step is padded to a multiple of 16 bytes (bytes per row step: Q4_0 / IQ4_NL / MXFP4 / NVFP4 /
 // Q4_K / IQ4_XS 144, Q4_1 160, Q5_K 176, Q6_K 224, Q8_0 272).  Tiles are stored [N/128][K/256][128 rows]
 // [row step], so one row-step tile is ONE contiguous run of 128 * bprs bytes: a single bulk copy
@@ -16,10 +17,12 @@
 // qgemm_decode_kernel<TYPE, BN> (swap-AB like the bf16 decode GEMM: 128 weight rows = MMA M, tokens = MMA N):
 //   warp 0 lane 0   producer: the CTA's activation slice [BN x Krange] is loaded ONCE by TMA and stays
 //                   resident in shared memory; the packed weight tiles stream through a ring of row steps;
-//   warps 4..7      dequant: thread r decodes row r of each 64-wide K sub-step into a bf16 128 x 64 tile in
-//                   the UMMA SWIZZLE_128B K-major layout (fp32 math in the reference's operation order, one
-//                   rounding to bf16), then fence.proxy.async + mbarrier arrive;
-//   warp 1 lane 0   tcgen05.mma (kind::f16, fp32 accumulator in TMEM) on each dequantized tile;
+//   warps 4..11     dequant: first convert the resident activation slice to f16 in place, then two threads per
+//                   weight row decode each 64-wide K sub-step into an f16 128 x 64 tile in the UMMA
+//                   SWIZZLE_128B K-major layout (FP4: hardware e2m1x2 -> f16x2 conversion times the block scale,
+//                   exact; 4/8-bit integer codes: 1024.0-magic f16 halves, one subtract, one fma), then
+//                   fence.proxy.async + mbarrier arrive;
+//   warp 1 lane 0   tcgen05.mma (kind::f16 with f16 operands, fp32 accumulator in TMEM) on each tile;
 //   warps 0..3      epilogue: tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the
 //                   consumer sums exactly like the bf16 decode GEMM's.
 // Every wait is bounded (nvb::mbar_wait -> device error word) so a broken pipeline returns instead of hanging.
@@ -125,12 +128,18 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ p, int e0, c
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = d * (float)(int8_t)q[j];
   } else if constexpr (TYPE == T_NVFP4) {
-    const int blk = e0 >> 6, ei = e0 & 63, i = ei >> 4, u0 = ei & 15;
-    const float d = ue4m3_half(p[blk * 4 + i]);
-    uint8_t q[8];
-    load8(p + 16 + blk * 32 + i * 8, q);
+    // repacked codes are pair-adjacent: byte t of a 64-element block holds elements 2t (low) and 2t+1 (high)
+    const int blk = e0 >> 6, ei = e0 & 63;
+    const float d = ue4m3_half(p[blk * 4 + (ei >> 4)]);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 16 + blk * 32 + (ei >> 1));
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = d * L.fp4[u0 ? (q[j] >> 4) : (q[j] & 0xF)];
+    for (int j = 0; j < 8; ++j) v[j] = d * L.fp4[(w >> (4 * j)) & 0xF];
+  } else if constexpr (TYPE == T_MXFP4) {
+    const int b = e0 >> 5, ei = e0 & 31;
+    const float d = e8m0_half(p[b]);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 16 + b * 16 + (ei >> 1));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = d * L.fp4[(w >> (4 * j)) & 0xF];
   } else {
     // 32-element blocks with 16 quant bytes: elements 0..15 low nibbles, 16..31 high nibbles
     const int b = e0 >> 5, i0 = e0 & 31;
@@ -150,10 +159,6 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ p, int e0, c
       const float d = h2f(p + 2 * b);
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = d * L.iq4[hi ? (q[j] >> 4) : (q[j] & 0xF)];
-    } else if constexpr (TYPE == T_MXFP4) {
-      const float d = e8m0_half(p[b]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = d * L.fp4[hi ? (q[j] >> 4) : (q[j] & 0xF)];
     } else {  // IQ4_XS
       const float d = h2f(p);
       const uint32_t sh = *reinterpret_cast<const uint16_t*>(p + 2);
@@ -174,6 +179,117 @@ __device__ __forceinline__ void init_luts(Luts& L) {
     L.fp4[threadIdx.x] = c_fp4[threadIdx.x];
     L.iq4[threadIdx.x] = c_iq4[threadIdx.x];
   }
+}
+
+// ------------------------------------------------------------------------------------------ f16 chunk decode
+// The fused GEMM multiplies in f16 (kind::f16 with f16 A and B): every FP4 value times its ue4m3 scale has at
+// most 6 significant bits, so the f16 weights are exact, and the K-quant formula keeps 11 mantissa bits instead
+// of bf16's 8.  decode_h8 returns elements [e0, e0 + 8) of a row step as 8 f16 (one 16-byte smem chunk).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+// eight e2m1 codes (4 bytes; low nibble -> low half of each f16x2) to four f16x2, hardware conversion
+__device__ __forceinline__ void e2m1x8_to_h2(uint32_t w, uint32_t (&d)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]) : "r"(w));
+}
+__device__ __forceinline__ uint32_t f2_to_h2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ uint32_t h2_bcast(float v) { return f2_to_h2(v, v); }
+
+// per f16 half: 1024.0 with the masked code bits as mantissa, (t & mask) | 0x6400
+__device__ __forceinline__ uint32_t nib_pair(uint32_t t, uint32_t mask) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(t), "r"(mask), "r"(0x64006400u));  // (a & b) | c
+  return d;
+}
+
+template <int TYPE>
+__device__ __forceinline__ uint4 decode_h8(const uint8_t* __restrict__ p, int e0, const Luts& L) {
+  uint4 o;
+  if constexpr (TYPE == T_NVFP4 || TYPE == T_MXFP4) {
+    uint32_t w;
+    float sc;
+    if constexpr (TYPE == T_NVFP4) {
+      const int blk = e0 >> 6, ei = e0 & 63;
+      w = *reinterpret_cast<const uint32_t*>(p + 16 + blk * 32 + (ei >> 1));
+      sc = 2.f * ue4m3_half(p[blk * 4 + (ei >> 4)]);   // cvt yields the true e2m1 value (half the grid)
+    } else {
+      const int b = e0 >> 5, ei = e0 & 31;
+      w = *reinterpret_cast<const uint32_t*>(p + 16 + b * 16 + (ei >> 1));
+      sc = 2.f * e8m0_half(p[b]);
+    }
+    const uint32_t s2 = h2_bcast(sc);
+    uint32_t h[4];
+    e2m1x8_to_h2(w, h);
+    o.x = hmul2(h[0], s2);
+    o.y = hmul2(h[1], s2);
+    o.z = hmul2(h[2], s2);
+    o.w = hmul2(h[3], s2);
+  } else if constexpr (TYPE == T_Q4_K) {
+    const int sb = e0 >> 5, i0 = e0 & 31;
+    const float d = h2f(p), dmin = h2f(p + 2);
+    const uint8_t* q = p + 4;
+    int sc, mn;
+    if (sb < 4) {
+      sc = q[sb] & 63;
+      mn = q[sb + 4] & 63;
+    } else {
+      sc = (q[sb + 4] & 0xF) | ((q[sb - 4] >> 6) << 4);
+      mn = (q[sb + 4] >> 4) | ((q[sb] >> 6) << 4);
+    }
+    const bool hi = sb & 1;
+    // 1024 + code in each f16 half (high nibbles land 4 bits up: 1024 + 16 code, scale / 16)
+    const float ds = d * (float)sc * (hi ? 0.0625f : 1.f);
+    const uint32_t s2 = h2_bcast(ds), m2 = h2_bcast(-(dmin * (float)mn));
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    const uint2 w = *reinterpret_cast<const uint2*>(p + 16 + (sb >> 1) * 32 + i0);
+    const uint32_t k1024 = 0x64006400u;
+    o.x = hfma2(hsub2(nib_pair(prmt(w.x, 0, 0x4140), mask), k1024), s2, m2);
+    o.y = hfma2(hsub2(nib_pair(prmt(w.x, 0, 0x4342), mask), k1024), s2, m2);
+    o.z = hfma2(hsub2(nib_pair(prmt(w.y, 0, 0x4140), mask), k1024), s2, m2);
+    o.w = hfma2(hsub2(nib_pair(prmt(w.y, 0, 0x4342), mask), k1024), s2, m2);
+  } else if constexpr (TYPE == T_Q8_0) {
+    const int b = e0 >> 5, i0 = e0 & 31;
+    const uint32_t s2 = h2_bcast(h2f(p + 2 * b));
+    const uint2 w = *reinterpret_cast<const uint2*>(p + 16 + b * 32 + i0);
+    const uint32_t x0 = w.x ^ 0x80808080u, x1 = w.y ^ 0x80808080u;  // two's complement -> offset binary
+    const uint32_t k1152 = 0x64806480u;                                 // 1024 + 128
+    o.x = hmul2(hsub2(prmt(x0, 0x64646464u, 0x4140), k1152), s2);
+    o.y = hmul2(hsub2(prmt(x0, 0x64646464u, 0x4342), k1152), s2);
+    o.z = hmul2(hsub2(prmt(x1, 0x64646464u, 0x4140), k1152), s2);
+    o.w = hmul2(hsub2(prmt(x1, 0x64646464u, 0x4342), k1152), s2);
+  } else {
+    float v[8];
+    decode8<TYPE>(p, e0, L, v);
+    o.x = f2_to_h2(v[0], v[1]);
+    o.y = f2_to_h2(v[2], v[3]);
+    o.z = f2_to_h2(v[4], v[5]);
+    o.w = f2_to_h2(v[6], v[7]);
+  }
+  return o;
 }
 
 // 1-D bulk copy global -> shared (no tensor map, no multicast); completion counted on ``bar``.
@@ -205,22 +321,31 @@ __host__ __device__ constexpr uint32_t q_pow2_cols(int n) {
   return c;
 }
 
+// kind::f16 instruction descriptor with f16 A and B, f32 accumulator, both K-major
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+constexpr int kQDequantWarps = 8;
+constexpr int kQThreads = 128 + 32 * kQDequantWarps;
+
 template <int TYPE, int BN>
-__global__ void __launch_bounds__(256, 1) qgemm_decode_kernel(const __grid_constant__ CUtensorMap xmap, QArgs a) {
-  constexpr uint32_t A_TILE = QBM * QBK * 2;  // 16 KB bf16 tile
+__global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid_constant__ CUtensorMap xmap, QArgs a) {
+  constexpr uint32_t A_TILE = QBM * QBK * 2;  // 16 KB f16 tile
   constexpr uint32_t X_BOX = BN * QBK * 2;    // one [BN x 64] activation box
   constexpr uint32_t TMEM_COLS = q_pow2_cols(BN);
-  constexpr uint32_t IDESC = nvb::idesc_bf16_f32(QBM, BN);
+  constexpr uint32_t IDESC = idesc_f16_f32(QBM, BN);
   const uint32_t stage_bytes = (uint32_t)a.bprs * QBM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xres = smem;                                           // kper * 4 boxes
-  uint8_t* atile = xres + (size_t)a.kper * 4 * X_BOX;             // kQAStages bf16 tiles (1 KB aligned)
+  uint8_t* atile = xres + (size_t)a.kper * 4 * X_BOX;             // kQAStages f16 tiles (1 KB aligned)
   uint8_t* wring = atile + (size_t)kQAStages * A_TILE;            // ws packed stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(wring + (size_t)a.ws * stage_bytes);
   uint64_t* xbar = bars;
-  uint64_t* wfull = bars + 1;
+  uint64_t* xready = bars + 1;
+  uint64_t* wfull = bars + 2;
   uint64_t* wempty = wfull + a.ws;
   uint64_t* afull = wempty + a.ws;
   uint64_t* aempty = afull + kQAStages;
@@ -240,12 +365,13 @@ __global__ void __launch_bounds__(256, 1) qgemm_decode_kernel(const __grid_const
   if (threadIdx.x == 0) {
     abort_flag = 0;
     nvb::mbar_init(xbar, 1);
+    nvb::mbar_init(xready, kQDequantWarps);
     for (int s = 0; s < a.ws; ++s) {
       nvb::mbar_init(&wfull[s], 1);
-      nvb::mbar_init(&wempty[s], 4);  // one arrival per dequant warp
+      nvb::mbar_init(&wempty[s], kQDequantWarps);
     }
     for (int s = 0; s < kQAStages; ++s) {
-      nvb::mbar_init(&afull[s], 4);
+      nvb::mbar_init(&afull[s], kQDequantWarps);
       nvb::mbar_init(&aempty[s], 1);
     }
     nvb::mbar_init(tfull, 1);
@@ -287,7 +413,7 @@ __global__ void __launch_bounds__(256, 1) qgemm_decode_kernel(const __grid_const
   } else if (warp == 1) {
     nvb::pdl_wait();
     if (lane == 0) {
-      bool ok = nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
+      bool ok = nvb::mbar_wait(xready, 0, a.err, &abort_flag);
       for (int i = 0; ok && i < nks; ++i) {
         for (int sub = 0; sub < 4; ++sub) {
           const int u = i * 4 + sub, t = u % kQAStages;
@@ -309,10 +435,25 @@ __global__ void __launch_bounds__(256, 1) qgemm_decode_kernel(const __grid_const
     }
   } else if (warp >= 4) {
     nvb::pdl_wait();
-    // dequant: thread r owns weight row r of the tile
-    const int r = threadIdx.x - 128;
+    const int dt = threadIdx.x - 128;       // 0 .. 32 * kQDequantWarps - 1
+    bool ok = nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
+    if (ok) {
+      // the resident activation slice becomes f16 in place (saturating; the layout is elementwise)
+      const uint32_t xbytes = (uint32_t)nks * 4 * X_BOX;
+      for (uint32_t off = (uint32_t)dt * 16; off < xbytes; off += 32 * kQDequantWarps * 16) {
+        uint4 v = *reinterpret_cast<const uint4*>(xres + off);
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = f2_to_h2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+        *reinterpret_cast<uint4*>(xres + off) = v;
+      }
+      nvb::fence_proxy_async();
+    }
+    __syncwarp();
+    if (lane == 0) nvb::mbar_arrive(xready);
+    // dequant: thread dt owns row dt % 128 of the tile, chunks [4h, 4h + 4) of each 64-wide sub-step
+    const int r = dt & 127, h = dt >> 7;
     const uint32_t swz = (uint32_t)(r & 7);
-    bool ok = true;
     for (int i = 0; ok && i < nks; ++i) {
       const int s = i % a.ws;
       if (!nvb::mbar_wait(&wfull[s], (i / a.ws) & 1u, a.err, &abort_flag)) break;
@@ -324,15 +465,10 @@ __global__ void __launch_bounds__(256, 1) qgemm_decode_kernel(const __grid_const
           break;
         }
         uint8_t* dst = atile + (size_t)t * A_TILE + (size_t)r * 128;
-#pragma unroll 2
-        for (int c = 0; c < 8; ++c) {
-          float v[8];
-          decode8<TYPE>(p, sub * QBK + c * 8, luts, v);
-          uint4 o;
-          o.x = nvb::pack_bf16x2(v[0], v[1]);
-          o.y = nvb::pack_bf16x2(v[2], v[3]);
-          o.z = nvb::pack_bf16x2(v[4], v[5]);
-          o.w = nvb::pack_bf16x2(v[6], v[7]);
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * h + cc;
+          const uint4 o = decode_h8<TYPE>(p, sub * QBK + c * 8, luts);
           *reinterpret_cast<uint4*>(dst + (((uint32_t)c ^ swz) << 4)) = o;
         }
         nvb::fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's async proxy
@@ -458,7 +594,7 @@ QPlan q_plan(int M, int N, int K, int type, int sms) {
   p.S = (ksteps + kper - 1) / kper;
   p.ws = ws;
   p.smem = 1024 + (size_t)kper * x_step + (size_t)kQAStages * QBM * QBK * 2 + (size_t)ws * stage +
-           (size_t)(1 + 2 * ws + 2 * kQAStages + 1) * 8 + 64;
+           (size_t)(2 + 2 * ws + 2 * kQAStages + 1) * 8 + 64;
   return p;
 }
 
@@ -467,7 +603,7 @@ void q_launch(const CUtensorMap& xm, const QArgs& a, const QPlan& p, cudaStream_
   auto kern = qgemm_decode_kernel<TYPE, BN>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
   const int groups = (a.N + QBM - 1) / QBM;
-  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(256), p.smem, st, xm, a));
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(kQThreads), p.smem, st, xm, a));
 }
 
 template <int TYPE>

@@ -27,6 +27,17 @@ def fused_supported(ggml_type: int, shape: Sequence[int]) -> bool:
     return ggml_type in FUSED_TYPES and len(shape) == 2 and shape[1] % STEP == 0
 
 
+def _pair_adjacent(qs: torch.Tensor, groups: int) -> torch.Tensor:
+    """FP4 code bytes of one block [..., nbytes] from GGUF order (per group of 2g codes: byte u holds codes u and
+    u + g) to pair-adjacent order (byte t holds codes 2t and 2t + 1, low nibble first): the order in which the
+    hardware e2m1x2 -> f16x2 conversion produces adjacent elements."""
+    shp = qs.shape
+    g = qs.reshape(*shp[:-1], groups, shp[-1] // groups)
+    codes = torch.cat([g & 0xF, g >> 4], -1).reshape(*shp[:-1], 2 * shp[-1])  # block element order
+    pairs = codes.reshape(*shp[:-1], shp[-1], 2)
+    return (pairs[..., 0] | (pairs[..., 1] << 4)).to(torch.uint8)
+
+
 def repack_tiles(raw: torch.Tensor, ggml_type: int, N: int, K: int) -> torch.Tensor:
     """Raw GGUF rows [N, row_bytes] -> flat uint8 [ceil(N/128), K/256, 128, bprs]: per 256-element row step the
     block fields are regrouped structure-of-arrays (scales, then quant bytes) and padded to 16-byte multiples;
@@ -50,10 +61,10 @@ def repack_tiles(raw: torch.Tensor, ggml_type: int, N: int, K: int) -> torch.Ten
         step = torch.cat([f(0, 2), f(2, 4), f(4, 20)], -1)
     elif t == 8:                           # Q8_0: d[8] | qs[8][32]
         step = torch.cat([f(0, 2), f(2, 34)], -1)
-    elif t == 39:                          # MXFP4: e[8] | pad 8 | qs[8][16]
-        step = torch.cat([f(0, 1), z(8), f(1, 17)], -1)
-    elif t == 40:                          # NVFP4 (4 blocks of 64): scales[4][4] | qs[4][32]
-        step = torch.cat([f(0, 4), f(4, 36)], -1)
+    elif t == 39:                          # MXFP4: e[8] | pad 8 | qs[8][16] (pair-adjacent codes)
+        step = torch.cat([f(0, 1), z(8), _pair_adjacent(B[..., 1:17], 1).reshape(N, S, 128)], -1)
+    elif t == 40:                          # NVFP4 (4 blocks of 64): scales[4][4] | qs[4][32] (pair-adjacent codes)
+        step = torch.cat([f(0, 4), _pair_adjacent(B[..., 4:36], 4).reshape(N, S, 128)], -1)
     elif t in (12, 13):                    # Q4_K / Q5_K: one super-block, already grouped
         step = B.reshape(N, S, bb)
     elif t == 14:                          # Q6_K: ql | qh | scales | d, padded 210 -> 224

@@ -50,11 +50,14 @@ def test_repack_is_a_lossless_byte_permutation(t):
     tiles = repack_tiles(w.raw, t, N, K)
     bprs = FUSED_TYPES[t]
     assert tiles.numel() == 3 * (K // 256) * 128 * bprs
-    # every raw byte value survives with its multiplicity (padding adds zeros only)
-    raw_hist = torch.bincount(w.raw.reshape(-1).long(), minlength=256)
-    tile_hist = torch.bincount(tiles.long(), minlength=256)
+    # every raw 4-bit field survives with its multiplicity (FP4 codes are regrouped pair-adjacent; padding adds
+    # zero bytes only)
+    def nibbles(b):
+        b = b.reshape(-1).long()
+        return torch.bincount(torch.cat([b & 0xF, b >> 4]), minlength=16)
     pad = tiles.numel() - w.raw.numel()
-    assert torch.equal(tile_hist[1:], raw_hist[1:]) and int(tile_hist[0] - raw_hist[0]) == pad
+    raw_h, tile_h = nibbles(w.raw), nibbles(tiles)
+    assert torch.equal(tile_h[1:], raw_h[1:]) and int(tile_h[0] - raw_h[0]) == 2 * pad
     # row r, step s of the tile-major layout starts at ((r // 128) * S + s) * 128 + r % 128
     S = K // 256
     t4 = tiles.reshape(3, S, 128, bprs)
