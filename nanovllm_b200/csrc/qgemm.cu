@@ -15,14 +15,19 @@
 // (cp.async.bulk, no tensor map, no multicast) per pipeline stage, and perfect DRAM streaming.
 //
 // qgemm_decode_kernel<TYPE, BN> (swap-AB like the bf16 decode GEMM: 128 weight rows = MMA M, tokens = MMA N):
-//   warp 0 lane 0   producer: the CTA's activation slice [BN x Krange] is loaded ONCE by TMA and stays
-//                   resident in shared memory; the packed weight tiles stream through a ring of row steps;
-//   warps 4..11     dequant: first convert the resident activation slice to f16 in place, then two threads per
-//                   weight row decode each 64-wide K sub-step into an f16 128 x 64 tile in the UMMA
-//                   SWIZZLE_128B K-major layout (FP4: hardware e2m1x2 -> f16x2 conversion times the block scale,
-//                   exact; 4/8-bit integer codes: 1024.0-magic f16 halves, one subtract, one fma), then
-//                   fence.proxy.async + mbarrier arrive;
-//   warp 1 lane 0   tcgen05.mma (kind::f16 with f16 operands, fp32 accumulator in TMEM) on each tile;
+//   warp 0 lane 0   producer: for small token tiles the CTA's activation slice [BN x Krange] is loaded ONCE
+//                   by TMA and stays resident in shared memory; the packed weight tiles stream through a ring
+//                   of row steps;
+//   warps 4..11     dequant: (resident mode) convert the activation slice to f16 in place; then two groups of
+//                   4 warps take alternate 64-wide K sub-steps, thread = weight row = TMEM lane, and write the
+//                   f16 sub-tile straight from registers into one of 8 TMEM slots (tcgen05.st) -- no shared-
+//                   memory tile, no proxy fence (FP4: hardware e2m1x2 -> f16x2 conversion times the block
+//                   scale, exact; 4/8-bit integer codes: 1024.0-magic f16 halves, one subtract, one fma);
+//   warp 1 lane 0   tcgen05.mma kind::f16 with the A operand read from TMEM, B (f16 activations) from shared
+//                   memory, fp32 accumulator in TMEM;
+// Token tiles of 64 and more use the streaming mode instead of the resident slice: an f16 copy of the
+// activations (q_to_f16_kernel) streams through a ring of row steps, so the K range -- and the number of fp32
+// split partials -- is not capped by shared memory.
 //   warps 0..3      epilogue: tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the
 //                   consumer sums exactly like the bf16 decode GEMM's.
 // Every wait is bounded (nvb::mbar_wait -> device error word) so a broken pipeline returns instead of hanging.
@@ -40,7 +45,9 @@ using bf16 = __nv_bfloat16;
 constexpr int QBM = 128, QBK = 64, QSTEP = 256;
 constexpr int kQXBytes = 128 * 1024;    // resident activation slice budget
 constexpr int kQRingBytes = 224 * 1024;  // activation slice + bf16 tiles + packed ring
-constexpr int kQAStages = 2;             // dequantized bf16 tiles in flight
+constexpr int kQAStages = 8;             // dequantized f16 tiles in flight (TMEM slots of 32 columns)
+constexpr uint32_t kQAcol0 = 256;         // TMEM column of the first A slot (the accumulator uses [0, BN))
+constexpr int kQMaxXS = 4;                // activation ring stages in streaming mode (at most)
 
 // GGML type ids (the GGUF on-disk codes)
 constexpr int T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ4_NL = 20,
@@ -292,6 +299,107 @@ __device__ __forceinline__ uint4 decode_h8(const uint8_t* __restrict__ p, int e0
   return o;
 }
 
+// Whole 64-element sub-step of a row (elements [64 sub, 64 sub + 64) of the row step) as 32 f16x2, block scales
+// decoded once.  Specialised for the formats of the serving configs; the rest go through decode_h8.
+__device__ __forceinline__ void e4m3x4_scales(uint32_t sc, uint32_t (&s2)[4]) {
+  // ue4m3 0x7F (NaN in e4m3) reads as 0, like the loader's decoder
+  const uint32_t nan = __vcmpeq4(sc, 0x7F7F7F7Fu);
+  sc &= ~nan;
+  uint32_t h01, h23;
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, lo;\n\tcvt.rn.f16x2.e4m3x2 %1, hi;\n\t}"
+      : "=r"(h01), "=r"(h23) : "r"(sc));
+  s2[0] = prmt(h01, h01, 0x1010);
+  s2[1] = prmt(h01, h01, 0x3232);
+  s2[2] = prmt(h23, h23, 0x1010);
+  s2[3] = prmt(h23, h23, 0x3232);
+}
+
+template <int TYPE>
+__device__ __forceinline__ void decode_sub64(const uint8_t* __restrict__ p, int sub, const Luts& L, uint32_t (&v)[32]) {
+  if constexpr (TYPE == T_NVFP4) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32 + 16);
+    uint32_t s2[4];
+    e4m3x4_scales(*reinterpret_cast<const uint32_t*>(p + sub * 4), s2);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t h[4];
+      e2m1x8_to_h2(w[k], h);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[4 * k + j] = hmul2(h[j], s2[k >> 1]);
+    }
+  } else if constexpr (TYPE == T_MXFP4) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32 + 16);
+    const uint32_t e0 = p[2 * sub], e1 = p[2 * sub + 1];
+    const uint32_t sa = h2_bcast(e0 ? __int_as_float((int)e0 << 23) : 0.f);
+    const uint32_t sb = h2_bcast(e1 ? __int_as_float((int)e1 << 23) : 0.f);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      uint32_t h[4];
+      e2m1x8_to_h2(w[k], h);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[4 * k + j] = hmul2(h[j], k < 4 ? sa : sb);
+    }
+  } else if constexpr (TYPE == T_Q4_K) {
+    const float d = h2f(p), dmin = h2f(p + 2);
+    const uint8_t* q = p + 4;
+    const int sl = 2 * sub, sh = 2 * sub + 1;  // low-nibble and high-nibble sub-blocks of this sub-step
+    int sc0, mn0, sc1, mn1;
+    if (sl < 4) {
+      sc0 = q[sl] & 63;
+      mn0 = q[sl + 4] & 63;
+      sc1 = q[sh] & 63;
+      mn1 = q[sh + 4] & 63;
+    } else {
+      sc0 = (q[sl + 4] & 0xF) | ((q[sl - 4] >> 6) << 4);
+      mn0 = (q[sl + 4] >> 4) | ((q[sl] >> 6) << 4);
+      sc1 = (q[sh + 4] & 0xF) | ((q[sh - 4] >> 6) << 4);
+      mn1 = (q[sh + 4] >> 4) | ((q[sh] >> 6) << 4);
+    }
+    const uint32_t s0 = h2_bcast(d * (float)sc0), m0 = h2_bcast(-(dmin * (float)mn0));
+    const uint32_t s1 = h2_bcast(d * (float)sc1 * 0.0625f), m1 = h2_bcast(-(dmin * (float)mn1));
+    const uint4 q0 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(p + 16 + sub * 32 + 16);
+    const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+    const uint32_t k1024 = 0x64006400u;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t t0 = prmt(w[k], 0, 0x4140), t1 = prmt(w[k], 0, 0x4342);
+      v[2 * k] = hfma2(hsub2(nib_pair(t0, 0x000F000Fu), k1024), s0, m0);
+      v[2 * k + 1] = hfma2(hsub2(nib_pair(t1, 0x000F000Fu), k1024), s0, m0);
+      v[16 + 2 * k] = hfma2(hsub2(nib_pair(t0, 0x00F000F0u), k1024), s1, m1);
+      v[16 + 2 * k + 1] = hfma2(hsub2(nib_pair(t1, 0x00F000F0u), k1024), s1, m1);
+    }
+  } else if constexpr (TYPE == T_Q8_0) {
+    const uint32_t dbits = *reinterpret_cast<const uint32_t*>(p + 4 * sub);  // d of blocks 2 sub, 2 sub + 1
+    const uint32_t da = prmt(dbits, dbits, 0x1010), db = prmt(dbits, dbits, 0x3232);
+    const uint32_t k1152 = 0x64806480u;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const uint4 q = *reinterpret_cast<const uint4*>(p + 16 + sub * 64 + 16 * h);
+      const uint32_t w[4] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u, q.z ^ 0x80808080u, q.w ^ 0x80808080u};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * h + 2 * k] = hmul2(hsub2(prmt(w[k], 0x64646464u, 0x4140), k1152), h < 2 ? da : db);
+        v[8 * h + 2 * k + 1] = hmul2(hsub2(prmt(w[k], 0x64646464u, 0x4342), k1152), h < 2 ? da : db);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 o = decode_h8<TYPE>(p, sub * QBK + c * 8, L);
+      v[4 * c] = o.x;
+      v[4 * c + 1] = o.y;
+      v[4 * c + 2] = o.z;
+      v[4 * c + 3] = o.w;
+    }
+  }
+}
+
 // 1-D bulk copy global -> shared (no tensor map, no multicast); completion counted on ``bar``.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -307,6 +415,7 @@ struct QArgs {
   int kper;         // row steps per split (the resident activation slice covers kper * 256 columns)
   int S;            // splits
   int ws;           // packed ring stages
+  int xs;           // activation ring stages (row steps); 0 = the CTA's activation slice is resident
   int bprs;         // bytes per row step
   const uint8_t* w; // tile-major packed weight
   bf16* out;
@@ -321,6 +430,31 @@ __host__ __device__ constexpr uint32_t q_pow2_cols(int n) {
   return c;
 }
 
+// D(tmem) (+)= A(tmem) * B(smem desc)^T, kind::f16: the A operand is read from tensor memory (128 lanes = rows,
+// each 32-bit column holds two consecutive K elements).
+__device__ __forceinline__ void tc_mma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 bit, 32 consecutive columns per thread (each thread writes its own lane)
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // kind::f16 instruction descriptor with f16 A and B, f32 accumulator, both K-major
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
   return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -331,17 +465,20 @@ constexpr int kQThreads = 128 + 32 * kQDequantWarps;
 
 template <int TYPE, int BN>
 __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid_constant__ CUtensorMap xmap, QArgs a) {
-  constexpr uint32_t A_TILE = QBM * QBK * 2;  // 16 KB f16 tile
   constexpr uint32_t X_BOX = BN * QBK * 2;    // one [BN x 64] activation box
-  constexpr uint32_t TMEM_COLS = q_pow2_cols(BN);
+  constexpr uint32_t TMEM_COLS = 512;         // accumulator [0, BN) + kQAStages A slots from column 256
   constexpr uint32_t IDESC = idesc_f16_f32(QBM, BN);
+  static_assert(BN <= (int)kQAcol0 && kQAcol0 + 32 * kQAStages <= TMEM_COLS, "TMEM plan");
   const uint32_t stage_bytes = (uint32_t)a.bprs * QBM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* xres = smem;                                           // kper * 4 boxes
-  uint8_t* atile = xres + (size_t)a.kper * 4 * X_BOX;             // kQAStages f16 tiles (1 KB aligned)
-  uint8_t* wring = atile + (size_t)kQAStages * A_TILE;            // ws packed stages
+  // resident mode (xs == 0): the CTA's whole activation slice (kper row steps), converted to f16 in place;
+  // streaming mode (xs > 0, larger token tiles): a ring of xs row steps of an f16 activation copy
+  const bool stream = a.xs > 0;
+  const int xslots = stream ? a.xs : a.kper;
+  uint8_t* xres = smem;                                           // xslots * 4 boxes
+  uint8_t* wring = xres + (size_t)xslots * 4 * X_BOX;             // ws packed stages
   uint64_t* bars = reinterpret_cast<uint64_t*>(wring + (size_t)a.ws * stage_bytes);
   uint64_t* xbar = bars;
   uint64_t* xready = bars + 1;
@@ -350,6 +487,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
   uint64_t* afull = wempty + a.ws;
   uint64_t* aempty = afull + kQAStages;
   uint64_t* tfull = aempty + kQAStages;
+  uint64_t* xfull = tfull + 1;      // streaming mode: [xs]
+  uint64_t* xempty = xfull + kQMaxXS;
   __shared__ Luts luts;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
@@ -371,10 +510,14 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
       nvb::mbar_init(&wempty[s], kQDequantWarps);
     }
     for (int s = 0; s < kQAStages; ++s) {
-      nvb::mbar_init(&afull[s], kQDequantWarps);
+      nvb::mbar_init(&afull[s], 4);  // the 4 warps of the dequant group that owns the sub-step
       nvb::mbar_init(&aempty[s], 1);
     }
     nvb::mbar_init(tfull, 1);
+    for (int s = 0; s < a.xs; ++s) {
+      nvb::mbar_init(&xfull[s], 1);
+      nvb::mbar_init(&xempty[s], 1);
+    }
     nvb::fence_mbar_init();
   }
   if (warp == 1) {
@@ -398,14 +541,32 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
       }
       nvb::tma_prefetch_desc(&xmap);
       nvb::pdl_wait();
-      nvb::mbar_arrive_expect_tx(xbar, (uint32_t)nks * 4 * X_BOX);
-      for (int b = 0; b < nks * 4; ++b)
-        nvb::tma_load_2d(xres + (size_t)b * X_BOX, &xmap, xbar, ks0 * QSTEP + b * QBK, 0);
-      for (int i = pre; i < nks; ++i) {
-        const int s = i % a.ws;
-        if (!nvb::mbar_wait(&wempty[s], ((i / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) break;
-        nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
-        bulk_load(wring + (size_t)s * stage_bytes, wsrc + (size_t)i * stage_bytes, stage_bytes, &wfull[s]);
+      if (!stream) {
+        nvb::mbar_arrive_expect_tx(xbar, (uint32_t)nks * 4 * X_BOX);
+        for (int b = 0; b < nks * 4; ++b)
+          nvb::tma_load_2d(xres + (size_t)b * X_BOX, &xmap, xbar, ks0 * QSTEP + b * QBK, 0);
+        for (int i = pre; i < nks; ++i) {
+          const int s = i % a.ws;
+          if (!nvb::mbar_wait(&wempty[s], ((i / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) break;
+          nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
+          bulk_load(wring + (size_t)s * stage_bytes, wsrc + (size_t)i * stage_bytes, stage_bytes, &wfull[s]);
+        }
+      } else {
+        // row step i's activations, then the weight row step that dequant frees by finishing row step i
+        for (int i = 0; i < nks; ++i) {
+          const int xsl = i % a.xs;
+          if (i >= a.xs && !nvb::mbar_wait(&xempty[xsl], ((i / a.xs) & 1u) ^ 1u, a.err, &abort_flag)) break;
+          nvb::mbar_arrive_expect_tx(&xfull[xsl], 4 * X_BOX);
+          for (int b = 0; b < 4; ++b)
+            nvb::tma_load_2d(xres + ((size_t)xsl * 4 + b) * X_BOX, &xmap, &xfull[xsl], (ks0 + i) * QSTEP + b * QBK, 0);
+          const int j = i + a.ws;
+          if (j < nks) {
+            const int s = j % a.ws;
+            if (!nvb::mbar_wait(&wempty[s], ((j / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) break;
+            nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
+            bulk_load(wring + (size_t)s * stage_bytes, wsrc + (size_t)j * stage_bytes, stage_bytes, &wfull[s]);
+          }
+        }
       }
     } else {
       nvb::pdl_wait();
@@ -413,31 +574,36 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
   } else if (warp == 1) {
     nvb::pdl_wait();
     if (lane == 0) {
-      bool ok = nvb::mbar_wait(xready, 0, a.err, &abort_flag);
-      for (int i = 0; ok && i < nks; ++i) {
-        for (int sub = 0; sub < 4; ++sub) {
-          const int u = i * 4 + sub, t = u % kQAStages;
-          if (!nvb::mbar_wait(&afull[t], (u / kQAStages) & 1u, a.err, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          nvb::tc_fence_after();
-          const uint32_t a_addr = nvb::smem_u32(atile + (size_t)t * A_TILE);
-          const uint32_t b_addr = nvb::smem_u32(xres + (size_t)u * X_BOX);
-#pragma unroll
-          for (int kk = 0; kk < QBK / 16; ++kk)
-            nvb::tc_mma_f16(tmem_base, nvb::sdesc_kmajor_sw128(a_addr + kk * 32), nvb::sdesc_kmajor_sw128(b_addr + kk * 32),
-                            IDESC, (u > 0 || kk > 0) ? 1u : 0u);
-          nvb::tc_commit(&aempty[t]);
+      bool ok = stream || nvb::mbar_wait(xready, 0, a.err, &abort_flag);
+      const int nsub = nks * 4;
+      for (int u = 0; ok && u < nsub; ++u) {
+        const int t = u % kQAStages, i = u >> 2;
+        if (stream && (u & 3) == 0 && !nvb::mbar_wait(&xfull[i % a.xs], (i / a.xs) & 1u, a.err, &abort_flag)) {
+          ok = false;
+          break;
         }
+        if (!nvb::mbar_wait(&afull[t], (u / kQAStages) & 1u, a.err, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        nvb::tc_fence_after();
+        const uint32_t a_tm = tmem_base + kQAcol0 + (uint32_t)t * 32;
+        const size_t box = stream ? (size_t)(i % a.xs) * 4 + (u & 3) : (size_t)u;
+        const uint32_t b_addr = nvb::smem_u32(xres + box * X_BOX);
+#pragma unroll
+        for (int kk = 0; kk < QBK / 16; ++kk)
+          tc_mma_f16_tmem_a(tmem_base, a_tm + kk * 8, nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
+                            (u > 0 || kk > 0) ? 1u : 0u);
+        nvb::tc_commit(&aempty[t]);
+        if (stream && (u & 3) == 3) nvb::tc_commit(&xempty[i % a.xs]);
       }
       if (ok) nvb::tc_commit(tfull);
     }
   } else if (warp >= 4) {
     nvb::pdl_wait();
     const int dt = threadIdx.x - 128;       // 0 .. 32 * kQDequantWarps - 1
-    bool ok = nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
-    if (ok) {
+    bool ok = stream || nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
+    if (ok && !stream) {
       // the resident activation slice becomes f16 in place (saturating; the layout is elementwise)
       const uint32_t xbytes = (uint32_t)nks * 4 * X_BOX;
       for (uint32_t off = (uint32_t)dt * 16; off < xbytes; off += 32 * kQDequantWarps * 16) {
@@ -450,28 +616,27 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
       nvb::fence_proxy_async();
     }
     __syncwarp();
-    if (lane == 0) nvb::mbar_arrive(xready);
-    // dequant: thread dt owns row dt % 128 of the tile, chunks [4h, 4h + 4) of each 64-wide sub-step
-    const int r = dt & 127, h = dt >> 7;
-    const uint32_t swz = (uint32_t)(r & 7);
+    if (lane == 0 && !stream) nvb::mbar_arrive(xready);
+    // dequant: two groups of 4 warps take alternate 64-wide K sub-steps; thread = weight row (its TMEM lane);
+    // the f16 tile goes straight from registers into a TMEM slot that the MMA reads as its A operand
+    const int quarter = warp & 3, r = quarter * 32 + lane, g = (warp - 4) >> 2;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
     for (int i = 0; ok && i < nks; ++i) {
       const int s = i % a.ws;
       if (!nvb::mbar_wait(&wfull[s], (i / a.ws) & 1u, a.err, &abort_flag)) break;
       const uint8_t* p = wring + (size_t)s * stage_bytes + (size_t)r * a.bprs;
-      for (int sub = 0; sub < 4; ++sub) {
+      for (int sub = g; sub < 4; sub += 2) {
         const int u = i * 4 + sub, t = u % kQAStages;
         if (u >= kQAStages && !nvb::mbar_wait(&aempty[t], ((u / kQAStages) & 1u) ^ 1u, a.err, &abort_flag)) {
           ok = false;
           break;
         }
-        uint8_t* dst = atile + (size_t)t * A_TILE + (size_t)r * 128;
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = 4 * h + cc;
-          const uint4 o = decode_h8<TYPE>(p, sub * QBK + c * 8, luts);
-          *reinterpret_cast<uint4*>(dst + (((uint32_t)c ^ swz) << 4)) = o;
-        }
-        nvb::fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's async proxy
+        nvb::tc_fence_after();
+        uint32_t v[32];
+        decode_sub64<TYPE>(p, sub, luts, v);
+        tmem_st_32x32b_x32(lane_base + kQAcol0 + (uint32_t)t * 32, v);
+        tmem_st_wait();
+        nvb::tc_fence_before();
         __syncwarp();
         if (lane == 0) nvb::mbar_arrive(&afull[t]);
       }
@@ -548,9 +713,24 @@ __global__ void qdequant_kernel(const uint8_t* __restrict__ w, int N, int K, int
 }
 
 struct QPlan {
-  int bn, kper, S, ws, bprs;
+  int bn, kper, S, ws, xs, bprs;
   size_t smem;
 };
+
+// bf16 -> f16 copy of the activations for the streaming mode (saturating), 8 elements per thread.
+__global__ void q_to_f16_kernel(const bf16* __restrict__ x, long ld, int M, int K, uint16_t* __restrict__ y) {
+  nvb::pdl_wait();
+  nvb::pdl_trigger();
+  const long per_row = K / 8, n = (long)M * per_row;
+  for (long c = blockIdx.x * (long)blockDim.x + threadIdx.x; c < n; c += (long)gridDim.x * blockDim.x) {
+    const long m = c / per_row, k = (c % per_row) * 8;
+    uint4 v = *reinterpret_cast<const uint4*>(x + m * ld + k);
+    uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[j] = f2_to_h2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+    *reinterpret_cast<uint4*>(y + m * (long)K + k) = v;
+  }
+}
 
 int q_num_sms() {
   static int n = -1;
@@ -575,26 +755,44 @@ QPlan q_plan(int M, int N, int K, int type, int sms) {
   p.bprs = row_step_bytes(type);
   const int ksteps = K / QSTEP, groups = (N + QBM - 1) / QBM;
   const int x_step = p.bn * QSTEP * 2;
-  int kper = kQXBytes / x_step;
+  // token tiles of 64 and more stream their activations (an f16 copy) through a ring of row steps: a resident
+  // slice would cap the K range at 512 and multiply the splits and their fp32 partials
+  p.xs = p.bn >= 64 ? (p.bn >= 256 ? 1 : p.bn >= 128 ? 2 : 3) : 0;
+  int kper = p.xs ? ksteps : kQXBytes / x_step;
   if (kper < 1) kper = 1;
-  const int s_fill = (sms + groups - 1) / groups;
-  const int kper_fill = (ksteps + s_fill - 1) / s_fill;
-  if (kper > kper_fill) kper = kper_fill;
   if (kper > ksteps) kper = ksteps;
-  if (kper < 1) kper = 1;
+  // with few waves of CTAs, take the K split (within the activation budget) whose CTAs fill the last wave best
+  // (fewer splits on a tie: fewer fp32 partials); with many waves the tail matters little and every extra
+  // split costs partial traffic, so keep the fewest
+  if (groups < 2 * sms) {
+    const int kmax = kper;
+    double best = -1.0;
+    for (int kp = kmax; kp >= 1; --kp) {
+      const int S = (ksteps + kp - 1) / kp;
+      if (kp < kmax && (ksteps + kp) / (kp + 1) == S) continue;  // same split count as a larger kper
+      const long ctas = (long)groups * S;
+      const long waves = (ctas + sms - 1) / sms;
+      const double eff = (double)ctas / (double)(waves * sms);
+      if (eff > best + 0.04) {
+        best = eff;
+        kper = kp;
+      }
+      if (S >= 16) break;
+    }
+  }
   const int stage = QBM * p.bprs;
   int ws = 0;
   for (;;) {
-    ws = (kQRingBytes - kper * x_step - kQAStages * QBM * QBK * 2) / stage;
-    if (ws >= 2 || kper == 1) break;
+    ws = (kQRingBytes - (p.xs ? p.xs : kper) * x_step) / stage;
+    if (ws >= 2 || kper == 1 || p.xs) break;
     kper = (kper + 1) / 2;
   }
   if (ws > 12) ws = 12;
   p.kper = kper;
   p.S = (ksteps + kper - 1) / kper;
   p.ws = ws;
-  p.smem = 1024 + (size_t)kper * x_step + (size_t)kQAStages * QBM * QBK * 2 + (size_t)ws * stage +
-           (size_t)(2 + 2 * ws + 2 * kQAStages + 1) * 8 + 64;
+  p.smem = 1024 + (size_t)(p.xs ? p.xs : kper) * x_step + (size_t)ws * stage +
+           (size_t)(2 + 2 * ws + 2 * kQAStages + 1 + 2 * kQMaxXS) * 8 + 64;
   return p;
 }
 
@@ -684,6 +882,7 @@ int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, in
   a.kper = p.kper;
   a.S = p.S;
   a.ws = p.ws;
+  a.xs = p.xs;
   a.bprs = p.bprs;
   a.w = w.data_ptr<uint8_t>();
   a.out = reinterpret_cast<bf16*>(out.data_ptr());
@@ -695,8 +894,23 @@ int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, in
                 "packed GEMM: fp32 partial buffer [S, M, N] required");
     a.partial = parts->data_ptr<float>();
   }
-  CUtensorMap xm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), p.bn);
   auto st = at::cuda::getCurrentCUDAStream();
+  torch::Tensor xh;
+  const void* xp = x.data_ptr();
+  long xld = x.stride(0);
+  if (p.xs) {  // streaming mode multiplies an f16 copy of the activations
+    xh = torch::empty({M, (long)K}, x.options().dtype(at::kHalf));
+    const long chunks = (long)M * (K / 8);
+    int blocks = (int)((chunks + 255) / 256);
+    if (blocks > q_num_sms() * 4) blocks = q_num_sms() * 4;
+    C10_CUDA_CHECK(nvb::launch(q_to_f16_kernel, dim3(blocks), dim3(256), 0, st,
+                               reinterpret_cast<const bf16*>(x.data_ptr()), xld, M, (int)K,
+                               reinterpret_cast<uint16_t*>(xh.data_ptr())));
+    xp = xh.data_ptr();
+    xld = K;
+  }
+  // 2-byte elements either way: the bf16 map describes the f16 copy just as well
+  CUtensorMap xm = nvb::make_tmap_2d_bf16(xp, M, K, xld, p.bn);
   Q_DISPATCH((int)type, q_launch_bn, xm, a, p, st);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (p.S > 1 && !partial_out)
