@@ -208,8 +208,9 @@ def run_ours(args):
             "dtype": "bf16", "data": "synthetic: random-init weights (seed 4), random prompt ids",
             "config": {"model": "Qwen3-8B-shape (36L, H4096, 32/8 heads, hd128, I12288, V151936)",
                        "weights": "bf16" if args.weights == "bf16" else
-                                  f"projections GGUF {args.weights.upper()} (packed, dequant-fused GEMM); "
-                                  f"embeddings / LM head bf16",
+                                  f"projections GGUF {args.weights.upper()} packed ("
+                                  + ("dequantized per multiply, then cuBLAS" if args.impl == "baseline"
+                                     else "dequant-fused GEMM") + "); embeddings / LM head bf16",
                        "global_batch": running, "seq_len": f"prompts U[{args.min_prompt},{args.max_prompt}]",
                        "parallelism": f"tp{world}", "l2": "inputs larger than L2 (weights of several GB + KV cache)",
                        "prefill_tokens": prefill_tokens, "prefill_s": round(prefill_s, 3),
