@@ -19,10 +19,12 @@
 //                   by TMA and stays resident in shared memory; the packed weight tiles stream through a ring
 //                   of row steps;
 //   warps 4..11     dequant: (resident mode) convert the activation slice to f16 in place; then two groups of
-//                   4 warps take alternate 64-wide K sub-steps, thread = weight row = TMEM lane, and write the
-//                   f16 sub-tile straight from registers into one of 8 TMEM slots (tcgen05.st) -- no shared-
-//                   memory tile, no proxy fence (FP4: hardware e2m1x2 -> f16x2 conversion times the block
-//                   scale, exact; 4/8-bit integer codes: 1024.0-magic f16 halves, one subtract, one fma);
+//                   4 warps take alternate 256-wide row steps, thread = weight row = TMEM lane, and write the
+//                   four f16 64-wide sub-tiles straight from registers into one of 3 TMEM row-step slots
+//                   (tcgen05.st) -- no shared-memory tile, no proxy fence (FP4: hardware e2m1x2 -> f16x2
+//                   conversion times the block scale, exact; 4/8-bit integer codes: 1024.0-magic f16 halves,
+//                   one subtract, one fma).  One hand-off per row step, not per sub-step: the hand-off round
+//                   trip, not the arithmetic, paced the kernel (measured 1.5x faster, LM-head shape 1.7x);
 //   warp 1 lane 0   tcgen05.mma kind::f16 with the A operand read from TMEM, B (f16 activations) from shared
 //                   memory, fp32 accumulator in TMEM;
 // Token tiles of 64 and more use the streaming mode instead of the resident slice: an f16 copy of the
@@ -45,8 +47,10 @@ using bf16 = __nv_bfloat16;
 constexpr int QBM = 128, QBK = 64, QSTEP = 256;
 constexpr int kQXBytes = 128 * 1024;    // resident activation slice budget
 constexpr int kQRingBytes = 224 * 1024;  // activation slice + bf16 tiles + packed ring
-constexpr int kQAStages = 8;             // dequantized f16 tiles in flight (TMEM slots of 32 columns)
-constexpr uint32_t kQAcol0 = 256;         // TMEM column of the first A slot (the accumulator uses [0, BN))
+constexpr int kQAStages = 3;             // dequantized f16 row steps in flight (TMEM slots of 4 x 32 columns)
+// TMEM column of the first A slot: the accumulator uses [0, BN); 128 leaves room for 3 row-step slots
+__host__ __device__ constexpr uint32_t q_acol0(int bn) { return bn <= 128 ? 128u : 256u; }
+__host__ __device__ constexpr int q_aslots(int bn) { return (int)((512u - q_acol0(bn)) / 128u); }
 constexpr int kQMaxXS = 4;                // activation ring stages in streaming mode (at most)
 
 // GGML type ids (the GGUF on-disk codes)
@@ -466,9 +470,11 @@ constexpr int kQThreads = 128 + 32 * kQDequantWarps;
 template <int TYPE, int BN>
 __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid_constant__ CUtensorMap xmap, QArgs a) {
   constexpr uint32_t X_BOX = BN * QBK * 2;    // one [BN x 64] activation box
-  constexpr uint32_t TMEM_COLS = 512;         // accumulator [0, BN) + kQAStages A slots from column 256
+  constexpr uint32_t TMEM_COLS = 512;         // accumulator [0, BN) + AS row-step slots of 128 columns
   constexpr uint32_t IDESC = idesc_f16_f32(QBM, BN);
-  static_assert(BN <= (int)kQAcol0 && kQAcol0 + 32 * kQAStages <= TMEM_COLS, "TMEM plan");
+  constexpr uint32_t ACOL0 = q_acol0(BN);
+  constexpr int AS = q_aslots(BN);            // 3 (BN <= 128) or 2 row-step slots
+  static_assert(BN <= (int)ACOL0 && AS <= kQAStages && ACOL0 + 128 * AS <= TMEM_COLS, "TMEM plan");
   const uint32_t stage_bytes = (uint32_t)a.bprs * QBM;
 
   extern __shared__ uint8_t smem_raw[];
@@ -507,10 +513,10 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
     nvb::mbar_init(xready, kQDequantWarps);
     for (int s = 0; s < a.ws; ++s) {
       nvb::mbar_init(&wfull[s], 1);
-      nvb::mbar_init(&wempty[s], kQDequantWarps);
+      nvb::mbar_init(&wempty[s], 4);  // the 4 warps of the dequant group that owns the row step
     }
     for (int s = 0; s < kQAStages; ++s) {
-      nvb::mbar_init(&afull[s], 4);  // the 4 warps of the dequant group that owns the sub-step
+      nvb::mbar_init(&afull[s], 4);
       nvb::mbar_init(&aempty[s], 1);
     }
     nvb::mbar_init(tfull, 1);
@@ -575,27 +581,30 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
     nvb::pdl_wait();
     if (lane == 0) {
       bool ok = stream || nvb::mbar_wait(xready, 0, a.err, &abort_flag);
-      const int nsub = nks * 4;
-      for (int u = 0; ok && u < nsub; ++u) {
-        const int t = u % kQAStages, i = u >> 2;
-        if (stream && (u & 3) == 0 && !nvb::mbar_wait(&xfull[i % a.xs], (i / a.xs) & 1u, a.err, &abort_flag)) {
+      // one hand-off per 256-wide row step: wait for its 4 dequantized sub-tiles, issue 16 MMAs, release
+      for (int i = 0; ok && i < nks; ++i) {
+        const int t = i % AS;
+        if (stream && !nvb::mbar_wait(&xfull[i % a.xs], (i / a.xs) & 1u, a.err, &abort_flag)) {
           ok = false;
           break;
         }
-        if (!nvb::mbar_wait(&afull[t], (u / kQAStages) & 1u, a.err, &abort_flag)) {
+        if (!nvb::mbar_wait(&afull[t], (i / AS) & 1u, a.err, &abort_flag)) {
           ok = false;
           break;
         }
         nvb::tc_fence_after();
-        const uint32_t a_tm = tmem_base + kQAcol0 + (uint32_t)t * 32;
-        const size_t box = stream ? (size_t)(i % a.xs) * 4 + (u & 3) : (size_t)u;
-        const uint32_t b_addr = nvb::smem_u32(xres + box * X_BOX);
 #pragma unroll
-        for (int kk = 0; kk < QBK / 16; ++kk)
-          tc_mma_f16_tmem_a(tmem_base, a_tm + kk * 8, nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
-                            (u > 0 || kk > 0) ? 1u : 0u);
+        for (int sub = 0; sub < 4; ++sub) {
+          const uint32_t a_tm = tmem_base + ACOL0 + (uint32_t)t * 128 + sub * 32;
+          const size_t box = stream ? (size_t)(i % a.xs) * 4 + sub : (size_t)i * 4 + sub;
+          const uint32_t b_addr = nvb::smem_u32(xres + box * X_BOX);
+#pragma unroll
+          for (int kk = 0; kk < QBK / 16; ++kk)
+            tc_mma_f16_tmem_a(tmem_base, a_tm + kk * 8, nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
+                              (i > 0 || sub > 0 || kk > 0) ? 1u : 0u);
+        }
         nvb::tc_commit(&aempty[t]);
-        if (stream && (u & 3) == 3) nvb::tc_commit(&xempty[i % a.xs]);
+        if (stream) nvb::tc_commit(&xempty[i % a.xs]);
       }
       if (ok) nvb::tc_commit(tfull);
     }
@@ -617,31 +626,29 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
     }
     __syncwarp();
     if (lane == 0 && !stream) nvb::mbar_arrive(xready);
-    // dequant: two groups of 4 warps take alternate 64-wide K sub-steps; thread = weight row (its TMEM lane);
-    // the f16 tile goes straight from registers into a TMEM slot that the MMA reads as its A operand
+    // dequant: two groups of 4 warps take alternate 256-wide row steps; thread = weight row (its TMEM lane);
+    // the f16 sub-tiles go straight from registers into a TMEM slot that the MMA reads as its A operand
     const int quarter = warp & 3, r = quarter * 32 + lane, g = (warp - 4) >> 2;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    for (int i = 0; ok && i < nks; ++i) {
-      const int s = i % a.ws;
+    for (int i = g; ok && i < nks; i += 2) {
+      const int s = i % a.ws, t = i % AS;
       if (!nvb::mbar_wait(&wfull[s], (i / a.ws) & 1u, a.err, &abort_flag)) break;
+      if (i >= AS && !nvb::mbar_wait(&aempty[t], ((i / AS) & 1u) ^ 1u, a.err, &abort_flag)) break;
+      nvb::tc_fence_after();
       const uint8_t* p = wring + (size_t)s * stage_bytes + (size_t)r * a.bprs;
-      for (int sub = g; sub < 4; sub += 2) {
-        const int u = i * 4 + sub, t = u % kQAStages;
-        if (u >= kQAStages && !nvb::mbar_wait(&aempty[t], ((u / kQAStages) & 1u) ^ 1u, a.err, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        nvb::tc_fence_after();
+#pragma unroll 1
+      for (int sub = 0; sub < 4; ++sub) {
         uint32_t v[32];
         decode_sub64<TYPE>(p, sub, luts, v);
-        tmem_st_32x32b_x32(lane_base + kQAcol0 + (uint32_t)t * 32, v);
-        tmem_st_wait();
-        nvb::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) nvb::mbar_arrive(&afull[t]);
+        tmem_st_32x32b_x32(lane_base + ACOL0 + (uint32_t)t * 128 + sub * 32, v);
       }
+      tmem_st_wait();
+      nvb::tc_fence_before();
       __syncwarp();
-      if (lane == 0) nvb::mbar_arrive(&wempty[s]);
+      if (lane == 0) {
+        nvb::mbar_arrive(&afull[t]);
+        nvb::mbar_arrive(&wempty[s]);  // the packed row step has been read
+      }
     }
   } else {
     nvb::pdl_wait();  // warps 2, 3: epilogue only
