@@ -27,11 +27,11 @@
 //                   trip, not the arithmetic, paced the kernel (measured 1.5x faster, LM-head shape 1.7x);
 //   warp 1 lane 0   tcgen05.mma kind::f16 with the A operand read from TMEM, B (f16 activations) from shared
 //                   memory, fp32 accumulator in TMEM;
+//   warps 0..3      epilogue: tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the
+//                   consumer sums exactly like the bf16 decode GEMM's.
 // Token tiles of 64 and more use the streaming mode instead of the resident slice: an f16 copy of the
 // activations (q_to_f16_kernel) streams through a ring of row steps, so the K range -- and the number of fp32
 // split partials -- is not capped by shared memory.
-//   warps 0..3      epilogue: tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the
-//                   consumer sums exactly like the bf16 decode GEMM's.
 // Every wait is bounded (nvb::mbar_wait -> device error word) so a broken pipeline returns instead of hanging.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
