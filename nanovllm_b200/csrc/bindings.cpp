@@ -22,6 +22,9 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
 int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out);
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act);
+int64_t gemm_sk_floats(int64_t M, int64_t N, int64_t K, int64_t act);
+void gemm_sk_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, torch::Tensor workspace,
+                  torch::Tensor counters, c10::optional<torch::Tensor> err);
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
 int64_t qgemm_splits_cuda(int64_t M, int64_t N, int64_t K, int64_t type);
 int64_t qgemm_row_step_bytes(int64_t type);
@@ -62,6 +65,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &prefill_attention_cuda);
   m.def("gemm", &gemm_cuda);
   m.def("gemm_splits_for", &gemm_splits_for);
+  m.def("gemm_sk_floats", &gemm_sk_floats);
+  m.def("gemm_sk", &gemm_sk_cuda);
   m.def("splitk_sum", &splitk_sum_cuda);
   m.def("qgemm_splits", &qgemm_splits_cuda);
   m.def("qgemm_row_step_bytes", &qgemm_row_step_bytes);

@@ -466,6 +466,224 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ------------------------------------------------------------------------------------------------ stream-K gate/up
+// Decode-sized fused gate/up GEMM (NA = 2: a 256-row group = 128 gate + 128 up rows) when there are fewer groups
+// than SMs (Qwen3-8B at TP1: 96 groups of 4096-long rows on 148 SMs, so a one-CTA-per-group grid leaves a third
+// of HBM bandwidth unused).  The (group, 64-wide K block) work units are laid out group-major and cut into one
+// contiguous, equal range per CTA (stream-K); a range covers the tail of one group and the head of the next, so a
+// CTA accumulates at most two segments, in two TMEM regions.  A segment that covers a whole group goes straight
+// through the act(gate) * up epilogue.  Otherwise the CTA writes its fp32 partial of the group to the workspace
+// and bumps the group's arrival counter; the last CTA to arrive (no CTA ever waits for another) adds the group's
+// partials in segment order -- fixed, so the result does not depend on timing -- applies the activation, writes
+// bf16 and resets the counter for the next launch.
+struct SkArgs {
+  int N, M, K, kblocks, groups, act;
+  bf16* out;
+  long out_ld;
+  float* ws;       // [groups][kSkMaxSeg][2][BN][128] fp32
+  int* counters;   // [groups], zero between launches
+  int* err;
+};
+constexpr int kSkMaxSeg = 3;
+
+__device__ __forceinline__ long sk_start(long units, int P, int c) { return units * c / P; }
+// CTA whose unit range contains unit x
+__device__ __forceinline__ int sk_owner(long units, int P, long x) {
+  int c = (int)((x * P) / units);
+  while (c + 1 < P && sk_start(units, P, c + 1) <= x) ++c;
+  while (c > 0 && sk_start(units, P, c) > x) --c;
+  return c;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(128, 1) gemm_decode_sk_kernel(const __grid_constant__ CUtensorMap amap,
+                                                                const __grid_constant__ CUtensorMap bmap,
+                                                                SkArgs args) {
+  constexpr int NA = 2;
+  constexpr int STAGES = decode_stages2(NA, BN, 1);
+  constexpr uint32_t A_SUB = BM * BK * 2;
+  constexpr uint32_t A_BYTES = NA * A_SUB;
+  constexpr uint32_t STAGE_BYTES = A_BYTES + BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = pow2_cols(2 * NA * BN);  // two segments x (gate, up)
+  constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
+  static_assert(2 * NA * BN <= 512, "two segments of gate/up accumulators must fit TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_flag;
+  __shared__ int last_flag[2];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int P = gridDim.x, cta = blockIdx.x;
+  const long units = (long)args.groups * args.kblocks;
+  const long u0 = sk_start(units, P, cta), u1 = sk_start(units, P, cta + 1);
+  const int g_first = (int)(u0 / args.kblocks);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      nvb::mbar_init(&full_bar[s], 1);
+      nvb::mbar_init(&empty_bar[s], 1);
+    }
+    nvb::mbar_init(tfull_bar, 1);
+    nvb::fence_mbar_init();
+  }
+  if (warp == 1) {
+    nvb::tmem_alloc(&tmem_base_sh, TMEM_COLS);
+    nvb::tmem_relinquish();
+  }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  nvb::pdl_trigger();
+
+  if (warp == 0 && lane == 0) {
+    nvb::tma_prefetch_desc(&amap);
+    nvb::tma_prefetch_desc(&bmap);
+    const long n = u1 - u0;
+    const int pre = n < STAGES ? (int)n : STAGES;
+    for (int it = 0; it < pre; ++it) {  // weights first, before the dependency wait
+      const long u = u0 + it;
+      const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
+      uint8_t* sa = smem + it * STAGE_BYTES;
+      nvb::mbar_arrive_expect_tx(&full_bar[it], STAGE_BYTES);
+#pragma unroll
+      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[it], kb * BK, g * (NA * BM) + j * BM);
+    }
+    nvb::pdl_wait();
+    for (int it = 0; it < pre; ++it) {
+      const int kb = (int)((u0 + it) % args.kblocks);
+      nvb::tma_load_2d(smem + it * STAGE_BYTES + A_BYTES, &bmap, &full_bar[it], kb * BK, 0);
+    }
+    for (long it = pre; it < n; ++it) {
+      const int s = (int)(it % STAGES);
+      if (!nvb::mbar_wait(&empty_bar[s], ((it / STAGES) & 1u) ^ 1u, args.err, &abort_flag)) break;
+      const long u = u0 + it;
+      const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
+      uint8_t* sa = smem + s * STAGE_BYTES;
+      nvb::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
+#pragma unroll
+      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[s], kb * BK, g * (NA * BM) + j * BM);
+      nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, 0);
+    }
+  } else {
+    nvb::pdl_wait();  // the epilogue writes outputs a previous kernel may still read
+  }
+  if (warp == 1 && lane == 0) {
+    bool ok = true;
+    const long n = u1 - u0;
+    for (long it = 0; it < n; ++it) {
+      const int s = (int)(it % STAGES);
+      if (!nvb::mbar_wait(&full_bar[s], (it / STAGES) & 1u, args.err, &abort_flag)) { ok = false; break; }
+      nvb::tc_fence_after();
+      const long u = u0 + it;
+      const int seg = (int)(u / args.kblocks) - g_first;             // 0 or 1
+      const bool first = (it == 0) || (u % args.kblocks == 0);       // first unit of its segment
+      const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES);
+      const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+      for (int j = 0; j < NA; ++j)
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          nvb::tc_mma_f16(tmem_base + (seg * NA + j) * BN, nvb::sdesc_kmajor_sw128(a_addr + j * A_SUB + kk * 32),
+                          nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC, (!first || kk > 0) ? 1u : 0u);
+      nvb::tc_commit(&empty_bar[s]);
+    }
+    if (ok) nvb::tc_commit(tfull_bar);
+  }
+  __syncwarp();
+  int ok = 0;
+  if (lane == 0) ok = nvb::mbar_wait(tfull_bar, 0, args.err, &abort_flag) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  ok = __syncthreads_and(ok);  // the epilogue has block barriers: every warp takes the same path
+  nvb::tc_fence_after();
+
+  const int r = threadIdx.x;  // TMEM lane = row inside each 128-row tile
+  const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
+  const int nseg = (u1 > u0) ? (int)((u1 - 1) / args.kblocks) - g_first + 1 : 0;
+  constexpr int CH = BN < 32 ? BN : 32;
+  for (int seg = 0; ok && seg < nseg; ++seg) {
+    const int g = g_first + seg;
+    const long gs = (long)g * args.kblocks, ge = gs + args.kblocks;
+    const int f = g * BM + r;  // output feature
+    const bool whole = u0 <= gs && u1 >= ge;
+    if (whole) {
+#pragma unroll 1
+      for (int c = 0; c < BN; c += CH) {
+        uint32_t gv[CH], uv[CH];
+#pragma unroll
+        for (int q = 0; q < CH; q += 16) {
+          nvb::tmem_ld_32x32b_x16(t_row + (seg * NA) * BN + c + q, gv + q);
+          nvb::tmem_ld_32x32b_x16(t_row + (seg * NA + 1) * BN + c + q, uv + q);
+        }
+        nvb::tmem_ld_wait();
+        nvb::reg_fence<CH>(gv);
+        nvb::reg_fence<CH>(uv);
+#pragma unroll
+        for (int j = 0; j < CH; ++j)
+          if (c + j < args.M) {
+            const float x = __uint_as_float(gv[j]), y = __uint_as_float(uv[j]);
+            args.out[(long)(c + j) * args.out_ld + f] =
+                __float2bfloat16((args.act == kActSiluMul ? silu(x) : gelu_tanh(x)) * y);
+          }
+      }
+      continue;
+    }
+    // partial segment: publish this CTA's fp32 partial, then let the last contributor finish the group
+    const int c_first = sk_owner(units, P, gs), c_last = sk_owner(units, P, ge - 1);
+    const int my = cta - c_first, nparts = c_last - c_first + 1;
+    if (nparts > kSkMaxSeg) {  // the host only picks stream-K when every group has at most kSkMaxSeg parts
+      if (threadIdx.x == 0) nvb::record_error(args.err, nvb::kErrBadArgument);
+      continue;
+    }
+    float* slot = args.ws + ((size_t)g * kSkMaxSeg + my) * 2 * BN * BM;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += CH) {
+      uint32_t gv[CH], uv[CH];
+#pragma unroll
+      for (int q = 0; q < CH; q += 16) {
+        nvb::tmem_ld_32x32b_x16(t_row + (seg * NA) * BN + c + q, gv + q);
+        nvb::tmem_ld_32x32b_x16(t_row + (seg * NA + 1) * BN + c + q, uv + q);
+      }
+      nvb::tmem_ld_wait();
+      nvb::reg_fence<CH>(gv);
+      nvb::reg_fence<CH>(uv);
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {
+        slot[(size_t)(c + j) * BM + r] = __uint_as_float(gv[j]);
+        slot[(size_t)(BN + c + j) * BM + r] = __uint_as_float(uv[j]);
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_flag[seg] = atomicAdd(&args.counters[g], 1) == nparts - 1;
+    __syncthreads();
+    if (!last_flag[seg]) continue;
+    __threadfence();
+    if (threadIdx.x == 0) args.counters[g] = 0;  // ready for the next launch
+    const float* base = args.ws + (size_t)g * kSkMaxSeg * 2 * BN * BM;
+#pragma unroll 1
+    for (int t = 0; t < args.M; ++t) {
+      float x = 0.f, y = 0.f;
+      for (int k = 0; k < nparts; ++k) {  // segment order
+        const float* sl = base + (size_t)k * 2 * BN * BM;
+        x += __ldcg(sl + (size_t)t * BM + r);
+        y += __ldcg(sl + (size_t)(BN + t) * BM + r);
+      }
+      args.out[(long)t * args.out_ld + f] = __float2bfloat16((args.act == kActSiluMul ? silu(x) : gelu_tanh(x)) * y);
+    }
+  }
+  nvb::tc_fence_before();
+  __syncthreads();
+  nvb::tc_fence_after();
+  if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
 // Split-K finish of the fused gate/up GEMM: partials [S][M][N] in the 128-row interleaved weight order
 // (block b = rows [256b, 256b + 128) gate, [256b + 128, 256b + 256) up); out[m][f] = act(sum gate) * sum up for
 // f = 128 b + j, sums in split order.  One thread per 4 consecutive features of one row.
@@ -734,6 +952,77 @@ int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
   if (act != 0 && groups * 2 > num_sms()) return 1;
   int s = decode_splits(groups, kblocks, num_sms());
   return s > kblocks ? kblocks : s;
+}
+
+// Stream-K fused gate/up (see gemm_decode_sk_kernel): fp32 workspace floats it needs for this shape, 0 when the
+// shape does not take it (a one-CTA-per-group grid already fills the SMs, or would with a split; or too few
+// groups for at most kSkMaxSeg contributors per group; or more than 128 tokens).
+int64_t gemm_sk_floats(int64_t M, int64_t N, int64_t K, int64_t act) {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* e = getenv("NVB_DECODE_STREAMK");
+    enabled = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  if (!enabled || act == 0 || M <= 0 || M > 128 || N % 256 != 0) return 0;
+  const int sms = num_sms();
+  const long groups = N / 256, kblocks = (K + BK - 1) / BK;
+  if (groups >= sms || groups * 2 <= sms) return 0;
+  const long units = groups * kblocks;
+  if (units / sms < (kblocks + 1) / 2) return 0;  // a group would span more than kSkMaxSeg CTAs
+  const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  return groups * kSkMaxSeg * 2 * (long)bn * BM;
+}
+
+template <int BN>
+void launch_decode_sk(const CUtensorMap& am, const CUtensorMap& bm, const SkArgs& a, int grid, cudaStream_t stream) {
+  auto kern = gemm_decode_sk_kernel<BN>;
+  constexpr int ST = decode_stages2(2, BN, 1);
+  constexpr size_t sm = 1024 + (size_t)ST * (2 * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
+  static_assert(sm <= 227 * 1024, "stream-K decode gemm shared memory");
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(128), sm, stream, am, bm, a));
+}
+
+// out[M, N/2] = act(x @ gate^T) * (x @ up^T) on 128-row-interleaved gate/up weights, stream-K over all SMs.
+void gemm_sk_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, torch::Tensor workspace,
+                  torch::Tensor counters, c10::optional<torch::Tensor> err) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm expects bf16 CUDA tensors");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && x.stride(1) == 1 && w.stride(1) == 1,
+              "shape mismatch");
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0 && K % 8 == 0, "16-byte TMA rows");
+  TORCH_CHECK(out.stride(-1) == 1 && out.size(0) == M && out.size(1) == N / 2, "out must be [M, N/2]");
+  const int64_t need = gemm_sk_floats(M, N, K, act);
+  TORCH_CHECK(need > 0, "stream-K gate/up not planned for this shape");
+  TORCH_CHECK(workspace.is_cuda() && workspace.scalar_type() == at::kFloat && workspace.numel() >= need,
+              "stream-K workspace too small");
+  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= N / 256,
+              "stream-K counters: int32 [N/256], zero between launches");
+  SkArgs a{};
+  a.N = N;
+  a.M = M;
+  a.K = K;
+  a.kblocks = (K + BK - 1) / BK;
+  a.groups = N / 256;
+  a.act = (int)act;
+  a.out = reinterpret_cast<bf16*>(out.data_ptr());
+  a.out_ld = out.stride(0);
+  a.ws = workspace.data_ptr<float>();
+  a.counters = counters.data_ptr<int>();
+  a.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
+  CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int grid = num_sms();
+  switch (bn) {
+    case 16: launch_decode_sk<16>(am, bm, a, grid, stream); break;
+    case 32: launch_decode_sk<32>(am, bm, a, grid, stream); break;
+    case 64: launch_decode_sk<64>(am, bm, a, grid, stream); break;
+    default: launch_decode_sk<128>(am, bm, a, grid, stream); break;
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // out [M, N] bf16 = sum over splits of parts [S, M, N] fp32 (fixed order).

@@ -263,6 +263,20 @@ def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap=0.0
 
 
 _CNT: Dict[int, torch.Tensor] = {}
+_SKCNT: Dict[int, torch.Tensor] = {}
+
+
+def _sk_counters(device: torch.device, need: int) -> Optional[torch.Tensor]:
+    """Zeroed int32 per-group arrival counters of the stream-K gate/up GEMM (the kernel leaves them zeroed);
+    created outside stream capture -- a capture that finds none takes the one-CTA-per-group path."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _SKCNT.get(idx)
+    if t is None or t.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        t = torch.zeros(max(need, 4096), dtype=torch.int32, device=device)
+        _SKCNT[idx] = t
+    return t
 
 
 def _combine_counters(device: torch.device, need: int) -> Optional[torch.Tensor]:
@@ -323,6 +337,17 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
     N = w.shape[0]
     ncols = N // 2 if act != ACT_NONE else N
     C = _cuda_ext()
+    if act != ACT_NONE and force_splits == 0:
+        sk = C.gemm_sk_floats(M, N, K, int(act))
+        cnt = _sk_counters(x.device, N // 256) if sk > 0 else None
+        if cnt is not None:
+            # fewer gate/up groups than SMs: stream-K over all SMs (csrc/gemm.cu gemm_decode_sk_kernel)
+            if out is None:
+                out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
+            ws = torch.empty(sk, dtype=torch.float32, device=x.device)
+            C.gemm_sk(x, w, out, int(act), ws, cnt, error_word(x.device))
+            add_launches(1)
+            return out
     parts = None
     splits = 1
     if M <= 256:
