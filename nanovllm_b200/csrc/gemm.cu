@@ -469,7 +469,7 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
 // ------------------------------------------------------------------------------------------------ stream-K gate/up
 // Decode-sized fused gate/up GEMM (NA = 2: a 256-row group = 128 gate + 128 up rows) when there are fewer groups
 // than SMs (Qwen3-8B at TP1: 96 groups of 4096-long rows on 148 SMs, so a one-CTA-per-group grid leaves a third
-// of HBM bandwidth unused).  The (group, 64-wide K block) work units are laid out group-major and cut into one
+// of HBM bandwidth unused; opt-in, see gemm_sk_floats for the measurement).  The (group, 64-wide K block) work units are laid out group-major and cut into one
 // contiguous, equal range per CTA (stream-K); a range covers the tail of one group and the head of the next, so a
 // CTA accumulates at most two segments, in two TMEM regions.  A segment that covers a whole group goes straight
 // through the act(gate) * up epilogue.  Otherwise the CTA writes its fp32 partial of the group to the workspace
@@ -954,15 +954,15 @@ int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
   return s > kblocks ? kblocks : s;
 }
 
-// Stream-K fused gate/up (see gemm_decode_sk_kernel): fp32 workspace floats it needs for this shape, 0 when the
-// shape does not take it (a one-CTA-per-group grid already fills the SMs, or would with a split; or too few
-// groups for at most kSkMaxSeg contributors per group; or more than 128 tokens).
+// Stream-K fused gate/up (see gemm_decode_sk_kernel): fp32 workspace floats it needs for this shape, 0 when it is
+// off or the shape does not take it (a one-CTA-per-group grid already fills the SMs, or would with a split; or
+// too few groups for at most kSkMaxSeg contributors per group; or more than 128 tokens).
+// Opt-in (NVB_DECODE_STREAMK=1): measured slower than the one-CTA-per-group kernel on B200 (Qwen3-8B gate_up:
+// 205 vs 45 us at 128 tokens, 59 vs 35 us at 16) -- the last contributor's serial fix-up of up to three fp32
+// partial tiles (up to 384 KB through one SM) sits on the critical path.
 int64_t gemm_sk_floats(int64_t M, int64_t N, int64_t K, int64_t act) {
-  static int enabled = -1;
-  if (enabled < 0) {
-    const char* e = getenv("NVB_DECODE_STREAMK");
-    enabled = (e && atoi(e) == 0) ? 0 : 1;
-  }
+  const char* e = getenv("NVB_DECODE_STREAMK");
+  const bool enabled = e && atoi(e) == 1;
   if (!enabled || act == 0 || M <= 0 || M > 128 || N % 256 != 0) return 0;
   const int sms = num_sms();
   const long groups = N / 256, kblocks = (K + BK - 1) / BK;

@@ -209,9 +209,10 @@ def test_gemm_fused_gate_up_split_k(splits):
 
 
 @pytest.mark.parametrize("M,I,K", [(1, 12288, 4096), (16, 12288, 4096), (100, 12288, 2048), (128, 10240, 4096)])
-def test_gemm_fused_gate_up_stream_k(M, I, K):
-    """Fused gate/up with fewer 256-row groups than SMs runs stream-K over all SMs (partial groups finished by
-    their last contributor); two launches in a row check that the arrival counters are left at zero."""
+def test_gemm_fused_gate_up_stream_k(M, I, K, monkeypatch):
+    """Opt-in stream-K fused gate/up (fewer 256-row groups than SMs; partial groups finished by their last
+    contributor); two launches in a row check that the arrival counters are left at zero."""
+    monkeypatch.setenv("NVB_DECODE_STREAMK", "1")
     C = ops._cuda_ext()
     if C.gemm_sk_floats(M, 2 * I, K, ops.ACT_SILU_MUL) == 0:
         pytest.skip("stream-K not planned for this shape on this GPU")
