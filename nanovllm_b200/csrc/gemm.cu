@@ -469,7 +469,8 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
 // ------------------------------------------------------------------------------------------------ stream-K gate/up
 // Decode-sized fused gate/up GEMM (NA = 2: a 256-row group = 128 gate + 128 up rows) when there are fewer groups
 // than SMs (Qwen3-8B at TP1: 96 groups of 4096-long rows on 148 SMs, so a one-CTA-per-group grid leaves a third
-// of HBM bandwidth unused; opt-in, see gemm_sk_floats for the measurement).  The (group, 64-wide K block) work units are laid out group-major and cut into one
+// of HBM bandwidth unused; opt-in, see gemm_sk_floats for the measurement).  The (group, 64-wide K block) work
+// units are laid out group-major and cut into one
 // contiguous, equal range per CTA (stream-K); a range covers the tail of one group and the head of the next, so a
 // CTA accumulates at most two segments, in two TMEM regions.  A segment that covers a whole group goes straight
 // through the act(gate) * up epilogue.  Otherwise the CTA writes its fp32 partial of the group to the workspace
