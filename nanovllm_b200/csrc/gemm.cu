@@ -266,6 +266,7 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 // the kernel that consumes the output (add+RMSNorm, RoPE) or by splitk_sum_kernel.
 struct DecodeArgs {
   int N, M, K, kblocks, S, act;
+  int cluster;  // 1: the S split CTAs of a row group form a cluster and reduce through distributed smem
   bf16* out;
   long out_ld;
   float* partial;
@@ -403,6 +404,65 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   ok = __shfl_sync(0xffffffffu, ok, 0);
   nvb::tc_fence_after();
 
+  if (args.cluster) {
+    // Split K reduced inside the cluster: every CTA parks its fp32 tile(s) in its own (now idle) ring memory,
+    // then CTA q of the cluster sums token columns [q*ch, (q+1)*ch) over the S peers in rank order (the same
+    // result whatever the timing) and writes the bf16 (or activated) output.  No fp32 partials leave the SMs.
+    // ``ok`` may differ between CTAs after a timeout: every CTA still joins both cluster barriers.
+    const int r = threadIdx.x;
+    const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
+    float* red = reinterpret_cast<float*>(smem);  // [NA][BN][128] fp32, fits the ring (checked on the host)
+    if (ok) {
+#pragma unroll
+      for (int jt = 0; jt < NA; ++jt) {
+        constexpr int CH = BN < 32 ? BN : 32;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CH) {
+          uint32_t v[CH];
+#pragma unroll
+          for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + jt * BN + c + q, v + q);
+          nvb::tmem_ld_wait();
+          nvb::reg_fence<CH>(v);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) red[((size_t)jt * BN + c + j) * BM + r] = __uint_as_float(v[j]);
+        }
+      }
+    }
+    nvb::cluster_sync();  // all partial tiles of the cluster are in place
+    const int q = split, S = args.S;
+    const int ch = (BN + S - 1) / S, t0 = q * ch, t1 = min(args.M, min(BN, t0 + ch));
+    const uint32_t red_addr = nvb::smem_u32(red);
+    if (ok) {
+      if (args.act != kActNone) {
+        const int f = group * BM + r;
+        for (int t = t0; t < t1; ++t) {
+          float gsum = 0.f, usum = 0.f;
+          for (int p = 0; p < S; ++p) {
+            const uint32_t peer = nvb::map_peer(red_addr, (uint32_t)p);
+            gsum += nvb::ld_dsmem_f32(peer + (uint32_t)(((size_t)t * BM + r) * 4));
+            usum += nvb::ld_dsmem_f32(peer + (uint32_t)(((size_t)(BN + t) * BM + r) * 4));
+          }
+          if (f < args.N / 2)
+            args.out[(long)t * args.out_ld + f] =
+                __float2bfloat16((args.act == kActSiluMul ? silu(gsum) : gelu_tanh(gsum)) * usum);
+        }
+      } else {
+#pragma unroll
+        for (int jt = 0; jt < NA; ++jt) {
+          const int f = row0 + jt * BM + r;
+          for (int t = t0; t < t1; ++t) {
+            float sum = 0.f;
+            for (int p = 0; p < S; ++p)
+              sum += nvb::ld_dsmem_f32(nvb::map_peer(red_addr, (uint32_t)p) +
+                                       (uint32_t)(((size_t)(jt * BN + t) * BM + r) * 4));
+            if (f < args.N) args.out[(long)t * args.out_ld + f] = __float2bfloat16(sum);
+          }
+        }
+      }
+    }
+    nvb::cluster_sync();  // no CTA leaves while a peer still reads its shared memory
+    ok = 0;               // the tile is written
+  }
   if (ok) {
     const int r = threadIdx.x;  // TMEM lane = row inside each tile
     const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
@@ -751,7 +811,16 @@ cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const De
   constexpr size_t sm = 1024 + (size_t)ST * KSUB * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
   static_assert(ST >= 1 && sm <= 227 * 1024, "decode gemm shared memory");
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a));
+  if (a.cluster) {
+    constexpr bool kFits = (size_t)NA * BN * BM * 4 <= (size_t)ST * KSUB * (NA * BM * BK * 2 + BN * BK * 2);
+    if constexpr (!kFits) {
+      return cudaErrorInvalidValue;  // the host never asks for it (NA * BN <= 256)
+    } else {
+      C10_CUDA_CHECK(nvb::launch_cluster(kern, dim3(groups * a.S), dim3(128), sm, stream, (unsigned)a.S, am, bm, a));
+    }
+  } else {
+    C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a));
+  }
   return cudaGetLastError();
 }
 
@@ -782,6 +851,14 @@ int decode_ksub() {
     k = (e && atoi(e) == 2) ? 2 : 1;
   }
   return k;
+}
+
+// Split K reduced through distributed shared memory inside a cluster of the split CTAs (NVB_DECODE_CLUSTER=1)
+// instead of fp32 partials in global memory summed by the consuming kernel.
+constexpr int kDecodeMaxCluster = 8;
+bool decode_cluster_enabled() {
+  const char* e = getenv("NVB_DECODE_CLUSTER");
+  return e && atoi(e) == 1;
 }
 
 // Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
@@ -879,23 +956,31 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
     d.kblocks = kblocks;
     d.act = (int)act;
     const int groups = (N + NA * BM - 1) / (NA * BM);
+    const bool clus = decode_cluster_enabled();
     if (force_splits > 0) {
       d.S = (int)force_splits;
+    } else if (clus) {
+      d.S = decode_splits(groups, kblocks, sms);
+      if (act != kActNone && groups * 2 > sms) d.S = 1;
     } else {
       d.S = workspace.has_value() ? decode_splits(groups, kblocks, sms) : 1;
     }
     if (d.S > kblocks) d.S = kblocks;
-    // with split K the activation runs after the split sum (splitk_act_kernel), not in the GEMM epilogue
-    if (d.S > 1 && act != kActNone) {
+    if (clus && d.S > kDecodeMaxCluster) d.S = kDecodeMaxCluster;
+    d.cluster = (clus && d.S > 1 && NA * bn <= 256) ? 1 : 0;
+    if (clus && !d.cluster && d.S > 1 && !workspace.has_value()) d.S = 1;  // no partial buffer to fall back on
+    // with split K the activation runs after the split sum (splitk_act_kernel), not in the GEMM epilogue --
+    // unless the split CTAs reduce inside their cluster, which applies it there
+    if (d.S > 1 && act != kActNone && !d.cluster) {
       TORCH_CHECK(!partial_out, "partial output is not offered for the fused-activation GEMM");
       TORCH_CHECK(out.stride(0) % 4 == 0, "activation output rows must be 8-byte aligned");
       d.act = kActNone;
     }
-    splits_used = d.S;
+    splits_used = d.cluster ? 1 : d.S;  // no partials leave a cluster-reduced GEMM
     d.out = reinterpret_cast<bf16*>(out.data_ptr());
     d.out_ld = out.stride(0);
     d.err = e;
-    if (d.S > 1) {
+    if (d.S > 1 && !d.cluster) {
       TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
                       workspace->numel() >= (long)d.S * M * N,
                   "decode gemm: fp32 partial buffer of S*M*N elements required");
@@ -910,7 +995,9 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
     cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, ksub, am, bm, d, groups, stream)
                             : launch_decode_bn<1>(bn, ksub, am, bm, d, groups, stream);
     TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
-    if (d.S > 1 && act != kActNone) {
+    if (d.cluster) {
+      // reduced (and activated) inside the cluster: out is final
+    } else if (d.S > 1 && act != kActNone) {
       const long work = (long)M * (N / 2) / 4;
       int blocks = (int)((work + 255) / 256);
       if (blocks > sms * 8) blocks = sms * 8;
@@ -943,6 +1030,7 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 
 // K splits (and so the fp32 partial slices of the workspace) the decode path uses for this shape.
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
+  if (decode_cluster_enabled()) return 1;  // split K is reduced inside clusters: callers keep no partials
   // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;
   const int NA = decode_na((int)N, (int)act);

@@ -356,9 +356,9 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
             parts = torch.empty(splits, M, N, dtype=torch.float32, device=x.device)
     if out is None:
         out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
-    C.gemm(x, w, out, int(act), parts, int(splits if parts is not None else (force_splits or 0)),
-           error_word(x.device), bool(partial_ok and parts is not None and act == ACT_NONE))
-    if parts is not None:
+    used = C.gemm(x, w, out, int(act), parts, int(splits if parts is not None else (force_splits or 0)),
+                  error_word(x.device), bool(partial_ok and parts is not None and act == ACT_NONE))
+    if parts is not None and used > 1:
         if partial_ok and act == ACT_NONE:
             add_launches(1)
             return SplitK(parts)

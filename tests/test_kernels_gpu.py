@@ -208,6 +208,33 @@ def test_gemm_fused_gate_up_split_k(splits):
     close(y, y_ref, 5e-3, 0.03)
 
 
+@pytest.mark.parametrize("M,N,K,act", [(1, 4096, 4096, 0), (16, 6144, 4096, 0), (128, 4096, 2048, 0),
+                                        (100, 4096, 12288, 0), (128, 12288, 4096, 1), (64, 24576, 4096, 0)])
+def test_gemm_decode_cluster_reduction(M, N, K, act, monkeypatch):
+    """Opt-in decode GEMM whose K splits reduce inside a thread-block cluster (distributed shared memory)
+    instead of fp32 partials in global memory: same result as the fp32 reference, bit-identical across launches."""
+    monkeypatch.setenv("NVB_DECODE_CLUSTER", "1")
+    g = torch.Generator().manual_seed(M + N + K)
+    x = (torch.randn(M, K, generator=g) * 0.5).bfloat16()
+    if act:
+        gate = (torch.randn(N // 2, K, generator=g) * 0.05).bfloat16()
+        up = (torch.randn(N // 2, K, generator=g) * 0.05).bfloat16()
+        w = ref.interleave_gate_up(torch.cat([gate, up]), 128).contiguous()
+        y_ref = (ref.silu(ref.linear(x, gate).float()) * ref.linear(x, up).float()).bfloat16()
+        a = ops.ACT_SILU_MUL
+    else:
+        w = (torch.randn(N, K, generator=g) * 0.05).bfloat16()
+        y_ref = ref.linear(x, w)
+        a = 0
+    xd, wd = x.to(DEV), w.to(DEV)
+    y1 = ops.materialize(ops.linear(xd, wd, a, partial_ok=True))
+    y2 = ops.materialize(ops.linear(xd, wd, a, partial_ok=True))
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    close(y1, y_ref, 5e-3, 0.03)
+    assert torch.equal(y1, y2)
+
+
 @pytest.mark.parametrize("M,I,K", [(1, 12288, 4096), (16, 12288, 4096), (100, 12288, 2048), (128, 10240, 4096)])
 def test_gemm_fused_gate_up_stream_k(M, I, K, monkeypatch):
     """Opt-in stream-K fused gate/up (fewer 256-row groups than SMs; partial groups finished by their last
