@@ -17,6 +17,7 @@ tensor, so every class here takes either.
 """
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -27,6 +28,10 @@ from ..parallel import symm
 
 
 from ..ops.quant import cat_rows, is_packed, shard_cols, shard_rows  # dense tensors and GgufPacked alike
+
+
+def _splitk_in_ar() -> bool:
+    return os.environ.get("NVB_TP_SPLITK_IN_AR", "0") == "1"
 
 
 class LinearBase:
@@ -158,9 +163,10 @@ class RowParallelLinear(LinearBase):
             ws = symm.workspace()
             T = x.shape[0]
             if ws is not None and ws.fits(T, w.shape[0]):
-                # partial sum straight into the symmetric buffer (or left split over K for the all-reduce
-                # kernel to sum); the consumer fuses all-reduce + norm
-                y = mm(out=ws.in_view(T), partial_ok=True)
+                # partial sum straight into the symmetric buffer; the consumer fuses all-reduce + norm.  With
+                # NVB_TP_SPLITK_IN_AR=1 a split-K GEMM leaves its fp32 slices for the all-reduce kernel to sum
+                # (one launch less, but measured slower at TP2: 10547 vs 10977 tok/s, so off by default)
+                y = mm(out=ws.in_view(T), partial_ok=_splitk_in_ar())
                 return ops.TPPartial(ws, T, y.parts if isinstance(y, ops.SplitK) else None)
         y = ops.materialize(mm())
         if self.reduce:
