@@ -861,25 +861,11 @@ bool decode_cluster_enabled() {
   return e && atoi(e) == 1;
 }
 
-// Gate/up with 65..128 tokens whose fused-activation grid (one CTA per 256-row group) would have to split K
-// (fewer than half as many groups as SMs, e.g. Qwen3-8B at TP2): one-tile-per-CTA GEMM without the split plus
-// a separate activation kernel is faster than the split + fp32 partials + split-activation kernel (measured
-// 25.9 + ~2 us vs 31.4 us on the TP2 shape).  NVB_DECODE_UNFUSED_ACT=0 turns it off.
-bool decode_unfused_act(int M, int N, int act, int sms) {
-  if (act == 0 || M <= 64 || M > 128 || N % 256 != 0) return false;
-  const char* e = getenv("NVB_DECODE_UNFUSED_ACT");
-  if (e && atoi(e) == 0) return false;
-  return (N / 256) * 2 <= sms && N / 128 <= sms;
-}
-
 // Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
 // one tile per CTA doubles the number of tile groups, which halves the K splits -- and the fp32 split partials
 // -- a small-N projection needs to fill the SMs.  The fused activation needs the gate/up pair (2).  Projections
 // with N <= NVB_DECODE_NA1_MAXN (default 8192) use one tile.
-int g_force_na = 0;  // set around an internal call that must use one weight tile per CTA
-
 int decode_na(int N, int act) {
-  if (g_force_na) return g_force_na;
   static int maxn = -1;
   if (maxn < 0) {
     const char* e = getenv("NVB_DECODE_NA1_MAXN");
@@ -935,8 +921,6 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
 
 }  // namespace
 
-void act_mul_cuda(torch::Tensor out, torch::Tensor x, int64_t act, bool interleaved);  // misc.cu
-
 // y = x @ w^T (x [M, K] bf16, w [N, K] bf16) with optional activation on 128-interleaved gate/up rows of w.
 // ``workspace``: fp32 [S, M, N] split-K partials for decode-sized M (S from gemm_splits_for); with ``partial_out``
 // the partials are left for the consumer to sum, otherwise a sum (or split-K activation) kernel follows.
@@ -962,14 +946,6 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
   a.act = (int)act;
   a.err = e;
   int64_t splits_used = 1;
-  if (M <= 256 && force_splits == 0 && decode_unfused_act(M, N, (int)act, sms)) {
-    auto tmp = torch::empty({(long)M, (long)N}, x.options());
-    g_force_na = 1;
-    gemm_cuda(x, w, tmp, kActNone, c10::nullopt, 0, err, false);
-    g_force_na = 0;
-    act_mul_cuda(out, tmp, act, true);
-    return 1;
-  }
   if (M <= 256) {
     const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
     const int NA = decode_na(N, (int)act);
@@ -1054,7 +1030,6 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 
 // K splits (and so the fp32 partial slices of the workspace) the decode path uses for this shape.
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
-  if (decode_unfused_act((int)M, (int)N, (int)act, num_sms())) return 1;
   if (decode_cluster_enabled()) return 1;  // split K is reduced inside clusters: callers keep no partials
   // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;
