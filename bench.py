@@ -29,6 +29,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -116,7 +117,7 @@ def run_ours(args):
     gen = torch.Generator().manual_seed(1234)
     lens = torch.randint(args.min_prompt, args.max_prompt + 1, (B,), generator=gen).tolist()
     prompts = [torch.randint(1, hf.vocab_size - 1, (n,), generator=gen).tolist() for n in lens]
-    extra = 4 * args.ttft_probe + args.profile_steps
+    extra = 4 * args.ttft_probe + args.profile_steps + 4
     max_len = args.max_prompt + args.warmup + args.steps + extra + 64
     cfg = EngineConfig(max_num_seqs=B, max_model_len=max_len, max_num_batched_tokens=args.prefill_chunk,
                        gpu_memory_utilization=0.92, stop_on_degenerate=False, cuda_graph_max_bs=B)
@@ -158,7 +159,7 @@ def run_ours(args):
         torch.cuda.cudart().cudaProfilerStop()
         step_ms.clear()
     ops.reset_launch_count()
-    clock_path = os.path.join("gpurun_out" if os.path.isdir("gpurun_out") else "/tmp", f"bench_clocks_r{rank}.csv")
+    clock_path = args.clock_log or os.path.join(tempfile.gettempdir(), f"nvb_bench_clocks_{os.getpid()}_r{rank}.csv")
     sampler = _clock_sampler_start(clock_path) if rank == 0 else None
     ps.barrier()
     torch.cuda.synchronize()
@@ -177,6 +178,15 @@ def run_ours(args):
     dev_ms = sum(step_ms)
     h2d = runner.last_h2d_bytes
     runner.step_events = None
+    if args.breakdown:
+        # per-kernel device time of a few more decode steps, traced per rank (attribution only, not the value)
+        from nanovllm_b200.utils.breakdown import format_breakdown, kernel_breakdown
+        bd = kernel_breakdown(lambda: llm.step(), 3)
+        with open(f"{args.breakdown}.r{rank}.txt", "w") as f:
+            f.write(f"tp{world} rank {rank}, batch {running}, impl {args.impl}, weights {args.weights}\n")
+            f.write(format_breakdown(bd, top=40) + "\n")
+        with open(f"{args.breakdown}.r{rank}.json", "w") as f:
+            json.dump(bd, f)
     # TTFT under load: new requests (prompt lengths from the same distribution) join the running batch one at a
     # time, two decode steps apart; TTFT = add_request -> first sampled token on the host
     probe = []
@@ -218,7 +228,7 @@ def run_ours(args):
                        "ttft_note": f"p50 over {len(probe)} requests joining a running batch of {running}; "
                                     f"the initial burst of {B} prompts had p50 {round(p50_ttft_burst * 1000, 1)} ms"},
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": 8 * running},
+                    "d2h_bytes_per_step": 8 * running + 4},  # sampled ids + device error word
             "gpu_launches": launches,
             "clocks": _clock_summary(clock_path, local),
         }
@@ -242,6 +252,10 @@ def main():
                     help="baseline: this engine with cuBLAS GEMMs (separate activation kernel) and NCCL all-reduce")
     ap.add_argument("--weights", choices=["bf16", "nvfp4", "q4_k", "q8_0", "mxfp4"], default="bf16",
                     help="projection weights: bf16, or random GGUF blocks kept packed (the NVFP4 copy of config 5)")
+    ap.add_argument("--breakdown", default="",
+                    help="path prefix: write a per-kernel device-time breakdown of 3 traced decode steps per rank")
+    ap.add_argument("--clock-log", default="",
+                    help="CSV file for the nvidia-smi clock samples taken during the timed region (default: a temp file)")
     ap.add_argument("--ttft-probe", type=int, default=8,
                     help="requests that join the running batch one at a time after the timed region (p50 TTFT)")
     args = ap.parse_args()

@@ -104,6 +104,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(
   const int G = nq / nkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int ctx = ctx_lens[b];
+  if ((long)ctx > (long)nsplit * part_tiles * KT || (long)ctx > (long)bt_stride * block_size) {
+    // more keys than the split grid or the block-table row covers: skip the sequence (every split CTA of it
+    // takes this branch, so the split-merge counter stays consistent) and report instead of truncating
+    if (tid == 0 && split == 0) nvb::record_error(err, nvb::kErrBadArgument);
+    return;
+  }
   const int ntiles = (ctx + KT - 1) / KT;
   const int win_start = window > 0 ? max(0, ctx - window) : 0;
   const int t_begin = max(split * part_tiles, win_start / KT);

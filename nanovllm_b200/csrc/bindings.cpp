@@ -54,7 +54,7 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
                             c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot,
-                            c10::optional<torch::Tensor> parts);
+                            c10::optional<torch::Tensor> parts, int64_t wait_ns);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";
@@ -86,5 +86,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_alloc", &symm_alloc_cuda);
   m.def("ipc_open", &ipc_open_cuda);
   m.def("ipc_close", &ipc_close_cuda);
-  m.def("tp_allreduce_norm", &tp_allreduce_norm_cuda);
+  m.def("tp_allreduce_norm", &tp_allreduce_norm_cuda, py::arg("in_ptrs"), py::arg("res_ptrs"), py::arg("out_ptrs"),
+        py::arg("sig_ptrs"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("weight"), py::arg("eps"),
+        py::arg("mode"), py::arg("counters"), py::arg("err"), py::arg("max_blocks"), py::arg("oneshot"),
+        py::arg("parts"), py::arg("wait_ns") = 0);
 }

@@ -1,30 +1,13 @@
-// Allocation-free C entry point for paged decode attention.
+// Allocation-free C entry point for paged decode attention; the interface, its callers and its contract are
+// documented in decode_noalloc.h.  This entry point has no counterpart in the reference: the Java library has
+// no GPU code and no C interface.
 //
-// This entry point has no counterpart in the reference: the Java library has no GPU code and no C interface.
-//
-// Who it is for.  The regular decode-attention op (paged_decode_cuda, driven from Python) takes its split-KV
-// scratch from the framework allocator.  Some callers cannot allocate device memory at the point where they
-// run attention: code that drives the GPU from another runtime through a plain C ABI (a JVM or a native
-// server calling through FFI has no access to this process's torch caching allocator, and a raw cudaMalloc /
-// cudaFree per call would synchronise the device and stall the decode loop), and real-time serving loops whose
-// policy forbids allocation after start-up.  For them, ``nvb_paged_decode_noalloc`` runs the same split-KV
-// kernels with the scratch taken from a fixed, file-scope device array; the caller passes only its own inputs
-// and the output buffer.
-//
-// Limits and contract:
-//  * The scratch is ``g_noalloc_scratch``, kNoallocScratchFloats fp32 values (16 MiB).  Every GPU that loads
-//    this library keeps that array resident until the process exits.  A call whose split partials
-//    (batch * q_heads * splits * (head_dim + 1) floats) would not fit is rejected with code
-//    NVB_NOALLOC_ERR_TOO_LARGE and a message from nvb_noalloc_last_error(); nothing is launched.
-//  * In host code the name ``g_noalloc_scratch`` is only a host-side stand-in for the device array, not a
-//    device address.  The device address is obtained once per device, with that device current, through
-//    cudaGetSymbolAddress; the first call on each device does this set-up, so make that first call before any
-//    CUDA stream capture begins.
-//  * Every call shares the one array and it keeps the previous call's contents.  The kernels overwrite every
-//    partial they later read, so nothing needs clearing except the bounded-wait error word, which each call
-//    resets with cudaMemsetAsync on the caller's stream.  Calls whose GPU work overlaps (different streams
-//    without ordering between them, or several host threads) race on the array: order them on one stream.
-//  * The function calls no cudaMalloc, cudaFree or other allocating routine, and no torch API.
+// Implementation notes:
+//  * The scratch is ``g_noalloc_scratch`` (kNoallocScratchFloats fp32 values, 16 MiB).  In host code that name
+//    is only a host-side stand-in for the device array; its device address comes from cudaGetSymbolAddress,
+//    once per device with that device current (setup_device), and is passed to the kernels as a pointer.
+//  * The kernels overwrite every partial they later read, so nothing in the scratch needs clearing; only the
+//    error word is reset (cudaMemsetAsync on the caller's stream) at the start of every call.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -33,6 +16,7 @@
 #include <mutex>
 
 #include "attention_kernels.cuh"
+#include "decode_noalloc.h"
 
 namespace {
 
@@ -44,6 +28,7 @@ __device__ __align__(256) int g_noalloc_err[4];
 
 float* g_scratch_dev[kMaxDevices] = {nullptr};
 int* g_err_dev[kMaxDevices] = {nullptr};
+int g_sms[kMaxDevices] = {0};
 std::mutex g_setup_mu;
 thread_local char g_last_error[256] = {0};
 
@@ -75,9 +60,36 @@ int setup_device(int dev) {
   if (r1 != cudaSuccess) return fail(3, cudaGetErrorString(r1));
   cudaError_t r2 = cudaGetSymbolAddress(&e, g_noalloc_err);
   if (r2 != cudaSuccess) return fail(3, cudaGetErrorString(r2));
+  // the kernels' dynamic shared-memory limit is a per-device function attribute: set it once here
+  const cudaError_t a1 = cudaFuncSetAttribute(paged_decode_kernel<64, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              (int)decode_smem<64, 4>());
+  const cudaError_t a2 = cudaFuncSetAttribute(paged_decode_kernel<128, 3>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem<128, 3>());
+  const cudaError_t a3 = cudaFuncSetAttribute(paged_decode_kernel<256, 2>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)decode_smem<256, 2>());
+  if (a1 != cudaSuccess || a2 != cudaSuccess || a3 != cudaSuccess)
+    return fail(NVB_NOALLOC_ERR_CUDA, "cudaFuncSetAttribute failed for the decode kernels");
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return fail(NVB_NOALLOC_ERR_CUDA, "cannot read the SM count");
+  g_sms[dev] = sms;
   g_scratch_dev[dev] = static_cast<float*>(s);
   g_err_dev[dev] = static_cast<int*>(e);
   return 0;
+}
+
+// Split rule shared with the framework op (ops.decode_partition): ~4 CTAs per SM, at most 16 tiles per split
+// and at most 64 splits.  Returns (tiles per split, splits).
+void split_rule(long B, long nkv, long max_len, int sms, long* per_out, long* nsplit_out) {
+  const long tiles = (max_len + KT - 1) / KT;
+  const long target = 4L * sms;
+  long per = (B * nkv * tiles + target - 1) / target;
+  if (per < 1) per = 1;
+  if (per > 16) per = 16;
+  const long per_min = (tiles + 63) / 64;
+  if (per < per_min) per = per_min;
+  *per_out = per;
+  *nsplit_out = (tiles + per - 1) / per;
 }
 
 bool encode_cache_map(CUtensorMap* m, const void* base, unsigned long long rows, int hd) {
@@ -95,9 +107,7 @@ cudaError_t launch(const CUtensorMap& km, const CUtensorMap& vm, dim3 grid, cuda
                    const int* bt, int bt_stride, const int* ctx, bf16* out, float* po, float* pl, int nq, int nkv,
                    int block_size, float scale, float softcap, int window, int part_tiles, int* err) {
   auto kern = paged_decode_kernel<HD, STAGES>;
-  const size_t sm = decode_smem<HD, STAGES>();
-  cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (r != cudaSuccess) return r;
+  const size_t sm = decode_smem<HD, STAGES>();  // attribute set once per device in setup_device
   kern<<<grid, 128, sm, st>>>(km, vm, q, bt, bt_stride, ctx, out, po, pl, nq, nkv, block_size, scale, softcap, window,
                               part_tiles, err, nullptr);  // split merge by the separate combine kernel below
   return cudaGetLastError();
@@ -107,34 +117,27 @@ cudaError_t launch(const CUtensorMap& km, const CUtensorMap& vm, dim3 grid, cuda
 
 extern "C" {
 
-enum {
-  NVB_NOALLOC_OK = 0,
-  NVB_NOALLOC_ERR_ARGS = 1,
-  NVB_NOALLOC_ERR_TOO_LARGE = 2,
-  NVB_NOALLOC_ERR_CUDA = 3,
-};
-
-// Capacity of the shared scratch, in fp32 elements.
 long nvb_noalloc_scratch_capacity(void) { return kNoallocScratchFloats; }
 
-// Message of the last failed call on this host thread ("" after a success).
 const char* nvb_noalloc_last_error(void) { return g_last_error; }
 
-// Device address of the bounded-wait error word of the current device (0 = no kernel gave up), or null before
-// the first call on that device.
 int* nvb_noalloc_error_word(void) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
   return g_err_dev[dev];
 }
 
-// Paged decode attention (one query token per sequence), same kernels and split rule as the framework op.
-//   q            bf16 [B, nq, hd], contiguous
-//   k_cache/v_cache bf16 [num_blocks, nkv, block_size, hd], contiguous
-//   block_tables int32 [B, bt_stride] physical block ids; ctx_lens int32 [B] keys per sequence
-//   out          bf16 [B, nq, hd]
-//   max_len      upper bound of ctx_lens (sizes the split grid); stream: cudaStream_t (null = legacy stream)
-// Returns NVB_NOALLOC_OK or an error code; see nvb_noalloc_last_error().
+int nvb_noalloc_num_splits(int B, int nkv, int max_len) {
+  int dev = 0;
+  if (B <= 0 || nkv <= 0 || max_len <= 0) return 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return 0;
+  if (setup_device(dev) != 0) return 0;
+  long per, nsplit;
+  split_rule(B, nkv, max_len, g_sms[dev], &per, &nsplit);
+  return (int)nsplit;
+}
+
+// Same kernels and split rule as the framework op; contract in decode_noalloc.h.
 int nvb_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_tables,
                              int bt_stride, const int* ctx_lens, void* out, int B, int nq, int nkv, int hd,
                              int num_blocks, int block_size, float scale, float softcap, int window, int max_len,
@@ -148,6 +151,8 @@ int nvb_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_c
   if (hd != 64 && hd != 128 && hd != 256) return fail(NVB_NOALLOC_ERR_ARGS, "head_dim must be 64, 128 or 256");
   if (block_size <= 0 || block_size % KT != 0) return fail(NVB_NOALLOC_ERR_ARGS, "block_size must be a multiple of 64");
   if (max_len <= 0 || num_blocks <= 0 || bt_stride <= 0) return fail(NVB_NOALLOC_ERR_ARGS, "bad sizes");
+  if ((long)max_len > (long)bt_stride * block_size)
+    return fail(NVB_NOALLOC_ERR_ARGS, "max_len exceeds what a block-table row (bt_stride * block_size) covers");
   if ((reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15))
     return fail(NVB_NOALLOC_ERR_ARGS, "caches must be 16-byte aligned");
   int dev = 0;
@@ -155,17 +160,8 @@ int nvb_paged_decode_noalloc(const void* q, const void* k_cache, const void* v_c
     return fail(NVB_NOALLOC_ERR_CUDA, "no current CUDA device");
   if (int rc = setup_device(dev)) return rc;
 
-  // split rule of the framework op: ~4 CTAs per SM, at most 16 tiles per split and 64 splits
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long tiles = (max_len + KT - 1) / KT;
-  const long target = 4L * sms;
-  long per = (B * (long)nkv * tiles + target - 1) / target;
-  if (per < 1) per = 1;
-  if (per > 16) per = 16;
-  const long per_min = (tiles + 63) / 64;
-  if (per < per_min) per = per_min;
-  const long nsplit = (tiles + per - 1) / per;
+  long per, nsplit;
+  split_rule(B, nkv, max_len, g_sms[dev], &per, &nsplit);
   const long need = nsplit > 1 ? (long)B * nq * nsplit * (hd + 1) : 0;
   if (need > kNoallocScratchFloats) {
     char msg[200];

@@ -15,7 +15,7 @@
 //   a block-level flag barrier before phase A (all partials written) and after phase B (all stores landed,
 //   all peers done reading this rank's partial buffer) keeps producer / consumer kernels ordered across GPUs.
 //
-// Every flag wait is bounded by kWaitLimitNs; on expiry the kernel records kErrFlagTimeout in the device error
+// Every flag wait is bounded (kWaitLimitNs unless the caller passes a shorter limit); on expiry the kernel records kErrFlagTimeout in the device error
 // word and returns instead of hanging.  Flags carry a per-block epoch kept in device memory, so the kernel can
 // be captured in CUDA graphs (every rank replays the same launches in the same order).  No TMA, no multicast.
 #include <torch/extension.h>
@@ -53,7 +53,7 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 // ``sync_first`` alone (no fence) publishes "this block is done reading": the loads' values were consumed
 // before bar.sync, and the release store orders them before the flag.
 __device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase, uint32_t epoch, int* err,
-                              bool publish_writes, bool sync_first = false) {
+                              uint64_t wait_ns, bool publish_writes, bool sync_first = false) {
   const int t = threadIdx.x;
   int ok = 1;
   if (publish_writes || sync_first) __syncthreads();
@@ -63,7 +63,7 @@ __device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase
     const uint32_t* mine = P.sig[rank] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + t);
     const uint64_t t0 = nvb::global_timer_ns();
     while ((int32_t)(ld_acquire_sys(mine) - epoch) < 0) {
-      if (nvb::global_timer_ns() - t0 > nvb::kWaitLimitNs) {
+      if (nvb::global_timer_ns() - t0 > wait_ns) {
         nvb::record_error(err, nvb::kErrFlagTimeout);
         ok = 0;
         break;
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
                                                                  const bf16* __restrict__ w, float eps, int mode,
                                                                  int has_res, uint32_t* counters, int* err,
                                                                  int oneshot, const float* __restrict__ parts,
-                                                                 int splits) {
+                                                                 int splits, uint64_t wait_ns) {
   nvb::pdl_wait();
   nvb::pdl_trigger();
   __shared__ float red[32];
@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
   __syncthreads();
   const uint32_t epoch = s_epoch;
   // with phase 0 the block's own stores must be visible to the peers before its arrival flag
-  if (!block_barrier(P, rank, nranks, 0, epoch, err, splits > 0)) {
+  if (!block_barrier(P, rank, nranks, 0, epoch, err, wait_ns, splits > 0)) {
     if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
     return;
   }
@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
         if (p >= p_lo && p < p_hi) *reinterpret_cast<uint4*>(P.out[p] + base + col) = packed;
     }
   }
-  block_barrier(P, rank, nranks, 1, epoch, err, !oneshot, true);
+  block_barrier(P, rank, nranks, 1, epoch, err, wait_ns, !oneshot, true);
   if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
 }
 
@@ -273,7 +273,7 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
                             c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot,
-                            c10::optional<torch::Tensor> parts) {
+                            c10::optional<torch::Tensor> parts, int64_t wait_ns) {
   const int R = (int)in.size();
   TORCH_CHECK(R >= 1 && R <= kMaxRanks && (int)out.size() == R && (int)sig.size() == R && (int)res.size() == R,
               "one pointer per rank (at most 8 ranks)");
@@ -316,9 +316,10 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   uint32_t* cnt = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
+  const uint64_t wait = wait_ns > 0 ? (uint64_t)wait_ns : nvb::kWaitLimitNs;
 #define LAUNCH(NV_)                                                                                              \
   C10_CUDA_CHECK(nvb::launch(tp_allreduce_norm_kernel<NV_>, dim3(grid), dim3(threads), 0, stream, P, (int)rank, R, (int)T, (int)H, w, (float)eps, \
-                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot, pp, splits))
+                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot, pp, splits, wait))
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

@@ -166,6 +166,7 @@ class ModelRunner:
         self.h_seeds = buf(S, torch.int64)
         self.h_sids = buf(S, torch.int64)
         self.h_steps = buf(S, torch.int32)
+        self._err_host = buf(1, torch.int32)
         # numpy views share the pinned memory: element writes from Python stay cheap
         for name in ("ids", "pos", "slots", "cu_q", "cu_k", "ctx", "last", "bt", "rows", "fresh", "temps", "topk",
                      "topp", "seeds", "sids", "steps"):
@@ -311,9 +312,16 @@ class ModelRunner:
         self.last_h2d_bytes = 0
         logits = self.forward_logits(seqs, is_prefill)
         toks = self.sample(logits, seqs)
+        if self.is_cuda:
+            # the device error word rides back with the sampled tokens (4 bytes on the same synchronisation): a
+            # bounded wait that gave up during this step surfaces here instead of as silently wrong tokens
+            self._err_host.copy_(ops.error_word(self.device), non_blocking=True)
         if self.step_events is not None:
             self.step_events[1].record()
-        return toks.tolist()
+        out = toks.tolist()
+        if self.is_cuda and int(self._err_host[0]) != 0:
+            ops.check_device_errors(self.device)
+        return out
 
     @torch.inference_mode()
     def forward_logits(self, seqs: List[Sequence], is_prefill: bool) -> torch.Tensor:

@@ -7,7 +7,8 @@ Mirrors the reference's exception tree (nano-vllm-java/src/main/java/com/igormaz
 wall-clock deadline passes; both are raised between engine steps, never from inside a kernel.
 
 ``DeviceWaitTimeout`` is new: fused multi-GPU kernels wait on peer flags with a bounded spin and report a
-timeout through an error word that the host turns into this exception.
+timeout through an error word that the host turns into this exception.  ``TensorParallelAbort`` is new too:
+a tensor-parallel rank whose step failed publishes the reason and every other rank raises this between steps.
 """
 
 
@@ -33,3 +34,7 @@ class GenerationTimeoutException(NanoLlvmException):
 
 class DeviceWaitTimeout(NanoLlvmException):
     """A device-side bounded wait (peer flag, mbarrier) gave up; the kernel returned an error status."""
+
+
+class TensorParallelAbort(NanoLlvmException):
+    """Another tensor-parallel rank failed; this rank stops before launching its next step."""

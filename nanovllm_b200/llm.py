@@ -25,7 +25,8 @@ from .config import EngineConfig, HfConfig
 from .engine.model_runner import ModelRunner
 from .engine.scheduler import Scheduler
 from .engine.sequence import Sequence
-from .exceptions import GenerationCancelledException, GenerationTimeoutException, NanoLlvmException
+from .exceptions import (GenerationCancelledException, GenerationTimeoutException, NanoLlvmException,
+                         TensorParallelAbort)
 from .parallel import state as ps
 from .sampling_params import SamplingParams
 
@@ -196,8 +197,16 @@ class LLM:
         return not self.scheduler.is_finished()
 
     def step(self, appended_out: Optional[list] = None):
+        ps.check_abort()  # a peer rank failed: stop before launching anything that would wait for it
         seqs, is_prefill = self.scheduler.schedule()
-        toks = self.runner.run(seqs, is_prefill)
+        try:
+            toks = self.runner.run(seqs, is_prefill)
+        except BaseException as e:
+            if ps.abort_requested():
+                # a peer failed first: this rank was released from a collective by the process-group timeout
+                raise TensorParallelAbort(ps.abort_reason()) from e
+            ps.signal_abort(f"{type(e).__name__}: {e}")
+            raise
         finished = self.scheduler.postprocess(seqs, toks, is_prefill, appended_out)
         for s in finished:
             s.t_finish = time.perf_counter()

@@ -227,8 +227,26 @@ def qk_norm_rope_store(qkv, positions, cos_sin, q_w, k_w, norm_mode, v_norm, eps
 DECODE_TILE = 64
 
 
-def decode_partition(batch: int, nkv: int, max_len: int, sms: int = 148) -> Tuple[int, int]:
-    """(tiles per split, number of splits) so that batch * nkv * splits covers ~4 CTAs per SM."""
+_SMS: Dict[int, int] = {}
+
+
+def num_sms(device: Optional[torch.device] = None) -> int:
+    """SM count of ``device`` (the current CUDA device by default; 148, a B200, without CUDA)."""
+    if not torch.cuda.is_available():
+        return 148
+    idx = device.index if (device is not None and device.index is not None) else torch.cuda.current_device()
+    n = _SMS.get(idx)
+    if n is None:
+        n = torch.cuda.get_device_properties(idx).multi_processor_count
+        _SMS[idx] = n
+    return n
+
+
+def decode_partition(batch: int, nkv: int, max_len: int, sms: Optional[int] = None) -> Tuple[int, int]:
+    """(tiles per split, number of splits) so that batch * nkv * splits covers ~4 CTAs per SM (the SM count of
+    the current device unless given; the allocation-free C entry point uses the same rule and source)."""
+    if sms is None:
+        sms = num_sms()
     tiles = max(1, (max_len + DECODE_TILE - 1) // DECODE_TILE)
     target = 4 * sms
     per = max(1, min(16, (batch * nkv * tiles + target - 1) // target))
@@ -244,7 +262,7 @@ def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap=0.0
     nkv = k_cache.shape[1]
     if max_len is None:
         max_len = block_tables.shape[1] * k_cache.shape[2]
-    per, nsplit = decode_partition(B, nkv, max_len)
+    per, nsplit = decode_partition(B, nkv, max_len, num_sms(q.device))
     if out is None:
         out = torch.empty_like(q)
     if nsplit > 1:

@@ -6,19 +6,113 @@ VocabParallelEmbedding.java:21-253) describe a TP decomposition that never shard
 ``init_tp`` joins the default process group (NCCL on GPUs, Gloo on CPU for tests) and every layer reads its
 rank/size from this module.  Engines run SPMD: every rank runs the same scheduler on the same requests and
 the sampler is deterministic, so ranks stay in lock-step without a per-step broadcast.
+
+Failure propagation: a rank whose step fails (a device wait that gave up, a host exception) publishes the
+reason under one key of the rendezvous TCP store (``signal_abort``).  Every rank runs a watcher thread blocked
+on that key, so the others learn of it on the host without a per-step round trip; ``check_abort`` (called at
+the start of every engine step) then raises ``TensorParallelAbort`` before the rank launches another kernel or
+collective.  A rank already blocked inside a collective with the failed peer is released by the process
+group's timeout and reports the same abort reason.
 """
 from __future__ import annotations
 
+import atexit
 import datetime
 import os
+import threading
 from typing import Optional
 
 import torch
 import torch.distributed as dist
 
+from ..exceptions import TensorParallelAbort
+
 _TP_SIZE = 1
 _TP_RANK = 0
 _GROUP = None
+
+_ABORT_KEY = "nanovllm_b200/abort"
+_ABORT = threading.Event()
+_ABORT_REASON = [""]
+_WATCH_STOP = threading.Event()
+_WATCH: Optional[threading.Thread] = None
+_STORE = None
+
+
+def _store():
+    """A client of the rendezvous TCP store (MASTER_ADDR:MASTER_PORT) owned by this module."""
+    global _STORE
+    if _STORE is None:
+        _STORE = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), int(os.environ["MASTER_PORT"]),
+                               is_master=False, timeout=datetime.timedelta(seconds=30), wait_for_workers=False)
+    return _STORE
+
+
+def _watch_abort() -> None:
+    try:
+        st = dist.TCPStore(os.environ.get("MASTER_ADDR", "127.0.0.1"), int(os.environ["MASTER_PORT"]),
+                           is_master=False, timeout=datetime.timedelta(seconds=30), wait_for_workers=False)
+    except Exception:  # noqa: BLE001 - no store to watch (single process); nothing to propagate
+        return
+    while not _WATCH_STOP.is_set():
+        try:
+            st.wait([_ABORT_KEY], datetime.timedelta(milliseconds=500))
+        except Exception as e:  # noqa: BLE001
+            if "imeout" in str(e) or "imed out" in str(e):
+                continue  # nothing signalled yet: poll again
+            return  # the store is gone (the job is shutting down): nothing left to watch
+        try:
+            _ABORT_REASON[0] = st.get(_ABORT_KEY).decode("utf-8", "replace")
+        except Exception:  # noqa: BLE001
+            _ABORT_REASON[0] = "a peer rank aborted"
+        _ABORT.set()
+        return
+
+
+def _stop_watcher() -> None:
+    global _WATCH
+    _WATCH_STOP.set()
+    if _WATCH is not None:
+        _WATCH.join(timeout=2.0)
+    _WATCH = None
+
+
+def _start_watcher() -> None:
+    global _WATCH
+    if _WATCH is not None or "MASTER_PORT" not in os.environ:
+        return
+    _ABORT.clear()
+    _WATCH_STOP.clear()
+    _WATCH = threading.Thread(target=_watch_abort, name="nvb-tp-abort-watch", daemon=True)
+    _WATCH.start()
+    atexit.register(_stop_watcher)  # stop it before interpreter shutdown tears the store client down
+
+
+def signal_abort(reason: str) -> None:
+    """Tell every rank that this rank's step failed (idempotent; the first reason wins)."""
+    if _TP_SIZE <= 1:
+        return
+    _ABORT_REASON[0] = _ABORT_REASON[0] or f"rank {_TP_RANK}: {reason}"
+    _ABORT.set()
+    try:
+        st = _store()
+        st.compare_set(_ABORT_KEY, "", f"rank {_TP_RANK}: {reason}")
+    except Exception:  # noqa: BLE001 - the store is gone too: the peers' collective timeouts end them
+        pass
+
+
+def abort_requested() -> bool:
+    return _ABORT.is_set()
+
+
+def abort_reason() -> str:
+    return _ABORT_REASON[0]
+
+
+def check_abort() -> None:
+    """Raise TensorParallelAbort when any rank has signalled a failure (called between engine steps)."""
+    if _ABORT.is_set():
+        raise TensorParallelAbort(_ABORT_REASON[0] or "a peer rank aborted")
 
 
 def init_tp(backend: Optional[str] = None, timeout_s: float = 120.0) -> None:
@@ -37,6 +131,7 @@ def init_tp(backend: Optional[str] = None, timeout_s: float = 120.0) -> None:
     _TP_SIZE = dist.get_world_size()
     _TP_RANK = dist.get_rank()
     _GROUP = dist.group.WORLD
+    _start_watcher()
 
 
 def set_tp_for_testing(rank: int, size: int, group=None) -> None:
@@ -100,7 +195,9 @@ def barrier() -> None:
 
 
 def destroy() -> None:
-    global _TP_SIZE, _TP_RANK, _GROUP
+    global _TP_SIZE, _TP_RANK, _GROUP, _STORE
+    _stop_watcher()
+    _STORE = None
     if dist.is_initialized():
         dist.destroy_process_group()
     _TP_SIZE, _TP_RANK, _GROUP = 1, 0, None
