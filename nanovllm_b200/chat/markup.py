@@ -1,16 +1,19 @@
 """Assistant-reply markup: think tags, chat special markers, reply parsing and salvage.
 
-Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/chat/{AssistantParts.java:23-261, ChatReply.java,
-ThinkTags.java:27-75, ChatSpecials.java:30-90}.  ``parse`` splits raw model output into (thinking, answer,
-think-still-open): text inside ``<think>..</think>`` (also several or an unclosed block) is thinking, the rest is
-the answer; chat special markers end the answer; an incomplete marker at the end of a streaming buffer is held
-back so it never flashes on screen.  ``salvage_from_thinking`` recovers a short answer from the thinking when the
-model never closed its think block (a stated "answer: ..." line, else the last brief line).
+Observable behaviour follows the reference's chat layer (nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/
+chat/AssistantParts.java, ChatReply.java, ThinkTags.java, ChatSpecials.java): text inside think tags is thinking
+(several blocks, or a block still open at the end), the rest is the answer; a chat special marker ends the
+answer; an incomplete marker at the end of a streaming buffer is held back so it never reaches the screen; an
+answer can be salvaged from the thinking when the model never produced one.
+
+The implementation is an incremental scanner (``ReplyScanner``): text is fed chunk by chunk as tokens stream in,
+every complete marker is consumed exactly once as a state transition (lead -> think / answer -> done), and only
+the unconsumed tail that could still grow into a marker is kept between feeds.  ``parse`` is a scanner fed once.
 """
 from __future__ import annotations
 
 import re
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import List, Optional, Tuple
 
 
@@ -53,47 +56,113 @@ class AssistantParts:
     think_open: bool
 
 
-def _hold_incomplete_suffix(text: str, markers: List[str]) -> str:
-    """Drop a trailing prefix of any marker (the rest may still be streaming in)."""
-    best = 0
-    for m in markers:
-        for k in range(min(len(m) - 1, len(text)), 0, -1):
-            if text.endswith(m[:k]):
-                best = max(best, k)
-                break
-    return text[:-best] if best else text
+# scanner states
+_LEAD, _THINK, _ANSWER, _DONE = "lead", "think", "answer", "done"
 
 
-def _join_think(a: str, b: str) -> str:
-    a, b = (a or "").strip(), (b or "").strip()
-    if not a:
-        return b
-    if not b:
-        return a
-    return a + "\n" + b
+@dataclass
+class ReplyScanner:
+    """Streaming splitter of raw assistant text into thinking and answer.
+
+    States: ``lead`` (no tag seen yet: the text is provisional -- a first close tag turns it into thinking, a
+    first open tag or a special marker into answer), ``think``, ``answer`` and ``done`` (a special marker or a
+    stray close tag ended the answer; later text is ignored).  Think and answer text accumulate as segments, one
+    per block; ``snapshot`` joins them."""
+    tags: ThinkTags = field(default_factory=ThinkTags)
+    specials: ChatSpecials = field(default_factory=ChatSpecials)
+    state: str = _LEAD
+    _tail: str = ""
+    _lead: List[str] = field(default_factory=list)
+    _think: List[List[str]] = field(default_factory=list)
+    _answer: List[List[str]] = field(default_factory=list)
+
+    def __post_init__(self):
+        self._markers = self.specials.search_markers(self.tags)
+        self._pattern = re.compile("|".join(re.escape(m) for m in sorted(set(self._markers), key=len, reverse=True)))
+
+    # -------------------------------------------------------------------------------- feeding
+    def feed(self, chunk: str) -> "ReplyScanner":
+        text = self._tail + (chunk or "")
+        pos = 0
+        for m in self._pattern.finditer(text):
+            self._emit(text[pos:m.start()])
+            self._on_marker(m.group(0))
+            pos = m.end()
+        rest = text[pos:]
+        keep = self._marker_prefix_len(rest)
+        self._emit(rest[:len(rest) - keep])
+        self._tail = rest[len(rest) - keep:]
+        return self
+
+    def _marker_prefix_len(self, text: str) -> int:
+        """Length of the longest suffix of ``text`` that is a proper prefix of some marker (held back)."""
+        best = 0
+        for m in self._markers:
+            for k in range(min(len(m) - 1, len(text)), best, -1):
+                if text.endswith(m[:k]):
+                    best = k
+                    break
+        return best
+
+    def _emit(self, s: str) -> None:
+        if not s or self.state == _DONE:
+            return
+        if self.state == _LEAD:
+            self._lead.append(s)
+        elif self.state == _THINK:
+            self._think[-1].append(s)
+        else:
+            self._answer[-1].append(s)
+
+    def _on_marker(self, mk: str) -> None:
+        st = self.state
+        if st == _DONE:
+            return
+        if mk == self.tags.open:
+            if st == _LEAD:
+                self._answer.append(self._lead)
+                self._lead = []
+            if st != _THINK:  # an open tag inside thinking is dropped
+                self._think.append([])
+                self.state = _THINK
+        elif mk == self.tags.close:
+            if st == _LEAD:  # everything before a first, unopened close tag was thinking
+                self._think.append(self._lead)
+                self._lead = []
+            if st in (_LEAD, _THINK):
+                self._answer.append([])
+                self.state = _ANSWER
+            else:  # a stray close tag in the answer ends it
+                self.state = _DONE
+        else:  # chat special marker: ends the answer, dropped from thinking
+            if st == _LEAD:
+                self._answer.append(self._lead)
+                self._lead = []
+                self.state = _DONE
+            elif st == _ANSWER:
+                self.state = _DONE
+
+    # -------------------------------------------------------------------------------- results
+    def snapshot(self) -> AssistantParts:
+        think = [("".join(seg)).strip() for seg in self._think]
+        thinking = "\n".join(t for t in think if t)
+        segments = list(self._answer)
+        if self.state == _LEAD:
+            segments = segments + [self._lead]
+        answer = ""
+        for seg in segments:
+            piece = "".join(seg)
+            if not piece.strip():
+                continue
+            answer = piece if not answer.strip() else answer.rstrip() + "\n" + piece.lstrip()
+        return AssistantParts(thinking, answer.strip(), self.state == _THINK)
 
 
-def _join_answer(a: str, b: str) -> str:
-    a, b = a or "", b or ""
-    if not a.strip():
-        return b
-    if not b.strip():
-        return a
-    return a.rstrip() + "\n" + b.lstrip()
-
-
-def _split_rest(text: str, tags: ThinkTags, markers: List[str]) -> Tuple[str, str, bool]:
-    """-> (thinking, answer, open) of the text after a closed think block."""
-    text = _hold_incomplete_suffix(text, markers)
-    s = text.find(tags.open)
-    if s < 0:
-        return "", text, False
-    before, inner = text[:s], text[s + len(tags.open):]
-    e = inner.find(tags.close)
-    if e < 0:
-        return inner, before, True
-    t2, a2, o2 = _split_rest(inner[e + len(tags.close):], tags, markers)
-    return _join_think(inner[:e], t2), _join_answer(before, a2), o2
+def parse(raw: Optional[str], tags: ThinkTags = ThinkTags(), specials: ChatSpecials = ChatSpecials()) -> AssistantParts:
+    """Split complete (or partially streamed) assistant text into thinking, answer and think-still-open."""
+    if raw is None or not raw.strip():
+        return AssistantParts("", "", False)
+    return ReplyScanner(tags, specials).feed(raw).snapshot()
 
 
 def strip_chat_markup(text: str, tags: ThinkTags = ThinkTags(), specials: ChatSpecials = ChatSpecials()) -> str:
@@ -103,63 +172,37 @@ def strip_chat_markup(text: str, tags: ThinkTags = ThinkTags(), specials: ChatSp
     return out.strip()
 
 
-def _sanitize_answer(text: str, markers: List[str]) -> str:
-    cleaned = _hold_incomplete_suffix(text, markers)
-    for m in markers:
-        at = cleaned.find(m)
-        if at >= 0:
-            cleaned = cleaned[:at]
-    return cleaned.strip()
-
-
-def parse(raw: Optional[str], tags: ThinkTags = ThinkTags(), specials: ChatSpecials = ChatSpecials()) -> AssistantParts:
-    if raw is None or not raw.strip():
-        return AssistantParts("", "", False)
-    markers = specials.search_markers(tags)
-    text = _hold_incomplete_suffix(raw, markers)
-    s = text.find(tags.open)
-    e = text.find(tags.close, s + len(tags.open)) if s >= 0 else text.find(tags.close)
-    if s >= 0 and e > s:
-        thinking = text[s + len(tags.open):e]
-        t2, after, is_open = _split_rest(text[e + len(tags.close):], tags, markers)
-        thinking = _join_think(thinking, t2)
-    elif s >= 0:
-        thinking, after, is_open = text[s + len(tags.open):], "", True
-    elif e >= 0:
-        thinking, after, is_open = _split_rest(text[e + len(tags.close):], tags, markers)
-        thinking = _join_think(text[:e], thinking)
-    else:
-        thinking, after, is_open = "", text, False
-    return AssistantParts(strip_chat_markup(thinking, tags, specials), _sanitize_answer(after, markers), is_open)
-
-
+# -------------------------------------------------------------------------------------------- salvage
+# A line that states its result: "answer: X", "final answer = X", "so the answer is - X", "therefore: X".
 _STATED = re.compile(r"(?i)\b(?:final answer|answer|so the answer is|therefore)\s*[:=\-]\s*(.+)$")
 
 
-def _brief(line: str) -> bool:
-    return 0 < len(line) <= 120 and not line.endswith("?")
+def _stated_value(line: str) -> str:
+    m = _STATED.search(line)
+    return re.sub(r"[.\"']+$", "", m.group(1).strip()) if m else ""
 
 
 def salvage_from_thinking(thinking: Optional[str]) -> str:
+    """Recover a short answer from thinking text when the model never produced one.
+
+    Candidate lines are the non-empty ones that are not list continuations ("+ ...").  Walking back from the
+    last candidate, the first line that states a result gives that result, and the first brief line (at most
+    120 characters, not a question) is taken as is; with neither, the last candidate is returned, cut to 200
+    characters."""
     if not thinking or not thinking.strip():
         return ""
-    lines = re.split(r"\r?\n", thinking.strip())
-    for line in reversed(lines):
-        line = line.strip()
-        if not line or line.startswith("+"):
-            continue
-        m = _STATED.search(line)
-        if m:
-            got = re.sub(r"[.\"']+$", "", m.group(1).strip())
-            if got:
-                return got
-        if _brief(line):
-            return line
-    for line in reversed(lines):
-        line = line.strip()
-        if line and not line.startswith("+"):
-            return line[:200].strip() + "…" if len(line) > 200 else line
-    return ""
+    candidates = [ln.strip() for ln in thinking.strip().splitlines()]
+    candidates = [ln for ln in candidates if ln and not ln.startswith("+")]
+    for ln in reversed(candidates):
+        stated = _stated_value(ln)
+        if stated:
+            return stated
+        if len(ln) <= 120 and not ln.endswith("?"):
+            return ln
+    if not candidates:
+        return ""
+    last = candidates[-1]
+    return last if len(last) <= 200 else last[:200].strip() + "…"
 
 
 def clean_assistant_text(raw: Optional[str], tags: ThinkTags = ThinkTags(),

@@ -20,7 +20,7 @@ REWRITE_STANDALONE = ("Turn this question into a few search keywords for a docum
                       "Reply with the keywords only, or NONE when there is nothing to search for.\n"
                       "Question: {q}")
 REWRITE_FOLLOW_UP = ("Turn this follow-up into a few search keywords for a document index.\n"
-                     "Use Prior to resolve pronouns and missing names.\n"
+                     "Where the follow-up says it, they or that, name what it means, taken from Prior.\n"
                      "Reply with the keywords only, or NONE when the follow-up has nothing to do with Prior.\n"
                      "Prior: {prior}\n"
                      "Follow-up: {q}")

@@ -22,9 +22,9 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
 int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out);
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act);
-int64_t gemm_sk_floats(int64_t M, int64_t N, int64_t K, int64_t act);
-void gemm_sk_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, torch::Tensor workspace,
-                  torch::Tensor counters, c10::optional<torch::Tensor> err);
+std::vector<int64_t> gemm_sp_cuda(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> out, int64_t act,
+                                  c10::optional<torch::Tensor> workspace, c10::optional<torch::Tensor> err,
+                                  bool partial_out, std::vector<int64_t> sp_plan, double eps);
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
 int64_t qgemm_splits_cuda(int64_t M, int64_t N, int64_t K, int64_t type);
 int64_t qgemm_row_step_bytes(int64_t type);
@@ -54,7 +54,13 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
                             c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot,
-                            c10::optional<torch::Tensor> parts, int64_t wait_ns);
+                            int64_t wait_ns);
+
+void sp_begin_cuda(int64_t epoch_ptr);
+int64_t sp_embed_rs_cuda(torch::Tensor table, torch::Tensor ids, double scale, int64_t vstart, int64_t vend,
+                         std::vector<int64_t> plan);
+int64_t sp_rs_push_cuda(torch::Tensor x, std::vector<int64_t> plan);
+void sp_ag_norm_cuda(std::vector<int64_t> plan, double eps, c10::optional<torch::Tensor> err);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";
@@ -65,8 +71,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &prefill_attention_cuda);
   m.def("gemm", &gemm_cuda);
   m.def("gemm_splits_for", &gemm_splits_for);
-  m.def("gemm_sk_floats", &gemm_sk_floats);
-  m.def("gemm_sk", &gemm_sk_cuda);
+  m.def("gemm_sp", &gemm_sp_cuda);
+  m.def("sp_begin", &sp_begin_cuda);
+  m.def("sp_embed_rs", &sp_embed_rs_cuda);
+  m.def("sp_rs_push", &sp_rs_push_cuda);
+  m.def("sp_ag_norm", &sp_ag_norm_cuda);
   m.def("splitk_sum", &splitk_sum_cuda);
   m.def("qgemm_splits", &qgemm_splits_cuda);
   m.def("qgemm_row_step_bytes", &qgemm_row_step_bytes);
@@ -89,5 +98,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_allreduce_norm", &tp_allreduce_norm_cuda, py::arg("in_ptrs"), py::arg("res_ptrs"), py::arg("out_ptrs"),
         py::arg("sig_ptrs"), py::arg("rank"), py::arg("T"), py::arg("H"), py::arg("weight"), py::arg("eps"),
         py::arg("mode"), py::arg("counters"), py::arg("err"), py::arg("max_blocks"), py::arg("oneshot"),
-        py::arg("parts"), py::arg("wait_ns") = 0);
+        py::arg("wait_ns") = 0);
 }

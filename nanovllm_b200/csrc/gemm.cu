@@ -14,14 +14,17 @@
 //  * prefill-sized M: A = activations, B = weights, bf16 output, optional fused SiLU(gate)*up / GELU(gate)*up
 //    on gate/up rows interleaved in 128-row blocks (one 256-wide tile holds 128 gate + 128 up columns).
 //  * decode-sized M (<= 256 tokens): gemm_decode_kernel swaps A/B so the weight rows fill the 128-lane MMA M
-//    dimension and the tokens are the N dimension; the K range is split over the CTAs of a thread-block
-//    cluster so every SM streams weights, and the split partials are reduced through distributed shared memory
-//    in a fixed order (deterministic), with the activation applied there.
+//    dimension and the tokens are the N dimension; the K range may be split over CTAs so every SM streams
+//    weights: the fp32 split partials then go to global memory and the consuming kernel (add+RMSNorm, RoPE,
+//    the split-activation or split-sum kernel) adds them in split order (deterministic).  Under tensor
+//    parallelism the decode kernel also carries the sequence-parallel collectives (sp_comm.cuh): an all-gather
+//    + RMSNorm prologue for column-parallel projections and a reduce-scatter epilogue for row-parallel ones.
 // Every mbarrier wait is bounded; on timeout the kernel records an error code and all roles exit, TMEM is
 // freed, and the host sees the code through the error word.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include "common.cuh"
+#include "sp_comm.cuh"
 #include "launch.h"
 #include "tma_host.h"
 
@@ -264,9 +267,18 @@ __global__ void __launch_bounds__(192, 1) gemm_tc_kernel(const __grid_constant__
 // one 128-feature block (128-row interleaved layout) and act(gate) * up is formed in the epilogue.  The K range
 // may be split over S CTAs; split partials are then written as fp32 [S][M][N] and summed, in a fixed order, by
 // the kernel that consumes the output (add+RMSNorm, RoPE) or by splitk_sum_kernel.
+//
+// SP (tensor-parallel sequence-parallel fusion, protocol in sp_comm.cuh):
+//   SP == 1  AG prologue: the weight tiles of the first ring stream in, then the CTAs that own rows of this
+//            rank's SP slice wait for the RS flags, reduce + residual + RMSNorm their rows and broadcast them
+//            into every rank's gather buffer; the TMA producer waits for all T rows to be flagged locally and
+//            only then loads the activation tiles (from the local gather buffer).
+//   SP == 2  RS epilogue (NA == 1): the output tile goes to the owners' receive buffers instead of ``out``.
+//            With split K the S CTAs of a row group meet on per-CTA flags (all CTAs of a decode grid are
+//            co-resident: at most one per SM), then CTA q sums token slice q over the S fp32 partials in split
+//            order (L2-resident) and pushes it -- no separate sum kernel and no extra HBM round trip.
 struct DecodeArgs {
   int N, M, K, kblocks, S, act;
-  int cluster;  // 1: the S split CTAs of a row group form a cluster and reduce through distributed smem
   bf16* out;
   long out_ld;
   float* partial;
@@ -287,13 +299,14 @@ __host__ __device__ constexpr uint32_t pow2_cols(int n) {
   while (c < (uint32_t)n) c <<= 1;
   return c;
 }
+constexpr int kSpTileLd = BM + 8;  // padded row (elements) of the bf16 output tile staged for the RS push
 
 // KSUB: 64-wide K boxes per pipeline stage.  Loading KSUB adjacent boxes of the same weight rows back to back
 // turns each weight row's 128-byte reads into KSUB * 128 contiguous bytes per stage (better DRAM page use).
-template <int BN, int NA, int KSUB>
+template <int BN, int NA, int KSUB, int SP>
 __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_constant__ CUtensorMap amap,
                                                              const __grid_constant__ CUtensorMap bmap,
-                                                             DecodeArgs args) {
+                                                             DecodeArgs args, const __grid_constant__ nvb::sp::Args sp) {
   constexpr int STAGES = decode_stages2(NA, BN, KSUB);
   constexpr uint32_t A_SUB = BM * BK * 2;
   constexpr uint32_t A_BYTES = NA * A_SUB;
@@ -301,6 +314,8 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   constexpr uint32_t STAGE_BYTES = KSUB * SUB_BYTES;
   constexpr uint32_t TMEM_COLS = pow2_cols(NA * BN);
   constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
+  static_assert(SP != 2 || NA == 1, "the RS epilogue handles one 128-row weight tile per CTA");
+  static_assert(SP != 2 || (size_t)BN * kSpTileLd * 2 <= (size_t)STAGES * STAGE_BYTES, "RS tile fits the ring");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -309,6 +324,7 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   uint64_t* tfull_bar = empty_bar + STAGES;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
+  __shared__ float red[32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int group = blockIdx.x / args.S, split = blockIdx.x % args.S;
@@ -316,6 +332,7 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   const int nsuper = args.kblocks / KSUB;  // the host picks KSUB > 1 only when it divides kblocks
   const int kb0 = (int)((long)nsuper * split / args.S);   // in stage (super-block) units
   const int kb1 = (int)((long)nsuper * (split + 1) / args.S);
+  const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -340,8 +357,7 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
     nvb::tma_prefetch_desc(&amap);
     nvb::tma_prefetch_desc(&bmap);
     // The weights are never written by earlier kernels: the first ring's weight tiles stream in before the
-    // dependency wait, overlapping the previous kernel's tail; the activation tiles follow after it.
-    const int pre = (kb1 - kb0) < STAGES ? (kb1 - kb0) : STAGES;
+    // dependency wait (and, with SP == 1, before the collective), overlapping the previous kernel's tail.
     for (int it = 0; it < pre; ++it) {
       uint8_t* sa = smem + it * STAGE_BYTES;
       nvb::mbar_arrive_expect_tx(&full_bar[it], STAGE_BYTES);
@@ -352,7 +368,24 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
           nvb::tma_load_2d(sa + ks * SUB_BYTES + j * A_SUB, &amap, &full_bar[it], ((kb0 + it) * KSUB + ks) * BK,
                            row0 + j * BM);
     }
-    nvb::pdl_wait();
+  }
+  if constexpr (SP != 0) nvb::sp::stamp(sp, 0);
+  nvb::pdl_wait();  // activations (and the outputs this kernel overwrites) belong to earlier kernels
+  if constexpr (SP != 0) nvb::sp::stamp(sp, 1);
+
+  if constexpr (SP == 1) {
+    // all-gather + RMSNorm prologue: CTAs 0 .. n_own-1 each reduce one row of this rank's slice
+    if ((int)blockIdx.x < nvb::sp::owned_rows(sp)) {
+      nvb::sp::wait_rs_flags(sp, args.err);  // on timeout the error is recorded and the step runs to its end
+      nvb::sp::stamp(sp, 2);
+      nvb::sp::ag_norm_rows(sp, blockIdx.x, gridDim.x, red);
+      nvb::sp::stamp(sp, 3);
+    }
+    if (warp == 0) nvb::sp::wait_ag_rows_warp(sp, args.err);
+    nvb::sp::stamp(sp, 4);
+  }
+
+  if (warp == 0 && lane == 0) {
     for (int it = 0; it < pre; ++it)
 #pragma unroll
       for (int ks = 0; ks < KSUB; ++ks)
@@ -372,8 +405,6 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
         nvb::tma_load_2d(sa + ks * SUB_BYTES + A_BYTES, &bmap, &full_bar[s], (kb * KSUB + ks) * BK, 0);
       }
     }
-  } else {
-    nvb::pdl_wait();  // the epilogue writes outputs a previous kernel may still read
   }
   if (warp == 1 && lane == 0) {
     uint32_t it = 0;
@@ -403,69 +434,87 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   if (lane == 0) ok = nvb::mbar_wait(tfull_bar, 0, args.err, &abort_flag) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   nvb::tc_fence_after();
+  if constexpr (SP != 0) nvb::sp::stamp(sp, 5);
 
-  if (args.cluster) {
-    // Split K reduced inside the cluster: every CTA parks its fp32 tile(s) in its own (now idle) ring memory,
-    // then CTA q of the cluster sums token columns [q*ch, (q+1)*ch) over the S peers in rank order (the same
-    // result whatever the timing) and writes the bf16 (or activated) output.  No fp32 partials leave the SMs.
-    // ``ok`` may differ between CTAs after a timeout: every CTA still joins both cluster barriers.
-    const int r = threadIdx.x;
-    const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
-    float* red = reinterpret_cast<float*>(smem);  // [NA][BN][128] fp32, fits the ring (checked on the host)
-    if (ok) {
-#pragma unroll
-      for (int jt = 0; jt < NA; ++jt) {
-        constexpr int CH = BN < 32 ? BN : 32;
+  const int r = threadIdx.x;  // TMEM lane = row inside each tile
+  const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
+  if constexpr (SP == 2) {
+    // ---------------------------------------------------------------- reduce-scatter epilogue (NA == 1)
+    // every thread takes part (block barriers); after a timeout ``ok`` is 0 and the CTA still publishes its
+    // flags, so peers do not wait for it (the error word already marks the step as failed)
+    bf16* tile = reinterpret_cast<bf16*>(smem);  // the ring is idle: all stages were consumed by the MMAs
+    const int f = row0 + r;
+    constexpr int CH = BN < 64 ? BN : 64;
+    if (args.S == 1) {
+      if (ok) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += CH) {
           uint32_t v[CH];
 #pragma unroll
-          for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + jt * BN + c + q, v + q);
+          for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + c + q, v + q);
           nvb::tmem_ld_wait();
           nvb::reg_fence<CH>(v);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) red[((size_t)jt * BN + c + j) * BM + r] = __uint_as_float(v[j]);
+          for (int j = 0; j < CH; ++j) tile[(c + j) * kSpTileLd + r] = __float2bfloat16(__uint_as_float(v[j]));
         }
       }
-    }
-    nvb::cluster_sync();  // all partial tiles of the cluster are in place
-    const int q = split, S = args.S;
-    const int ch = (BN + S - 1) / S, t0 = q * ch, t1 = min(args.M, min(BN, t0 + ch));
-    const uint32_t red_addr = nvb::smem_u32(red);
-    if (ok) {
-      if (args.act != kActNone) {
-        const int f = group * BM + r;
-        for (int t = t0; t < t1; ++t) {
-          float gsum = 0.f, usum = 0.f;
-          for (int p = 0; p < S; ++p) {
-            const uint32_t peer = nvb::map_peer(red_addr, (uint32_t)p);
-            gsum += nvb::ld_dsmem_f32(peer + (uint32_t)(((size_t)t * BM + r) * 4));
-            usum += nvb::ld_dsmem_f32(peer + (uint32_t)(((size_t)(BN + t) * BM + r) * 4));
-          }
-          if (f < args.N / 2)
-            args.out[(long)t * args.out_ld + f] =
-                __float2bfloat16((args.act == kActSiluMul ? silu(gsum) : gelu_tanh(gsum)) * usum);
-        }
-      } else {
+      __syncthreads();
+      nvb::sp::rs_push_tile(sp, tile, kSpTileLd, 0, args.M, row0);
+    } else {
+      if (ok && f < args.N) {
+        float* dst = args.partial + (long)split * args.M * args.N + f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CH) {
+          uint32_t v[CH];
 #pragma unroll
-        for (int jt = 0; jt < NA; ++jt) {
-          const int f = row0 + jt * BM + r;
-          for (int t = t0; t < t1; ++t) {
-            float sum = 0.f;
-            for (int p = 0; p < S; ++p)
-              sum += nvb::ld_dsmem_f32(nvb::map_peer(red_addr, (uint32_t)p) +
-                                       (uint32_t)(((size_t)(jt * BN + t) * BM + r) * 4));
-            if (f < args.N) args.out[(long)t * args.out_ld + f] = __float2bfloat16(sum);
-          }
+          for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + c + q, v + q);
+          nvb::tmem_ld_wait();
+          nvb::reg_fence<CH>(v);
+#pragma unroll
+          for (int j = 0; j < CH; ++j)
+            if (c + j < args.M) dst[(long)(c + j) * args.N] = __uint_as_float(v[j]);
         }
       }
+      // meet the other split CTAs of this row group (co-resident: the decode grid has at most one CTA per SM)
+      const uint32_t ep = *sp.epoch;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) nvb::sp::st_release_gpu(sp.split_flag + blockIdx.x, ep);
+      int met = 1;
+      if ((int)threadIdx.x < args.S) {
+        const uint64_t t0 = nvb::global_timer_ns();
+        if (!nvb::sp::wait_eq_gpu(sp.split_flag + group * args.S + threadIdx.x, ep, t0, sp.wait_ns, args.err)) {
+          nvb::record_error(args.err, nvb::kErrFlagTimeout);
+          met = 0;
+        }
+      }
+      __syncthreads_and(met);
+      nvb::sp::stamp(sp, 6);
+      // token slice ``split`` of the group: sum the S partials in split order (float4 over 4 features, all loads
+      // of an item independent so many are in flight from L2), stage bf16, push
+      const int ch = (args.M + args.S - 1) / args.S;
+      const int t0 = min(args.M, split * ch), t1 = min(args.M, t0 + ch);
+      const int items = (t1 - t0) * (BM / 4);
+#pragma unroll 4
+      for (int idx = threadIdx.x; idx < items; idx += blockDim.x) {
+        const int t = t0 + idx / (BM / 4), q = idx % (BM / 4);
+        const int ff = row0 + q * 4;
+        if (ff >= args.N) continue;  // N % 4 == 0 (checked on the host): a float4 never straddles N
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < args.S; ++s) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(args.partial + ((long)s * args.M + t) * args.N + ff));
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        uint2 packed = make_uint2(nvb::pack_bf16x2(acc.x, acc.y), nvb::pack_bf16x2(acc.z, acc.w));
+        *reinterpret_cast<uint2*>(tile + (t - t0) * kSpTileLd + q * 4) = packed;
+      }
+      __syncthreads();
+      nvb::sp::rs_push_tile(sp, tile, kSpTileLd, t0, t1, row0);
     }
-    nvb::cluster_sync();  // no CTA leaves while a peer still reads its shared memory
-    ok = 0;               // the tile is written
-  }
-  if (ok) {
-    const int r = threadIdx.x;  // TMEM lane = row inside each tile
-    const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
+    nvb::sp::stamp(sp, 7);
+    nvb::sp::rs_publish(sp, blockIdx.x);
+    nvb::sp::stamp(sp, 8);
+  } else if (ok) {
     if (args.act != kActNone) {
       // NA == 2: tile 0 = gate rows, tile 1 = up rows of feature block ``group``
       const int f = group * BM + r;
@@ -526,224 +575,6 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
-// ------------------------------------------------------------------------------------------------ stream-K gate/up
-// Decode-sized fused gate/up GEMM (NA = 2: a 256-row group = 128 gate + 128 up rows) when there are fewer groups
-// than SMs (Qwen3-8B at TP1: 96 groups of 4096-long rows on 148 SMs, so a one-CTA-per-group grid leaves a third
-// of HBM bandwidth unused; opt-in, see gemm_sk_floats for the measurement).  The (group, 64-wide K block) work
-// units are laid out group-major and cut into one
-// contiguous, equal range per CTA (stream-K); a range covers the tail of one group and the head of the next, so a
-// CTA accumulates at most two segments, in two TMEM regions.  A segment that covers a whole group goes straight
-// through the act(gate) * up epilogue.  Otherwise the CTA writes its fp32 partial of the group to the workspace
-// and bumps the group's arrival counter; the last CTA to arrive (no CTA ever waits for another) adds the group's
-// partials in segment order -- fixed, so the result does not depend on timing -- applies the activation, writes
-// bf16 and resets the counter for the next launch.
-struct SkArgs {
-  int N, M, K, kblocks, groups, act;
-  bf16* out;
-  long out_ld;
-  float* ws;       // [groups][kSkMaxSeg][2][BN][128] fp32
-  int* counters;   // [groups], zero between launches
-  int* err;
-};
-constexpr int kSkMaxSeg = 3;
-
-__device__ __forceinline__ long sk_start(long units, int P, int c) { return units * c / P; }
-// CTA whose unit range contains unit x
-__device__ __forceinline__ int sk_owner(long units, int P, long x) {
-  int c = (int)((x * P) / units);
-  while (c + 1 < P && sk_start(units, P, c + 1) <= x) ++c;
-  while (c > 0 && sk_start(units, P, c) > x) --c;
-  return c;
-}
-
-template <int BN>
-__global__ void __launch_bounds__(128, 1) gemm_decode_sk_kernel(const __grid_constant__ CUtensorMap amap,
-                                                                const __grid_constant__ CUtensorMap bmap,
-                                                                SkArgs args) {
-  constexpr int NA = 2;
-  constexpr int STAGES = decode_stages2(NA, BN, 1);
-  constexpr uint32_t A_SUB = BM * BK * 2;
-  constexpr uint32_t A_BYTES = NA * A_SUB;
-  constexpr uint32_t STAGE_BYTES = A_BYTES + BN * BK * 2;
-  constexpr uint32_t TMEM_COLS = pow2_cols(2 * NA * BN);  // two segments x (gate, up)
-  constexpr uint32_t IDESC = nvb::idesc_bf16_f32(BM, BN);
-  static_assert(2 * NA * BN <= 512, "two segments of gate/up accumulators must fit TMEM");
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tfull_bar = empty_bar + STAGES;
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_flag;
-  __shared__ int last_flag[2];
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int P = gridDim.x, cta = blockIdx.x;
-  const long units = (long)args.groups * args.kblocks;
-  const long u0 = sk_start(units, P, cta), u1 = sk_start(units, P, cta + 1);
-  const int g_first = (int)(u0 / args.kblocks);
-
-  if (threadIdx.x == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      nvb::mbar_init(&full_bar[s], 1);
-      nvb::mbar_init(&empty_bar[s], 1);
-    }
-    nvb::mbar_init(tfull_bar, 1);
-    nvb::fence_mbar_init();
-  }
-  if (warp == 1) {
-    nvb::tmem_alloc(&tmem_base_sh, TMEM_COLS);
-    nvb::tmem_relinquish();
-  }
-  nvb::tc_fence_before();
-  __syncthreads();
-  nvb::tc_fence_after();
-  const uint32_t tmem_base = tmem_base_sh;
-  nvb::pdl_trigger();
-
-  if (warp == 0 && lane == 0) {
-    nvb::tma_prefetch_desc(&amap);
-    nvb::tma_prefetch_desc(&bmap);
-    const long n = u1 - u0;
-    const int pre = n < STAGES ? (int)n : STAGES;
-    for (int it = 0; it < pre; ++it) {  // weights first, before the dependency wait
-      const long u = u0 + it;
-      const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
-      uint8_t* sa = smem + it * STAGE_BYTES;
-      nvb::mbar_arrive_expect_tx(&full_bar[it], STAGE_BYTES);
-#pragma unroll
-      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[it], kb * BK, g * (NA * BM) + j * BM);
-    }
-    nvb::pdl_wait();
-    for (int it = 0; it < pre; ++it) {
-      const int kb = (int)((u0 + it) % args.kblocks);
-      nvb::tma_load_2d(smem + it * STAGE_BYTES + A_BYTES, &bmap, &full_bar[it], kb * BK, 0);
-    }
-    for (long it = pre; it < n; ++it) {
-      const int s = (int)(it % STAGES);
-      if (!nvb::mbar_wait(&empty_bar[s], ((it / STAGES) & 1u) ^ 1u, args.err, &abort_flag)) break;
-      const long u = u0 + it;
-      const int g = (int)(u / args.kblocks), kb = (int)(u % args.kblocks);
-      uint8_t* sa = smem + s * STAGE_BYTES;
-      nvb::mbar_arrive_expect_tx(&full_bar[s], STAGE_BYTES);
-#pragma unroll
-      for (int j = 0; j < NA; ++j) nvb::tma_load_2d(sa + j * A_SUB, &amap, &full_bar[s], kb * BK, g * (NA * BM) + j * BM);
-      nvb::tma_load_2d(sa + A_BYTES, &bmap, &full_bar[s], kb * BK, 0);
-    }
-  } else {
-    nvb::pdl_wait();  // the epilogue writes outputs a previous kernel may still read
-  }
-  if (warp == 1 && lane == 0) {
-    bool ok = true;
-    const long n = u1 - u0;
-    for (long it = 0; it < n; ++it) {
-      const int s = (int)(it % STAGES);
-      if (!nvb::mbar_wait(&full_bar[s], (it / STAGES) & 1u, args.err, &abort_flag)) { ok = false; break; }
-      nvb::tc_fence_after();
-      const long u = u0 + it;
-      const int seg = (int)(u / args.kblocks) - g_first;             // 0 or 1
-      const bool first = (it == 0) || (u % args.kblocks == 0);       // first unit of its segment
-      const uint32_t a_addr = nvb::smem_u32(smem + s * STAGE_BYTES);
-      const uint32_t b_addr = a_addr + A_BYTES;
-#pragma unroll
-      for (int j = 0; j < NA; ++j)
-#pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk)
-          nvb::tc_mma_f16(tmem_base + (seg * NA + j) * BN, nvb::sdesc_kmajor_sw128(a_addr + j * A_SUB + kk * 32),
-                          nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC, (!first || kk > 0) ? 1u : 0u);
-      nvb::tc_commit(&empty_bar[s]);
-    }
-    if (ok) nvb::tc_commit(tfull_bar);
-  }
-  __syncwarp();
-  int ok = 0;
-  if (lane == 0) ok = nvb::mbar_wait(tfull_bar, 0, args.err, &abort_flag) ? 1 : 0;
-  ok = __shfl_sync(0xffffffffu, ok, 0);
-  ok = __syncthreads_and(ok);  // the epilogue has block barriers: every warp takes the same path
-  nvb::tc_fence_after();
-
-  const int r = threadIdx.x;  // TMEM lane = row inside each 128-row tile
-  const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
-  const int nseg = (u1 > u0) ? (int)((u1 - 1) / args.kblocks) - g_first + 1 : 0;
-  constexpr int CH = BN < 32 ? BN : 32;
-  for (int seg = 0; ok && seg < nseg; ++seg) {
-    const int g = g_first + seg;
-    const long gs = (long)g * args.kblocks, ge = gs + args.kblocks;
-    const int f = g * BM + r;  // output feature
-    const bool whole = u0 <= gs && u1 >= ge;
-    if (whole) {
-#pragma unroll 1
-      for (int c = 0; c < BN; c += CH) {
-        uint32_t gv[CH], uv[CH];
-#pragma unroll
-        for (int q = 0; q < CH; q += 16) {
-          nvb::tmem_ld_32x32b_x16(t_row + (seg * NA) * BN + c + q, gv + q);
-          nvb::tmem_ld_32x32b_x16(t_row + (seg * NA + 1) * BN + c + q, uv + q);
-        }
-        nvb::tmem_ld_wait();
-        nvb::reg_fence<CH>(gv);
-        nvb::reg_fence<CH>(uv);
-#pragma unroll
-        for (int j = 0; j < CH; ++j)
-          if (c + j < args.M) {
-            const float x = __uint_as_float(gv[j]), y = __uint_as_float(uv[j]);
-            args.out[(long)(c + j) * args.out_ld + f] =
-                __float2bfloat16((args.act == kActSiluMul ? silu(x) : gelu_tanh(x)) * y);
-          }
-      }
-      continue;
-    }
-    // partial segment: publish this CTA's fp32 partial, then let the last contributor finish the group
-    const int c_first = sk_owner(units, P, gs), c_last = sk_owner(units, P, ge - 1);
-    const int my = cta - c_first, nparts = c_last - c_first + 1;
-    if (nparts > kSkMaxSeg) {  // the host only picks stream-K when every group has at most kSkMaxSeg parts
-      if (threadIdx.x == 0) nvb::record_error(args.err, nvb::kErrBadArgument);
-      continue;
-    }
-    float* slot = args.ws + ((size_t)g * kSkMaxSeg + my) * 2 * BN * BM;
-#pragma unroll 1
-    for (int c = 0; c < BN; c += CH) {
-      uint32_t gv[CH], uv[CH];
-#pragma unroll
-      for (int q = 0; q < CH; q += 16) {
-        nvb::tmem_ld_32x32b_x16(t_row + (seg * NA) * BN + c + q, gv + q);
-        nvb::tmem_ld_32x32b_x16(t_row + (seg * NA + 1) * BN + c + q, uv + q);
-      }
-      nvb::tmem_ld_wait();
-      nvb::reg_fence<CH>(gv);
-      nvb::reg_fence<CH>(uv);
-#pragma unroll
-      for (int j = 0; j < CH; ++j) {
-        slot[(size_t)(c + j) * BM + r] = __uint_as_float(gv[j]);
-        slot[(size_t)(BN + c + j) * BM + r] = __uint_as_float(uv[j]);
-      }
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last_flag[seg] = atomicAdd(&args.counters[g], 1) == nparts - 1;
-    __syncthreads();
-    if (!last_flag[seg]) continue;
-    __threadfence();
-    if (threadIdx.x == 0) args.counters[g] = 0;  // ready for the next launch
-    const float* base = args.ws + (size_t)g * kSkMaxSeg * 2 * BN * BM;
-#pragma unroll 1
-    for (int t = 0; t < args.M; ++t) {
-      float x = 0.f, y = 0.f;
-      for (int k = 0; k < nparts; ++k) {  // segment order
-        const float* sl = base + (size_t)k * 2 * BN * BM;
-        x += __ldcg(sl + (size_t)t * BM + r);
-        y += __ldcg(sl + (size_t)(BN + t) * BM + r);
-      }
-      args.out[(long)t * args.out_ld + f] = __float2bfloat16((args.act == kActSiluMul ? silu(x) : gelu_tanh(x)) * y);
-    }
-  }
-  nvb::tc_fence_before();
-  __syncthreads();
-  nvb::tc_fence_after();
-  if (warp == 1) nvb::tmem_dealloc(tmem_base, TMEM_COLS);
-}
 
 // Split-K finish of the fused gate/up GEMM: partials [S][M][N] in the 128-row interleaved weight order
 // (block b = rows [256b, 256b + 128) gate, [256b + 128, 256b + 256) up); out[m][f] = act(sum gate) * sum up for
@@ -803,44 +634,42 @@ __global__ void splitk_sum_kernel(const float* __restrict__ partial, int S, long
   }
 }
 
-template <int BN, int NA, int KSUB>
-cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
-                          cudaStream_t stream) {
-  auto kern = gemm_decode_kernel<BN, NA, KSUB>;
+template <int BN, int NA, int KSUB, int SP>
+cudaError_t launch_decode(const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a,
+                          const nvb::sp::Args& sp, int groups, cudaStream_t stream) {
+  auto kern = gemm_decode_kernel<BN, NA, KSUB, SP>;
   constexpr int ST = decode_stages2(NA, BN, KSUB);
   constexpr size_t sm = 1024 + (size_t)ST * KSUB * (NA * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
   static_assert(ST >= 1 && sm <= 227 * 1024, "decode gemm shared memory");
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  if (a.cluster) {
-    constexpr bool kFits = (size_t)NA * BN * BM * 4 <= (size_t)ST * KSUB * (NA * BM * BK * 2 + BN * BK * 2);
-    if constexpr (!kFits) {
-      return cudaErrorInvalidValue;  // the host never asks for it (NA * BN <= 256)
-    } else {
-      C10_CUDA_CHECK(nvb::launch_cluster(kern, dim3(groups * a.S), dim3(128), sm, stream, (unsigned)a.S, am, bm, a));
-    }
-  } else {
-    C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a));
+  static bool attr_set[64] = {false};  // per device: the attribute is a per-device function property
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (r != cudaSuccess) return r;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(128), sm, stream, am, bm, a, sp));
   return cudaGetLastError();
 }
 
-template <int NA, int KSUB>
-cudaError_t launch_decode_bn_k(int bn, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a, int groups,
-                               cudaStream_t st) {
+template <int NA, int KSUB, int SP>
+cudaError_t launch_decode_bn_k(int bn, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a,
+                               const nvb::sp::Args& sp, int groups, cudaStream_t st) {
   switch (bn) {
-    case 16: return launch_decode<16, NA, KSUB>(am, bm, a, groups, st);
-    case 32: return launch_decode<32, NA, KSUB>(am, bm, a, groups, st);
-    case 64: return launch_decode<64, NA, KSUB>(am, bm, a, groups, st);
-    case 128: return launch_decode<128, NA, KSUB>(am, bm, a, groups, st);
-    default: return launch_decode<256, NA, 1>(am, bm, a, groups, st);  // 256-token tiles keep one box per stage
+    case 16: return launch_decode<16, NA, KSUB, SP>(am, bm, a, sp, groups, st);
+    case 32: return launch_decode<32, NA, KSUB, SP>(am, bm, a, sp, groups, st);
+    case 64: return launch_decode<64, NA, KSUB, SP>(am, bm, a, sp, groups, st);
+    case 128: return launch_decode<128, NA, KSUB, SP>(am, bm, a, sp, groups, st);
+    default: return launch_decode<256, NA, 1, SP>(am, bm, a, sp, groups, st);  // 256-token tiles: one box per stage
   }
 }
 
-template <int NA>
+template <int NA, int SP>
 cudaError_t launch_decode_bn(int bn, int ksub, const CUtensorMap& am, const CUtensorMap& bm, const DecodeArgs& a,
-                             int groups, cudaStream_t st) {
-  return ksub == 2 ? launch_decode_bn_k<NA, 2>(bn, am, bm, a, groups, st)
-                   : launch_decode_bn_k<NA, 1>(bn, am, bm, a, groups, st);
+                             const nvb::sp::Args& sp, int groups, cudaStream_t st) {
+  return ksub == 2 ? launch_decode_bn_k<NA, 2, SP>(bn, am, bm, a, sp, groups, st)
+                   : launch_decode_bn_k<NA, 1, SP>(bn, am, bm, a, sp, groups, st);
 }
 
 // 64-wide K boxes per decode pipeline stage (NVB_DECODE_KSUB, 1 or 2; default 1).
@@ -851,14 +680,6 @@ int decode_ksub() {
     k = (e && atoi(e) == 2) ? 2 : 1;
   }
   return k;
-}
-
-// Split K reduced through distributed shared memory inside a cluster of the split CTAs (NVB_DECODE_CLUSTER=1)
-// instead of fp32 partials in global memory summed by the consuming kernel.
-constexpr int kDecodeMaxCluster = 8;
-bool decode_cluster_enabled() {
-  const char* e = getenv("NVB_DECODE_CLUSTER");
-  return e && atoi(e) == 1;
 }
 
 // Weight tiles per CTA.  Two 128-row tiles share one activation tile per K step (half the activation traffic);
@@ -919,6 +740,93 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
   C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(192), sm, stream, am, bm, a));
 }
 
+// Decode launch shared by gemm_cuda and gemm_sp_cuda.  Returns the K splits used.
+int64_t run_decode(torch::Tensor x, torch::Tensor w, bf16* out, long out_ld, int act, float* partial,
+                   long partial_cap, int force_splits, int* err, bool partial_out, const nvb::sp::Args& sp,
+                   int* grid_out) {
+  const int M = x.size(0), K = x.size(1), N = w.size(0);
+  const int sms = num_sms();
+  const int kblocks = (K + BK - 1) / BK;
+  const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int NA = sp.mode == 2 ? 1 : decode_na(N, act);
+  DecodeArgs d{};
+  d.N = N;
+  d.M = M;
+  d.K = K;
+  d.kblocks = kblocks;
+  d.act = act;
+  const int groups = (N + NA * BM - 1) / (NA * BM);
+  if (force_splits > 0) {
+    d.S = force_splits;
+  } else {
+    d.S = partial != nullptr ? decode_splits(groups, kblocks, sms) : 1;
+  }
+  if (d.S > kblocks) d.S = kblocks;
+  if (sp.mode == 2) {
+    TORCH_CHECK(groups * d.S <= sms && groups * d.S <= nvb::sp::kMaxProd,
+                "RS epilogue: the split CTAs of a group meet, so the grid must fit one wave");
+    TORCH_CHECK(N % 4 == 0, "RS epilogue: N % 4 == 0 (float4 split reduction)");
+  }
+  // with split K the activation runs after the split sum (splitk_act_kernel), not in the GEMM epilogue
+  if (d.S > 1 && act != kActNone) {
+    TORCH_CHECK(!partial_out, "partial output is not offered for the fused-activation GEMM");
+    TORCH_CHECK(out_ld % 4 == 0, "activation output rows must be 8-byte aligned");
+    d.act = kActNone;
+  }
+  d.out = out;
+  d.out_ld = out_ld;
+  d.err = err;
+  if (d.S > 1) {
+    TORCH_CHECK(partial != nullptr && partial_cap >= (long)d.S * M * N,
+                "decode gemm: fp32 partial buffer of S*M*N elements required");
+    d.partial = partial;
+  }
+  if (getenv("NVB_GEMM_DEBUG"))
+    printf("[gemm decode] M=%d N=%d K=%d bn=%d NA=%d groups=%d S=%d sp=%d\n", M, N, K, bn, NA, groups, d.S, sp.mode);
+  CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
+  CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
+  int ksub = decode_ksub();
+  if (bn > 128 || kblocks % ksub != 0 || d.S > kblocks / ksub) ksub = 1;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  cudaError_t r;
+  if (sp.mode == 1)
+    r = NA == 2 ? launch_decode_bn<2, 1>(bn, ksub, am, bm, d, sp, groups, stream)
+                : launch_decode_bn<1, 1>(bn, ksub, am, bm, d, sp, groups, stream);
+  else if (sp.mode == 2)
+    r = launch_decode_bn<1, 2>(bn, ksub, am, bm, d, sp, groups, stream);
+  else
+    r = NA == 2 ? launch_decode_bn<2, 0>(bn, ksub, am, bm, d, sp, groups, stream)
+                : launch_decode_bn<1, 0>(bn, ksub, am, bm, d, sp, groups, stream);
+  TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
+  if (grid_out) *grid_out = groups * d.S;
+  if (sp.mode == 2) return d.S;  // the epilogue reduced the splits and pushed the rows
+  if (d.S > 1 && act != kActNone) {
+    const long work = (long)M * (N / 2) / 4;
+    int blocks = (int)((work + 255) / 256);
+    if (blocks > sms * 8) blocks = sms * 8;
+    C10_CUDA_CHECK(nvb::launch(splitk_act_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, M, N, d.out,
+                               d.out_ld, act));
+  } else if (d.S > 1 && partial_out) {
+    // the caller consumes the partials itself (fused into its next kernel)
+  } else if (d.S > 1) {
+    const long MN = (long)M * N;
+    int blocks = (int)((MN / 4 + 255) / 256);
+    if (blocks > sms * 8) blocks = sms * 8;
+    C10_CUDA_CHECK(nvb::launch(splitk_sum_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, MN, d.out, N,
+                               d.out_ld));
+  }
+  return d.S;
+}
+
+void check_gemm_operands(const torch::Tensor& x, const torch::Tensor& w) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "gemm expects bf16 CUDA tensors");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "shape mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "K must be the contiguous dimension");
+  TORCH_CHECK(x.size(1) % 8 == 0, "K must be a multiple of 8 (16-byte TMA rows)");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
+}
+
 }  // namespace
 
 // y = x @ w^T (x [M, K] bf16, w [N, K] bf16) with optional activation on 128-interleaved gate/up rows of w.
@@ -926,112 +834,126 @@ void launch_gemm(const CUtensorMap& am, const CUtensorMap& bm, GemmArgs& a, cuda
 // the partials are left for the consumer to sum, otherwise a sum (or split-K activation) kernel follows.
 int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, c10::optional<torch::Tensor> workspace,
                   int64_t force_splits, c10::optional<torch::Tensor> err, bool partial_out) {
-  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
-              "gemm expects bf16 CUDA tensors");
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "shape mismatch");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "K must be the contiguous dimension");
+  check_gemm_operands(x, w);
   const int M = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK(K % 8 == 0, "K must be a multiple of 8 (16-byte TMA rows)");
-  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "row strides must be 16-byte multiples");
   TORCH_CHECK(out.stride(-1) == 1, "output rows must be contiguous");
   if (act != kActNone) TORCH_CHECK(N % 256 == 0, "fused gate/up activation needs N % 256 == 0");
   if (M == 0) return 0;
   int* e = err.has_value() ? err->data_ptr<int>() : nullptr;
-  auto stream = at::cuda::getCurrentCUDAStream();
-  const int sms = num_sms();
-  const int kblocks = (K + BK - 1) / BK;
+  if (M <= 256) {
+    float* part = nullptr;
+    long cap = 0;
+    if (workspace.has_value()) {
+      TORCH_CHECK(workspace->scalar_type() == at::kFloat && workspace->is_cuda(), "fp32 workspace");
+      part = workspace->data_ptr<float>();
+      cap = workspace->numel();
+    }
+    nvb::sp::Args none{};
+    const int64_t s = run_decode(x, w, reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0), (int)act, part, cap,
+                                 (int)force_splits, e, partial_out, none, nullptr);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return s;
+  }
+  constexpr int BN = 256;
   GemmArgs a{};
   a.K = K;
-  a.kblocks = kblocks;
+  a.kblocks = (K + BK - 1) / BK;
   a.act = (int)act;
   a.err = e;
-  int64_t splits_used = 1;
-  if (M <= 256) {
-    const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-    const int NA = decode_na(N, (int)act);
-    DecodeArgs d{};
-    d.N = N;
-    d.M = M;
-    d.K = K;
-    d.kblocks = kblocks;
-    d.act = (int)act;
-    const int groups = (N + NA * BM - 1) / (NA * BM);
-    const bool clus = decode_cluster_enabled();
-    if (force_splits > 0) {
-      d.S = (int)force_splits;
-    } else if (clus) {
-      d.S = decode_splits(groups, kblocks, sms);
-      if (act != kActNone && groups * 2 > sms) d.S = 1;
-    } else {
-      d.S = workspace.has_value() ? decode_splits(groups, kblocks, sms) : 1;
-    }
-    if (d.S > kblocks) d.S = kblocks;
-    if (clus && d.S > kDecodeMaxCluster) d.S = kDecodeMaxCluster;
-    d.cluster = (clus && d.S > 1 && NA * bn <= 256) ? 1 : 0;
-    if (clus && !d.cluster && d.S > 1 && !workspace.has_value()) d.S = 1;  // no partial buffer to fall back on
-    // with split K the activation runs after the split sum (splitk_act_kernel), not in the GEMM epilogue --
-    // unless the split CTAs reduce inside their cluster, which applies it there
-    if (d.S > 1 && act != kActNone && !d.cluster) {
-      TORCH_CHECK(!partial_out, "partial output is not offered for the fused-activation GEMM");
-      TORCH_CHECK(out.stride(0) % 4 == 0, "activation output rows must be 8-byte aligned");
-      d.act = kActNone;
-    }
-    splits_used = d.cluster ? 1 : d.S;  // no partials leave a cluster-reduced GEMM
-    d.out = reinterpret_cast<bf16*>(out.data_ptr());
-    d.out_ld = out.stride(0);
-    d.err = e;
-    if (d.S > 1 && !d.cluster) {
-      TORCH_CHECK(workspace.has_value() && workspace->scalar_type() == at::kFloat &&
-                      workspace->numel() >= (long)d.S * M * N,
-                  "decode gemm: fp32 partial buffer of S*M*N elements required");
-      d.partial = workspace->data_ptr<float>();
-    }
-    if (getenv("NVB_GEMM_DEBUG"))
-      printf("[gemm decode] M=%d N=%d K=%d bn=%d NA=%d groups=%d S=%d\n", M, N, K, bn, NA, groups, d.S);
-    CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
-    CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
-    int ksub = decode_ksub();
-    if (bn > 128 || kblocks % ksub != 0 || d.S > kblocks / ksub) ksub = 1;
-    cudaError_t r = NA == 2 ? launch_decode_bn<2>(bn, ksub, am, bm, d, groups, stream)
-                            : launch_decode_bn<1>(bn, ksub, am, bm, d, groups, stream);
-    TORCH_CHECK(r == cudaSuccess, "decode gemm launch failed: ", cudaGetErrorString(r));
-    if (d.cluster) {
-      // reduced (and activated) inside the cluster: out is final
-    } else if (d.S > 1 && act != kActNone) {
-      const long work = (long)M * (N / 2) / 4;
-      int blocks = (int)((work + 255) / 256);
-      if (blocks > sms * 8) blocks = sms * 8;
-      C10_CUDA_CHECK(nvb::launch(splitk_act_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, M, N, d.out, d.out_ld, (int)act));
-    } else if (d.S > 1 && partial_out) {
-      // the caller consumes the partials itself (fused into its next kernel)
-    } else if (d.S > 1) {
-      const long MN = (long)M * N;
-      int blocks = (int)((MN / 4 + 255) / 256);
-      if (blocks > sms * 8) blocks = sms * 8;
-      C10_CUDA_CHECK(nvb::launch(splitk_sum_kernel, dim3(blocks), dim3(256), 0, stream, d.partial, d.S, MN, d.out, N, d.out_ld));
-    }
-  } else {
-    constexpr int BN = 256;
-    a.Ma = M;
-    a.Nb = N;
-    a.tiles_m = (M + BM - 1) / BM;
-    a.tiles_n = (N + BN - 1) / BN;
-    a.splits = 1;
-    a.out_mode = kOutBf16;
-    a.out = out.data_ptr();
-    a.out_ld = out.stride(0);
-    CUtensorMap am = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), BM);
-    CUtensorMap bm = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BN);
-    launch_gemm<BN, 4>(am, bm, a, stream, sms);
-  }
+  a.Ma = M;
+  a.Nb = N;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (N + BN - 1) / BN;
+  a.splits = 1;
+  a.out_mode = kOutBf16;
+  a.out = out.data_ptr();
+  a.out_ld = out.stride(0);
+  CUtensorMap am = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), BM);
+  CUtensorMap bm = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BN);
+  launch_gemm<BN, 4>(am, bm, a, at::cuda::getCurrentCUDAStream(), num_sms());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  return M <= 256 ? splits_used : 1;
+  return 1;
+}
+
+// Host view of the sequence-parallel plan built by nanovllm_b200/parallel/sp.py (one int64 per field; device
+// addresses as integers; per-rank arrays padded to 8).
+nvb::sp::Args sp_args_from(const std::vector<int64_t>& v, double eps) {
+  // layout: mode, rank, R, T, per, per_max, H, n_prod, has_res, norm_mode, wait_ns, epoch, split_flag, my_recv,
+  //         my_rs_flag, residual, norm_w, recv[8], rs_flag[8], gather[8], ag_flag[8], trace
+  TORCH_CHECK(v.size() == 18 + 4 * nvb::sp::kMaxRanks, "bad SP plan");
+  nvb::sp::Args a{};
+  a.mode = (int)v[0];
+  a.rank = (int)v[1];
+  a.R = (int)v[2];
+  a.T = (int)v[3];
+  a.per = (int)v[4];
+  a.per_max = (int)v[5];
+  a.H = (int)v[6];
+  a.n_prod = (int)v[7];
+  a.has_res = (int)v[8];
+  a.norm_mode = (int)v[9];
+  a.wait_ns = v[10] > 0 ? (uint64_t)v[10] : nvb::kWaitLimitNs;
+  a.eps = (float)eps;
+  a.epoch = reinterpret_cast<const uint32_t*>(v[11]);
+  a.split_flag = reinterpret_cast<uint32_t*>(v[12]);
+  a.my_recv = reinterpret_cast<const bf16*>(v[13]);
+  a.my_rs_flag = reinterpret_cast<const uint32_t*>(v[14]);
+  a.residual = reinterpret_cast<bf16*>(v[15]);
+  a.norm_w = reinterpret_cast<const bf16*>(v[16]);
+  for (int p = 0; p < nvb::sp::kMaxRanks; ++p) {
+    a.recv[p] = reinterpret_cast<bf16*>(v[17 + p]);
+    a.rs_flag[p] = reinterpret_cast<uint32_t*>(v[25 + p]);
+    a.gather[p] = reinterpret_cast<bf16*>(v[33 + p]);
+    a.ag_flag[p] = reinterpret_cast<uint32_t*>(v[41 + p]);
+  }
+  a.trace = reinterpret_cast<unsigned long long*>(v[49]);
+  TORCH_CHECK(a.R >= 1 && a.R <= nvb::sp::kMaxRanks && a.rank >= 0 && a.rank < a.R, "bad SP rank / size");
+  TORCH_CHECK(a.T >= 1 && a.T <= nvb::sp::kMaxRows && a.per >= 1 && a.per <= a.per_max, "bad SP rows");
+  TORCH_CHECK(a.H % 8 == 0 && a.H <= 128 * 8 * nvb::sp::kMaxChunks, "SP rows need H % 8 == 0 and H <= 8192");
+  return a;
+}
+
+// Sequence-parallel fused decode GEMM.  ``sp_plan[0]`` selects the fusion:
+//   1: y = RMSNorm-all-gathered activations @ w^T -- ``x`` must be this rank's gather buffer [T, K]; the prologue
+//      reduces the RS slot named in the plan, updates the residual slice, normalises and broadcasts, waits for
+//      all rows, then runs the GEMM exactly like gemm_cuda (split-K partials, activation, ``partial_out``);
+//   2: y = x @ w^T pushed to the owners' receive buffers (reduce-scatter); ``out`` is unused.
+// Returns (K splits used, CTAs launched); the CTA count is the producer count a consumer of mode 2 waits for.
+std::vector<int64_t> gemm_sp_cuda(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> out, int64_t act,
+                                  c10::optional<torch::Tensor> workspace, c10::optional<torch::Tensor> err,
+                                  bool partial_out, std::vector<int64_t> sp_plan, double eps) {
+  check_gemm_operands(x, w);
+  const int M = x.size(0), N = w.size(0);
+  TORCH_CHECK(M >= 1 && M <= 256, "the SP-fused GEMM is the decode path: 1..256 tokens");
+  nvb::sp::Args sp = sp_args_from(sp_plan, eps);
+  TORCH_CHECK(sp.T == M, "plan rows must equal the GEMM's M");
+  TORCH_CHECK(sp.mode == 1 || sp.mode == 2, "SP mode must be 1 (AG prologue) or 2 (RS epilogue)");
+  if (sp.mode == 2) TORCH_CHECK(act == kActNone && sp.H == N, "RS epilogue: plain projection onto H features");
+  if (sp.mode == 1) TORCH_CHECK(sp.H == x.size(1), "AG prologue: rows of H = K features");
+  if (act != kActNone) TORCH_CHECK(N % 256 == 0, "fused gate/up activation needs N % 256 == 0");
+  int* e = err.has_value() ? err->data_ptr<int>() : nullptr;
+  float* part = nullptr;
+  long cap = 0;
+  if (workspace.has_value()) {
+    TORCH_CHECK(workspace->scalar_type() == at::kFloat && workspace->is_cuda(), "fp32 workspace");
+    part = workspace->data_ptr<float>();
+    cap = workspace->numel();
+  }
+  bf16* o = nullptr;
+  long ld = 0;
+  if (sp.mode == 1) {
+    TORCH_CHECK(out.has_value() && out->stride(-1) == 1, "AG GEMM output rows must be contiguous");
+    o = reinterpret_cast<bf16*>(out->data_ptr());
+    ld = out->stride(0);
+  }
+  int grid = 0;
+  const int64_t s = run_decode(x, w, o, ld, (int)act, part, cap, 0, e, partial_out, sp, &grid);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {s, grid};
 }
 
 // K splits (and so the fp32 partial slices of the workspace) the decode path uses for this shape.
 int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
-  if (decode_cluster_enabled()) return 1;  // split K is reduced inside clusters: callers keep no partials
-  // K splits the decode path uses when the caller provides a partial buffer
   if (M > 256 || M <= 0) return 1;
   const int NA = decode_na((int)N, (int)act);
   const int groups = (int)((N + NA * BM - 1) / (NA * BM));
@@ -1043,76 +965,6 @@ int64_t gemm_splits_for(int64_t M, int64_t N, int64_t K, int64_t act) {
   return s > kblocks ? kblocks : s;
 }
 
-// Stream-K fused gate/up (see gemm_decode_sk_kernel): fp32 workspace floats it needs for this shape, 0 when it is
-// off or the shape does not take it (a one-CTA-per-group grid already fills the SMs, or would with a split; or
-// too few groups for at most kSkMaxSeg contributors per group; or more than 128 tokens).
-// Opt-in (NVB_DECODE_STREAMK=1): measured slower than the one-CTA-per-group kernel on B200 (Qwen3-8B gate_up:
-// 205 vs 45 us at 128 tokens, 59 vs 35 us at 16) -- the last contributor's serial fix-up of up to three fp32
-// partial tiles (up to 384 KB through one SM) sits on the critical path.
-int64_t gemm_sk_floats(int64_t M, int64_t N, int64_t K, int64_t act) {
-  const char* e = getenv("NVB_DECODE_STREAMK");
-  const bool enabled = e && atoi(e) == 1;
-  if (!enabled || act == 0 || M <= 0 || M > 128 || N % 256 != 0) return 0;
-  const int sms = num_sms();
-  const long groups = N / 256, kblocks = (K + BK - 1) / BK;
-  if (groups >= sms || groups * 2 <= sms) return 0;
-  const long units = groups * kblocks;
-  if (units / sms < (kblocks + 1) / 2) return 0;  // a group would span more than kSkMaxSeg CTAs
-  const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
-  return groups * kSkMaxSeg * 2 * (long)bn * BM;
-}
-
-template <int BN>
-void launch_decode_sk(const CUtensorMap& am, const CUtensorMap& bm, const SkArgs& a, int grid, cudaStream_t stream) {
-  auto kern = gemm_decode_sk_kernel<BN>;
-  constexpr int ST = decode_stages2(2, BN, 1);
-  constexpr size_t sm = 1024 + (size_t)ST * (2 * BM * BK * 2 + BN * BK * 2) + (2 * ST + 1) * 8 + 64;
-  static_assert(sm <= 227 * 1024, "stream-K decode gemm shared memory");
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-  C10_CUDA_CHECK(nvb::launch(kern, dim3(grid), dim3(128), sm, stream, am, bm, a));
-}
-
-// out[M, N/2] = act(x @ gate^T) * (x @ up^T) on 128-row-interleaved gate/up weights, stream-K over all SMs.
-void gemm_sk_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t act, torch::Tensor workspace,
-                  torch::Tensor counters, c10::optional<torch::Tensor> err) {
-  TORCH_CHECK(x.is_cuda() && w.is_cuda() && x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
-              "gemm expects bf16 CUDA tensors");
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1) && x.stride(1) == 1 && w.stride(1) == 1,
-              "shape mismatch");
-  const int M = x.size(0), K = x.size(1), N = w.size(0);
-  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0 && K % 8 == 0, "16-byte TMA rows");
-  TORCH_CHECK(out.stride(-1) == 1 && out.size(0) == M && out.size(1) == N / 2, "out must be [M, N/2]");
-  const int64_t need = gemm_sk_floats(M, N, K, act);
-  TORCH_CHECK(need > 0, "stream-K gate/up not planned for this shape");
-  TORCH_CHECK(workspace.is_cuda() && workspace.scalar_type() == at::kFloat && workspace.numel() >= need,
-              "stream-K workspace too small");
-  TORCH_CHECK(counters.is_cuda() && counters.scalar_type() == at::kInt && counters.numel() >= N / 256,
-              "stream-K counters: int32 [N/256], zero between launches");
-  SkArgs a{};
-  a.N = N;
-  a.M = M;
-  a.K = K;
-  a.kblocks = (K + BK - 1) / BK;
-  a.groups = N / 256;
-  a.act = (int)act;
-  a.out = reinterpret_cast<bf16*>(out.data_ptr());
-  a.out_ld = out.stride(0);
-  a.ws = workspace.data_ptr<float>();
-  a.counters = counters.data_ptr<int>();
-  a.err = err.has_value() ? err->data_ptr<int>() : nullptr;
-  const int bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
-  CUtensorMap am = nvb::make_tmap_2d_bf16(w.data_ptr(), N, K, w.stride(0), BM);
-  CUtensorMap bm = nvb::make_tmap_2d_bf16(x.data_ptr(), M, K, x.stride(0), bn);
-  auto stream = at::cuda::getCurrentCUDAStream();
-  const int grid = num_sms();
-  switch (bn) {
-    case 16: launch_decode_sk<16>(am, bm, a, grid, stream); break;
-    case 32: launch_decode_sk<32>(am, bm, a, grid, stream); break;
-    case 64: launch_decode_sk<64>(am, bm, a, grid, stream); break;
-    default: launch_decode_sk<128>(am, bm, a, grid, stream); break;
-  }
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
 
 // out [M, N] bf16 = sum over splits of parts [S, M, N] fp32 (fixed order).
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out) {

@@ -10,8 +10,6 @@
 //              bit), adds the residual, and
 //     phase B  writes the new residual rows and the RMS-normalised rows into every rank's residual / output
 //              buffers (peer stores), i.e. the all-gather is fused into the norm epilogue;
-//   (phase 0, optional: when the local GEMM left its partial split over K as fp32 slices, each block first sums
-//    the rows its peers will read into the local bf16 partial buffer -- the split-K reduction rides along);
 //   a block-level flag barrier before phase A (all partials written) and after phase B (all stores landed,
 //   all peers done reading this rank's partial buffer) keeps producer / consumer kernels ordered across GPUs.
 //
@@ -106,8 +104,7 @@ template <int NV>
 __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int rank, int nranks, int T, int H,
                                                                  const bf16* __restrict__ w, float eps, int mode,
                                                                  int has_res, uint32_t* counters, int* err,
-                                                                 int oneshot, const float* __restrict__ parts,
-                                                                 int splits, uint64_t wait_ns) {
+                                                                 int oneshot, uint64_t wait_ns) {
   nvb::pdl_wait();
   nvb::pdl_trigger();
   __shared__ float red[32];
@@ -115,40 +112,9 @@ __global__ void __launch_bounds__(1024) tp_allreduce_norm_kernel(PeerPtrs P, int
   if (threadIdx.x == 0) s_epoch = counters[blockIdx.x] + 1;
   const int per = oneshot ? T : (T + nranks - 1) / nranks;
   const int tid = threadIdx.x, nt = blockDim.x;
-  if (splits > 0) {
-    // Phase 0: this rank's partial is still split over K (fp32 [splits][T][H] from the decode GEMM).  Sum it
-    // into the local bf16 ``in`` rows that block b of every rank reads after the barrier (rows owner*per + b,
-    // + grid, ...), in split order 0..splits-1 -- the same rounding as a separate sum kernel, one launch less.
-    bf16* mine = const_cast<bf16*>(P.in[rank]);
-    const int owners = oneshot ? 1 : nranks;
-    for (int k = 0; k < owners; ++k) {
-      const int q1 = min(T, (k + 1) * per);
-      for (int row = k * per + blockIdx.x; row < q1; row += gridDim.x) {
-#pragma unroll
-        for (int i = 0; i < NV; ++i) {
-          const int col = (tid + i * nt) * 8;
-          if (col >= H) continue;
-          float acc[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-          const float* src = parts + (size_t)row * H + col;
-          const size_t split_stride = (size_t)T * H;
-#pragma unroll 4
-          for (int s = 0; s < splits; ++s) {
-            const float4 a = *reinterpret_cast<const float4*>(src + s * split_stride);
-            const float4 b = *reinterpret_cast<const float4*>(src + s * split_stride + 4);
-            acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
-            acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
-          }
-          *reinterpret_cast<uint4*>(mine + (size_t)row * H + col) = pack8(acc);
-        }
-      }
-    }
-  }
   __syncthreads();
   const uint32_t epoch = s_epoch;
-  // with phase 0 the block's own stores must be visible to the peers before its arrival flag
-  if (!block_barrier(P, rank, nranks, 0, epoch, err, wait_ns, splits > 0)) {
+  if (!block_barrier(P, rank, nranks, 0, epoch, err, wait_ns, false)) {
     if (threadIdx.x == 0) counters[blockIdx.x] = epoch;
     return;
   }
@@ -273,7 +239,7 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
                             std::vector<int64_t> sig, int64_t rank, int64_t T, int64_t H,
                             c10::optional<torch::Tensor> weight, double eps, int64_t mode, torch::Tensor counters,
                             c10::optional<torch::Tensor> err, int64_t max_blocks, int64_t oneshot,
-                            c10::optional<torch::Tensor> parts, int64_t wait_ns) {
+                            int64_t wait_ns) {
   const int R = (int)in.size();
   TORCH_CHECK(R >= 1 && R <= kMaxRanks && (int)out.size() == R && (int)sig.size() == R && (int)res.size() == R,
               "one pointer per rank (at most 8 ranks)");
@@ -304,22 +270,12 @@ void tp_allreduce_norm_cuda(std::vector<int64_t> in, std::vector<int64_t> res, s
   if (grid > kMaxBlocks) grid = kMaxBlocks;
   if (grid < 1) grid = 1;
   int* e = err.has_value() ? err->data_ptr<int>() : nullptr;
-  const float* pp = nullptr;
-  int splits = 0;
-  if (parts.has_value() && parts->defined()) {
-    TORCH_CHECK(parts->is_cuda() && parts->scalar_type() == at::kFloat && parts->is_contiguous() &&
-                    parts->dim() == 3 && parts->size(1) == T && parts->size(2) == H,
-                "split-K partials must be contiguous fp32 [splits, T, H]");
-    TORCH_CHECK((reinterpret_cast<uintptr_t>(parts->data_ptr()) & 15) == 0, "split-K partials must be 16-byte aligned");
-    pp = parts->data_ptr<float>();
-    splits = (int)parts->size(0);
-  }
   auto stream = at::cuda::getCurrentCUDAStream();
   uint32_t* cnt = reinterpret_cast<uint32_t*>(counters.data_ptr<int>());
   const uint64_t wait = wait_ns > 0 ? (uint64_t)wait_ns : nvb::kWaitLimitNs;
 #define LAUNCH(NV_)                                                                                              \
   C10_CUDA_CHECK(nvb::launch(tp_allreduce_norm_kernel<NV_>, dim3(grid), dim3(threads), 0, stream, P, (int)rank, R, (int)T, (int)H, w, (float)eps, \
-                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot, pp, splits, wait))
+                                                              (int)mode, has_res ? 1 : 0, cnt, e, (int)oneshot, wait))
   switch (nv) {
     case 1: LAUNCH(1); break;
     case 2: LAUNCH(2); break;

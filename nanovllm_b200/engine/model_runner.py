@@ -58,8 +58,10 @@ class ModelRunner:
         self.final_softcap = getattr(model, "final_softcap", 0.0)
         if self.is_cuda and ps.tp_size() > 1:
             # symmetric buffers for the fused all-reduce + RMSNorm kernels (collective: same point on all ranks)
-            from ..parallel import symm
+            from ..parallel import sp, symm
             symm.init_workspace(max(cfg.max_num_batched_tokens, cfg.max_num_seqs), hf.hidden_size, device)
+            # sequence-parallel buffers for the fused decode path (GEMM + reduce-scatter, all-gather + norm + GEMM)
+            sp.init_workspace(min(cfg.max_num_seqs, sp.MAX_ROWS), hf.hidden_size, device)
         self._allocate_kv()
         self._allocate_state()
         self._attn_scratch = None

@@ -3,8 +3,10 @@
 Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/layers/VocabParallelEmbedding.java:32-253.
 The embedding gathers rows (optionally scaled, Gemma's sqrt(H)); the LM head scores only the LAST token of each
 prefill sequence (cu_seqlens_q[i+1] - 1, VocabParallelEmbedding.java:227-252) and every row in decode.
-With TP each rank owns V/TP vocabulary rows: the embedding zeroes ids outside its range and all-reduces; the
-head computes its logit slice and all-gathers it so every rank samples the same token.
+With TP each rank owns V/TP vocabulary rows: the embedding zeroes ids outside its range and all-reduces (or, on
+the sequence-parallel decode path, pushes its rows to their owners: the gather is fused with the reduce-scatter,
+``sp_push``); the head computes its logit slice -- with the final all-gather + RMSNorm fused into its GEMM on the
+SP path -- and all-gathers the logits so every rank samples the same token.
 """
 from __future__ import annotations
 
@@ -38,6 +40,18 @@ class VocabParallelEmbedding:
             y = ops.embedding(w, ids, self.scale, self.vstart, self.vend)
         return ps.all_reduce(y)
 
+    def sp_push(self, ids: torch.Tensor, ws):
+        """Vocab-parallel gather fused with the reduce-scatter into the SP row owners (csrc/tp_sp.cu)."""
+        from ..parallel.sp import SPPartial
+        w = self.weight
+        if not isinstance(w, torch.Tensor):  # packed embedding table: gather, then push
+            y = w.embedding(ids, self.scale, self.vstart, self.vend)
+            return ws.rs_push(y)
+        slot, plan = ws.producer_plan()
+        n = ops._cuda_ext().sp_embed_rs(w, ids.long(), float(self.scale), int(self.vstart), int(self.vend), plan)
+        ops.add_launches(1)
+        return SPPartial(ws, slot, int(n), ws.T)
+
 
 class ParallelLMHead:
     def __init__(self, weight: torch.Tensor, vocab: Optional[int] = None):
@@ -53,11 +67,19 @@ class ParallelLMHead:
             self.weight = weight
 
     def __call__(self, hidden: torch.Tensor, gather_last: bool = True) -> torch.Tensor:
+        w = self.weight
+        if isinstance(hidden, ops.SPHidden):
+            ctx = get_context()
+            if gather_last and ctx.is_prefill:
+                hidden = hidden.materialize()  # all-gather + final norm, then score only the last tokens
+            else:
+                # decode: every row is scored; the final all-gather + RMSNorm runs in the LM-head GEMM prologue
+                logits = ops.linear_sp_consume(hidden.part, hidden.norm_w, hidden.eps, hidden.norm_mode, True, w)
+                return ps.all_gather_last(logits)[:, :self.vocab] if ps.tp_size() > 1 else logits
         if gather_last:
             ctx = get_context()
             if ctx.is_prefill:
                 hidden = ops.gather_rows(hidden, ctx.last_token_idx)
-        w = self.weight
         logits = w.linear(hidden) if hasattr(w, "linear") else ops.linear(hidden, w)
         if ps.tp_size() > 1:
             logits = ps.all_gather_last(logits)[:, :self.vocab]

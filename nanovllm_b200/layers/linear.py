@@ -8,8 +8,10 @@ Merged / Qkv subclasses are TP names that never shard.  Here:
 * ``MergedColumnParallelLinear`` (gate_up) keeps each rank's gate and up slice and stores them interleaved in
   128-row blocks so the GEMM epilogue computes act(gate) * up on one tile;
 * ``QKVParallelLinear`` keeps each rank's q heads and kv heads (kv heads are replicated when nkv < TP);
-* ``RowParallelLinear`` keeps columns [r*K/TP, (r+1)*K/TP) of W and all-reduces (or reduce-scatters in the
-  sequence-parallel path) the partial outputs.
+* ``RowParallelLinear`` keeps columns [r*K/TP, (r+1)*K/TP) of W and all-reduces the partial outputs -- or, on
+  the sequence-parallel decode path (``sp_produce``), pushes them to the token-row owners from the GEMM epilogue
+  (reduce-scatter); the column-parallel classes' ``sp_consume`` fuses the matching all-gather + RMSNorm into
+  their GEMM prologue.
 
 Weights may also be packed (GGUF blocks kept in block format, ``ops.quant.GgufPacked``): they expose
 ``linear(x, out, partial_ok)`` and the same row / K sharding, concatenation and row permutation as a dense
@@ -28,10 +30,6 @@ from ..parallel import symm
 
 
 from ..ops.quant import cat_rows, is_packed, shard_cols, shard_rows  # dense tensors and GgufPacked alike
-
-
-def _splitk_in_ar() -> bool:
-    return os.environ.get("NVB_TP_SPLITK_IN_AR", "0") == "1"
 
 
 class LinearBase:
@@ -55,6 +53,19 @@ class LinearBase:
         return y
 
 
+class ColumnSPMixin:
+    """Column-parallel projection of an SP forward: all-gather + RMSNorm of the producer's partial rows fused
+    into the GEMM prologue (``ops.linear_sp_consume``)."""
+
+    def sp_consume(self, part, norm, has_res: bool, partial_ok: bool = False):
+        w = self.weight
+        act = self.act if getattr(self, "interleaved", True) else ops.ACT_NONE
+        if self.bias is not None or (self.act != ops.ACT_NONE and not getattr(self, "interleaved", True)):
+            x = part.ws.ag_norm(part, norm.weight, norm.eps, norm.mode, has_res)
+            return self(x)
+        return ops.linear_sp_consume(part, norm.weight, norm.eps, norm.mode, has_res, w, act, partial_ok)
+
+
 class ReplicatedLinear(LinearBase):
     def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None):
         super().__init__()
@@ -64,7 +75,7 @@ class ReplicatedLinear(LinearBase):
         return self._mm(x)
 
 
-class ColumnParallelLinear(LinearBase):
+class ColumnParallelLinear(ColumnSPMixin, LinearBase):
     def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, shard: bool = True):
         super().__init__()
         r, s = ps.tp_rank(), ps.tp_size()
@@ -75,7 +86,7 @@ class ColumnParallelLinear(LinearBase):
         return self._mm(x)
 
 
-class MergedColumnParallelLinear(LinearBase):
+class MergedColumnParallelLinear(ColumnSPMixin, LinearBase):
     """gate_up: per-rank [gate_r; up_r] interleaved in 128-row blocks; __call__ returns act(gate) * up."""
 
     def __init__(self, gate: torch.Tensor, up: torch.Tensor, act: int, interleave_block: int = 128):
@@ -104,7 +115,7 @@ class MergedColumnParallelLinear(LinearBase):
         return ops.act_mul(y, self.act, interleaved=self.interleaved)
 
 
-class QKVParallelLinear(LinearBase):
+class QKVParallelLinear(ColumnSPMixin, LinearBase):
     """q/k/v merged; without a bias the decode output may stay split-K (the RoPE kernel sums it)."""
     def __init__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, num_heads: int, num_kv_heads: int,
                  head_dim: int, bq=None, bk=None, bv=None):
@@ -139,6 +150,9 @@ class QKVParallelLinear(LinearBase):
             return ops.linear(x, self.weight, partial_ok=True)
         return self._mm(x)
 
+    def sp_consume(self, part, norm, has_res: bool, partial_ok: bool = True):
+        return super().sp_consume(part, norm, has_res, partial_ok=partial_ok and self.bias is None)
+
 
 class RowParallelLinear(LinearBase):
     def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor] = None, reduce: bool = True):
@@ -163,14 +177,17 @@ class RowParallelLinear(LinearBase):
             ws = symm.workspace()
             T = x.shape[0]
             if ws is not None and ws.fits(T, w.shape[0]):
-                # partial sum straight into the symmetric buffer; the consumer fuses all-reduce + norm.  With
-                # NVB_TP_SPLITK_IN_AR=1 a split-K GEMM leaves its fp32 slices for the all-reduce kernel to sum
-                # (one launch less, but measured slower at TP2: 10547 vs 10977 tok/s, so off by default)
-                y = mm(out=ws.in_view(T), partial_ok=_splitk_in_ar())
-                return ops.TPPartial(ws, T, y.parts if isinstance(y, ops.SplitK) else None)
+                # partial sum straight into the symmetric buffer; the consumer fuses all-reduce + norm
+                mm(out=ws.in_view(T))
+                return ops.TPPartial(ws, T)
         y = ops.materialize(mm())
         if self.reduce:
             ps.all_reduce(y)
         if self.bias is not None:
             ops.bias_act_(y, self.bias, ops.BIAS_ACT_NONE)
         return y
+
+    def sp_produce(self, x, ws):
+        """GEMM + reduce-scatter of an SP forward: the partial rows go to their owners (``ops.linear_sp_produce``)."""
+        assert self.reduce and self.bias is None, "SP producers are bias-free reducing projections"
+        return ops.linear_sp_produce(ws, x, self.weight)

@@ -19,6 +19,7 @@ from ..layers.attention import Attention
 from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
 from ..layers.linear import MergedColumnParallelLinear, QKVParallelLinear, RowParallelLinear
 from ..layers.norms import RMSNorm, RotaryTables
+from ..parallel import sp
 from ..parallel import state as ps
 from .base import CausalLMBase, WeightBag, random_weights
 
@@ -107,6 +108,9 @@ class Qwen3ForCausalLM(CausalLMBase):
             L.attn.bind_cache(k, v)
 
     def forward(self, ids: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        ws = sp.active_for(ids.shape[0], self.hf.hidden_size, ids.is_cuda)
+        if ws is not None:
+            return self._forward_sp(ids, positions, ws)
         h = self.embed(ids)
         residual = None
         for L in self.layers:
@@ -121,6 +125,21 @@ class Qwen3ForCausalLM(CausalLMBase):
             h = L.down(L.gate_up(x))
         out, _ = self.norm(h, residual)
         return out
+
+    def _forward_sp(self, ids: torch.Tensor, positions: torch.Tensor, ws):
+        """Tensor-parallel forward with the sequence-parallel residual: per layer
+        [AG + RMSNorm + qkv GEMM] -> [q/k-norm + RoPE + KV store] -> [paged attention] -> [o_proj GEMM + RS]
+        -> [AG + RMSNorm + gate_up GEMM + SiLU*up] -> [down GEMM + RS]; the residual stream never leaves its
+        owner rank and no NCCL call remains inside the layers."""
+        ws.begin(ids.shape[0])
+        part = self.embed.sp_push(ids, ws)
+        for i, L in enumerate(self.layers):
+            qkv = L.qkv.sp_consume(part, L.input_norm, has_res=i > 0)
+            a = L.attn(qkv, positions)
+            part = L.o_proj.sp_produce(a, ws)
+            x = L.gate_up.sp_consume(part, L.post_norm, has_res=True)
+            part = L.down.sp_produce(x, ws)
+        return ops.SPHidden(part, self.norm.weight, self.norm.eps, self.norm.mode)
 
     def compute_logits(self, hidden: torch.Tensor) -> torch.Tensor:
         return self.lm_head(hidden)

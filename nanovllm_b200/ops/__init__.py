@@ -71,12 +71,11 @@ class TPPartial:
     """This rank's row-parallel partial sum [T, H], already in the symmetric workspace's ``in`` slot.
 
     A following RMSNorm (with or without residual) runs the fused all-reduce + residual + RMSNorm kernel over
-    peer memory; anything else calls ``materialize`` (a plain fused all-reduce).  ``parts``: the partial is
-    still split over K (fp32 [splits, T, H]); the all-reduce kernel sums the slices into ``in`` first."""
-    __slots__ = ("ws", "T", "parts")
+    peer memory; anything else calls ``materialize`` (a plain fused all-reduce)."""
+    __slots__ = ("ws", "T")
 
-    def __init__(self, ws, T: int, parts: Optional[torch.Tensor] = None):
-        self.ws, self.T, self.parts = ws, T, parts
+    def __init__(self, ws, T: int):
+        self.ws, self.T = ws, T
 
     @property
     def shape(self):
@@ -99,9 +98,12 @@ class TPPartial:
 
 
 def materialize(x):
-    """bf16 tensor from a SplitK (one fused sum kernel) or a TPPartial (fused all-reduce), identity otherwise."""
+    """bf16 tensor from a SplitK (one fused sum kernel), a TPPartial (fused all-reduce) or an SPHidden (all-gather
+    + final norm), identity otherwise."""
+    if isinstance(x, SPHidden):
+        return x.materialize()
     if isinstance(x, TPPartial):
-        return x.ws.allreduce_norm(x.T, None, 0.0, 3, None, parts=x.parts)[0]
+        return x.ws.allreduce_norm(x.T, None, 0.0, 3, None)[0]
     if isinstance(x, SplitK):
         out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
         _cuda_ext().splitk_sum(x.parts, out)
@@ -134,7 +136,8 @@ def error_word(device: torch.device) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     t = _ERR.get(idx)
     if t is None:
-        t = torch.zeros(1, dtype=torch.int32, device=device)
+        with torch.inference_mode(False):  # a normal tensor: the host zeroes it in and outside inference mode
+            t = torch.zeros(1, dtype=torch.int32, device=device)
         _ERR[idx] = t
     return t
 
@@ -173,7 +176,7 @@ def rms_norm(x: torch.Tensor, weight: Optional[torch.Tensor], eps: float, mode: 
              ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
     """Returns (normed, residual).  With ``residual`` the sum x + residual is written back into it."""
     if isinstance(x, TPPartial):
-        return x.ws.allreduce_norm(x.T, weight, eps, mode, residual, parts=x.parts)
+        return x.ws.allreduce_norm(x.T, weight, eps, mode, residual)
     if not x.is_cuda:
         y, r = ref.rms_norm(x, weight, eps, mode, residual)
         if residual is not None:
@@ -281,20 +284,6 @@ def paged_decode(q, k_cache, v_cache, block_tables, ctx_lens, scale, softcap=0.0
 
 
 _CNT: Dict[int, torch.Tensor] = {}
-_SKCNT: Dict[int, torch.Tensor] = {}
-
-
-def _sk_counters(device: torch.device, need: int) -> Optional[torch.Tensor]:
-    """Zeroed int32 per-group arrival counters of the stream-K gate/up GEMM (the kernel leaves them zeroed);
-    created outside stream capture -- a capture that finds none takes the one-CTA-per-group path."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _SKCNT.get(idx)
-    if t is None or t.numel() < need:
-        if torch.cuda.is_current_stream_capturing():
-            return None
-        t = torch.zeros(max(need, 4096), dtype=torch.int32, device=device)
-        _SKCNT[idx] = t
-    return t
 
 
 def _combine_counters(device: torch.device, need: int) -> Optional[torch.Tensor]:
@@ -355,17 +344,6 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
     N = w.shape[0]
     ncols = N // 2 if act != ACT_NONE else N
     C = _cuda_ext()
-    if act != ACT_NONE and force_splits == 0:
-        sk = C.gemm_sk_floats(M, N, K, int(act))
-        cnt = _sk_counters(x.device, N // 256) if sk > 0 else None
-        if cnt is not None:
-            # fewer gate/up groups than SMs: stream-K over all SMs (csrc/gemm.cu gemm_decode_sk_kernel)
-            if out is None:
-                out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
-            ws = torch.empty(sk, dtype=torch.float32, device=x.device)
-            C.gemm_sk(x, w, out, int(act), ws, cnt, error_word(x.device))
-            add_launches(1)
-            return out
     parts = None
     splits = 1
     if M <= 256:
@@ -376,6 +354,80 @@ def linear(x: torch.Tensor, w: torch.Tensor, act: int = ACT_NONE, out: Optional[
         out = torch.empty(M, ncols, dtype=x.dtype, device=x.device)
     used = C.gemm(x, w, out, int(act), parts, int(splits if parts is not None else (force_splits or 0)),
                   error_word(x.device), bool(partial_ok and parts is not None and act == ACT_NONE))
+    if parts is not None and used > 1:
+        if partial_ok and act == ACT_NONE:
+            add_launches(1)
+            return SplitK(parts)
+        add_launches(2)
+        return out
+    add_launches(1)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ SP fused linear
+class SPHidden:
+    """Hidden states of an SP forward before the final norm: the last producer's partial rows sit in the owners'
+    receive buffers.  The LM head fuses the final all-gather + RMSNorm into its GEMM; ``materialize`` runs the
+    stand-alone all-gather + norm and returns the gathered normalised rows [T, H] (a view of the workspace)."""
+    __slots__ = ("part", "norm_w", "eps", "norm_mode", "_rows")
+
+    def __init__(self, part, norm_w, eps: float, norm_mode: int):
+        self.part, self.norm_w, self.eps, self.norm_mode = part, norm_w, eps, norm_mode
+        self._rows = None
+
+    @property
+    def shape(self):
+        return self.part.shape
+
+    @property
+    def is_cuda(self):
+        return True
+
+    def materialize(self) -> torch.Tensor:
+        # once only: the owner's reduce adds the partials into the residual slice in place
+        if self._rows is None:
+            self._rows = self.part.ws.ag_norm(self.part, self.norm_w, self.eps, self.norm_mode, True)
+        return self._rows
+
+
+def linear_sp_produce(ws, x: torch.Tensor, w: torch.Tensor):
+    """Row-parallel projection fused with the reduce-scatter: y = x @ w^T pushed to the row owners."""
+    from ..parallel.sp import SPPartial
+    x = materialize(x)
+    if library_gemm() or not isinstance(w, torch.Tensor):
+        y = w.linear(x) if hasattr(w, "linear") else linear(x, w)
+        return ws.rs_push(materialize(y).contiguous())
+    M, K = x.shape
+    N = w.shape[0]
+    C = _cuda_ext()
+    splits = C.gemm_splits_for(M, N, K, 0)
+    parts = workspace(x.device, splits * M * N) if splits > 1 else None
+    slot, plan = ws.producer_plan()
+    _, grid = C.gemm_sp(x, w, None, 0, parts, error_word(x.device), False, plan, 0.0)
+    add_launches(1)
+    return SPPartial(ws, slot, int(grid), ws.T)
+
+
+def linear_sp_consume(part, norm_w, eps: float, norm_mode: int, has_res: bool, w, act: int = ACT_NONE,
+                      partial_ok: bool = False):
+    """Column-parallel projection whose input is all-gathered + RMSNorm'ed in the GEMM prologue."""
+    ws = part.ws
+    if library_gemm() or not isinstance(w, torch.Tensor):
+        x = ws.ag_norm(part, norm_w, eps, norm_mode, has_res)
+        if hasattr(w, "linear"):
+            y = w.linear(x)
+            return act_mul(y, act, interleaved=True) if act != ACT_NONE else y
+        return linear(x, w, act, partial_ok=partial_ok)
+    x = ws.gather_view(part.T)
+    M, K = x.shape
+    N = w.shape[0]
+    C = _cuda_ext()
+    splits = C.gemm_splits_for(M, N, K, int(act))
+    parts = torch.empty(splits, M, N, dtype=torch.float32, device=x.device) if splits > 1 else None
+    out = torch.empty(M, N // 2 if act != ACT_NONE else N, dtype=torch.bfloat16, device=x.device)
+    plan = ws.consumer_plan(part, norm_w, norm_mode, has_res)
+    used, _ = C.gemm_sp(x, w, out, int(act), parts, error_word(x.device), bool(partial_ok and act == ACT_NONE),
+                        plan, float(eps))
     if parts is not None and used > 1:
         if partial_ok and act == ACT_NONE:
             add_launches(1)

@@ -85,13 +85,11 @@ class TPWorkspace:
         return self.in_buf[:T]
 
     def allreduce_norm(self, T: int, weight: Optional[torch.Tensor], eps: float, mode: int,
-                       residual: Optional[torch.Tensor], oneshot: int = -1,
-                       parts: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
+                       residual: Optional[torch.Tensor], oneshot: int = -1
+                       ) -> Tuple[torch.Tensor, Optional[torch.Tensor]]:
         """Sum the ranks' partials in ``in[:T]``; with ``residual``: residual += sum (kept in the workspace);
         returns (rmsnorm(result) or the plain sum for mode 3, new residual).  ``oneshot``: 1 every rank reads
-        all rows from every peer, 0 two-shot (reduce-scatter + all-gather), -1 pick by message size.
-        ``parts``: this rank's partial still split over K (fp32 [splits, T, H]); the kernel sums it into
-        ``in[:T]`` before the exchange."""
+        all rows from every peer, 0 two-shot (reduce-scatter + all-gather), -1 pick by message size."""
         from .. import ops
         res_ptrs = self._no_res
         res_view = None
@@ -102,7 +100,7 @@ class TPWorkspace:
             res_ptrs = self.res_ptrs
         self.C.tp_allreduce_norm(self.in_ptrs, res_ptrs, self.out_ptrs, self.sig_ptrs, self.rank, int(T),
                                  self.hidden, weight if mode in (0, 1) else None, float(eps), int(mode),
-                                 self.counters, ops.error_word(self.buf.device), MAX_BLOCKS, int(oneshot), parts)
+                                 self.counters, ops.error_word(self.buf.device), MAX_BLOCKS, int(oneshot))
         ops.add_launches(1)
         return self.out_buf[:T], res_view
 

@@ -204,3 +204,18 @@ def test_chat_session_on_tiny_model_cpu():
     assert s.history[-1].role == "assistant" and s.history[-1].content == r.answer
     s.send("again")
     assert [m.role for m in s.history] == ["system", "user", "assistant", "user", "assistant"]
+
+
+def test_reply_scanner_streams_token_by_token_like_a_single_parse():
+    from nanovllm_b200.chat.markup import ReplyScanner
+    raw = "<think>plan: add\nthe numbers</think>The answer is 4.<|im_end|>tail"
+    sc = ReplyScanner()
+    shown = []
+    for i in range(0, len(raw), 3):  # 3-character chunks split every marker somewhere
+        shown.append(sc.feed(raw[i:i + 3]).snapshot().answer)
+    final = sc.snapshot()
+    assert final == parse(raw)
+    assert final.answer == "The answer is 4." and final.thinking == "plan: add\nthe numbers"
+    assert all("<" not in s for s in shown), "a partial marker leaked into the displayed answer"
+    # answers only ever grow while streaming
+    assert all(b.startswith(a) for a, b in zip(shown, shown[1:]))

@@ -28,7 +28,7 @@ def test_peer_flag_wait_times_out_and_reports_on_the_host():
     t0 = time.perf_counter()
     C.tp_allreduce_norm([t.data_ptr() for t in inp], [0, 0], [t.data_ptr() for t in out],
                         [t.data_ptr() for t in sig], 0, T, H, None, 1e-6, 3, counters, ops.error_word(dev), 148, 1,
-                        None, wait_ns=5_000_000)
+                        wait_ns=5_000_000)
     torch.cuda.synchronize()
     elapsed = time.perf_counter() - t0
     assert elapsed < 1.0, f"the bounded wait should give up after ~5 ms, took {elapsed:.3f} s"

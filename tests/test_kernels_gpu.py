@@ -208,58 +208,6 @@ def test_gemm_fused_gate_up_split_k(splits):
     close(y, y_ref, 5e-3, 0.03)
 
 
-@pytest.mark.parametrize("M,N,K,act", [(1, 4096, 4096, 0), (16, 6144, 4096, 0), (128, 4096, 2048, 0),
-                                        (100, 4096, 12288, 0), (128, 12288, 4096, 1), (64, 24576, 4096, 0)])
-def test_gemm_decode_cluster_reduction(M, N, K, act, monkeypatch):
-    """Opt-in decode GEMM whose K splits reduce inside a thread-block cluster (distributed shared memory)
-    instead of fp32 partials in global memory: same result as the fp32 reference, bit-identical across launches."""
-    monkeypatch.setenv("NVB_DECODE_CLUSTER", "1")
-    g = torch.Generator().manual_seed(M + N + K)
-    x = (torch.randn(M, K, generator=g) * 0.5).bfloat16()
-    if act:
-        gate = (torch.randn(N // 2, K, generator=g) * 0.05).bfloat16()
-        up = (torch.randn(N // 2, K, generator=g) * 0.05).bfloat16()
-        w = ref.interleave_gate_up(torch.cat([gate, up]), 128).contiguous()
-        y_ref = (ref.silu(ref.linear(x, gate).float()) * ref.linear(x, up).float()).bfloat16()
-        a = ops.ACT_SILU_MUL
-    else:
-        w = (torch.randn(N, K, generator=g) * 0.05).bfloat16()
-        y_ref = ref.linear(x, w)
-        a = 0
-    xd, wd = x.to(DEV), w.to(DEV)
-    y1 = ops.materialize(ops.linear(xd, wd, a, partial_ok=True))
-    y2 = ops.materialize(ops.linear(xd, wd, a, partial_ok=True))
-    torch.cuda.synchronize()
-    ops.check_device_errors()
-    close(y1, y_ref, 5e-3, 0.03)
-    assert torch.equal(y1, y2)
-
-
-@pytest.mark.parametrize("M,I,K", [(1, 12288, 4096), (16, 12288, 4096), (100, 12288, 2048), (128, 10240, 4096)])
-def test_gemm_fused_gate_up_stream_k(M, I, K, monkeypatch):
-    """Opt-in stream-K fused gate/up (fewer 256-row groups than SMs; partial groups finished by their last
-    contributor); two launches in a row check that the arrival counters are left at zero."""
-    monkeypatch.setenv("NVB_DECODE_STREAMK", "1")
-    C = ops._cuda_ext()
-    if C.gemm_sk_floats(M, 2 * I, K, ops.ACT_SILU_MUL) == 0:
-        pytest.skip("stream-K not planned for this shape on this GPU")
-    g = torch.Generator().manual_seed(M + I)
-    x = (torch.randn(M, K, generator=g) * 0.5).bfloat16()
-    gate = (torch.randn(I, K, generator=g) * 0.05).bfloat16()
-    up = (torch.randn(I, K, generator=g) * 0.05).bfloat16()
-    w = ref.interleave_gate_up(torch.cat([gate, up]), 128).contiguous().to(DEV)
-    yg, yu = ref.linear(x, gate).float(), ref.linear(x, up).float()
-    y_ref = (ref.silu(yg) * yu).bfloat16()
-    xd = x.to(DEV)
-    y1 = ops.linear(xd, w, ops.ACT_SILU_MUL)
-    y2 = ops.linear(xd, w, ops.ACT_SILU_MUL)
-    torch.cuda.synchronize()
-    ops.check_device_errors()
-    close(y1, y_ref, 5e-3, 0.03)
-    assert torch.equal(y1, y2)  # fixed partial order: bit-identical across launches
-    assert int(ops._SKCNT[torch.cuda.current_device()][: 2 * I // 256].abs().sum()) == 0
-
-
 @pytest.mark.parametrize("M,N,K", [(5, 4096, 4096), (128, 6144, 4096), (200, 4096, 12288)])
 def test_gemm_split_partials_fused_into_consumers(M, N, K):
     """Split-K partials summed by add+RMSNorm / RoPE match the materialised GEMM result."""

@@ -35,9 +35,9 @@ def _prefill_logits(llm, ids):
     return out
 
 
-def _run(rank, world, port, q, eager, fused="1"):
+def _run(rank, world, port, q, eager, fused="1", spv="1"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NVB_TP_FUSED=fused)
+                      LOCAL_RANK=str(rank), NVB_TP_FUSED=fused, NVB_SP=spv)
     from nanovllm_b200.config import EngineConfig
     from nanovllm_b200.llm import LLM
     from nanovllm_b200.models.registry import init_random_weights
@@ -58,8 +58,11 @@ def _run(rank, world, port, q, eager, fused="1"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("eager,fused", [(True, "1"), (False, "1"), (False, "0")])
-def test_tp2_gpu_matches_tp1(eager, fused):
+@pytest.mark.parametrize("eager,fused,spv", [(True, "1", "1"), (False, "1", "1"), (False, "1", "0"),
+                                             (False, "0", "1")])
+def test_tp2_gpu_matches_tp1(eager, fused, spv):
+    """fused + sp: sequence-parallel GEMM+RS / AG+norm+GEMM path for every step of <= 256 tokens; sp 0: GEMM
+    then the fused all-reduce + RMSNorm kernel; fused 0: NCCL all-reduces."""
     from nanovllm_b200.config import EngineConfig
     from nanovllm_b200.llm import LLM
     from nanovllm_b200.models.registry import init_random_weights
@@ -68,7 +71,7 @@ def test_tp2_gpu_matches_tp1(eager, fused):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, q, eager, fused)) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, 2, port, q, eager, fused, spv)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -118,19 +121,6 @@ def _ar_run(rank, world, port, q):
     ws.in_view(T).copy_(parts[rank].to(dev))
     plain = ops.materialize(ops.TPPartial(ws, T)).float().cpu()
     errs.append(float((plain - total.bfloat16().float()).abs().max()))
-    # partials still split over K (fp32 slices): the kernel sums them locally before the exchange
-    S = 3
-    sl = [torch.randn(S, T, H, generator=torch.Generator().manual_seed(40 + r)) for r in range(world)]
-    tot2 = torch.zeros(T, H)
-    for t in sl:
-        tot2 += t.sum(0).bfloat16().float()
-    want2, _ = ref.rms_norm(tot2.bfloat16(), w, 1e-6, 0)
-    for shot in (1, 0):
-        o2, _ = ws.allreduce_norm(T, w.to(dev), 1e-6, 0, None, oneshot=shot, parts=sl[rank].to(dev))
-        torch.cuda.synchronize()
-        errs.append(float((o2.float().cpu() - want2.float()).abs().max()))
-    plain2 = ops.materialize(ops.TPPartial(ws, T, sl[rank].to(dev))).float().cpu()
-    errs.append(float(((plain2 - tot2) / (1.0 + tot2.abs())).abs().max()))
     # captured in a CUDA graph and replayed twice
     x_in = parts[rank].to(dev)
     w_dev = w.to(dev)
@@ -172,3 +162,127 @@ def test_fused_allreduce_rmsnorm_over_peer_memory(world):
     for r, errs in res.items():
         # residual: fp32 sum of bf16 partials, rounded once (exact up to one bf16 ulp); outputs bf16-rounded
         assert max(errs) < 0.07, (r, errs)
+
+
+def _sp_run(rank, world, port, q):
+    """Sequence-parallel fused kernels on ``world`` GPUs against an fp32 CPU restatement: embedding gather +
+    reduce-scatter, row-parallel GEMM + reduce-scatter (with and without split K), all-gather + RMSNorm fused
+    into the column-parallel GEMM (plain, fused SiLU*up, split-K partial output), the stand-alone all-gather,
+    and graph replays that advance the epoch."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NVB_TP_FUSED="1")
+    from nanovllm_b200 import ops
+    from nanovllm_b200.ops import reference_cpu as ref
+    from nanovllm_b200.parallel import sp
+    from nanovllm_b200.parallel import state as ps
+    ps.init_tp("nccl", timeout_s=60)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    H, Kt, V = 1024, 2048, 1000
+    ws = sp.init_workspace(256, H, dev)
+    g = torch.Generator().manual_seed(5)
+    Wrow = (torch.randn(H, Kt, generator=g) * 0.03).bfloat16()          # row-parallel: K sharded
+    Wcol = (torch.randn(768, H, generator=g) * 0.03).bfloat16()          # column-parallel: N sharded
+    gate = (torch.randn(512, H, generator=g) * 0.03).bfloat16()
+    up = (torch.randn(512, H, generator=g) * 0.03).bfloat16()
+    table = torch.randn(V, H, generator=g).bfloat16()
+    nw = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16()
+    ks, kn = Kt // world, 768 // world
+    Wrow_r = Wrow[:, rank * ks:(rank + 1) * ks].contiguous().to(dev)
+    Wcol_r = Wcol[rank * kn:(rank + 1) * kn].contiguous().to(dev)
+    gi = 512 // world
+    gu_r = ref.interleave_gate_up(torch.cat([gate[rank * gi:(rank + 1) * gi], up[rank * gi:(rank + 1) * gi]]),
+                                  128).contiguous().to(dev) if gi % 128 == 0 else None
+    per_v = (V + world - 1) // world
+    v0, v1 = rank * per_v, min(V, (rank + 1) * per_v)
+    table_r = table[v0:v1].contiguous().to(dev)
+    errs = []
+    for T in (1, 5, 77, 128, 256):
+        x = (torch.randn(T, Kt, generator=torch.Generator().manual_seed(T)) * 0.5).bfloat16()
+        ids = torch.randint(0, V, (T,), generator=torch.Generator().manual_seed(100 + T))
+        # ---- fp32 restatement: per-rank partials rounded to bf16, summed in rank order, rounded (residual)
+        emb = table[ids].float()
+        res0 = emb.bfloat16()
+        h0, _ = ref.rms_norm(res0, nw, 1e-6, 0)
+        y0 = ref.linear(h0, Wcol)
+        parts = [(x[:, r * ks:(r + 1) * ks].float() @ Wrow[:, r * ks:(r + 1) * ks].float().t()).bfloat16()
+                 for r in range(world)]
+        tot = torch.zeros(T, H)
+        for p_ in parts:
+            tot += p_.float()
+        res1 = (tot + res0.float()).bfloat16()
+        h1, _ = ref.rms_norm(res1, nw, 1e-6, 0)
+        y1 = ref.linear(h1, Wcol)
+        act_ref = (ref.silu(ref.linear(h1, gate).float()) * ref.linear(h1, up).float()).bfloat16()
+        # ---- device: embedding RS -> AG+norm+GEMM (no residual) ; GEMM RS -> AG+norm+GEMM (residual)
+        ws.begin(T)
+        from nanovllm_b200.layers.embedding import VocabParallelEmbedding  # noqa: F401 (layer path below)
+        slot, plan = ws.producer_plan()
+        n = ops._cuda_ext().sp_embed_rs(table_r, ids.to(dev), 1.0, v0, v1, plan)
+        part = sp.SPPartial(ws, slot, int(n), T)
+        out0 = ops.materialize(ops.linear_sp_consume(part, nw.to(dev), 1e-6, 0, False, Wcol_r, partial_ok=True))
+        part = ops.linear_sp_produce(ws, x[:, rank * ks:(rank + 1) * ks].contiguous().to(dev), Wrow_r)
+        if gu_r is not None:
+            out1 = ops.linear_sp_consume(part, nw.to(dev), 1e-6, 0, True, gu_r, ops.ACT_SILU_MUL)
+        else:
+            out1 = ops.linear_sp_consume(part, nw.to(dev), 1e-6, 0, True, Wcol_r)
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        errs.append(("y0", T, float((out0.float().cpu() - y0[:, rank * kn:(rank + 1) * kn].float()).abs().max())))
+        if gu_r is not None:
+            want = act_ref[:, rank * gi:(rank + 1) * gi]
+        else:
+            want = y1[:, rank * kn:(rank + 1) * kn]
+        # relative to magnitude: SiLU*up outputs reach ~10, where one bf16 ulp is 0.0625
+        errs.append(("y1", T, float(((out1.float().cpu() - want.float()).abs() / (1 + want.float().abs())).max())))
+        own0, own1 = rank * ws.per, min(T, (rank + 1) * ws.per)
+        if own1 > own0:
+            errs.append(("res", T, float((ws.residual_view().float().cpu() - res1[own0:own1].float()).abs().max())))
+        errs.append(("gather", T, float((ws.gather_view(T).float().cpu() - h1.float()).abs().max())))
+    # the stand-alone all-gather + norm after a stand-alone push, replayed from a CUDA graph twice
+    T = 64
+    xr = torch.randn(T, H, generator=torch.Generator().manual_seed(3 + rank)).bfloat16().to(dev)
+    allx = [torch.randn(T, H, generator=torch.Generator().manual_seed(3 + r)).bfloat16() for r in range(world)]
+    tot = torch.zeros(T, H)
+    for a in allx:
+        tot += a.float()
+    want_g, _ = ref.rms_norm(tot.bfloat16(), nw, 1e-6, 0)
+    nwd = nw.to(dev)
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph):
+            ws.begin(T)
+            pp = ws.rs_push(xr)
+            gout = ws.ag_norm(pp, nwd, 1e-6, 0, False)
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        errs.append(("graph", T, float((gout.float().cpu() - want_g.float()).abs().max())))
+    ops.check_device_errors(dev)
+    del graph
+    q.put((rank, errs))
+    sp.release_workspace()
+    ps.barrier()
+    ps.destroy()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sequence_parallel_fused_kernels_match_fp32(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sp_run, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r, errs in res.items():
+        bad = [e for e in errs if e[2] > 0.06]
+        assert not bad, (r, bad)
