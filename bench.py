@@ -237,6 +237,105 @@ def run_ours(args):
         ps.destroy()
 
 
+def run_serve(args):
+    """BASELINE config 5 as a serving run: ``--serve-requests`` requests arrive as a Poisson process of rate
+    ``--serve-rate`` req/s (exponential gaps, fixed seed), prompts U[min_prompt, max_prompt] random ids, outputs
+    U[128, 1024] tokens (ignore_eos); continuous batching through ``LLM.add_request`` / ``LLM.step``.
+
+    Rank 0's host clock decides which requests have arrived before each step and broadcasts the count, so every
+    TP rank admits the same requests at the same step.  Reported: output tokens / wall time of the whole run
+    (max over ranks), p50 / p99 TTFT over all requests (scheduled arrival -> first sampled token on the host),
+    p50 TPOT.  A throw-away batch warms the engine up before the first arrival."""
+    import random
+    from nanovllm_b200.config import EngineConfig
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel import state as ps
+    from nanovllm_b200.sampling_params import SamplingParams
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        ps.init_tp("nccl", timeout_s=600)
+    rank = ps.tp_rank()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    hf = qwen3_8b_config()
+    weights = init_random_weights(hf, seed=4, device=dev)
+    rnd = random.Random(2024)
+    N = args.serve_requests
+    arrivals, t = [], 0.0
+    for _ in range(N):
+        t += rnd.expovariate(args.serve_rate)
+        arrivals.append(t)
+    plens = [rnd.randint(args.min_prompt, args.max_prompt) for _ in range(N)]
+    olens = [rnd.randint(128, 1024) for _ in range(N)]
+    cfg = EngineConfig(max_num_seqs=args.batch, max_model_len=args.max_prompt + 1024 + 64,
+                       max_num_batched_tokens=args.prefill_chunk, gpu_memory_utilization=0.92,
+                       stop_on_degenerate=False, cuda_graph_max_bs=args.batch)
+    llm = LLM((hf, weights), cfg, device=dev)
+    del weights
+    gen = torch.Generator().manual_seed(77)
+    for _ in range(4):
+        llm.add_request(torch.randint(1, hf.vocab_size - 1, (600,), generator=gen).tolist(),
+                        SamplingParams(max_tokens=args.warmup + 2, ignore_eos=True).deterministic())
+    while llm.has_unfinished():
+        llm.step()
+    prompts = [torch.randint(1, hf.vocab_size - 1, (n,), generator=gen).tolist() for n in plens]
+    flag = torch.zeros(1, dtype=torch.int64, device=dev)
+    seqs = []
+    admitted = steps = 0
+    ps.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    while admitted < N or llm.has_unfinished():
+        due = admitted
+        if rank == 0:  # only rank 0's clock decides: the others follow the broadcast count
+            now = time.perf_counter() - t0
+            if not llm.has_unfinished() and admitted < N and arrivals[admitted] > now:
+                time.sleep(arrivals[admitted] - now)  # idle until the next arrival
+                now = time.perf_counter() - t0
+            while due < N and arrivals[due] <= now:
+                due += 1
+        if world > 1:
+            flag.fill_(due)
+            torch.distributed.broadcast(flag, 0)
+            due = int(flag.item())
+        for i in range(admitted, due):
+            s = llm.add_request(prompts[i], SamplingParams(max_tokens=olens[i], ignore_eos=True).deterministic())
+            s.t_arrival = t0 + arrivals[i]  # the scheduled arrival, not the moment the loop noticed it
+            seqs.append(s)
+        admitted = due
+        if llm.has_unfinished():
+            llm.step()
+            steps += 1
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ttft = sorted(s.t_first_token - s.t_arrival for s in seqs)
+    tpot = sorted((s.t_finish - s.t_first_token) / max(1, s.num_completion_tokens - 1) for s in seqs)
+    out_tokens = sum(s.num_completion_tokens for s in seqs)
+    tt = torch.tensor([wall, ttft[len(ttft) // 2], ttft[min(len(ttft) - 1, int(len(ttft) * 0.99))],
+                       tpot[len(tpot) // 2]], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    wall, p50, p99, tpot50 = (float(x) for x in tt.tolist())
+    llm.close()
+    if rank == 0:
+        print(json.dumps({
+            "impl": args.impl, "metric": "serving: output tok/s and p50 TTFT (Poisson arrivals) Qwen3-8B-shape",
+            "value": round(out_tokens / wall, 1), "unit": "output tokens/s", "n_gpus": world,
+            "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic: random-init weights (seed 4), random prompt ids",
+            "config": {"model": "Qwen3-8B-shape", "requests": N, "rate_per_s": args.serve_rate,
+                       "prompt_len": f"U[{args.min_prompt},{args.max_prompt}]", "output_len": "U[128,1024]",
+                       "max_num_seqs": args.batch, "parallelism": f"tp{world}"},
+            "p50_ttft_ms": round(p50 * 1000, 1), "p99_ttft_ms": round(p99 * 1000, 1),
+            "p50_tpot_ms": round(tpot50 * 1000, 2), "wall_s": round(wall, 2), "engine_steps": steps,
+            "output_tokens": out_tokens, "prompt_tokens": sum(plens)}), flush=True)
+    if world > 1:
+        ps.destroy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -256,6 +355,10 @@ def main():
                     help="path prefix: write a per-kernel device-time breakdown of 3 traced decode steps per rank")
     ap.add_argument("--clock-log", default="",
                     help="CSV file for the nvidia-smi clock samples taken during the timed region (default: a temp file)")
+    ap.add_argument("--serve", action="store_true",
+                    help="serving run (BASELINE config 5): Poisson arrivals, output lengths U[128,1024], p50 TTFT")
+    ap.add_argument("--serve-requests", type=int, default=512)
+    ap.add_argument("--serve-rate", type=float, default=4.0, help="Poisson arrival rate (requests / s)")
     ap.add_argument("--ttft-probe", type=int, default=8,
                     help="requests that join the running batch one at a time after the timed region (p50 TTFT)")
     args = ap.parse_args()
@@ -266,6 +369,9 @@ def main():
         return
     if args.impl == "baseline":
         os.environ["NVB_BASELINE"] = "1"  # cuBLAS GEMMs + separate activation + NCCL all-reduce
+    if args.serve:
+        run_serve(args)
+        return
     run_ours(args)
 
 

@@ -61,6 +61,9 @@ int64_t sp_embed_rs_cuda(torch::Tensor table, torch::Tensor ids, double scale, i
                          std::vector<int64_t> plan);
 int64_t sp_rs_push_cuda(torch::Tensor x, std::vector<int64_t> plan);
 void sp_ag_norm_cuda(std::vector<int64_t> plan, double eps, c10::optional<torch::Tensor> err);
+void sp_argmax_cuda(torch::Tensor logits, int64_t ncols, int64_t col0, double softcap, torch::Tensor out,
+                    int64_t rank, std::vector<int64_t> exch, std::vector<int64_t> flags, int64_t epoch,
+                    int64_t wait_ns, c10::optional<torch::Tensor> err);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nanovllm_b200 sm_100a kernels";
@@ -76,6 +79,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sp_embed_rs", &sp_embed_rs_cuda);
   m.def("sp_rs_push", &sp_rs_push_cuda);
   m.def("sp_ag_norm", &sp_ag_norm_cuda);
+  m.def("sp_argmax", &sp_argmax_cuda);
   m.def("splitk_sum", &splitk_sum_cuda);
   m.def("qgemm_splits", &qgemm_splits_cuda);
   m.def("qgemm_row_step_bytes", &qgemm_row_step_bytes);

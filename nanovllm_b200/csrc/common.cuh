@@ -128,6 +128,13 @@ NV_DEVICE void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar
       : "memory");
 }
 
+// Prefetch a 2-D tile into L2 (no shared-memory destination, no completion tracking, no multicast).
+NV_DEVICE void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 3-D tiled TMA load (no multicast).
 NV_DEVICE void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(

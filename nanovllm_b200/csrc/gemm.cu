@@ -374,11 +374,21 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
   if constexpr (SP != 0) nvb::sp::stamp(sp, 1);
 
   if constexpr (SP == 1) {
-    // all-gather + RMSNorm prologue: CTAs 0 .. n_own-1 each reduce one row of this rank's slice
-    if ((int)blockIdx.x < nvb::sp::owned_rows(sp)) {
+    // while the collective is in flight, pull this CTA's remaining weight tiles (beyond the first ring) into L2
+    if (warp == 0 && lane == 0)
+      for (int kb = kb0 + pre; kb < kb1; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < KSUB; ++ks)
+#pragma unroll
+          for (int j = 0; j < NA; ++j) nvb::tma_prefetch_l2_2d(&amap, (kb * KSUB + ks) * BK, row0 + j * BM);
+    // all-gather + RMSNorm prologue: the first row_ctas CTAs reduce this rank's rows (stride row_ctas).  Only
+    // CTAs of the first wave take rows: every CTA waits for all rows below, so a row owned by a CTA that could
+    // only start after another exits would never arrive (a grid can exceed one wave, e.g. the LM head).
+    const int row_ctas = min((int)gridDim.x, nvb::sp::kRowCtas);
+    if ((int)blockIdx.x < min(nvb::sp::owned_rows(sp), row_ctas)) {
       nvb::sp::wait_rs_flags(sp, args.err);  // on timeout the error is recorded and the step runs to its end
       nvb::sp::stamp(sp, 2);
-      nvb::sp::ag_norm_rows(sp, blockIdx.x, gridDim.x, red);
+      nvb::sp::ag_norm_rows(sp, blockIdx.x, row_ctas, red);
       nvb::sp::stamp(sp, 3);
     }
     if (warp == 0) nvb::sp::wait_ag_rows_warp(sp, args.err);
@@ -477,8 +487,7 @@ __global__ void __launch_bounds__(128, 1) gemm_decode_kernel(const __grid_consta
       }
       // meet the other split CTAs of this row group (co-resident: the decode grid has at most one CTA per SM)
       const uint32_t ep = *sp.epoch;
-      __threadfence();
-      __syncthreads();
+      __syncthreads();  // the CTA's partial stores precede the release below (cumulative)
       if (threadIdx.x == 0) nvb::sp::st_release_gpu(sp.split_flag + blockIdx.x, ep);
       int met = 1;
       if ((int)threadIdx.x < args.S) {
@@ -879,8 +888,8 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 // addresses as integers; per-rank arrays padded to 8).
 nvb::sp::Args sp_args_from(const std::vector<int64_t>& v, double eps) {
   // layout: mode, rank, R, T, per, per_max, H, n_prod, has_res, norm_mode, wait_ns, epoch, split_flag, my_recv,
-  //         my_rs_flag, residual, norm_w, recv[8], rs_flag[8], gather[8], ag_flag[8], trace
-  TORCH_CHECK(v.size() == 18 + 4 * nvb::sp::kMaxRanks, "bad SP plan");
+  //         my_rs_flag, residual, norm_w, recv[8], rs_flag[8], gather[8], ag_flag[8], trace, oneshot
+  TORCH_CHECK(v.size() == 19 + 4 * nvb::sp::kMaxRanks, "bad SP plan");
   nvb::sp::Args a{};
   a.mode = (int)v[0];
   a.rank = (int)v[1];
@@ -907,8 +916,10 @@ nvb::sp::Args sp_args_from(const std::vector<int64_t>& v, double eps) {
     a.ag_flag[p] = reinterpret_cast<uint32_t*>(v[41 + p]);
   }
   a.trace = reinterpret_cast<unsigned long long*>(v[49]);
+  a.oneshot = (int)v[50];
   TORCH_CHECK(a.R >= 1 && a.R <= nvb::sp::kMaxRanks && a.rank >= 0 && a.rank < a.R, "bad SP rank / size");
   TORCH_CHECK(a.T >= 1 && a.T <= nvb::sp::kMaxRows && a.per >= 1 && a.per <= a.per_max, "bad SP rows");
+  TORCH_CHECK(!a.oneshot || a.T <= a.per_max, "one-shot SP: every rank holds all T rows of every source");
   TORCH_CHECK(a.H % 8 == 0 && a.H <= 128 * 8 * nvb::sp::kMaxChunks, "SP rows need H % 8 == 0 and H <= 8192");
   return a;
 }

@@ -9,7 +9,9 @@
 //
 //   RS (in the producer's epilogue)  every CTA pushes the rows of its output tile to their owners' receive
 //        buffers -- recv[owner][src = this rank][row - owner*per][:] -- with peer stores, then publishes one
-//        flag per (this rank, CTA) on every rank: fence.sc.sys + st.release.sys of the forward's epoch.
+//        flag per (this rank, CTA) on every rank: bar.sync, then st.release.sys of the forward's epoch by one
+//        thread per rank (the release is cumulative over the CTA's stores that the barrier ordered before it,
+//        so no full system fence -- measured at 7-9 us per publish -- is needed).
 //   AG (in the consumer's prologue)  the owner waits for the R x n_prod flags of its slot, sums the R partial
 //        rows in rank order (every owner rounds identically), adds the residual slice, writes it back, applies
 //        RMSNorm and stores the normalised row into EVERY rank's gather buffer (peer stores), then flags each
@@ -32,9 +34,11 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxProd = 256;     // producer CTAs per rank per slot (flag array width)
 constexpr int kMaxRows = 256;     // tokens of one SP step (decode buckets)
 constexpr int kMaxChunks = 8;     // 16-byte chunks per thread in the row kernels: H <= 128 * 8 * 8 = 8192
+constexpr int kRowCtas = 128;     // CTAs that reduce rows: always co-resident (one per SM, 148 SMs)
 
 struct Args {
   int mode;        // 0 off, 1 AG + RMSNorm prologue (consumer), 2 RS epilogue (producer)
+  int oneshot;     // 1: producers push every row to every rank and each rank reduces all rows itself
   int rank, R, T, per, per_max, H;
   int n_prod;      // consumer: producer CTAs per rank of the slot it consumes
   int has_res, norm_mode;
@@ -122,8 +126,12 @@ NV_DEVICE float block_sum(float v, float* red) {
   return s;
 }
 
-// Rows of this rank's SP slice that CTA ``cta`` of ``ncta`` handles are local rows cta, cta + ncta, ...
+// Rows this rank reduces: its SP slice [rank*per, ...) -- or, one-shot, all T rows (every rank holds every
+// partial and computes the same rounded sums in rank order, so the replicated results agree bit for bit).
+// CTA ``cta`` of ``ncta`` handles local rows cta, cta + ncta, ...
+__host__ __device__ __forceinline__ int row0_of(const Args& a) { return a.oneshot ? 0 : a.rank * a.per; }
 __host__ __device__ __forceinline__ int owned_rows(const Args& a) {
+  if (a.oneshot) return a.T;
   const int r0 = a.rank * a.per;
   const int r1 = a.T < r0 + a.per ? a.T : r0 + a.per;
   return r1 > r0 ? r1 - r0 : 0;
@@ -155,8 +163,9 @@ NV_DEVICE void ag_norm_rows(const Args& a, int cta, int ncta, float* red) {
   const int n_own = owned_rows(a);
   const int H = a.H;
   const int tid = threadIdx.x, nt = blockDim.x;
+  const int r0 = row0_of(a);
   for (int i = cta; i < n_own; i += ncta) {
-    const int t = a.rank * a.per + i;
+    const int t = r0 + i;
     float v[kMaxChunks][8];
     float ss = 0.f;
 #pragma unroll
@@ -213,15 +222,21 @@ NV_DEVICE void ag_norm_rows(const Args& a, int cta, int ncta, float* red) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = v[j][e] * inv * g[e];
       const uint4 packed = pack8(o);
+      if (a.oneshot) {
+        *reinterpret_cast<uint4*>(a.gather[a.rank] + (size_t)t * H + c) = packed;  // local rows only
+      } else {
 #pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.R) *reinterpret_cast<uint4*>(a.gather[p] + (size_t)t * H + c) = packed;
+        for (int p = 0; p < kMaxRanks; ++p)
+          if (p < a.R) *reinterpret_cast<uint4*>(a.gather[p] + (size_t)t * H + c) = packed;
+      }
     }
   }
-  __syncthreads();  // every thread's peer stores precede the flags below
-  if (tid < a.R) {
-    __threadfence_system();
-    for (int i = cta; i < n_own; i += ncta) st_release_sys(a.ag_flag[tid] + a.rank * a.per + i, ep);
+  __syncthreads();  // every thread's stores precede the flags below (release is cumulative)
+  if (a.oneshot) {
+    if (tid == 0)
+      for (int i = cta; i < n_own; i += ncta) st_release_gpu(a.ag_flag[a.rank] + r0 + i, ep);
+  } else if (tid < a.R) {
+    for (int i = cta; i < n_own; i += ncta) st_release_sys(a.ag_flag[tid] + r0 + i, ep);
   }
 }
 
@@ -234,7 +249,7 @@ NV_DEVICE bool wait_ag_rows_warp(const Args& a, int* err) {
   int ok = 1;
   const uint32_t* flags = a.ag_flag[a.rank];
   for (int t = lane; t < a.T && ok; t += 32)
-    if (!wait_eq_sys(flags + t, ep, t0, a.wait_ns, err)) {
+    if (!(a.oneshot ? wait_eq_gpu(flags + t, ep, t0, a.wait_ns, err) : wait_eq_sys(flags + t, ep, t0, a.wait_ns, err))) {
       record_error(err, kErrFlagTimeout);
       ok = 0;
     }
@@ -247,23 +262,27 @@ NV_DEVICE bool wait_ag_rows_warp(const Args& a, int* err) {
 // After this CTA's pushes: one flag per (this rank, CTA) on every rank.  Called by all threads.
 NV_DEVICE void rs_publish(const Args& a, int cta) {
   __syncthreads();
-  if ((int)threadIdx.x < a.R) {
-    __threadfence_system();
-    st_release_sys(a.rs_flag[threadIdx.x] + a.rank * kMaxProd + cta, *a.epoch);
-  }
+  if ((int)threadIdx.x < a.R) st_release_sys(a.rs_flag[threadIdx.x] + a.rank * kMaxProd + cta, *a.epoch);
 }
 
 // Push a bf16 tile held in shared memory -- rows = tokens [t0, t1), 128 features starting at feature f0,
-// row stride ``ld`` elements -- to the owners' receive buffers (16-byte peer stores).
+// row stride ``ld`` elements -- to the owners' receive buffers (16-byte peer stores); one-shot: to every rank.
 NV_DEVICE void rs_push_tile(const Args& a, const __nv_bfloat16* tile, int ld, int t0, int t1, int f0) {
   const int chunks = 16;  // 128 features = 16 x 8
   const int n = (t1 - t0) * chunks;
   for (int idx = threadIdx.x; idx < n; idx += blockDim.x) {
     const int t = t0 + idx / chunks, ch = idx % chunks;
     if (f0 + ch * 8 >= a.H) continue;  // the last 128-row weight tile may overhang H
-    const int owner = t / a.per, local = t - owner * a.per;
     const uint4 v = *reinterpret_cast<const uint4*>(tile + (size_t)(t - t0) * ld + ch * 8);
-    *reinterpret_cast<uint4*>(a.recv[owner] + ((size_t)a.rank * a.per_max + local) * a.H + f0 + ch * 8) = v;
+    if (a.oneshot) {
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.R)
+          *reinterpret_cast<uint4*>(a.recv[p] + ((size_t)a.rank * a.per_max + t) * a.H + f0 + ch * 8) = v;
+    } else {
+      const int owner = t / a.per, local = t - owner * a.per;
+      *reinterpret_cast<uint4*>(a.recv[owner] + ((size_t)a.rank * a.per_max + local) * a.H + f0 + ch * 8) = v;
+    }
   }
 }
 

@@ -47,7 +47,7 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 
 // Thread t < nranks publishes this block's arrival to rank t and waits (bounded) for rank t's arrival.  With
 // ``publish_writes`` the block's earlier global stores (peer stores included) are made visible at system scope
-// before the flag: bar.sync orders them before the signalling thread's fence + release store.
+// before the flag: bar.sync orders them before the signalling thread's (cumulative) release store.
 // ``sync_first`` alone (no fence) publishes "this block is done reading": the loads' values were consumed
 // before bar.sync, and the release store orders them before the flag.
 __device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase, uint32_t epoch, int* err,
@@ -56,7 +56,8 @@ __device__ bool block_barrier(const PeerPtrs& P, int rank, int nranks, int phase
   int ok = 1;
   if (publish_writes || sync_first) __syncthreads();
   if (t < nranks) {
-    if (publish_writes) __threadfence_system();
+    // the release store is cumulative over the block's writes that bar.sync ordered before it: no full system
+    // fence (fence.sc.sys cost 7-9 us per barrier on B200)
     st_release_sys(P.sig[t] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + rank), epoch);
     const uint32_t* mine = P.sig[rank] + ((size_t)(phase * kMaxBlocks + blockIdx.x) * kMaxRanks + t);
     const uint64_t t0 = nvb::global_timer_ns();

@@ -291,8 +291,15 @@ class ModelRunner:
                                                 self.h_steps))
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
+        n = len(seqs)
+        head = getattr(self.model, "lm_head", None)
+        if head is not None and getattr(head, "sharded", False):
+            # vocab-parallel logits: greedy rows need only the distributed argmax (exact, no logit gather)
+            if all(s.top_k == 1 for s in seqs):
+                return head.argmax(logits[:n], self.final_softcap)
+            logits = head.gather_full(logits[:n])
         t = self._sampling_tensors(seqs)
-        return ops.sample(logits[:len(seqs)], *t, softcap=self.final_softcap)
+        return ops.sample(logits[:n], *t, softcap=self.final_softcap)
 
     # ------------------------------------------------------------------ execution
     def _decode_scratch(self, bs: int) -> Optional[torch.Tensor]:

@@ -57,13 +57,16 @@ class ParallelLMHead:
     def __init__(self, weight: torch.Tensor, vocab: Optional[int] = None):
         r, s = ps.tp_rank(), ps.tp_size()
         self.vocab = vocab or weight.shape[0]
-        if s > 1 and weight.shape[0] == self.vocab:
+        self.sharded = s > 1 and weight.shape[0] == self.vocab
+        if self.sharded:
             per = (self.vocab + s - 1) // s
+            self.vstart, self.ncols = r * per, max(0, min(self.vocab, (r + 1) * per) - r * per)
             w = weight[r * per:min(self.vocab, (r + 1) * per)]
             if w.shape[0] < per:  # pad the last shard so all_gather sees equal shapes
                 w = torch.cat([w, torch.zeros(per - w.shape[0], w.shape[1], dtype=w.dtype, device=w.device)])
             self.weight = w.contiguous()
         else:
+            self.vstart, self.ncols = 0, self.vocab
             self.weight = weight
 
     def __call__(self, hidden: torch.Tensor, gather_last: bool = True) -> torch.Tensor:
@@ -74,13 +77,38 @@ class ParallelLMHead:
                 hidden = hidden.materialize()  # all-gather + final norm, then score only the last tokens
             else:
                 # decode: every row is scored; the final all-gather + RMSNorm runs in the LM-head GEMM prologue
-                logits = ops.linear_sp_consume(hidden.part, hidden.norm_w, hidden.eps, hidden.norm_mode, True, w)
-                return ps.all_gather_last(logits)[:, :self.vocab] if ps.tp_size() > 1 else logits
+                return ops.linear_sp_consume(hidden.part, hidden.norm_w, hidden.eps, hidden.norm_mode, True, w)
         if gather_last:
             ctx = get_context()
             if ctx.is_prefill:
                 hidden = ops.gather_rows(hidden, ctx.last_token_idx)
-        logits = w.linear(hidden) if hasattr(w, "linear") else ops.linear(hidden, w)
-        if ps.tp_size() > 1:
-            logits = ps.all_gather_last(logits)[:, :self.vocab]
-        return logits
+        return w.linear(hidden) if hasattr(w, "linear") else ops.linear(hidden, w)
+
+    # Under TP the head returns this rank's vocabulary slice [T, ceil(V/TP)] (columns past ``ncols`` are padding);
+    # the sampler either takes the distributed argmax (greedy rows) or gathers the full logits.
+    def gather_full(self, logits: torch.Tensor) -> torch.Tensor:
+        """[T, V] logits on every rank from the per-rank slices (NCCL / gloo all-gather)."""
+        if not self.sharded:
+            return logits
+        return ps.all_gather_last(ops.materialize(logits))[:, :self.vocab]
+
+    def argmax(self, logits: torch.Tensor, softcap: float = 0.0) -> torch.Tensor:
+        """Greedy tokens [T] (ties to the lowest id) without gathering the logits: each rank reduces its slice and
+        only (value, id) pairs are exchanged -- over peer memory with the SP workspace, else an all-gather."""
+        logits = ops.materialize(logits)
+        from ..parallel import sp
+        ws = sp.workspace()
+        T = logits.shape[0]
+        if self.sharded and logits.is_cuda and ws is not None and T <= sp.MAX_ROWS:
+            return ws.argmax(logits, self.ncols, self.vstart, softcap)
+        x = logits[:, :self.ncols].float()
+        if softcap > 0:
+            x = softcap * torch.tanh(x / softcap)
+        val, idx = x.max(dim=1)  # first maximum: lowest id on ties
+        if not self.sharded:
+            return idx
+        pair = torch.stack([val.double(), (idx + self.vstart).double()], 1)
+        allp = ps.all_gather_last(pair.unsqueeze(1)).view(T, -1, 2)  # [T, R, 2]
+        best_v = allp[:, :, 0].max(dim=1, keepdim=True).values
+        ids = torch.where(allp[:, :, 0] == best_v, allp[:, :, 1], torch.full_like(allp[:, :, 1], float("inf")))
+        return ids.min(dim=1).values.long()

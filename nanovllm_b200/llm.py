@@ -202,8 +202,10 @@ class LLM:
         try:
             toks = self.runner.run(seqs, is_prefill)
         except BaseException as e:
-            if ps.abort_requested():
-                # a peer failed first: this rank was released from a collective by the process-group timeout
+            # a communication error usually means a peer failed first (its connection closed, or the process-group
+            # timeout released this rank): give its abort reason a moment to reach the store before blaming itself
+            comm = isinstance(e, torch.distributed.DistError)
+            if ps.peer_aborted(wait_s=2.0 if comm else 0.0):
                 raise TensorParallelAbort(ps.abort_reason()) from e
             ps.signal_abort(f"{type(e).__name__}: {e}")
             raise

@@ -86,7 +86,8 @@ def main() -> None:
     wqkv, wo = rnd(QKV // R, H), rnd(H, H // R)
     wgu, wd = rnd(2 * I // R, H), rnd(H, I // R)
     nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
-    ws_sp = spmod.init_workspace(256, H, dev)
+    ws_os = spmod.SPWorkspace(256, H, dev, oneshot=True)
+    ws_rs = spmod.SPWorkspace(256, H, dev, oneshot=False)
     ws_ar = symm.init_workspace(256, H, dev)
     peak = _peak_hbm()
     rows = []
@@ -96,7 +97,7 @@ def main() -> None:
         res = rnd(T, H, std=0.5)
         ws_ar.res_buf[:T].copy_(res)
 
-        def sp_layer():
+        def sp_layer(ws_sp):
             ws_sp.begin(T)
             part = ws_sp.rs_push(x0)
             ops.materialize(ops.linear_sp_consume(part, nw, 1e-6, 0, False, wqkv, partial_ok=True))
@@ -127,30 +128,32 @@ def main() -> None:
             dist.all_reduce(y)
             ops.rms_norm(y, nw, 1e-6, residual=res2)
 
-        t_sp = _time(sp_layer, args.iters)
+        t_sp = _time(lambda: sp_layer(ws_os), args.iters)
+        t_rs = _time(lambda: sp_layer(ws_rs), args.iters)
         t_ar = _time(ar_layer, args.iters)
         t_nc = _time(nccl_layer, args.iters)
         wbytes = (wqkv.numel() + wo.numel() + wgu.numel() + wd.numel()) * 2
         link = 4 * (R - 1) / R * T * H * 2
-        roof = max(wbytes / (peak * 1e3), link / (LINK_GBS * 1e3))
-        rows.append({"tokens": T, "sp_us": round(t_sp, 2), "ar_us": round(t_ar, 2), "nccl_cublas_us": round(t_nc, 2),
-                     "roofline_us": round(roof, 2), "sp_frac_of_roofline": round(roof / t_sp, 3),
+        roof = max(wbytes / (peak * 1e3), link / (LINK_GBS * 1e3))  # rsag bytes; one-shot moves (R/2)x more
+        rows.append({"tokens": T, "sp_oneshot_us": round(t_sp, 2), "sp_rsag_us": round(t_rs, 2),
+                     "ar_us": round(t_ar, 2), "nccl_cublas_us": round(t_nc, 2),
+                     "roofline_us": round(roof, 2), "sp_frac_of_roofline": round(roof / min(t_sp, t_rs), 3),
                      "weights_MB": round(wbytes / 1e6, 1), "nvlink_MB": round(link / 1e6, 3)})
-        if args.trace and rank == 0:
-            ws_sp.trace.zero_()
-            torch.cuda.synchronize()
         if args.trace:
-            dist.barrier()
-            sp_layer()
-            torch.cuda.synchronize()
-            rep = ws_sp.trace_report(4)
-            if rank == 0:
-                print(f"trace T={T} rank 0 (us):\n{rep}", flush=True)
+            for name, w_ in (("oneshot", ws_os), ("rsag", ws_rs)):
+                for _ in range(3):  # a few traced layers back to back; the last one is reported
+                    dist.barrier()
+                    sp_layer(w_)
+                torch.cuda.synchronize()
+                rep = w_.trace_report(4)
+                if rank == 0:
+                    print(f"trace {name} T={T} rank 0 (us):\n{rep}", flush=True)
     ops.check_device_errors(dev)
     if rank == 0:
         for r in rows:
             print(json.dumps({"tp": R, **r}), flush=True)
-    spmod.release_workspace()
+    ws_os.close()
+    ws_rs.close()
     symm.release_workspace()
     ps.barrier()
     ps.destroy()

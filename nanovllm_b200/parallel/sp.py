@@ -17,6 +17,7 @@ its peers once):
   recv                     bf16   [R][per_max][H]    partial rows pushed to this rank (its SP slice)
   gather                   bf16   [max_tokens][H]    normalised rows of all ranks (the consumer GEMM's input)
   residual                 bf16   [per_max][H]       this rank's slice of the residual stream
+  exch / exch_flags        (f32, u32) [R][256] and uint32 [R][256]: the distributed greedy sampler's exchange
 
 A forward takes its flag slots in call order (``producer_plan`` / ``consumer_plan``), so the same graph replays
 the same slots with a new epoch.  The reference names the TP decomposition (nano-vllm-java/.../layers/
@@ -47,13 +48,15 @@ def _round(n: int) -> int:
 
 
 def sp_enabled() -> bool:
-    """The fused SP decode path (default on under TP on CUDA).  ``NVB_SP=0`` keeps the replicated-residual
-    path (GEMM -> fused all-reduce + RMSNorm kernel); ``NVB_BASELINE=1`` turns every fused collective off."""
+    """The fused sequence-parallel decode path, ``NVB_SP=1``.  Off by default: at TP2 on B200 the replicated-
+    residual path (decode GEMM writing its partial into symmetric memory -> fused all-reduce + residual + RMSNorm
+    kernel) measured faster (11.0k vs 10.0k decode tok/s), because each SP junction serialises two NVLink
+    hand-offs.  ``NVB_BASELINE=1`` turns every fused collective off."""
     if os.environ.get("NVB_BASELINE", "0") not in ("0", "", "false", "no"):
         return False
     if os.environ.get("NVB_TP_FUSED", "1") in ("0", "false", "no"):
         return False
-    return os.environ.get("NVB_SP", "1") not in ("0", "false", "no")
+    return os.environ.get("NVB_SP", "0") not in ("0", "false", "no")
 
 
 @dataclass
@@ -74,14 +77,19 @@ class SPPartial:
 
 
 class SPWorkspace:
-    def __init__(self, max_tokens: int, hidden: int, device: torch.device, wait_ns: int = 0):
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device, wait_ns: int = 0,
+                 oneshot: Optional[bool] = None):
         from .. import ops
         self.C = ops._cuda_ext()
         self.R, self.rank = ps.tp_size(), ps.tp_rank()
         assert self.R <= MAX_RANKS, "at most 8 ranks"
         self.max_tokens = min(int(max_tokens), MAX_ROWS)
         self.hidden = int(hidden)
-        self.per_max = (self.max_tokens + self.R - 1) // self.R
+        # one-shot mode: every rank receives every source's partial of every row (sized for it in both modes)
+        self.per_max = self.max_tokens
+        # one-shot (default): one NVLink hand-off per junction, (R-1) x the bytes; rsag: reduce-scatter to the row
+        # owner, then all-gather of the normalised rows (two hand-offs, 2 (R-1)/R x the bytes)
+        self.oneshot = (os.environ.get("NVB_SP_MODE", "rsag") == "oneshot") if oneshot is None else bool(oneshot)
         self.wait_ns = int(wait_ns)
         H = self.hidden
         self.off_rs = 256
@@ -90,7 +98,9 @@ class SPWorkspace:
         self.off_recv = self.off_split + _round(SLOTS * MAX_PROD * 4)
         self.off_gather = self.off_recv + _round(self.R * self.per_max * H * 2)
         self.off_res = self.off_gather + _round(MAX_ROWS * H * 2)
-        total = self.off_res + _round(self.per_max * H * 2)
+        self.off_exch = self.off_res + _round(self.per_max * H * 2)
+        self.off_xflag = self.off_exch + _round(MAX_RANKS * MAX_ROWS * 8)
+        total = self.off_xflag + _round(MAX_RANKS * MAX_ROWS * 4)
         with torch.cuda.device(device):
             self.buf, handle = self.C.symm_alloc(total)
         self.device = self.buf.device
@@ -112,6 +122,7 @@ class SPWorkspace:
         self.slot = 0
         self.T = 0
         self.per = 0
+        self.sample_epoch = 0
         # optional phase trace of CTA 0 of every fused kernel (NVB_SP_TRACE=1): int64 [SLOTS][2][16] globaltimer
         # stamps, row 0 the slot's producer, row 1 its consumer (see ``trace_report``)
         self.trace = None
@@ -126,13 +137,15 @@ class SPWorkspace:
     def begin(self, T: int) -> None:
         """Start an SP forward of T tokens: bump the epoch (one tiny kernel) and restart the slot sequence."""
         self.T = int(T)
-        self.per = (self.T + self.R - 1) // self.R
+        self.per = self.T if self.oneshot else (self.T + self.R - 1) // self.R
         self.slot = 0
         self.C.sp_begin(self.epoch_ptr)
         from .. import ops
         ops.add_launches(1)
 
     def owned_rows(self) -> int:
+        if self.oneshot:
+            return self.T
         r0 = self.rank * self.per
         return max(0, min(self.T, r0 + self.per) - r0)
 
@@ -140,8 +153,14 @@ class SPWorkspace:
         return self.gather_buf[:(T or self.T)]
 
     def residual_view(self) -> torch.Tensor:
-        """This rank's residual rows (valid after the last consumer of the forward ran)."""
+        """This rank's residual rows (valid after the last consumer of the forward ran): its SP slice, or all T
+        rows in one-shot mode."""
         return self.res_buf[:self.owned_rows()]
+
+    def owned_range(self):
+        """Global rows [r0, r1) of ``residual_view``."""
+        r0 = 0 if self.oneshot else self.rank * self.per
+        return r0, r0 + self.owned_rows()
 
     def _plan(self, mode: int, slot: int, n_prod: int = 0, has_res: int = 0, norm_mode: int = 2,
               norm_w: Optional[torch.Tensor] = None) -> List[int]:
@@ -159,7 +178,7 @@ class SPWorkspace:
                  int(norm_mode), self.wait_ns, self.epoch_ptr, me + self.off_split + slot * MAX_PROD * 4,
                  me + self.off_recv, rs[self.rank], me + self.off_res,
                  norm_w.data_ptr() if norm_w is not None else 0]
-                + recv + pad + rs + pad + gather + pad + ag + pad + [trace])
+                + recv + pad + rs + pad + gather + pad + ag + pad + [trace, 1 if self.oneshot else 0])
 
     def producer_plan(self):
         """(slot, plan) for the next reduce-scatter producer of this forward."""
@@ -185,6 +204,18 @@ class SPWorkspace:
         n = self.C.sp_rs_push(x, plan)
         ops.add_launches(1)
         return SPPartial(self, slot, int(n), self.T)
+
+    def argmax(self, logits: torch.Tensor, ncols: int, col0: int, softcap: float = 0.0) -> torch.Tensor:
+        """Greedy tokens [T] over the vocab-parallel logits: each rank's slice is [T, >= ncols] for global token
+        ids [col0, col0 + ncols); exact (ties to the lowest id), 8 bytes per row and rank over NVLink."""
+        from .. import ops
+        self.sample_epoch += 1  # host-side, equal on every rank (ranks step in lock-step)
+        out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
+        self.C.sp_argmax(logits, int(ncols), int(col0), float(softcap), out, self.rank,
+                         [p + self.off_exch for p in self.bases], [p + self.off_xflag for p in self.bases],
+                         self.sample_epoch & 0x7FFFFFFF, self.wait_ns, ops.error_word(self.device))
+        ops.add_launches(1)
+        return out
 
     def trace_report(self, slots: int) -> str:
         """Phase durations (us) of CTA 0 of each fused kernel of the last traced forward (NVB_SP_TRACE=1).

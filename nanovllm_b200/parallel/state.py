@@ -56,11 +56,11 @@ def _watch_abort() -> None:
         return
     while not _WATCH_STOP.is_set():
         try:
-            st.wait([_ABORT_KEY], datetime.timedelta(milliseconds=500))
-        except Exception as e:  # noqa: BLE001
-            if "imeout" in str(e) or "imed out" in str(e):
-                continue  # nothing signalled yet: poll again
-            return  # the store is gone (the job is shutting down): nothing left to watch
+            if not st.check([_ABORT_KEY]):  # non-blocking: a blocking wait would log every time it times out
+                _WATCH_STOP.wait(0.2)
+                continue
+        except Exception:  # noqa: BLE001 - the store is gone (the job is shutting down): nothing left to watch
+            return
         try:
             _ABORT_REASON[0] = st.get(_ABORT_KEY).decode("utf-8", "replace")
         except Exception:  # noqa: BLE001
@@ -103,6 +103,29 @@ def signal_abort(reason: str) -> None:
 
 def abort_requested() -> bool:
     return _ABORT.is_set()
+
+
+def peer_aborted(wait_s: float = 0.0) -> bool:
+    """Whether a peer has signalled a failure, asking the store directly (not only the watcher's last poll) and
+    waiting up to ``wait_s`` for the signal to appear."""
+    if _ABORT.is_set():
+        return True
+    if _TP_SIZE <= 1 or "MASTER_PORT" not in os.environ:
+        return False
+    import time
+    deadline = time.monotonic() + wait_s
+    while True:
+        try:
+            st = _store()
+            if st.check([_ABORT_KEY]):
+                _ABORT_REASON[0] = st.get(_ABORT_KEY).decode("utf-8", "replace")
+                _ABORT.set()
+                return True
+        except Exception:  # noqa: BLE001 - store unreachable: nothing to learn from it
+            return False
+        if time.monotonic() >= deadline:
+            return False
+        time.sleep(0.05)
 
 
 def abort_reason() -> str:

@@ -23,7 +23,7 @@ def _tiny():
                     tie_word_embeddings=False)
 
 
-def _run(rank, world, port, q):
+def _run(rank, world, port, q, greedy=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from nanovllm_b200.config import EngineConfig
@@ -35,14 +35,19 @@ def _run(rank, world, port, q):
     hf = _tiny()
     llm = LLM((hf, init_random_weights(hf, 0)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
                                                              max_num_batched_tokens=256), device="cpu")
-    outs = llm.generate_token_ids([[1, 2, 3, 4, 5], list(range(20, 90))],
-                                  SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))
+    sp_ = (SamplingParams(max_tokens=6, ignore_eos=True).deterministic() if greedy else
+           SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))
+    outs = llm.generate_token_ids([[1, 2, 3, 4, 5], list(range(20, 90))], sp_)
     q.put((rank, [o.token_ids for o in outs]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_tp2_matches_tp1_on_cpu():
+@pytest.mark.parametrize("greedy", [False])
+def test_tp2_matches_tp1_on_cpu(greedy):
+    """Sampled rows gather the full logits and must reproduce the TP=1 tokens (greedy rows take the distributed
+    argmax, checked exactly by test_distributed_argmax_is_exact: on random-init models bf16 logits tie often
+    enough that a different summation order legitimately flips a greedy token)."""
     from nanovllm_b200.config import EngineConfig
     from nanovllm_b200.llm import LLM
     from nanovllm_b200.models.registry import init_random_weights
@@ -50,12 +55,13 @@ def test_tp2_matches_tp1_on_cpu():
     hf = _tiny()
     ref = LLM((hf, init_random_weights(hf, 0)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
                                                              max_num_batched_tokens=256), device="cpu")
-    want = [o.token_ids for o in ref.generate_token_ids(
-        [[1, 2, 3, 4, 5], list(range(20, 90))], SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))]
+    sp_ = (SamplingParams(max_tokens=6, ignore_eos=True).deterministic() if greedy else
+           SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))
+    want = [o.token_ids for o in ref.generate_token_ids([[1, 2, 3, 4, 5], list(range(20, 90))], sp_)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_run, args=(r, 2, port, q, greedy)) for r in range(2)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=240) for _ in procs)
@@ -65,3 +71,44 @@ def test_tp2_matches_tp1_on_cpu():
     assert got[0] == got[1], "ranks diverged"
     # fp32 math on CPU: sharded reductions change summation order only
     assert got[0] == want
+
+
+def _argmax_run(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nanovllm_b200.layers.embedding import ParallelLMHead
+    from nanovllm_b200.parallel import state as ps
+    ps.init_tp("gloo")
+    V, H, T = 301, 8, 6
+    head = ParallelLMHead(torch.zeros(V, H), V)
+    g = torch.Generator().manual_seed(0)
+    full = torch.randn(T, V, generator=g).bfloat16()
+    full[1, 7] = full[1, 290] = 50.0           # tie across ranks: the lower id wins
+    full[2, 100] = full[2, 101] = 40.0         # tie inside one slice
+    full[3, :] = -5.0                          # all equal: id 0
+    per = head.weight.shape[0]
+    mine = torch.full((T, per), 1e4).bfloat16()  # padding columns past the vocabulary must be ignored
+    mine[:, :head.ncols] = full[:, head.vstart:head.vstart + head.ncols]
+    got = head.argmax(mine, 0.0).tolist()
+    capped = head.argmax(mine, 3.0).tolist()     # soft-capped values tie more often; still lowest id
+    q.put((rank, got, capped, torch.argmax(full.float(), 1).tolist(),
+           torch.argmax(3.0 * torch.tanh(full.float() / 3.0), 1).tolist()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_distributed_argmax_is_exact(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_argmax_run, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict((r, rest) for r, *rest in (q.get(timeout=240) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, (toks, capped, want, want_capped) in got.items():
+        assert toks == want, (r, toks, want)
+        assert capped == want_capped, (r, capped, want_capped)

@@ -90,7 +90,8 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
     assert cap > 0
     q, kc, vc, bt, lens = _case(3, B=2, max_len=512)
     big_b = 4096  # claims 4096 sequences: the partials would exceed the fixed array; nothing is launched
-    rc = lib.nvb_paged_decode_noalloc(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), bt.shape[1],
+    # (a block-table row of 256 blocks covers max_len 65536; the size check rejects the call before any launch)
+    rc = lib.nvb_paged_decode_noalloc(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), bt.data_ptr(), 256,
                                       lens.data_ptr(), q.data_ptr(), big_b, 32, 8, 128, kc.shape[0], 256,
                                       0.088, 0.0, 0, 65536, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 2
