@@ -400,9 +400,9 @@ def linear_sp_produce(ws, x: torch.Tensor, w: torch.Tensor):
     M, K = x.shape
     N = w.shape[0]
     C = _cuda_ext()
-    # no split K by default: the split CTAs of a row group would have to meet before the push (5.5 us measured at
-    # TP2), more than the extra weight-streaming time of one CTA per 128 rows at these K; NVB_SP_SPLITK=1 splits
-    splits = C.gemm_splits_for(M, N, K, 0) if os.environ.get("NVB_SP_SPLITK", "0") == "1" else 1
+    # split K as the plain decode GEMM does: one CTA streams only ~50 GB/s of weights (measured: down_proj at TP2
+    # 28 us with one CTA per 128 rows vs 10.8 us + a 5.5 us split rendezvous with 4 splits); NVB_SP_SPLITK=0 off
+    splits = C.gemm_splits_for(M, N, K, 0) if os.environ.get("NVB_SP_SPLITK", "1") == "1" else 1
     parts = workspace(x.device, splits * M * N) if splits > 1 else None
     slot, plan = ws.producer_plan()
     _, grid = C.gemm_sp(x, w, None, 0, parts, error_word(x.device), False, plan, 0.0)

@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from nanovllm_b200 import ops
+from nanovllm_b200.exceptions import DeviceWaitTimeout
 from nanovllm_b200.ops import reference_cpu as ref
 
 pytestmark = pytest.mark.gpu
@@ -102,11 +103,27 @@ def test_paged_decode(hd, nq, nkv, window, softcap):
     torch.cuda.synchronize()
     ops.check_device_errors()
     close(o, o_ref, 2e-2)
-    # single split (grid.x == 1) path
-    o1 = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), ctx.to(DEV), scale, softcap, window,
+    # single split (grid.x == 1) path: contexts that fit max_len = 64
+    ctx64 = ctx.clamp(max=64)
+    o1_ref = ref.paged_decode(q, kc, vc, bt, ctx64, scale, softcap, window)
+    o1 = ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), ctx64.to(DEV), scale, softcap, window,
                           max_len=64)
-    if max(lens) <= 64:
-        close(o1, o_ref, 2e-2)
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    close(o1, o1_ref, 2e-2)
+
+
+def test_paged_decode_reports_context_beyond_max_len():
+    """A context longer than the split grid (max_len) is skipped and reported, never silently truncated."""
+    lens = [10, 700]
+    kc, vc, bt = _paged_setup(2, 8, 8, 128, lens, seed=3)
+    q = torch.randn(2, 8, 128, generator=torch.Generator().manual_seed(1)).bfloat16()
+    ops.error_word(torch.device(DEV)).zero_()
+    ops.paged_decode(q.to(DEV), kc.to(DEV), vc.to(DEV), bt.to(DEV), torch.tensor(lens, dtype=torch.int32).to(DEV),
+                     128 ** -0.5, max_len=64)
+    torch.cuda.synchronize()
+    with pytest.raises(DeviceWaitTimeout):
+        ops.check_device_errors()
 
 
 @pytest.mark.parametrize("hd,nq,nkv", [(128, 32, 8), (64, 8, 8), (256, 4, 1), (128, 16, 8)])

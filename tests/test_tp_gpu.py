@@ -16,6 +16,23 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _collect(q, procs, timeout=300):
+    """One result per child; fails at once (instead of after ``timeout``) when a child exits without one."""
+    import queue as _queue
+    import time as _time
+    out, deadline = [], _time.monotonic() + timeout
+    while len(out) < len(procs):
+        try:
+            out.append(q.get(timeout=2))
+        except _queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead:
+                raise AssertionError(f"a rank exited with {dead} before reporting")
+            if _time.monotonic() > deadline:
+                raise AssertionError("ranks did not report in time")
+    return out
+
+
 def _tiny():
     from nanovllm_b200.config import HfConfig
     return HfConfig(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
@@ -79,8 +96,7 @@ def test_tp2_gpu_matches_tp1(eager, fused, spv):
     for p in procs:
         p.start()
     res = {}
-    for _ in procs:
-        r, toks, logits = q.get(timeout=300)
+    for r, toks, logits in _collect(q, procs):
         res[r] = (toks, logits)
     for p in procs:
         p.join(timeout=120)
@@ -159,7 +175,7 @@ def test_fused_allreduce_rmsnorm_over_peer_memory(world):
     procs = [ctx.Process(target=_ar_run, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    res = dict(_collect(q, procs))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
@@ -174,7 +190,7 @@ def _sp_run(rank, world, port, q, mode="oneshot"):
     into the column-parallel GEMM (plain, fused SiLU*up, split-K partial output), the stand-alone all-gather,
     and graph replays that advance the epoch."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
-                      LOCAL_RANK=str(rank), NVB_TP_FUSED="1", NVB_SP_MODE=mode)
+                      LOCAL_RANK=str(rank), NVB_TP_FUSED="1", NVB_SP="1", NVB_SP_MODE=mode)
     from nanovllm_b200 import ops
     from nanovllm_b200.ops import reference_cpu as ref
     from nanovllm_b200.parallel import sp
@@ -305,7 +321,7 @@ def test_sequence_parallel_fused_kernels_match_fp32(world, mode):
     procs = [ctx.Process(target=_sp_run, args=(r, world, port, q, mode)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in procs)
+    res = dict(_collect(q, procs))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
