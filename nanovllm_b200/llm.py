@@ -299,3 +299,52 @@ class LLM:
         ids = self.tokenizer.encode(prompt, allow_special=True)
         out = self.generate_token_ids([ids], sampling)[0]
         return self.tokenizer.decode(out.token_ids, skip_special=True)
+
+    # ------------------------------------------------------------------ sessions (LLM.java:1066-1128, 1332-1362)
+    def _assert_open(self) -> None:
+        if self._closed:
+            raise NanoLlvmException("this engine is closed")
+
+    def chat(self, sampling: Optional[Union[SamplingParams, int]] = None, **session_options):
+        """A multi-turn ``ChatSession`` on this engine (history, think-tag parsing, streaming events, advisors).
+        ``sampling``: a SamplingParams for every turn, or an int = max new tokens per turn with the engine's
+        default temperature / top-k / top-p; extra keyword options go to ``ChatSession``."""
+        self._assert_open()
+        from .chat.session import ChatSession
+        if isinstance(sampling, int):
+            if sampling < 1:
+                raise ValueError("max_tokens must be >= 1")
+            sampling = self.default_sampling.with_(max_tokens=sampling)
+        return ChatSession(self, sampling=sampling, **session_options)
+
+    def rag(self, index, max_tokens: Optional[int] = None, **session_options):
+        """A retrieval-augmented session over ``index`` (BM25 / dense / hybrid): every turn retrieves passages and
+        chat-generates from them; thinking is off and grounded turns cap the temperature."""
+        self._assert_open()
+        if index is None:
+            raise ValueError("index must not be None")
+        from .rag.session import RagSession
+        sp = None
+        if max_tokens is not None:
+            if max_tokens < 1:
+                raise ValueError("max_tokens must be >= 1")
+            sp = self.default_sampling.with_(max_tokens=int(max_tokens))
+        return RagSession(self, index, sampling=sp, **session_options)
+
+    def run_advisors(self, model_user_text: str, prior_dialog=(), sampling: Optional[SamplingParams] = None):
+        """Run this engine's advisors (``LLM.Builder.advisors``) as ONE batched generate over the user text and
+        the prior dialog; returns the ``AdvisorEnrichment`` (mixed prompt, per-advisor notes)."""
+        self._assert_open()
+        if model_user_text is None:
+            raise ValueError("model_user_text must not be None")
+        from .chat.markup import ThinkTags
+        from .chat.session import AdvisorRunner
+        return AdvisorRunner.enrich(self, list(self.advisors or []), model_user_text, list(prior_dialog or []),
+                                    sampling or self.default_sampling, mixer=self.advisor_mixer,
+                                    tags=self.think_tags or ThinkTags())
+
+    def new_conversation(self):
+        """Fresh dialog history: the engine's system prompt as a system turn when it is not blank."""
+        self._assert_open()
+        from .chat.messages import ChatMessage
+        return [ChatMessage.system(self.system_prompt)] if (self.system_prompt or "").strip() else []

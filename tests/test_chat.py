@@ -219,3 +219,44 @@ def test_reply_scanner_streams_token_by_token_like_a_single_parse():
     assert all("<" not in s for s in shown), "a partial marker leaked into the displayed answer"
     # answers only ever grow while streaming
     assert all(b.startswith(a) for a, b in zip(shown, shown[1:]))
+
+
+class FrontDoorLLM(ScriptedLLM):
+    """Scripted engine carrying the real ``LLM`` front-door methods (chat / rag / run_advisors)."""
+    from nanovllm_b200.llm import LLM as _LLM
+    chat = _LLM.chat
+    rag = _LLM.rag
+    run_advisors = _LLM.run_advisors
+    new_conversation = _LLM.new_conversation
+    _assert_open = _LLM._assert_open
+
+    def __init__(self, replies, advisors=(), system_prompt=""):
+        super().__init__(replies)
+        self._closed = False
+        self.advisors = list(advisors)
+        self.advisor_mixer = None
+        self.think_tags = None
+        self.system_prompt = system_prompt
+        self.listener = None
+
+
+def test_llm_front_door_chat_rag_and_advisors():
+    from nanovllm_b200.rag import RagFactory
+    llm = FrontDoorLLM(["Four.", "Paris lies on the Seine.", "note A", "note B"], system_prompt="Be brief.")
+    s = llm.chat(7)  # int: max new tokens per turn, engine defaults otherwise
+    assert s.sampling.max_tokens == 7 and s.sampling.temperature == llm.default_sampling.temperature
+    assert s.send("2+2?").answer == "Four."
+    ix = RagFactory.of("Paris is the capital of France. It lies on the Seine river.")
+    r = llm.rag(ix, max_tokens=32)
+    assert r.send("Where does Paris lie?").answer == "Paris lies on the Seine."
+    assert r.base_sampling.max_tokens == 32  # (turns without hits raise it to the no-hits floor, as designed)
+    llm.advisors = [LlmAdvisor("a", "Say A."), LlmAdvisor("b", "Say B.")]
+    enr = llm.run_advisors("What is the capital?", [], SamplingParams(max_tokens=100))
+    assert [x.name for x in enr.responses] == ["a", "b"] and len(llm.calls[-1][0]) == 2  # one batched generate
+    conv = llm.new_conversation()
+    assert [m.role for m in conv] == ["system"] and conv[0].content == "Be brief."
+    with pytest.raises(ValueError):
+        llm.chat(0)
+    llm._closed = True
+    with pytest.raises(Exception):
+        llm.chat()
