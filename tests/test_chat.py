@@ -252,7 +252,7 @@ def test_llm_front_door_chat_rag_and_advisors():
     assert r.base_sampling.max_tokens == 32  # (turns without hits raise it to the no-hits floor, as designed)
     llm.advisors = [LlmAdvisor("a", "Say A."), LlmAdvisor("b", "Say B.")]
     enr = llm.run_advisors("What is the capital?", [], SamplingParams(max_tokens=100))
-    assert [x.name for x in enr.responses] == ["a", "b"] and len(llm.calls[-1][0]) == 2  # one batched generate
+    assert [x.advisor_name for x in enr.responses] == ["a", "b"] and len(llm.calls[-1][0]) == 2  # one batched generate
     conv = llm.new_conversation()
     assert [m.role for m in conv] == ["system"] and conv[0].content == "Be brief."
     with pytest.raises(ValueError):
