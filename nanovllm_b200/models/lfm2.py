@@ -21,6 +21,7 @@ from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
 from ..layers.linear import ColumnParallelLinear, MergedColumnParallelLinear, QKVParallelLinear, ReplicatedLinear, \
     RowParallelLinear
 from ..layers.norms import RMSNorm, RotaryTables
+from ..ops.quant import cat_rows, is_packed
 from ..parallel import state as ps
 from .base import CausalLMBase, WeightBag, random_weights
 
@@ -50,13 +51,31 @@ def init_random(hf: HfConfig, seed: int, device="cpu") -> Dict[str, torch.Tensor
 
 
 class ShortConv:
-    """in_proj -> fused gated conv kernel (state in the arena) -> out_proj."""
+    """in_proj -> fused gated conv kernel (state in the arena) -> out_proj.
+
+    Under TP the conv is channel-parallel (the depthwise conv and the gating never mix channels): rank r keeps
+    channels [r*H/TP, (r+1)*H/TP) of each of the B, C and x thirds of in_proj (column-parallel), the same rows of
+    the conv weight and a recurrent state of H/TP channels per sequence, and out_proj is row-parallel (its partial
+    output is all-reduced, fused with the next add + RMSNorm like o_proj)."""
 
     def __init__(self, in_proj, conv_w: torch.Tensor, out_proj, hidden: int, layer: int):
-        self.in_w = in_proj
+        r, s = ps.tp_rank(), ps.tp_size()
+        if s > 1:
+            if hidden % s != 0:
+                raise ValueError(f"hidden size {hidden} is not divisible by TP={s}")
+            hl = hidden // s
+
+            def rows(w, a, b):
+                return w.rows(a, b) if is_packed(w) else w[a:b]
+
+            in_proj = cat_rows([rows(in_proj, j * hidden + r * hl, j * hidden + (r + 1) * hl) for j in range(3)])
+            conv_w = conv_w[r * hl:(r + 1) * hl]
+        else:
+            hl = hidden
+        self.in_proj = ReplicatedLinear(in_proj)   # this rank's [B | C | x] channels (packed weights stay packed)
         self.conv_w = conv_w.float().contiguous()
-        self.out_proj = ReplicatedLinear(out_proj)
-        self.H = hidden
+        self.out_proj = RowParallelLinear(out_proj)
+        self.H = hl
         self.L = conv_w.shape[1]
         self.layer = layer
         self.state = None
@@ -65,7 +84,7 @@ class ShortConv:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         ctx = get_context()
-        proj = ops.linear(x, self.in_w)
+        proj = self.in_proj(x)
         if ctx.is_prefill:
             cu = ctx.cu_seqlens_q
         else:

@@ -112,3 +112,52 @@ def test_distributed_argmax_is_exact(world):
     for r, (toks, capped, want, want_capped) in got.items():
         assert toks == want, (r, toks, want)
         assert capped == want_capped, (r, capped, want_capped)
+
+
+def _lfm2_run(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nanovllm_b200.config import EngineConfig
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel import state as ps
+    from nanovllm_b200.sampling_params import SamplingParams
+    from tests.test_models_cpu import lfm2_tiny
+    ps.init_tp("gloo")
+    hf = lfm2_tiny()
+    llm = LLM((hf, init_random_weights(hf, 3)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
+                                                             max_num_batched_tokens=64), device="cpu")
+    conv = next(L.conv for L in llm.model.layers if L.is_conv)
+    outs = llm.generate_token_ids([list(range(5, 90)), [7, 8, 9]],
+                                  SamplingParams(max_tokens=5, ignore_eos=True, temperature=0.8, seed=11))
+    q.put((rank, [o.token_ids for o in outs], conv.H, tuple(conv.conv_w.shape)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_lfm2_conv_layers_shard_channels_under_tp2():
+    """LFM2's short-conv layers are channel-parallel under TP (in_proj thirds column-sharded, conv weight and
+    recurrent state per channel slice, out_proj row-parallel): TP=2 reproduces the TP=1 tokens through chunked
+    prefill (64-token budget) and decode."""
+    from nanovllm_b200.config import EngineConfig
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.sampling_params import SamplingParams
+    from tests.test_models_cpu import lfm2_tiny
+    hf = lfm2_tiny()
+    ref = LLM((hf, init_random_weights(hf, 3)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
+                                                             max_num_batched_tokens=64), device="cpu")
+    want = [o.token_ids for o in ref.generate_token_ids(
+        [list(range(5, 90)), [7, 8, 9]], SamplingParams(max_tokens=5, ignore_eos=True, temperature=0.8, seed=11))]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lfm2_run, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {r: rest for r, *rest in (q.get(timeout=240) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0][0] == got[1][0] == want
+    assert got[0][1] == hf.hidden_size // 2 and got[0][2][0] == hf.hidden_size // 2
