@@ -78,6 +78,55 @@ def qwen3_8b_config():
                     architectures=["Qwen3ForCausalLM"], torch_dtype="bfloat16")
 
 
+def gemma3_270m_config():
+    """Gemma3-270M architecture (5:1 sliding(512) / global interleave, head_dim 256)."""
+    from nanovllm_b200.config import HfConfig
+    return HfConfig(vocab_size=262144, hidden_size=640, intermediate_size=2048, num_hidden_layers=18,
+                    num_attention_heads=4, num_key_value_heads=1, head_dim=256, max_position_embeddings=32768,
+                    rms_norm_eps=1e-6, rope_theta=1_000_000.0, rope_local_base_freq=10000.0, sliding_window=512,
+                    query_pre_attn_scalar=256, tie_word_embeddings=True, model_type="gemma3_text",
+                    architectures=["Gemma3ForCausalLM"], torch_dtype="bfloat16",
+                    layer_types=(["sliding_attention"] * 5 + ["full_attention"]) * 3)
+
+
+LFM2_ATTENTION_LAYERS = (2, 5, 8, 10, 12, 14, 16, 18)  # 8 GQA layers among 30; the other 22 are short-conv
+
+
+def lfm2_2_6b_config():
+    """LFM2-2.6B-shaped hybrid (22 short-conv + 8 GQA layers, hidden 2048, FFN 10752)."""
+    from nanovllm_b200.config import HfConfig
+    kv = [8 if i in LFM2_ATTENTION_LAYERS else 0 for i in range(30)]
+    return HfConfig(vocab_size=65536, hidden_size=2048, intermediate_size=10752, num_hidden_layers=30,
+                    num_attention_heads=32, num_key_value_heads=8, head_dim=64, max_position_embeddings=128000,
+                    rms_norm_eps=1e-5, rope_theta=1_000_000.0, model_type="lfm2", architectures=["Lfm2ForCausalLM"],
+                    layer_types=["full_attention" if k else "conv" for k in kv], layer_kv_heads=kv, conv_l_cache=3,
+                    tie_word_embeddings=True, torch_dtype="bfloat16")
+
+
+# model -> (config builder, init seed, default batch, default prompt range, sampling, label)
+MODELS = {
+    "qwen3-8b": (qwen3_8b_config, 4, 128, (512, 8192), "greedy",
+                 "Qwen3-8B-shape (36L, H4096, 32/8 heads, hd128, I12288, V151936)"),
+    "gemma3-270m": (gemma3_270m_config, 2, 64, (128, 2048), "t0.7-p0.9",
+                    "Gemma3-270M-shape (18L, H640, 4/1 heads, hd256, GeGLU 2048, V262144, 5:1 sliding 512/global)"),
+    "lfm2-2.6b": (lfm2_2_6b_config, 3, 128, (256, 4096), "greedy",
+                  "LFM2-2.6B-shape (30L: 22 short-conv + 8 GQA 32/8 hd64, H2048, I10752, V65536)"),
+}
+
+
+def _pack_lfm2_q4_k_m(weights, dev):
+    """The Q4_K_M copy of config 4: projections as random Q4_K blocks, ffn_down as Q6_K (embeddings bf16)."""
+    import re
+    from nanovllm_b200.loaders.dequant import TYPE_BY_NAME
+    from nanovllm_b200.ops.quant import random_packed
+    proj = re.compile(r"(attn_q|attn_k|attn_v|attn_output|ffn_gate|ffn_up|ffn_down|in_proj|out_proj)\.weight$")
+    for i, name in enumerate(sorted(weights)):
+        if proj.search(name):
+            N, K = weights[name].shape
+            t = "Q6_K" if "ffn_down" in name else "Q4_K"
+            weights[name] = random_packed(TYPE_BY_NAME[t], N, K, 6000 + i, dev)
+
+
 def run_reference(args):
     line = {"impl": "reference",
             "unavailable": "the reference is a Java 21 / Maven CPU library: pip cannot install it (no setup.py or "
@@ -100,9 +149,13 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    hf = qwen3_8b_config()
-    weights = init_random_weights(hf, seed=4, device=dev)
-    if args.weights != "bf16":
+    cfg_fn, seed, _, _, sampling_kind, label = MODELS[args.model]
+    hf = cfg_fn()
+    weights = init_random_weights(hf, seed=seed, device=dev)
+    if args.weights == "q4_k_m":
+        _pack_lfm2_q4_k_m(weights, dev)
+        torch.cuda.empty_cache()
+    elif args.weights != "bf16":
         # the GGUF copy of config 5: every projection as random packed blocks, multiplied packed
         import re
         from nanovllm_b200.loaders.dequant import TYPE_BY_NAME
@@ -123,8 +176,13 @@ def run_ours(args):
                        gpu_memory_utilization=0.92, stop_on_degenerate=False, cuda_graph_max_bs=B)
     llm = LLM((hf, weights), cfg, device=dev)
     del weights
-    sp = SamplingParams(max_tokens=args.warmup + args.steps + extra + 8, ignore_eos=True).deterministic()
-    seqs = [llm.add_request(p, sp) for p in prompts]
+    n_new = args.warmup + args.steps + extra + 8
+    if sampling_kind == "greedy":
+        sps = [SamplingParams(max_tokens=n_new, ignore_eos=True).deterministic()] * B
+    else:  # config 3: temperature 0.7 / top-p 0.9, a fixed seed per request
+        sps = [SamplingParams(max_tokens=n_new, ignore_eos=True, temperature=0.7, top_p=0.9, seed=1000 + i)
+               for i in range(B)]
+    seqs = [llm.add_request(p, sp) for p, sp in zip(prompts, sps)]
     torch.cuda.synchronize()
     t_pf = time.perf_counter()
     while any(s.num_completion_tokens == 0 for s in seqs):
@@ -211,13 +269,16 @@ def run_ours(args):
         e2e = tokens / (wall_ms / 1000.0)
         line = {
             "impl": args.impl,
-            "metric": "decode tok/s (box, max over ranks) Qwen3-8B-shape TP1/2/4/8; p50 TTFT",
+            "metric": ("decode tok/s (box, max over ranks) Qwen3-8B-shape TP1/2/4/8; p50 TTFT"
+                       if args.model == "qwen3-8b" else f"decode tok/s (box, max over ranks) {args.model}"),
             "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None if BASELINE_VALUE is None else value / BASELINE_VALUE,
             "dtype": "bf16", "data": "synthetic: random-init weights (seed 4), random prompt ids",
-            "config": {"model": "Qwen3-8B-shape (36L, H4096, 32/8 heads, hd128, I12288, V151936)",
+            "config": {"model": label, "sampling": sampling_kind,
                        "weights": "bf16" if args.weights == "bf16" else
+                                  "GGUF Q4_K_M: projections Q4_K, ffn_down Q6_K, packed (dequant-fused GEMM); "
+                                  "embeddings / LM head bf16" if args.weights == "q4_k_m" else
                                   f"projections GGUF {args.weights.upper()} packed ("
                                   + ("dequantized per multiply, then cuBLAS" if args.impl == "baseline"
                                      else "dequant-fused GEMM") + "); embeddings / LM head bf16",
@@ -233,6 +294,95 @@ def run_ours(args):
             "clocks": _clock_summary(clock_path, local),
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        ps.destroy()
+
+
+def gte_small_config():
+    """gte-small-shaped BERT encoder (12 layers, hidden 384, 12 heads, GELU FFN 1536)."""
+    from nanovllm_b200.config import HfConfig
+    return HfConfig(vocab_size=30522, hidden_size=384, intermediate_size=1536, num_hidden_layers=12,
+                    num_attention_heads=12, num_key_value_heads=12, head_dim=32, max_position_embeddings=512,
+                    layer_norm_eps=1e-12, model_type="bert", architectures=["BertModel"], torch_dtype="float16")
+
+
+def run_embed(args):
+    """sentence embeddings, data-parallel over N GPUs (one replica per rank).
+
+    Every step embeds a global batch of ``--batch`` (default 256) sequences of random ids with lengths U[16, 512]:
+    the sequences are dealt to the ranks by token count (``parallel/dp.py``), each rank encodes its share as
+    packed varlen batches (tcgen05 GEMMs, varlen bidirectional attention, fused LayerNorm / GELU epilogues,
+    mean-pool + L2) and one all-gather returns all [batch, 384] embeddings to every rank.  ``value``: sequences
+    per second of device time (CUDA events around the step, max over ranks); ``e2e``: the same over host wall
+    time including the host->device copies of each step's ids and the device->host read of its embeddings."""
+    from nanovllm_b200.models.bert import BertEncoder
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel import state as ps
+    from nanovllm_b200.parallel.dp import DataParallelEmbedder
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        ps.init_tp("nccl", timeout_s=300)
+    rank = ps.tp_rank()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    hf = gte_small_config()
+    weights = init_random_weights(hf, seed=1, device=dev)
+    if args.weights == "q8_0":  # the GGUF Q8_0 copy: packed blocks, expanded once at load for the encoder GEMMs
+        from nanovllm_b200.loaders.dequant import TYPE_BY_NAME
+        from nanovllm_b200.ops.quant import random_packed
+        for i, name in enumerate(sorted(weights)):
+            if name.endswith(".weight") and weights[name].dim() == 2 and "embd" not in name:
+                N, K = weights[name].shape
+                weights[name] = random_packed(TYPE_BY_NAME["Q8_0"], N, K, 7000 + i, dev)
+    enc = BertEncoder(hf, weights, dev)
+    del weights
+    dp = DataParallelEmbedder(enc)
+    B = args.batch or 256
+    gen = torch.Generator().manual_seed(99)
+    batches = []
+    for _ in range(args.warmup + args.steps):
+        lens = torch.randint(16, 513, (B,), generator=gen)
+        batches.append([[101] + torch.randint(1000, hf.vocab_size, (int(n) - 2,), generator=gen).tolist() + [102]
+                        for n in lens])
+    for b in batches[:args.warmup]:
+        dp.embed_ids(b)
+    torch.cuda.synchronize()
+    ps.barrier()
+    dev_ms, tokens = 0.0, 0
+    t0 = time.perf_counter()
+    for b in batches[args.warmup:]:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = dp.embed_ids(b)
+        e1.record()
+        host = out.cpu()  # the step's result read back (D2H)
+        dev_ms += e0.elapsed_time(e1)
+        tokens += sum(len(x) for x in b)
+    torch.cuda.synchronize()
+    wall_ms = (time.perf_counter() - t0) * 1000.0
+    ps.barrier()
+    t = torch.tensor([dev_ms, wall_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    dev_ms, wall_ms = float(t[0]), float(t[1])
+    ok = bool(torch.allclose(host.norm(dim=1), torch.ones(B), atol=1e-2))
+    if rank == 0:
+        seqs = B * args.steps
+        print(json.dumps({
+            "impl": args.impl, "metric": "embeddings/s (sequences, max over ranks) gte-small-shape DP1/2/4/8",
+            "value": round(seqs / (dev_ms / 1000.0), 1), "unit": "sequences/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init weights (seed 1), random ids, lengths U[16,512]",
+            "config": {"model": "gte-small-shape BERT (12L, H384, 12 heads, FFN 1536, V30522, pos 512)",
+                       "weights": "GGUF Q8_0 blocks expanded at load" if args.weights == "q8_0" else "bf16",
+                       "global_batch": B, "seq_len": "U[16,512]", "parallelism": f"dp{world}",
+                       "tokens_per_s": round(tokens / (dev_ms / 1000.0), 1), "unit_norm_ok": ok},
+            "e2e": {"value": round(seqs / (wall_ms / 1000.0), 1), "unit": "sequences/s",
+                    "h2d_bytes_per_step": 16 * tokens // args.steps, "d2h_bytes_per_step": 4 * B * hf.hidden_size},
+        }), flush=True)
     if world > 1:
         ps.destroy()
 
@@ -341,15 +491,17 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--warmup", type=int, default=8)
-    ap.add_argument("--batch", type=int, default=128)
-    ap.add_argument("--min-prompt", type=int, default=512)
-    ap.add_argument("--max-prompt", type=int, default=8192)
+    ap.add_argument("--model", choices=sorted(MODELS) + ["gte-small"], default="qwen3-8b",
+                    help="BASELINE config: qwen3-8b (5, the headline), gemma3-270m (3), lfm2-2.6b (4), gte-small (2)")
+    ap.add_argument("--batch", type=int, default=None, help="concurrent requests (default per model)")
+    ap.add_argument("--min-prompt", type=int, default=None)
+    ap.add_argument("--max-prompt", type=int, default=None)
     ap.add_argument("--prefill-chunk", type=int, default=16384)
     ap.add_argument("--profile-steps", type=int, default=0,
                     help="decode steps run between cudaProfilerStart/Stop before the timed region")
     ap.add_argument("--impl", choices=["ours", "reference", "baseline"], default="ours",
                     help="baseline: this engine with cuBLAS GEMMs (separate activation kernel) and NCCL all-reduce")
-    ap.add_argument("--weights", choices=["bf16", "nvfp4", "q4_k", "q8_0", "mxfp4"], default="bf16",
+    ap.add_argument("--weights", choices=["bf16", "nvfp4", "q4_k", "q8_0", "mxfp4", "q4_k_m"], default=None,
                     help="projection weights: bf16, or random GGUF blocks kept packed (the NVFP4 copy of config 5)")
     ap.add_argument("--breakdown", default="",
                     help="path prefix: write a per-kernel device-time breakdown of 3 traced decode steps per rank")
@@ -364,6 +516,13 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.model in MODELS:
+        _, _, batch, (lo, hi), _, _ = MODELS[args.model]
+        args.batch = args.batch or batch
+        args.min_prompt = args.min_prompt or lo
+        args.max_prompt = args.max_prompt or hi
+    if args.weights is None:
+        args.weights = "q4_k_m" if args.model == "lfm2-2.6b" else "bf16"
     if args.impl == "reference":
         run_reference(args)
         return
@@ -371,6 +530,9 @@ def main():
         os.environ["NVB_BASELINE"] = "1"  # cuBLAS GEMMs + separate activation + NCCL all-reduce
     if args.serve:
         run_serve(args)
+        return
+    if args.model == "gte-small":
+        run_embed(args)
         return
     run_ours(args)
 

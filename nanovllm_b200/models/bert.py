@@ -4,8 +4,8 @@ Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/models/interna
 token + position + token-type(0) embeddings -> LayerNorm -> N post-LN blocks [biased q/k/v -> bidirectional MHA
 -> o -> LN(x + attn) -> GELU(tanh) FFN -> LN(x + ffn)] -> masked mean pool -> L2 normalise.  The reference
 encodes one text at a time; here a whole batch of variable-length sequences is packed into one [T, H] tensor
-(cu_seqlens) and run through the varlen bidirectional attention kernel, and batches can be spread data-parallel
-over GPUs (``embed_ids`` on each rank's shard).
+(cu_seqlens) and run through the varlen bidirectional attention kernel; ``parallel/dp.py`` spreads a batch
+data-parallel over GPUs (one replica per rank, token-balanced shares, one all-gather of the embeddings).
 """
 from __future__ import annotations
 

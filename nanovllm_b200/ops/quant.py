@@ -215,10 +215,16 @@ def shard_rows(w, rank: int, size: int):
 
 
 def shard_cols(w, rank: int, size: int):
+    """Row-parallel K shard.  A packed weight stays packed when the shard falls on 256-element boundaries; a
+    shard that would cut GGML super-blocks (e.g. LFM2's ffn_down K 10752 over TP 4 or 8) is expanded to bf16."""
     n = w.shape[1]
     assert n % size == 0, f"dimension {n} not divisible by TP={size}"
     k = n // size
-    return w.cols(rank * k, (rank + 1) * k) if is_packed(w) else w[:, rank * k:(rank + 1) * k]
+    if is_packed(w):
+        if k % STEP == 0:
+            return w.cols(rank * k, (rank + 1) * k)
+        w = w.dequantize(torch.bfloat16)
+    return w[:, rank * k:(rank + 1) * k]
 
 
 def cat_rows(parts):

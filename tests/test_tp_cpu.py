@@ -161,3 +161,54 @@ def test_lfm2_conv_layers_shard_channels_under_tp2():
         assert p.exitcode == 0
     assert got[0][0] == got[1][0] == want
     assert got[0][1] == hf.hidden_size // 2 and got[0][2][0] == hf.hidden_size // 2
+
+
+def _dp_run(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nanovllm_b200.models.bert import BertEncoder
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel import state as ps
+    from nanovllm_b200.parallel.dp import DataParallelEmbedder
+    from tests.test_models_cpu import bert_tiny
+    ps.init_tp("gloo")
+    hf = bert_tiny()
+    enc = BertEncoder(hf, init_random_weights(hf, 1), "cpu", torch.float32)
+    g = torch.Generator().manual_seed(4)
+    batch = [torch.randint(0, hf.vocab_size, (int(n),), generator=g).tolist()
+             for n in torch.randint(2, 100, (13,), generator=g)]
+    dp = DataParallelEmbedder(enc)
+    mine, _ = dp.shard(batch)
+    q.put((rank, dp.embed_ids(batch).numpy(), sum(len(batch[i]) for i in mine)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_bert_data_parallel_embeddings_match_single_process():
+    """BERT DP across 3 gloo ranks: token-balanced deal, replicas encode their share, one all-gather restores the
+    input order -- every rank returns the single-process embeddings."""
+    from nanovllm_b200.models.bert import BertEncoder
+    from nanovllm_b200.models.registry import init_random_weights
+    from nanovllm_b200.parallel.dp import deal_by_tokens
+    from tests.test_models_cpu import bert_tiny
+    hf = bert_tiny()
+    g = torch.Generator().manual_seed(4)
+    batch = [torch.randint(0, hf.vocab_size, (int(n),), generator=g).tolist()
+             for n in torch.randint(2, 100, (13,), generator=g)]
+    want = BertEncoder(hf, init_random_weights(hf, 1), "cpu", torch.float32).embed_ids(batch)
+    plan = deal_by_tokens([len(s) for s in batch], 3)
+    assert sorted(i for p in plan for i in p) == list(range(len(batch)))
+    loads = [sum(len(batch[i]) for i in p) for p in plan]
+    assert max(loads) - min(loads) <= max(len(s) for s in batch)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dp_run, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    got = {r: (torch.from_numpy(e), n) for r, e, n in (q.get(timeout=240) for _ in procs)}
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r, (emb, _) in got.items():
+        assert torch.allclose(emb, want, atol=1e-5), (r, (emb - want).abs().max())
