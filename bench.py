@@ -333,7 +333,7 @@ def run_embed(args):
         from nanovllm_b200.loaders.dequant import TYPE_BY_NAME
         from nanovllm_b200.ops.quant import random_packed
         for i, name in enumerate(sorted(weights)):
-            if name.endswith(".weight") and weights[name].dim() == 2 and "embd" not in name:
+            if name.startswith("blk.") and name.endswith(".weight") and weights[name].dim() == 2:
                 N, K = weights[name].shape
                 weights[name] = random_packed(TYPE_BY_NAME["Q8_0"], N, K, 7000 + i, dev)
     enc = BertEncoder(hf, weights, dev)

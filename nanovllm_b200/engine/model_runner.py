@@ -53,6 +53,7 @@ class ModelRunner:
         self.num_blocks = 0
         self.kv_arenas: List[torch.Tensor] = []
         self.state_arena: Optional[torch.Tensor] = None
+        self.state_capacity: Optional[int] = None  # live sequences the recurrent-state arena can hold
         self.state_rows: Dict[int, int] = {}
         self.free_state_rows: List[int] = []
         self.final_softcap = getattr(model, "final_softcap", 0.0)
@@ -124,7 +125,10 @@ class ModelRunner:
         if not specs:
             return
         width = sum(w for _, w in specs)
-        rows = self.cfg.max_num_seqs + 1
+        # live sequences can outnumber max_num_seqs (that caps each batch, not admission): keep twice as many rows;
+        # the scheduler admits no new sequence while every row is taken (``state_capacity``)
+        rows = 2 * self.cfg.max_num_seqs + 1
+        self.state_capacity = rows - 1
         self.state_arena = torch.zeros(rows, width, dtype=torch.float32, device=self.device)
         self.free_state_rows = list(range(rows - 1, 0, -1))  # row 0 is a scratch row for padding
         self.model.bind_state(self.state_arena)

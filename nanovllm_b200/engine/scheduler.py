@@ -29,8 +29,11 @@ from .sequence import Sequence, SequenceStatus
 
 class Scheduler:
     def __init__(self, cfg: EngineConfig, num_blocks: int, stop_token_ids: Seq[int] = (),
-                 on_release: Optional[Callable[[Sequence], None]] = None):
+                 on_release: Optional[Callable[[Sequence], None]] = None, max_live_seqs: Optional[int] = None):
         self.max_num_seqs = cfg.max_num_seqs
+        # models with per-sequence recurrent state (LFM2) hold one state row per live sequence: no new sequence
+        # is admitted while ``max_live_seqs`` are running or part-way through prefill
+        self.max_live_seqs = max_live_seqs
         self.max_num_batched_tokens = cfg.max_num_batched_tokens
         self.max_model_len = cfg.max_model_len
         self.block_size = cfg.kvcache_block_size
@@ -75,6 +78,9 @@ class Scheduler:
         if self.on_release is not None:
             self.on_release(seq)
 
+    def _live(self) -> int:
+        return len(self.running) + sum(1 for s in self.waiting if s.block_table)
+
     # ------------------------------------------------------------------ scheduling
     def schedule(self) -> Tuple[List[Sequence], bool]:
         batch = self._try_schedule_prefill()
@@ -92,6 +98,8 @@ class Scheduler:
             if remaining == 0:
                 break
             if not seq.block_table:
+                if self.max_live_seqs is not None and self._live() >= self.max_live_seqs:
+                    break
                 cached_blocks = bm.can_allocate(seq)
                 if cached_blocks == -1:
                     break

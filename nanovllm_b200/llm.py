@@ -105,7 +105,8 @@ class LLM:
         if self.model.state_specs():
             self.cfg.enable_prefix_caching = False
         self.runner = ModelRunner(self.model, hf, self.cfg, self.device)
-        self.scheduler = Scheduler(self.cfg, self.runner.num_blocks, stop, on_release=self.runner.release_state)
+        self.scheduler = Scheduler(self.cfg, self.runner.num_blocks, stop, on_release=self.runner.release_state,
+                                   max_live_seqs=self.runner.state_capacity)
         self._lock = threading.Lock()
         self._cancel = threading.Event()
         self._closed = False

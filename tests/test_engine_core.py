@@ -191,3 +191,20 @@ def test_abort_and_clear_release_blocks():
     assert sch.abort(a.seq_id) and a in released
     sch.clear()
     assert sch.block_manager.num_free_blocks == 8 and sch.is_finished()
+
+
+def test_scheduler_caps_live_sequences_for_recurrent_state():
+    """With a state arena of N rows no (N+1)-th sequence is admitted until one finishes."""
+    from nanovllm_b200.config import EngineConfig
+    from nanovllm_b200.engine.scheduler import Scheduler
+    from nanovllm_b200.engine.sequence import Sequence
+    from nanovllm_b200.sampling_params import SamplingParams
+    cfg = EngineConfig(max_num_seqs=2, max_model_len=1024, kvcache_block_size=256, max_num_batched_tokens=4096)
+    sch = Scheduler(cfg, 64, max_live_seqs=3)
+    seqs = [Sequence(list(range(10)), SamplingParams(max_tokens=4, ignore_eos=True), 256) for _ in range(5)]
+    for s in seqs:
+        sch.add(s)
+    first, pf = sch.schedule()
+    second, pf2 = sch.schedule()
+    assert pf and pf2 and len(first) == 2 and len(second) == 1  # the batch cap, then the live cap
+    assert len(sch.running) == 3 and len(sch.waiting) == 2
