@@ -27,7 +27,7 @@ class VocabParallelEmbedding:
             per = (self.vocab + s - 1) // s
             self.vstart = r * per
             self.vend = min(self.vocab, (r + 1) * per)
-            self.weight = weight[self.vstart:self.vend].contiguous()
+            self.weight = weight[self.vstart:self.vend].clone()  # a copy: the full table can be freed
         else:
             self.vstart, self.vend, self.weight = 0, self.vocab, weight
         self.scale = scale
@@ -62,9 +62,11 @@ class ParallelLMHead:
             per = (self.vocab + s - 1) // s
             self.vstart, self.ncols = r * per, max(0, min(self.vocab, (r + 1) * per) - r * per)
             w = weight[r * per:min(self.vocab, (r + 1) * per)]
-            if w.shape[0] < per:  # pad the last shard so all_gather sees equal shapes
+            if w.shape[0] < per:  # pad the last shard so all_gather sees equal shapes (torch.cat copies)
                 w = torch.cat([w, torch.zeros(per - w.shape[0], w.shape[1], dtype=w.dtype, device=w.device)])
-            self.weight = w.contiguous()
+            else:
+                w = w.clone()  # a row slice is a view of the full head: copy it so the full tensor can be freed
+            self.weight = w
         else:
             self.vstart, self.ncols = 0, self.vocab
             self.weight = weight

@@ -87,7 +87,9 @@ class LLM:
             tokenizer = None
         self.hf: HfConfig = hf
         self.tokenizer = tokenizer
-        self.model_handle = model
+        # keep the LlmModel handle (think tags, options, engine refcount); a bare (config, weights) tuple is not
+        # kept: the graph holds this rank's (sharded) copies, and the full tensors can be freed by the caller
+        self.model_handle = model if isinstance(model, LlmModel) else None
         self.cfg = cfg or EngineConfig()
         self.cfg.clamp_to_model(hf)
         self.default_sampling = sampling or SamplingParams()

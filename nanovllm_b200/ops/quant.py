@@ -208,10 +208,12 @@ def is_packed(w) -> bool:
 
 
 def shard_rows(w, rank: int, size: int):
+    """Column-parallel row shard; a dense shard is a copy, so the full tensor is freed once the loader drops it
+    (a row slice is a view that would keep all TP shards alive on every rank)."""
     n = w.shape[0]
     assert n % size == 0, f"dimension {n} not divisible by TP={size}"
     k = n // size
-    return w.rows(rank * k, (rank + 1) * k) if is_packed(w) else w[rank * k:(rank + 1) * k]
+    return w.rows(rank * k, (rank + 1) * k) if is_packed(w) else w[rank * k:(rank + 1) * k].clone()
 
 
 def shard_cols(w, rank: int, size: int):
