@@ -127,7 +127,7 @@ class GgufPacked:
 
     # ---------------------------------------------------------------- sharding (row-parallel splits K)
     def rows(self, a: int, b: int) -> "GgufPacked":
-        return GgufPacked(self._need_raw()[a:b], self.ggml_type, b - a, self.K)
+        return GgufPacked(self._need_raw()[a:b].clone(), self.ggml_type, b - a, self.K)  # a copy, not a view
 
     def cols(self, a: int, b: int) -> "GgufPacked":
         be, bb = DQ.block_info(self.ggml_type)
