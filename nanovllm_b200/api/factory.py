@@ -45,6 +45,13 @@ def _load_device(device) -> torch.device:
 
 class LlmModelFactory:
     @staticmethod
+    def catalog(path):
+        """Bind ``path`` from its headers only (architecture, config, tensor names / shapes / types), without
+        reading any tensor payload; ``.require_complete()`` checks it against the architecture's schema."""
+        from ..loaders.catalog import ContainerCatalog
+        return ContainerCatalog.bind(path)
+
+    @staticmethod
     def make(path, options: Optional[dict] = None, device=None, dtype=torch.bfloat16) -> LlmModel:
         """``path``: a model folder, a .gguf file, or a ``ModelFileSource`` (api.sources)."""
         from .sources import ModelFileSource

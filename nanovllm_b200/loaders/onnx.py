@@ -148,8 +148,9 @@ def _node_weight_name(node_name: str) -> Optional[str]:
     return ".".join(parts[:-1]) + ".weight"
 
 
-def read_initializers(path: str) -> Dict[str, torch.Tensor]:
-    """All loadable float weights of an ONNX file, MatMul operands transposed to [out, in]."""
+def _scan(path: str):
+    """(initializer records by name, MatMul B-operand name -> node name): the graph structure only; no tensor
+    payload is decoded."""
     with open(path, "rb") as f:
         data = f.read()
     graph = None
@@ -176,6 +177,34 @@ def read_initializers(path: str) -> Dict[str, torch.Tensor]:
                     op = pw.as_str(v2)
             if op == "MatMul" and len(ins) >= 2:
                 matmul_b[ins[1]] = name
+    return inits, matmul_b
+
+
+def _graph_name(name: str, matmul_b: Dict[str, str]) -> str:
+    if name in matmul_b and "onnx::" in name:
+        alias = _node_weight_name(matmul_b[name])
+        if alias is not None:
+            return alias
+    return name
+
+
+def initializer_infos(path: str) -> Dict[str, tuple]:
+    """name -> (shape as loaded, ONNX data_type) of every loadable weight, from the graph records alone (MatMul
+    operands reported transposed to [out, in]); used to bind a model before reading any payload."""
+    inits, matmul_b = _scan(path)
+    out: Dict[str, tuple] = {}
+    for name, t in inits.items():
+        if t.dtype in _LOADABLE and len(t.dims) >= 1:
+            dims = tuple(int(d) for d in t.dims)
+            if name in matmul_b and len(dims) == 2:
+                dims = (dims[1], dims[0])
+            out[_graph_name(name, matmul_b)] = (dims, int(t.dtype))
+    return out
+
+
+def read_initializers(path: str) -> Dict[str, torch.Tensor]:
+    """All loadable float weights of an ONNX file, MatMul operands transposed to [out, in]."""
+    inits, matmul_b = _scan(path)
     base = os.path.dirname(os.path.abspath(path))
     out: Dict[str, torch.Tensor] = {}
     for name, t in inits.items():
@@ -184,11 +213,7 @@ def read_initializers(path: str) -> Dict[str, torch.Tensor]:
             w = _tensor_to_torch(t, base)
             if name in matmul_b:
                 w = w.t().contiguous() if w.dim() == 2 else w
-                if "onnx::" in name:
-                    alias = _node_weight_name(matmul_b[name])
-                    if alias is not None:
-                        name = alias
-            out[name] = w
+            out[_graph_name(name, matmul_b)] = w
         elif t.dtype in _SKIP or rank == 0:
             continue
         else:
