@@ -46,10 +46,14 @@ class LlmListeners:
         return lambda source, ev: None
 
     @staticmethod
-    def to_print_streams(out: TextIO = sys.stdout, err: TextIO = sys.stderr) -> LlmListener:
-        """Assistant text to ``out``; thinking, status and diagnostics to ``err``."""
+    def to_print_streams(out: Optional[TextIO] = None, err: Optional[TextIO] = None) -> LlmListener:
+        """Assistant text to ``out``; thinking, status and diagnostics to ``err`` (default: the process's
+        stdout / stderr at the time of each event)."""
         def listener(source, ev: LlmTextEvent):
-            stream = out if ev.kind == LlmTextKind.TEXT_ASSISTANT else err
+            if ev.kind == LlmTextKind.TEXT_ASSISTANT:
+                stream = out if out is not None else sys.stdout
+            else:
+                stream = err if err is not None else sys.stderr
             if ev.kind in (LlmTextKind.TEXT_RAW, LlmTextKind.TEXT_DEBUG):
                 return
             stream.write(ev.text)
