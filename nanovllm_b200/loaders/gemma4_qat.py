@@ -101,6 +101,30 @@ class QatWeight:
         s = self.scales.reshape(self.rows, self.scale_cols).float().repeat_interleave(block, dim=1)
         return (self.unpack() * s).to(dtype)
 
+    def to_gguf_blocks(self):
+        """The same integers as GGUF blocks the dequant-fused GEMM multiplies in place: int4 and int2 codes as
+        Q4_0 (value = nibble - 8; 2-bit codes ride in the 4-bit container), int8 as Q8_0.  Every 32-element
+        block takes its (row, column block) scale rounded to fp16 -- the only change to the values: a relative
+        error of at most 2^-11 on each scale, finer than the bf16 rounding of every weight that expanding to
+        bf16 would cost.  None when the layout cannot be expressed (scale blocks not a multiple of 32 columns,
+        or a width the fused kernel does not take)."""
+        from ..ops.quant import STEP, GgufPacked
+        block = self.cols // self.scale_cols
+        if block % 32 or self.cols % STEP:
+            return None
+        q = self.unpack().to(torch.int16)                                      # [rows, cols]
+        s32 = self.scales.reshape(self.rows, self.scale_cols).float().repeat_interleave(block // 32, dim=1)
+        d = s32.to(torch.float16).contiguous().view(torch.uint8).reshape(self.rows, -1, 2)
+        nblk = self.cols // 32
+        if self.bits == 8:
+            codes = q.to(torch.int8).reshape(self.rows, nblk, 32).view(torch.uint8)
+            blocks, t = torch.cat([d, codes], -1), 8                           # Q8_0: d | 32 x int8
+        else:
+            u = (q + 8).to(torch.uint8).reshape(self.rows, nblk, 32)
+            codes = u[..., :16] | (u[..., 16:] << 4)                           # Q4_0: element i low, i + 16 high
+            blocks, t = torch.cat([d, codes], -1), 2
+        return GgufPacked(blocks.reshape(-1).contiguous(), t, self.rows, self.cols)
+
     def dequantize_row(self, r: int) -> torch.Tensor:
         one = QatWeight(self.name, self.packed.reshape(self.rows, -1)[r:r + 1].contiguous(),
                         self.scales.reshape(self.rows, -1)[r:r + 1].contiguous(), 1, self.cols, self.bits,

@@ -22,6 +22,7 @@ one kernel.  Tensor parallelism is not offered for this family (mobile-sized mod
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, List, Optional, Sequence
 
 import torch
@@ -31,6 +32,7 @@ from ..config import HfConfig
 from ..layers.attention import Attention
 from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
 from ..layers.norms import RMSNorm, RotaryTables
+from ..ops.quant import cat_rows
 from ..parallel import state as tp
 from .base import CausalLMBase, WeightBag, random_weights
 
@@ -80,14 +82,36 @@ def _srq_scales(t) -> tuple:
     return (float(getattr(t, "in_scale", 0.0)), float(getattr(t, "out_scale", 0.0)))
 
 
+def _packed(w) -> bool:
+    return not isinstance(w, torch.Tensor) and hasattr(w, "linear")
+
+
+def qat_group_weights(bag, names: Sequence[str], device) -> list:
+    """The group's weights as GGUF blocks for the dequant-fused GEMM (QatWeight.to_gguf_blocks) when every
+    member converts and packed execution is on (a CUDA device unless NVB_GGUF_PACKED=0; "force" also on the
+    CPU), else dense bf16 for all members -- one GEMM never mixes the two."""
+    mode = os.environ.get("NVB_GGUF_PACKED", "1")
+    on = mode == "force" or (torch.device(device).type == "cuda" and mode not in ("0", "false", "no"))
+    if on:
+        raws = [bag.tensors.get(n) for n in names]
+        blocks = [r.to_gguf_blocks() if hasattr(r, "to_gguf_blocks") else None for r in raws]
+        if all(b is not None for b in blocks):
+            for n in names:
+                bag.used.add(n)
+            return [b.to_device(device) for b in blocks]
+    return [bag.dense(n) for n in names]
+
+
 class QatLinearGroup:
     """One GEMM over several packed projections that read the same input (q/k/v or gate/up).
 
     SRQ: the input is fake-quantised once when every member shares its input scale (else each member runs its
     own GEMM on its own quantised copy); output SRQ is applied per member column range.  ``gelu_mul`` (members
-    = [gate, up]) fuses GELU-tanh(gate) * up into the GEMM epilogue when no member has an output scale."""
+    = [gate, up]) fuses GELU-tanh(gate) * up into the GEMM epilogue when no member has an output scale.
+    Members are dense bf16 tensors or GGUF blocks (``qat_group_weights``): packed members are multiplied by the
+    dequant-fused GEMM without ever being expanded in memory (the QAT integers stay 4 / 8-bit on the device)."""
 
-    def __init__(self, weights: Sequence[torch.Tensor], srq: Sequence[tuple], gelu_mul: bool = False):
+    def __init__(self, weights: Sequence, srq: Sequence[tuple], gelu_mul: bool = False):
         self.widths = [int(w.shape[0]) for w in weights]
         self.in_scales = [s[0] for s in srq]
         self.out_scales = [s[1] for s in srq]
@@ -95,23 +119,39 @@ class QatLinearGroup:
         self.shared_in = len(set(self.in_scales)) == 1
         self.fused_act = gelu_mul and not any(self.out_scales) and self.widths[0] % 128 == 0
         if self.fused_act:
-            self.w = ops.ref.interleave_gate_up(torch.cat([weights[0], weights[1]], 0)).contiguous()
+            if _packed(weights[0]):
+                gu = cat_rows([weights[0], weights[1]])
+                order = ops.ref.interleave_gate_up(torch.arange(gu.shape[0]).unsqueeze(1), 128).squeeze(1)
+                self.w = gu.permute_rows(order)
+            else:
+                self.w = ops.ref.interleave_gate_up(torch.cat([weights[0], weights[1]], 0)).contiguous()
         elif self.shared_in:
-            self.w = torch.cat(list(weights), 0).contiguous() if len(weights) > 1 else weights[0].contiguous()
+            if len(weights) > 1:
+                self.w = cat_rows(list(weights))
+                self.w = self.w if _packed(self.w) else self.w.contiguous()
+            else:
+                self.w = weights[0] if _packed(weights[0]) else weights[0].contiguous()
         else:
-            self.ws = [w.contiguous() for w in weights]
+            self.ws = [w if _packed(w) else w.contiguous() for w in weights]
 
     @staticmethod
     def _quant_in(x, s):
         return ops.srq_(ops.materialize(x).clone(), s) if s else x
 
+    @staticmethod
+    def _mm(x, w, act: int = ops.ACT_NONE):
+        if _packed(w):
+            y = w.linear(ops.materialize(x))
+            return ops.act_mul(y, act, interleaved=True) if act != ops.ACT_NONE else y
+        return ops.linear(x, w, act)
+
     def __call__(self, x):
         if self.fused_act:
-            return ops.linear(self._quant_in(x, self.in_scales[0]), self.w, ops.ACT_GELU_MUL)
+            return self._mm(self._quant_in(x, self.in_scales[0]), self.w, ops.ACT_GELU_MUL)
         if self.shared_in:
-            y = ops.materialize(ops.linear(self._quant_in(x, self.in_scales[0]), self.w))
+            y = ops.materialize(self._mm(self._quant_in(x, self.in_scales[0]), self.w))
         else:
-            y = torch.cat([ops.materialize(ops.linear(self._quant_in(x, s), w))
+            y = torch.cat([ops.materialize(self._mm(self._quant_in(x, s), w))
                            for w, s in zip(self.ws, self.in_scales)], 1)
         off = 0
         for width, s in zip(self.widths, self.out_scales):
@@ -162,9 +202,11 @@ class Gemma4ForCausalLM(CausalLMBase):
             Ly.scalar = float(bag.require(p + "layer_scalar").float().reshape(-1)[0])
             names = ["q_proj"] if shared else ["q_proj", "k_proj", "v_proj"]
             raw = [bag.require(p + f"self_attn.{n}.weight") for n in names]
-            Ly.qkv = QatLinearGroup([bag.dense(p + f"self_attn.{n}.weight") for n in names], [_srq_scales(r) for r in raw])
+            Ly.qkv = QatLinearGroup(qat_group_weights(bag, [p + f"self_attn.{n}.weight" for n in names], device),
+                                    [_srq_scales(r) for r in raw])
             o_raw = bag.require(p + "self_attn.o_proj.weight")
-            Ly.o_proj = QatLinearGroup([bag.dense(p + "self_attn.o_proj.weight")], [_srq_scales(o_raw)])
+            Ly.o_proj = QatLinearGroup(qat_group_weights(bag, [p + "self_attn.o_proj.weight"], device),
+                                       [_srq_scales(o_raw)])
             rope = (self.rope.get(hd, hf.rope_local_base_freq) if sliding
                     else self.rope.get(hd, hf.rope_theta, g4.full_partial_rotary_factor))
             q_norm = bag.require(p + "self_attn.q_norm.weight")
@@ -173,14 +215,16 @@ class Gemma4ForCausalLM(CausalLMBase):
                                 k_norm, 0, eps, v_norm=not shared, window=hf.layer_window(i),
                                 softcap=hf.attn_logit_softcapping, write_kv=not shared, q_only=shared)
             g_raw, u_raw = bag.require(p + "mlp.gate_proj.weight"), bag.require(p + "mlp.up_proj.weight")
-            Ly.gate_up = QatLinearGroup([bag.dense(p + "mlp.gate_proj.weight"), bag.dense(p + "mlp.up_proj.weight")],
-                                        [_srq_scales(g_raw), _srq_scales(u_raw)], gelu_mul=True)
+            Ly.gate_up = QatLinearGroup(qat_group_weights(bag, [p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"],
+                                                          device), [_srq_scales(g_raw), _srq_scales(u_raw)], gelu_mul=True)
             d_raw = bag.require(p + "mlp.down_proj.weight")
-            Ly.down = QatLinearGroup([bag.dense(p + "mlp.down_proj.weight")], [_srq_scales(d_raw)])
+            Ly.down = QatLinearGroup(qat_group_weights(bag, [p + "mlp.down_proj.weight"], device), [_srq_scales(d_raw)])
             pg_raw = bag.require(p + "per_layer_input_gate.weight")
-            Ly.ple_gate = QatLinearGroup([bag.dense(p + "per_layer_input_gate.weight")], [_srq_scales(pg_raw)])
+            Ly.ple_gate = QatLinearGroup(qat_group_weights(bag, [p + "per_layer_input_gate.weight"], device),
+                                         [_srq_scales(pg_raw)])
             pp_raw = bag.require(p + "per_layer_projection.weight")
-            Ly.ple_proj = QatLinearGroup([bag.dense(p + "per_layer_projection.weight")], [_srq_scales(pp_raw)])
+            Ly.ple_proj = QatLinearGroup(qat_group_weights(bag, [p + "per_layer_projection.weight"], device),
+                                         [_srq_scales(pp_raw)])
             self.layers.append(Ly)
         self.norm = RMSNorm(bag.require("model.norm.weight"), eps)
         head = bag.dense("lm_head.weight") if bag.has("lm_head.weight") else emb

@@ -198,3 +198,53 @@ def test_gemma4_qat_folder_round_trip(tmp_path):
     llm = LLM(model, _cfg(), device="cpu")
     toks = llm.generate_token_ids([list(range(5, 25))], SamplingParams(max_tokens=4, ignore_eos=True).deterministic())
     assert len(toks[0].token_ids) == 4
+
+
+def test_gemma4_qat_projections_run_packed(tmp_path, monkeypatch):
+    """QAT int4 / int2 / int8 projections become GGUF Q4_0 / Q8_0 blocks for the dequant-fused GEMM (no bf16
+    expansion): same logits as the expanded path within the fp16 rounding of the block scales."""
+    from nanovllm_b200.api.factory import LlmModelFactory
+    from nanovllm_b200.models.gemma4 import QatLinearGroup
+    from nanovllm_b200.models.writers import byte_level_tokenizer_json
+    hf = gemma4_tiny(hidden_size=256, intermediate_size=256)
+    dense = init_random_weights(hf, 8)
+    d = write_gemma4_qat_folder(str(tmp_path / "g4p"), hf, dense, scale_cols=4,
+                                tokenizer_json=byte_level_tokenizer_json(300))
+    ids = list(range(5, 37))
+    monkeypatch.setenv("NVB_GGUF_PACKED", "0")
+    want = _engine_logits(LLM(LlmModelFactory.make(d, device="cpu"), _cfg(), device="cpu"), ids).float()
+    monkeypatch.setenv("NVB_GGUF_PACKED", "force")
+    llm = LLM(LlmModelFactory.make(d, device="cpu"), _cfg(), device="cpu")
+    groups = [g for L in llm.model.layers for g in (L.qkv, L.o_proj, L.gate_up, L.down)]
+    packed = [g for g in groups if not isinstance(getattr(g, "w", None), torch.Tensor) and hasattr(g, "w")]
+    assert packed, "no projection took the packed path"
+    assert all(isinstance(g, QatLinearGroup) for g in groups)
+    got = _engine_logits(llm, ids).float()
+    assert torch.nn.functional.cosine_similarity(got, want, dim=0) > 0.999
+    assert (got - want).abs().max() < 0.05
+
+
+@pytest.mark.gpu
+def test_gemma4_qat_packed_gemm_on_gpu(tmp_path, monkeypatch):
+    """On the GPU the converted QAT projections run the dequant-fused tcgen05 GEMM (decode) and the dequant +
+    dense GEMM (prefill); tokens and logits agree with the bf16-expanded engine."""
+    from nanovllm_b200 import ops
+    from nanovllm_b200.api.factory import LlmModelFactory
+    from nanovllm_b200.models.writers import byte_level_tokenizer_json
+    hf = gemma4_tiny(hidden_size=256, intermediate_size=256)
+    d = write_gemma4_qat_folder(str(tmp_path / "g4g"), hf, init_random_weights(hf, 8), scale_cols=4,
+                                tokenizer_json=byte_level_tokenizer_json(300))
+    ids = list(range(5, 37))
+    dev = torch.device("cuda", 0)
+    monkeypatch.setenv("NVB_GGUF_PACKED", "0")
+    dense = LLM(LlmModelFactory.make(d, device="cpu"), _cfg(), device=dev)
+    want = _engine_logits(dense, ids).float().cpu()
+    dense.close()
+    monkeypatch.setenv("NVB_GGUF_PACKED", "1")
+    llm = LLM(LlmModelFactory.make(d, device="cpu"), _cfg(), device=dev)
+    got = _engine_logits(llm, ids).float().cpu()
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    assert torch.nn.functional.cosine_similarity(got, want, dim=0) > 0.999
+    out = llm.generate_token_ids([ids], SamplingParams(max_tokens=4, ignore_eos=True).deterministic())
+    assert len(out[0].token_ids) == 4
