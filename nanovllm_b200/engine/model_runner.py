@@ -26,6 +26,7 @@ import torch
 from .. import ops
 from ..config import EngineConfig, HfConfig
 from ..parallel import state as ps
+from ..utils.trace import nvtx
 from .context import StepContext, set_context
 from .sequence import Sequence
 
@@ -323,8 +324,10 @@ class ModelRunner:
     def run(self, seqs: List[Sequence], is_prefill: bool) -> List[int]:
         self._started = False
         self.last_h2d_bytes = 0
-        logits = self.forward_logits(seqs, is_prefill)
-        toks = self.sample(logits, seqs)
+        with nvtx("forward"):
+            logits = self.forward_logits(seqs, is_prefill)
+        with nvtx("sample"):
+            toks = self.sample(logits, seqs)
         if self.is_cuda:
             # the device error word rides back with the sampled tokens (4 bytes on the same synchronisation): a
             # bounded wait that gave up during this step surfaces here instead of as silently wrong tokens

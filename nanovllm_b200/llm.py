@@ -28,6 +28,7 @@ from .engine.sequence import Sequence
 from .exceptions import (GenerationCancelledException, GenerationTimeoutException, NanoLlvmException,
                          TensorParallelAbort)
 from .parallel import state as ps
+from .utils.trace import nvtx
 from .sampling_params import SamplingParams
 
 
@@ -201,9 +202,11 @@ class LLM:
 
     def step(self, appended_out: Optional[list] = None):
         ps.check_abort()  # a peer rank failed: stop before launching anything that would wait for it
-        seqs, is_prefill = self.scheduler.schedule()
+        with nvtx("schedule"):
+            seqs, is_prefill = self.scheduler.schedule()
         try:
-            toks = self.runner.run(seqs, is_prefill)
+            with nvtx("step:prefill" if is_prefill else "step:decode"):
+                toks = self.runner.run(seqs, is_prefill)
         except BaseException as e:
             # a communication error usually means a peer failed first (its connection closed, or the process-group
             # timeout released this rank): give its abort reason a moment to reach the store before blaming itself
@@ -212,7 +215,8 @@ class LLM:
                 raise TensorParallelAbort(ps.abort_reason()) from e
             ps.signal_abort(f"{type(e).__name__}: {e}")
             raise
-        finished = self.scheduler.postprocess(seqs, toks, is_prefill, appended_out)
+        with nvtx("postprocess"):
+            finished = self.scheduler.postprocess(seqs, toks, is_prefill, appended_out)
         for s in finished:
             s.t_finish = time.perf_counter()
         return seqs, is_prefill, finished

@@ -208,3 +208,14 @@ def test_scheduler_caps_live_sequences_for_recurrent_state():
     second, pf2 = sch.schedule()
     assert pf and pf2 and len(first) == 2 and len(second) == 1  # the batch cap, then the live cap
     assert len(sch.running) == 3 and len(sch.waiting) == 2
+
+
+def test_nvtx_ranges_are_off_by_default_and_harmless_on_cpu():
+    from nanovllm_b200.utils import trace
+    assert not trace.enabled()
+    trace.set_enabled(True)
+    try:
+        with trace.nvtx("x"):  # no CUDA here: a no-op, not an error
+            pass
+    finally:
+        trace.set_enabled(False)
