@@ -54,11 +54,14 @@ __host__ __device__ constexpr int q_aslots(int bn) { return (int)((512u - q_acol
 constexpr int kQMaxXS = 4;                // activation ring stages in streaming mode (at most)
 
 // GGML type ids (the GGUF on-disk codes)
-constexpr int T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ4_NL = 20,
-              T_IQ4_XS = 23, T_MXFP4 = 39, T_NVFP4 = 40;
+constexpr int T_Q4_0 = 2, T_Q4_1 = 3, T_Q5_0 = 6, T_Q5_1 = 7, T_Q8_0 = 8, T_Q2_K = 10, T_Q3_K = 11, T_Q4_K = 12,
+              T_Q5_K = 13, T_Q6_K = 14, T_IQ4_NL = 20, T_IQ4_XS = 23, T_TQ1_0 = 34, T_TQ2_0 = 35, T_MXFP4 = 39,
+              T_NVFP4 = 40;
 
+// bytes of one 256-element row step in the repacked layout (a multiple of 16: bulk copies and uint2 loads)
 __host__ __device__ constexpr int row_step_bytes(int t) {
-  return t == T_Q4_1 ? 160 : t == T_Q8_0 ? 272 : t == T_Q5_K ? 176 : t == T_Q6_K ? 224 : 144;
+  return t == T_Q4_1 ? 160 : t == T_Q8_0 ? 272 : t == T_Q5_K ? 176 : t == T_Q6_K ? 224 : t == T_Q5_0 ? 176
+       : t == T_Q5_1 ? 192 : t == T_Q2_K ? 96 : t == T_Q3_K ? 112 : t == T_TQ1_0 ? 64 : t == T_TQ2_0 ? 80 : 144;
 }
 
 __device__ __forceinline__ float h2f(const uint8_t* p) {
@@ -151,6 +154,79 @@ __device__ __forceinline__ void decode8(const uint8_t* __restrict__ p, int e0, c
     const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 16 + b * 16 + (ei >> 1));
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = d * L.fp4[(w >> (4 * j)) & 0xF];
+  } else if constexpr (TYPE == T_Q5_0 || TYPE == T_Q5_1) {
+    // d[8] | (m[8]) | qh[8] (u32, bit i = fifth bit of element i) | qs[8][16] (low nibbles 0..15, high 16..31)
+    constexpr int kM = TYPE == T_Q5_1 ? 16 : 0;
+    const int b = e0 >> 5, i0 = e0 & 31;
+    const float d = h2f(p + 2 * b);
+    const uint32_t qh = *reinterpret_cast<const uint32_t*>(p + 16 + kM + 4 * b) >> i0;
+    uint8_t q[8];
+    load8(p + 48 + kM + b * 16 + (i0 & 15), q);
+    const bool hi = i0 >= 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = (hi ? (q[j] >> 4) : (q[j] & 0xF)) | (int)(((qh >> j) & 1) << 4);
+      if constexpr (TYPE == T_Q5_0) v[j] = d * (float)(n - 16);
+      else v[j] = d * (float)n + h2f(p + 16 + 2 * b);
+    }
+  } else if constexpr (TYPE == T_Q2_K || TYPE == T_Q3_K || TYPE == T_TQ2_0) {
+    // 2-bit planes: byte (half * 32 + l) holds elements half * 128 + j * 32 + l at bits 2j (j = 0..3)
+    const int half = e0 >> 7, j2 = (e0 >> 5) & 3, l0 = e0 & 31;
+    constexpr int kQs = TYPE == T_Q2_K ? 16 : TYPE == T_Q3_K ? 32 : 0;
+    uint8_t q[8];
+    load8(p + kQs + half * 32 + l0, q);
+    if constexpr (TYPE == T_Q2_K) {
+      // scales[16] (low nibble scale, high nibble min; one per 16 elements) | qs[64] | d | dmin
+      const uint32_t sc = p[half * 8 + j2 * 2 + (l0 >> 4)];
+      const float dl = h2f(p + 80) * (float)(sc & 0xF), ml = h2f(p + 82) * (float)(sc >> 4);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = dl * (float)((q[j] >> (2 * j2)) & 3) - ml;
+    } else if constexpr (TYPE == T_Q3_K) {
+      // hmask[32] | qs[64] | 12 bytes of 6-bit scales (+32 bias) | d; a clear hmask bit subtracts 4
+      const int si = half * 8 + j2 * 2 + (l0 >> 4), w = si >> 2, k = si & 3;
+      const uint32_t lo = (uint32_t)p[96 + ((w & 1) ? 4 : 0) + k] >> ((w >> 1) * 4);
+      const int sc = (int)((lo & 0xF) | ((((uint32_t)p[104 + k] >> (2 * w)) & 3) << 4)) - 32;
+      const float dl = h2f(p + 108) * (float)sc;
+      uint8_t h[8];
+      load8(p + l0, h);
+      const int hb = half * 4 + j2;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = dl * (float)((int)((q[j] >> (2 * j2)) & 3) - (((h[j] >> hb) & 1) ? 0 : 4));
+    } else {  // TQ2_0: qs[64] | d, value d * (q - 1)
+      const float d = h2f(p + 64);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = d * (float)((int)((q[j] >> (2 * j2)) & 3) - 1);
+    }
+  } else if constexpr (TYPE == T_TQ1_0) {
+    // base-3 digits: bytes 0..31 carry 5 digits (elements k * 32 + m), bytes 32..47 carry 5 (160 + k * 16 + m),
+    // bytes 48..51 carry 4 (240 + k * 4 + m); digit k of byte x is ((x * 3^k mod 256) * 3) >> 8, minus 1
+    const float d = h2f(p + 52);
+    int kd[8];
+    uint8_t x[8];
+    if (e0 < 160) {
+      load8(p + (e0 & 31), x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kd[j] = e0 >> 5;
+    } else if (e0 < 240) {
+      load8(p + 32 + ((e0 - 160) & 15), x);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) kd[j] = (e0 - 160) >> 4;
+    } else {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(p + 48);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = e0 - 240 + j;
+        kd[j] = e >> 2;
+        x[j] = (uint8_t)(w >> (8 * (e & 3)));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t pw = kd[j] == 0 ? 1u : kd[j] == 1 ? 3u : kd[j] == 2 ? 9u : kd[j] == 3 ? 27u : 81u;
+      const uint32_t r = ((uint32_t)x[j] * pw) & 0xFF;
+      v[j] = d * (float)((int)((r * 3) >> 8) - 1);
+    }
   } else {
     // 32-element blocks with 16 quant bytes: elements 0..15 low nibbles, 16..31 high nibbles
     const int b = e0 >> 5, i0 = e0 & 31;
@@ -750,8 +826,9 @@ int q_num_sms() {
 }
 
 bool q_type_supported(int t) {
-  return t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_IQ4_NL ||
-         t == T_IQ4_XS || t == T_MXFP4 || t == T_NVFP4;
+  return t == T_Q4_0 || t == T_Q4_1 || t == T_Q5_0 || t == T_Q5_1 || t == T_Q8_0 || t == T_Q2_K || t == T_Q3_K ||
+         t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_IQ4_NL || t == T_IQ4_XS || t == T_TQ1_0 ||
+         t == T_TQ2_0 || t == T_MXFP4 || t == T_NVFP4;
 }
 
 // K split: the resident activation slice (BN x kper*256 bf16) must fit kQXBytes, the splits should give every SM
@@ -835,12 +912,18 @@ void q_dequant_launch(const uint8_t* w, int N, int K, int bprs, bf16* out, cudaS
   switch (type) {                                                        \
     case T_Q4_0: FN<T_Q4_0>(__VA_ARGS__); break;                         \
     case T_Q4_1: FN<T_Q4_1>(__VA_ARGS__); break;                         \
+    case T_Q5_0: FN<T_Q5_0>(__VA_ARGS__); break;                         \
+    case T_Q5_1: FN<T_Q5_1>(__VA_ARGS__); break;                         \
     case T_Q8_0: FN<T_Q8_0>(__VA_ARGS__); break;                         \
+    case T_Q2_K: FN<T_Q2_K>(__VA_ARGS__); break;                         \
+    case T_Q3_K: FN<T_Q3_K>(__VA_ARGS__); break;                         \
     case T_Q4_K: FN<T_Q4_K>(__VA_ARGS__); break;                         \
     case T_Q5_K: FN<T_Q5_K>(__VA_ARGS__); break;                         \
     case T_Q6_K: FN<T_Q6_K>(__VA_ARGS__); break;                         \
     case T_IQ4_NL: FN<T_IQ4_NL>(__VA_ARGS__); break;                     \
     case T_IQ4_XS: FN<T_IQ4_XS>(__VA_ARGS__); break;                     \
+    case T_TQ1_0: FN<T_TQ1_0>(__VA_ARGS__); break;                       \
+    case T_TQ2_0: FN<T_TQ2_0>(__VA_ARGS__); break;                       \
     case T_MXFP4: FN<T_MXFP4>(__VA_ARGS__); break;                       \
     case T_NVFP4: FN<T_NVFP4>(__VA_ARGS__); break;                       \
     default: TORCH_CHECK(false, "packed GEMM: unsupported GGML type ", type); \

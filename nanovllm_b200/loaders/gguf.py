@@ -276,6 +276,23 @@ def pack_random_blocks(ggml_type: int, shape: Tuple[int, ...], seed: int, std: f
         raw[:, 0] = 128 + int(round(math.log2(std / 5.7)))
     elif name == "NVFP4":  # four ue4m3 sub-scales of 4 * 2^-10
         raw[:, 0:4] = 0x04
+    elif name == "Q5_0":  # codes -16..15 (std 9.2)
+        raw[:, 0:2] = f16(std / 9.2)
+    elif name == "Q5_1":  # d * code + m, codes 0..31 centred by m
+        raw[:, 0:2] = f16(std / 9.2)
+        raw[:, 2:4] = f16(-15.5 * std / 9.2)
+    elif name == "Q2_K":  # 16 scale bytes (scale 1, min 1), 64 qs, d, dmin; codes 0..3 (std 1.1) centred by dmin
+        raw[:, 0:16] = 0x11
+        raw[:, 80:82] = f16(std / 1.1)
+        raw[:, 82:84] = f16(1.5 * std / 1.1)
+    elif name == "Q3_K":  # 32 hmask, 64 qs, 6-bit scales all 1 (+32 bias: low nibbles 1, high pairs 2), d
+        raw[:, 96:104] = 0x11
+        raw[:, 104:108] = 0xAA
+        raw[:, 108:110] = f16(std / 2.3)
+    elif name == "TQ1_0":  # trits -1..1 (std 0.82)
+        raw[:, 52:54] = f16(std / 0.82)
+    elif name == "TQ2_0":  # codes -1..2 (std 1.1)
+        raw[:, 64:66] = f16(std / 1.1)
     else:
         raise ValueError(f"random packing not provided for {name}")
     return raw.tobytes()

@@ -18,7 +18,8 @@ import torch
 from ..loaders import dequant as DQ
 
 # types the fused kernel decodes, with the bytes of one 256-element row step in the repacked layout
-FUSED_TYPES = {2: 144, 3: 160, 8: 272, 12: 144, 13: 176, 14: 224, 20: 144, 23: 144, 39: 144, 40: 144}
+FUSED_TYPES = {2: 144, 3: 160, 6: 176, 7: 192, 8: 272, 10: 96, 11: 112, 12: 144, 13: 176, 14: 224, 20: 144, 23: 144,
+               34: 64, 35: 80, 39: 144, 40: 144}
 STEP = 256
 TILE_ROWS = 128
 
@@ -59,8 +60,14 @@ def repack_tiles(raw: torch.Tensor, ggml_type: int, N: int, K: int) -> torch.Ten
         step = torch.cat([f(0, 2), f(2, 18)], -1)
     elif t == 3:                           # Q4_1: d[8] | m[8] | qs[8][16]
         step = torch.cat([f(0, 2), f(2, 4), f(4, 20)], -1)
+    elif t == 6:                           # Q5_0: d[8] | qh[8] (u32) | qs[8][16]
+        step = torch.cat([f(0, 2), f(2, 6), f(6, 22)], -1)
+    elif t == 7:                           # Q5_1: d[8] | m[8] | qh[8] (u32) | qs[8][16]
+        step = torch.cat([f(0, 2), f(2, 4), f(4, 8), f(8, 24)], -1)
     elif t == 8:                           # Q8_0: d[8] | qs[8][32]
         step = torch.cat([f(0, 2), f(2, 34)], -1)
+    elif t in (10, 11, 34, 35):            # Q2_K / Q3_K / TQ1_0 / TQ2_0: one super-block, zero-padded to 16 B
+        step = torch.cat([B.reshape(N, S, bb), z(FUSED_TYPES[t] - bb)], -1)
     elif t == 39:                          # MXFP4: e[8] | pad 8 | qs[8][16] (pair-adjacent codes)
         step = torch.cat([f(0, 1), z(8), _pair_adjacent(B[..., 1:17], 1).reshape(N, S, 128)], -1)
     elif t == 40:                          # NVFP4 (4 blocks of 64): scales[4][4] | qs[4][32] (pair-adjacent codes)

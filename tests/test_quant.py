@@ -108,3 +108,62 @@ def test_gguf_model_with_packed_projections_matches_dequantized(tmp_path, monkey
     b, kb = logits("0")
     assert "GgufPacked" in ka and "GgufPacked" not in kb
     assert torch.allclose(a, b, atol=2e-2, rtol=2e-2), (a - b).abs().max()
+
+
+def _h(p, o):
+    return float(np.frombuffer(bytes(p[o:o + 2]), dtype=np.float16)[0])
+
+
+def _decode8_model(p, t, e0):
+    """Host model of the fused kernel's decode8 for the low-bit families (csrc/qgemm.cu), read from one repacked
+    row step ``p`` (bytes): the kernel's field offsets and index arithmetic, element by element."""
+    out = []
+    for j in range(8):
+        e = e0 + j
+        if t in (6, 7):
+            m_off = 16 if t == 7 else 0
+            b, i = e >> 5, e & 31
+            qh = int.from_bytes(bytes(p[16 + m_off + 4 * b:20 + m_off + 4 * b]), "little")
+            q = p[48 + m_off + b * 16 + (i & 15)]
+            n = (q >> 4 if i >= 16 else q & 0xF) | (((qh >> i) & 1) << 4)
+            out.append(_h(p, 2 * b) * (n - 16) if t == 6 else _h(p, 2 * b) * n + _h(p, 16 + 2 * b))
+        elif t in (10, 11, 35):
+            half, j2, l = e >> 7, (e >> 5) & 3, e & 31
+            qs = {10: 16, 11: 32, 35: 0}[t]
+            q = (p[qs + half * 32 + l] >> (2 * j2)) & 3
+            if t == 10:
+                sc = p[half * 8 + j2 * 2 + (l >> 4)]
+                out.append(_h(p, 80) * (sc & 0xF) * q - _h(p, 82) * (sc >> 4))
+            elif t == 11:
+                si = half * 8 + j2 * 2 + (l >> 4)
+                w, k = si >> 2, si & 3
+                lo = p[96 + (4 if w & 1 else 0) + k] >> ((w >> 1) * 4)
+                sc = ((lo & 0xF) | (((p[104 + k] >> (2 * w)) & 3) << 4)) - 32
+                h = (p[l] >> (half * 4 + j2)) & 1
+                out.append(_h(p, 108) * sc * (q - (0 if h else 4)))
+            else:
+                out.append(_h(p, 64) * (q - 1))
+        else:  # TQ1_0
+            if e < 160:
+                x, k = p[e & 31], e >> 5
+            elif e < 240:
+                x, k = p[32 + ((e - 160) & 15)], (e - 160) >> 4
+            else:
+                x, k = p[48 + ((e - 240) & 3)], (e - 240) >> 2
+            r = (x * 3 ** k) & 0xFF
+            out.append(_h(p, 52) * (((r * 3) >> 8) - 1))
+    return out
+
+
+@pytest.mark.parametrize("t", [6, 7, 10, 11, 34, 35])
+def test_low_bit_repacked_layout_decodes_like_the_reference_decoder(t):
+    N, K = 128, 512
+    w = _packed(t, N=N, K=K, seed=11)
+    want = w.dequantize(torch.float32).numpy()
+    tiles = repack_tiles(w.raw, t, N, K).reshape(1, K // 256, 128, FUSED_TYPES[t]).numpy()
+    for r in (0, 77):
+        for s in range(K // 256):
+            p = tiles[0, s, r].tolist()
+            got = [v for e0 in range(0, 256, 8) for v in _decode8_model(p, t, e0)]
+            np.testing.assert_allclose(np.array(got, dtype=np.float32), want[r, s * 256:(s + 1) * 256], rtol=1e-6,
+                                       atol=1e-7)
