@@ -28,6 +28,7 @@ std::vector<int64_t> gemm_sp_cuda(torch::Tensor x, torch::Tensor w, c10::optiona
 void splitk_sum_cuda(torch::Tensor parts, torch::Tensor out);
 int64_t qgemm_splits_cuda(int64_t M, int64_t N, int64_t K, int64_t type);
 int64_t qgemm_row_step_bytes(int64_t type);
+void qgemm_set_trace(c10::optional<torch::Tensor> t);
 int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, int64_t K, torch::Tensor out,
                    c10::optional<torch::Tensor> parts, c10::optional<torch::Tensor> err, bool partial_out);
 void qdequant_cuda(torch::Tensor w, int64_t type, int64_t N, int64_t K, torch::Tensor out);
@@ -83,6 +84,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("splitk_sum", &splitk_sum_cuda);
   m.def("qgemm_splits", &qgemm_splits_cuda);
   m.def("qgemm_row_step_bytes", &qgemm_row_step_bytes);
+  m.def("qgemm_set_trace", &qgemm_set_trace);
   m.def("qgemm", &qgemm_cuda);
   m.def("qdequant", &qdequant_cuda);
   m.def("embedding", &embedding_cuda);

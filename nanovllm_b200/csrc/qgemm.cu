@@ -14,27 +14,31 @@
 // [row step], so one row-step tile is ONE contiguous run of 128 * bprs bytes: a single bulk copy
 // (cp.async.bulk, no tensor map, no multicast) per pipeline stage, and perfect DRAM streaming.
 //
-// qgemm_decode_kernel<TYPE, BN> (swap-AB like the bf16 decode GEMM: 128 weight rows = MMA M, tokens = MMA N):
-//   warp 0 lane 0   producer: for small token tiles the CTA's activation slice [BN x Krange] is loaded ONCE
-//                   by TMA and stays resident in shared memory; the packed weight tiles stream through a ring
-//                   of row steps;
-//   warps 4..11     dequant: (resident mode) convert the activation slice to f16 in place; then two groups of
-//                   4 warps take alternate 256-wide row steps, thread = weight row = TMEM lane, and write the
-//                   four f16 64-wide sub-tiles straight from registers into one of 3 TMEM row-step slots
-//                   (tcgen05.st) -- no shared-memory tile, no proxy fence (FP4: hardware e2m1x2 -> f16x2
-//                   conversion times the block scale, exact; 4/8-bit integer codes: 1024.0-magic f16 halves,
-//                   one subtract, one fma).  One hand-off per row step, not per sub-step: the hand-off round
-//                   trip, not the arithmetic, paced the kernel (measured 1.5x faster, LM-head shape 1.7x);
+// qgemm_decode_kernel<TYPE, BN> (swap-AB like the bf16 decode GEMM: 128 weight rows = MMA M, tokens = MMA N) is
+// persistent: one CTA per SM walks its work units (128-row group, K split) with every ring running across unit
+// boundaries, so set-up is paid once per SM and the packed stream never drains between units.
+//   warp 0 lane 0   producer: the packed row steps stream through a ring of up to 12 stages (the first ring is
+//                   requested before the dependency wait); small token tiles keep one K split per CTA and load
+//                   its activation slice [BN x Krange] ONCE by TMA;
+//   warps 4..11     dequant: two groups of 4 warps take alternate 256-wide row steps, thread = weight row =
+//                   TMEM lane, and write the four f16 64-wide sub-tiles straight from registers into one of 3
+//                   TMEM row-step slots (tcgen05.st) -- no shared-memory tile, no proxy fence (FP4: hardware
+//                   e2m1x2 -> f16x2 conversion times the block scale, exact; integer codes: 1024.0-magic f16
+//                   halves with the code bits placed by prmt/lop3, one subtract, one multiply or fma);
 //   warp 1 lane 0   tcgen05.mma kind::f16 with the A operand read from TMEM, B (f16 activations) from shared
-//                   memory, fp32 accumulator in TMEM;
-//   warps 0..3      epilogue: tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the
-//                   consumer sums exactly like the bf16 decode GEMM's.
+//                   memory, fp32 accumulators in TMEM (two, so a unit's epilogue overlaps the next unit);
+//   warp 2          for token tiles up to 32: does the MMA issuer's mbarrier waits and hands each row step over
+//                   through a named barrier (see mma_handoff);
+//   warps 3, 12-14  epilogue: (resident mode) first convert the activation slice to f16 in place; then per unit
+//                   tcgen05.ld, bf16 output (one split) or fp32 split-K partials [S][M][N] that the consumer sums
+//                   exactly like the bf16 decode GEMM's.
 // Token tiles of 64 and more use the streaming mode instead of the resident slice: an f16 copy of the
 // activations (q_to_f16_kernel) streams through a ring of row steps, so the K range -- and the number of fp32
 // split partials -- is not capped by shared memory.
 // Every wait is bounded (nvb::mbar_wait -> device error word) so a broken pipeline returns instead of hanging.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <algorithm>
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include "common.cuh"
@@ -48,8 +52,8 @@ constexpr int QBM = 128, QBK = 64, QSTEP = 256;
 constexpr int kQXBytes = 128 * 1024;    // resident activation slice budget
 constexpr int kQRingBytes = 224 * 1024;  // activation slice + bf16 tiles + packed ring
 constexpr int kQAStages = 3;             // dequantized f16 row steps in flight (TMEM slots of 4 x 32 columns)
-// TMEM column of the first A slot: the accumulator uses [0, BN); 128 leaves room for 3 row-step slots
-__host__ __device__ constexpr uint32_t q_acol0(int bn) { return bn <= 128 ? 128u : 256u; }
+// TMEM column of the first A slot: the accumulators use [0, NACC * NCH * BN); 128 leaves room for 3 row-step slots
+__host__ __device__ constexpr uint32_t q_acol0(int bn) { return bn <= 64 ? 128u : 256u; }
 __host__ __device__ constexpr int q_aslots(int bn) { return (int)((512u - q_acol0(bn)) / 128u); }
 constexpr int kQMaxXS = 4;                // activation ring stages in streaming mode (at most)
 
@@ -368,6 +372,110 @@ __device__ __forceinline__ uint4 decode_h8(const uint8_t* __restrict__ p, int e0
     o.y = hmul2(hsub2(prmt(x0, 0x64646464u, 0x4342), k1152), s2);
     o.z = hmul2(hsub2(prmt(x1, 0x64646464u, 0x4140), k1152), s2);
     o.w = hmul2(hsub2(prmt(x1, 0x64646464u, 0x4342), k1152), s2);
+  } else if constexpr (TYPE == T_Q4_0 || TYPE == T_Q4_1) {
+    // nibble codes as 1024 + q (low) or 1024 + 16 q (high nibble, scale / 16)
+    const int b = e0 >> 5, i0 = e0 & 31;
+    const bool hi = i0 >= 16;
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    const float d = h2f(p + 2 * b) * (hi ? 0.0625f : 1.f);
+    const uint2 w = *reinterpret_cast<const uint2*>(p + (TYPE == T_Q4_1 ? 32 : 16) + b * 16 + (i0 & 15));
+    const uint32_t s2 = h2_bcast(d);
+    uint32_t q[4] = {nib_pair(prmt(w.x, 0, 0x4140), mask), nib_pair(prmt(w.x, 0, 0x4342), mask),
+                     nib_pair(prmt(w.y, 0, 0x4140), mask), nib_pair(prmt(w.y, 0, 0x4342), mask)};
+    if constexpr (TYPE == T_Q4_0) {
+      const uint32_t kb = hi ? 0x64806480u : 0x64086408u;  // 1024 + 8 code units
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[j] = hmul2(hsub2(q[j], kb), s2);
+    } else {
+      const uint32_t m2 = h2_bcast(h2f(p + 16 + 2 * b));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q[j] = hfma2(hsub2(q[j], 0x64006400u), s2, m2);
+    }
+    o = make_uint4(q[0], q[1], q[2], q[3]);
+  } else if constexpr (TYPE == T_Q5_K) {
+    const int sb = e0 >> 5, i0 = e0 & 31;
+    const float d = h2f(p), dmin = h2f(p + 2);
+    const uint8_t* qq = p + 4;
+    int sc, mn;
+    if (sb < 4) {
+      sc = qq[sb] & 63;
+      mn = qq[sb + 4] & 63;
+    } else {
+      sc = (qq[sb + 4] & 0xF) | ((qq[sb - 4] >> 6) << 4);
+      mn = (qq[sb + 4] >> 4) | ((qq[sb] >> 6) << 4);
+    }
+    const bool hi = sb & 1;
+    const float ds = d * (float)sc * (hi ? 0.0625f : 1.f);
+    const uint32_t s2 = h2_bcast(ds), m2 = h2_bcast(-(dmin * (float)mn));
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    // the fifth bit (bit sb of the qh byte) lands at 16 (low nibble) or 256 (high nibble) code units
+    const uint32_t hmask = hi ? 0x01000100u : 0x00100010u;
+    const int hsh = hi ? 8 : 4;
+    const uint2 w = *reinterpret_cast<const uint2*>(p + 48 + (sb >> 1) * 32 + i0);
+    const uint2 h = *reinterpret_cast<const uint2*>(p + 16 + i0);
+    const uint32_t sel[2] = {0x4140, 0x4342};
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t wq = j < 2 ? w.x : w.y, hq = j < 2 ? h.x : h.y;
+      const uint32_t hb = ((prmt(hq, 0, sel[j & 1]) >> sb) << hsh) & hmask;
+      r[j] = hfma2(hsub2(nib_pair(prmt(wq, 0, sel[j & 1]), mask) | hb, 0x64006400u), s2, m2);
+    }
+    o = make_uint4(r[0], r[1], r[2], r[3]);
+  } else if constexpr (TYPE == T_Q6_K) {
+    const int hh = e0 >> 7, wv = e0 & 127, k = wv >> 5, l0 = wv & 31;
+    const uint2 ql = *reinterpret_cast<const uint2*>(p + hh * 64 + (k & 1) * 32 + l0);
+    const uint2 qh = *reinterpret_cast<const uint2*>(p + 128 + hh * 32 + l0);
+    const float s = (float)reinterpret_cast<const int8_t*>(p + 192)[hh * 8 + 2 * k + (l0 >> 4)];
+    const bool hi = k >> 1;
+    // 6-bit code q = nibble | 2 high bits << 4, as 1024 + q (low nibble) or 1024 + 16 q (high nibble)
+    const uint32_t mask = hi ? 0x00F000F0u : 0x000F000Fu;
+    const uint32_t hmask = hi ? 0x03000300u : 0x00300030u;
+    const int hsh = hi ? 8 : 4;
+    const uint32_t s2 = h2_bcast(h2f(p + 208) * s * (hi ? 0.0625f : 1.f));
+    const uint32_t kb = hi ? 0x66006600u : 0x64206420u;  // 1024 + 32 code units
+    const uint32_t sel[2] = {0x4140, 0x4342};
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t lq = j < 2 ? ql.x : ql.y, hq = j < 2 ? qh.x : qh.y;
+      const uint32_t hb = ((prmt(hq, 0, sel[j & 1]) >> (2 * k)) << hsh) & hmask;
+      r[j] = hmul2(hsub2(nib_pair(prmt(lq, 0, sel[j & 1]), mask) | hb, kb), s2);
+    }
+    o = make_uint4(r[0], r[1], r[2], r[3]);
+  } else if constexpr (TYPE == T_Q2_K || TYPE == T_Q3_K || TYPE == T_TQ2_0) {
+    const int half = e0 >> 7, j2 = (e0 >> 5) & 3, l0 = e0 & 31;
+    constexpr int kQs = TYPE == T_Q2_K ? 16 : TYPE == T_Q3_K ? 32 : 0;
+    const uint2 w = *reinterpret_cast<const uint2*>(p + kQs + half * 32 + l0);
+    uint32_t s2, m2 = 0, kb = 0x64006400u;
+    uint2 hm = make_uint2(0, 0);
+    int hb = 0;
+    if constexpr (TYPE == T_Q2_K) {
+      const uint32_t sc = p[half * 8 + j2 * 2 + (l0 >> 4)];
+      s2 = h2_bcast(h2f(p + 80) * (float)(sc & 0xF));
+      m2 = h2_bcast(-(h2f(p + 82) * (float)(sc >> 4)));
+    } else if constexpr (TYPE == T_Q3_K) {
+      const int si = half * 8 + j2 * 2 + (l0 >> 4), ww = si >> 2, kk = si & 3;
+      const uint32_t lo = (uint32_t)p[96 + ((ww & 1) ? 4 : 0) + kk] >> ((ww >> 1) * 4);
+      const int sc = (int)((lo & 0xF) | ((((uint32_t)p[104 + kk] >> (2 * ww)) & 3) << 4)) - 32;
+      s2 = h2_bcast(h2f(p + 108) * (float)sc);
+      hm = *reinterpret_cast<const uint2*>(p + l0);
+      hb = half * 4 + j2;
+      kb = 0x64046404u;  // 3-bit code (hmask bit as bit 2) minus 4
+    } else {
+      s2 = h2_bcast(h2f(p + 64));
+      kb = 0x64016401u;  // code - 1
+    }
+    const uint32_t sel[2] = {0x4140, 0x4342};
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t t = ((prmt(j < 2 ? w.x : w.y, 0, sel[j & 1]) >> (2 * j2)) & 0x00030003u) | 0x64006400u;
+      if constexpr (TYPE == T_Q3_K) t |= ((prmt(j < 2 ? hm.x : hm.y, 0, sel[j & 1]) >> hb) << 2) & 0x00040004u;
+      t = hsub2(t, kb);
+      r[j] = TYPE == T_Q2_K ? hfma2(t, s2, m2) : hmul2(t, s2);
+    }
+    o = make_uint4(r[0], r[1], r[2], r[3]);
   } else {
     float v[8];
     decode8<TYPE>(p, e0, L, v);
@@ -494,6 +602,8 @@ struct QArgs {
   int ksteps;       // K / 256
   int kper;         // row steps per split (the resident activation slice covers kper * 256 columns)
   int S;            // splits
+  int groups;       // 128-row groups: ceil(N / 128)
+  int per_split;    // resident mode: CTAs per split (the grid is per_split * S)
   int ws;           // packed ring stages
   int xs;           // activation ring stages (row steps); 0 = the CTA's activation slice is resident
   int bprs;         // bytes per row step
@@ -502,13 +612,13 @@ struct QArgs {
   long out_ld;
   float* partial;
   int* err;
+  long long* trace;  // optional per-role clock64 trace of CTA 0: [6 roles][64 steps][4 events]
 };
 
-__host__ __device__ constexpr uint32_t q_pow2_cols(int n) {
-  uint32_t c = 32;
-  while (c < (uint32_t)n) c <<= 1;
-  return c;
-}
+#define QTRACE(role, idx, ev)                                                                   \
+  do {                                                                                          \
+    if (tr != nullptr) tr[((role) * 64 + min((int)(idx), 63)) * 4 + (ev)] = (long long)clock64(); \
+  } while (0)
 
 // D(tmem) (+)= A(tmem) * B(smem desc)^T, kind::f16: the A operand is read from tensor memory (128 lanes = rows,
 // each 32-bit column holds two consecutive K elements).
@@ -541,22 +651,87 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
 }
 
 constexpr int kQDequantWarps = 8;
-constexpr int kQThreads = 128 + 32 * kQDequantWarps;
+// warps: 0 producer, 1 MMA issuer, 2 MMA waiter, 3 and 12-14 epilogue (TMEM lane quarters 3, 0, 1, 2),
+// 4-11 dequant
+constexpr int kQThreads = 32 * 15;
+
+// Named barrier 1 between the MMA issuer warp and its waiter warp, AND-reducing an ok flag.  The issuer never
+// touches shared memory between MMA batches: measured on B200, an mbarrier wait (even on a completed phase) or
+// any shared-memory load issued by the thread right after a batch of narrow tcgen05.mma stalls until the
+// batch has drained, idling the tensor pipe (16 MMAs of N=16: ~880 cycles of issue, ~3000 with an in-thread
+// wait), while a named barrier does not.
+__device__ __forceinline__ bool mma_handoff(int ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, 1, 64, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"(ok)
+      : "memory");
+  return r != 0;
+}
+
+// Work unit u of a CTA = (row group, K split).  Resident mode keeps one split per CTA (its activation slice is
+// loaded once): CTA c takes split c % S and row groups c / S + i * per_split.  Streaming mode deals the units
+// out round-robin, split-major.
+__device__ __forceinline__ bool q_unit(const QArgs& a, int i, int& group, int& split) {
+  if (a.xs == 0) {
+    split = (int)blockIdx.x % a.S;
+    group = (int)blockIdx.x / a.S + i * a.per_split;
+  } else {
+    const int u = (int)blockIdx.x + i * (int)gridDim.x;
+    group = u % a.groups;
+    split = u / a.groups;
+    if (split >= a.S) return false;
+  }
+  return group < a.groups;
+}
+
+// Walks a CTA's row steps in order: unit i, step j of the unit's K range.
+struct QCursor {
+  int i, j, nks, group, split, ks0;
+  bool ok;
+  __device__ __forceinline__ void load(const QArgs& a) {
+    ok = q_unit(a, i, group, split);
+    if (ok) {
+      ks0 = split * a.kper;
+      nks = min(a.ksteps, ks0 + a.kper) - ks0;
+    }
+  }
+  __device__ __forceinline__ void start(const QArgs& a) {
+    i = 0;
+    j = 0;
+    load(a);
+  }
+  __device__ __forceinline__ void next_step(const QArgs& a) {
+    if (++j == nks) next_unit(a);
+  }
+  __device__ __forceinline__ void next_unit(const QArgs& a) {
+    j = 0;
+    ++i;
+    load(a);
+  }
+};
 
 template <int TYPE, int BN>
 __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid_constant__ CUtensorMap xmap, QArgs a) {
   constexpr uint32_t X_BOX = BN * QBK * 2;    // one [BN x 64] activation box
-  constexpr uint32_t TMEM_COLS = 512;         // accumulator [0, BN) + AS row-step slots of 128 columns
+  constexpr uint32_t TMEM_COLS = 512;         // accumulators [0, NACC * BN) + AS row-step slots of 128 columns
   constexpr uint32_t IDESC = idesc_f16_f32(QBM, BN);
+  constexpr int NACC = BN <= 128 ? 2 : 1;     // two accumulators: a unit's epilogue overlaps the next unit's MMAs
+  constexpr bool WAITER = BN <= 32;           // warp 2 waits for the MMA issuer (see mma_handoff)
+  // independent accumulation chains per unit (summed in the epilogue): narrow MMAs issued back to back into one
+  // accumulator serialise on it
+  constexpr int NCH = BN <= 16 ? 4 : BN <= 32 ? 2 : 1;
   constexpr uint32_t ACOL0 = q_acol0(BN);
   constexpr int AS = q_aslots(BN);            // 3 (BN <= 128) or 2 row-step slots
-  static_assert(BN <= (int)ACOL0 && AS <= kQAStages && ACOL0 + 128 * AS <= TMEM_COLS, "TMEM plan");
+  static_assert(NACC * NCH * BN <= (int)ACOL0 && AS <= kQAStages && ACOL0 + 128 * AS <= TMEM_COLS, "TMEM plan");
   const uint32_t stage_bytes = (uint32_t)a.bprs * QBM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // resident mode (xs == 0): the CTA's whole activation slice (kper row steps), converted to f16 in place;
-  // streaming mode (xs > 0, larger token tiles): a ring of xs row steps of an f16 activation copy
+  // resident mode (xs == 0): the CTA's activation slice (kper row steps of its split), converted to f16 in
+  // place once; streaming mode (xs > 0, larger token tiles): a ring of xs row steps of an f16 activation copy
   const bool stream = a.xs > 0;
   const int xslots = stream ? a.xs : a.kper;
   uint8_t* xres = smem;                                           // xslots * 4 boxes
@@ -568,25 +743,22 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
   uint64_t* wempty = wfull + a.ws;
   uint64_t* afull = wempty + a.ws;
   uint64_t* aempty = afull + kQAStages;
-  uint64_t* tfull = aempty + kQAStages;
-  uint64_t* xfull = tfull + 1;      // streaming mode: [xs]
+  uint64_t* tfull = aempty + kQAStages;   // [2]
+  uint64_t* tempty = tfull + 2;           // [2]
+  uint64_t* xfull = tempty + 2;           // streaming mode: [xs]
   uint64_t* xempty = xfull + kQMaxXS;
   __shared__ Luts luts;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int group = blockIdx.x / a.S, split = blockIdx.x % a.S;
-  const int row0 = group * QBM;
-  const int ks0 = split * a.kper;
-  const int ks1 = min(a.ksteps, ks0 + a.kper);
-  const int nks = ks1 - ks0;
+  long long* tr = (blockIdx.x == 0 && lane == 0) ? a.trace : nullptr;
 
   init_luts(luts);
   if (threadIdx.x == 0) {
     abort_flag = 0;
     nvb::mbar_init(xbar, 1);
-    nvb::mbar_init(xready, kQDequantWarps);
+    nvb::mbar_init(xready, 4);  // the 4 epilogue warps convert the resident activation slice
     for (int s = 0; s < a.ws; ++s) {
       nvb::mbar_init(&wfull[s], 1);
       nvb::mbar_init(&wempty[s], 4);  // the 4 warps of the dequant group that owns the row step
@@ -595,7 +767,10 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
       nvb::mbar_init(&afull[s], 4);
       nvb::mbar_init(&aempty[s], 1);
     }
-    nvb::mbar_init(tfull, 1);
+    for (int b = 0; b < 2; ++b) {
+      nvb::mbar_init(&tfull[b], 1);
+      nvb::mbar_init(&tempty[b], 4);  // the 4 epilogue warps
+    }
     for (int s = 0; s < a.xs; ++s) {
       nvb::mbar_init(&xfull[s], 1);
       nvb::mbar_init(&xempty[s], 1);
@@ -611,105 +786,174 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
   nvb::tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   nvb::pdl_trigger();
+  if (threadIdx.x == 0) QTRACE(5, 0, 0);
 
-  const uint8_t* wsrc = a.w + ((size_t)group * a.ksteps + ks0) * stage_bytes;
   if (warp == 0) {
     if (lane == 0) {
+      // ------------------------------------------------------------------ producer
+      QCursor wc, xc;
+      wc.start(a);
+      uint32_t wit = 0, xit = 0;
+      bool ok = true;
       // packed weights are never written by earlier kernels: the first ring streams in before the dependency
-      const int pre = nks < a.ws ? nks : a.ws;
-      for (int i = 0; i < pre; ++i) {
-        nvb::mbar_arrive_expect_tx(&wfull[i], stage_bytes);
-        bulk_load(wring + (size_t)i * stage_bytes, wsrc + (size_t)i * stage_bytes, stage_bytes, &wfull[i]);
+      for (; wc.ok && wit < (uint32_t)a.ws; ++wit, wc.next_step(a)) {
+        nvb::mbar_arrive_expect_tx(&wfull[wit], stage_bytes);
+        bulk_load(wring + (size_t)wit * stage_bytes,
+                  a.w + ((size_t)wc.group * a.ksteps + wc.ks0 + wc.j) * stage_bytes, stage_bytes, &wfull[wit]);
       }
       nvb::tma_prefetch_desc(&xmap);
       nvb::pdl_wait();
+      xc.start(a);
       if (!stream) {
-        nvb::mbar_arrive_expect_tx(xbar, (uint32_t)nks * 4 * X_BOX);
-        for (int b = 0; b < nks * 4; ++b)
-          nvb::tma_load_2d(xres + (size_t)b * X_BOX, &xmap, xbar, ks0 * QSTEP + b * QBK, 0);
-        for (int i = pre; i < nks; ++i) {
-          const int s = i % a.ws;
-          if (!nvb::mbar_wait(&wempty[s], ((i / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) break;
-          nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
-          bulk_load(wring + (size_t)s * stage_bytes, wsrc + (size_t)i * stage_bytes, stage_bytes, &wfull[s]);
+        if (xc.ok) {
+          nvb::mbar_arrive_expect_tx(xbar, (uint32_t)xc.nks * 4 * X_BOX);
+          for (int b = 0; b < xc.nks * 4; ++b)
+            nvb::tma_load_2d(xres + (size_t)b * X_BOX, &xmap, xbar, xc.ks0 * QSTEP + b * QBK, 0);
         }
-      } else {
-        // row step i's activations, then the weight row step that dequant frees by finishing row step i
-        for (int i = 0; i < nks; ++i) {
-          const int xsl = i % a.xs;
-          if (i >= a.xs && !nvb::mbar_wait(&xempty[xsl], ((i / a.xs) & 1u) ^ 1u, a.err, &abort_flag)) break;
+      }
+      while (ok && (stream ? xc.ok : wc.ok)) {
+        if (stream) {
+          // row step xit's activations, then the weight row step ws further on
+          const int xsl = xit % a.xs;
+          if (xit >= (uint32_t)a.xs &&
+              !nvb::mbar_wait(&xempty[xsl], ((xit / a.xs) & 1u) ^ 1u, a.err, &abort_flag)) {
+            ok = false;
+            break;
+          }
           nvb::mbar_arrive_expect_tx(&xfull[xsl], 4 * X_BOX);
           for (int b = 0; b < 4; ++b)
-            nvb::tma_load_2d(xres + ((size_t)xsl * 4 + b) * X_BOX, &xmap, &xfull[xsl], (ks0 + i) * QSTEP + b * QBK, 0);
-          const int j = i + a.ws;
-          if (j < nks) {
-            const int s = j % a.ws;
-            if (!nvb::mbar_wait(&wempty[s], ((j / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) break;
-            nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
-            bulk_load(wring + (size_t)s * stage_bytes, wsrc + (size_t)j * stage_bytes, stage_bytes, &wfull[s]);
-          }
+            nvb::tma_load_2d(xres + ((size_t)xsl * 4 + b) * X_BOX, &xmap, &xfull[xsl], (xc.ks0 + xc.j) * QSTEP + b * QBK, 0);
+          ++xit;
+          xc.next_step(a);
+          if (!wc.ok) continue;
         }
+        const int s = wit % a.ws;
+        if (!nvb::mbar_wait(&wempty[s], ((wit / a.ws) & 1u) ^ 1u, a.err, &abort_flag)) {
+          ok = false;
+          break;
+        }
+        QTRACE(0, wit, 0);
+        nvb::mbar_arrive_expect_tx(&wfull[s], stage_bytes);
+        bulk_load(wring + (size_t)s * stage_bytes, a.w + ((size_t)wc.group * a.ksteps + wc.ks0 + wc.j) * stage_bytes,
+                  stage_bytes, &wfull[s]);
+        ++wit;
+        wc.next_step(a);
+      }
+      if (!ok) {
+        // bounded drain of copies that may still be landing in shared memory
+        for (uint32_t j = (wit > (uint32_t)a.ws ? wit - a.ws : 0); j < wit; ++j)
+          nvb::mbar_wait(&wfull[j % a.ws], (j / a.ws) & 1u, nullptr, nullptr);
+        if (stream)
+          for (uint32_t j = (xit > (uint32_t)a.xs ? xit - a.xs : 0); j < xit; ++j)
+            nvb::mbar_wait(&xfull[j % a.xs], (j / a.xs) & 1u, nullptr, nullptr);
+        else
+          nvb::mbar_wait(xbar, 0, nullptr, nullptr);
       }
     } else {
       nvb::pdl_wait();
     }
   } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (lane 0 issues)
+    // Narrow token tiles (the MMA floor is per instruction) hand their waits to warp 2 and meet it at a named
+    // barrier; wide ones, whose MMAs outlast a wait anyway, wait in lane 0 themselves.
     nvb::pdl_wait();
-    if (lane == 0) {
+    // the 16 MMAs of row step ``it`` (step j of its unit) into accumulator d_tm; then release its slots
+    auto issue_step = [&](uint32_t it, int j, uint32_t d_tm) {
+      const int t = it % AS;
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub) {
+        const uint32_t a_tm = tmem_base + ACOL0 + (uint32_t)t * 128 + sub * 32;
+        const size_t box = stream ? (size_t)(it % a.xs) * 4 + sub : (size_t)j * 4 + sub;
+        const uint32_t b_addr = nvb::smem_u32(xres + box * X_BOX);
+#pragma unroll
+        for (int kk = 0; kk < QBK / 16; ++kk) {
+          const int ch = (sub * 4 + kk) % NCH;
+          tc_mma_f16_tmem_a(d_tm + ch * BN, a_tm + kk * 8, nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
+                            (j > 0 || sub > 0 || kk >= NCH) ? 1u : 0u);
+        }
+      }
+      nvb::tc_commit(&aempty[t]);
+      if (stream) nvb::tc_commit(&xempty[it % a.xs]);
+    };
+    QCursor c;
+    c.start(a);
+    uint32_t it = 0;
+    if constexpr (WAITER) {
+      bool ok = mma_handoff(1);  // the waiter has seen the activations
+      for (uint32_t unit = 0; ok && c.ok; ++unit, c.next_unit(a)) {
+        const uint32_t b = unit % NACC;
+        for (int j = 0; j < c.nks; ++j, ++it) {
+          ok = mma_handoff(1);  // the waiter has seen this row step's operands
+          if (!ok) break;
+          nvb::tc_fence_after();
+          if (lane == 0) issue_step(it, j, tmem_base + b * (NCH * BN));
+          __syncwarp();
+        }
+        if (!ok) break;
+        if (lane == 0) nvb::tc_commit(&tfull[b]);
+        __syncwarp();
+      }
+    } else if (lane == 0) {
       bool ok = stream || nvb::mbar_wait(xready, 0, a.err, &abort_flag);
-      // one hand-off per 256-wide row step: wait for its 4 dequantized sub-tiles, issue 16 MMAs, release
-      for (int i = 0; ok && i < nks; ++i) {
-        const int t = i % AS;
-        if (stream && !nvb::mbar_wait(&xfull[i % a.xs], (i / a.xs) & 1u, a.err, &abort_flag)) {
-          ok = false;
-          break;
+      for (uint32_t unit = 0; ok && c.ok; ++unit, c.next_unit(a)) {
+        const uint32_t b = unit % NACC, use = unit / NACC;
+        for (int j = 0; j < c.nks; ++j, ++it) {
+          if (j == 0 && !nvb::mbar_wait(&tempty[b], (use & 1u) ^ 1u, a.err, &abort_flag)) ok = false;
+          if (ok && stream && !nvb::mbar_wait(&xfull[it % a.xs], (it / a.xs) & 1u, a.err, &abort_flag)) ok = false;
+          if (ok && !nvb::mbar_wait(&afull[it % AS], (it / AS) & 1u, a.err, &abort_flag)) ok = false;
+          if (!ok) break;
+          QTRACE(1, it, 0);
+          nvb::tc_fence_after();
+          issue_step(it, j, tmem_base + b * (NCH * BN));
+          QTRACE(1, it, 1);
         }
-        if (!nvb::mbar_wait(&afull[t], (i / AS) & 1u, a.err, &abort_flag)) {
-          ok = false;
-          break;
-        }
-        nvb::tc_fence_after();
-#pragma unroll
-        for (int sub = 0; sub < 4; ++sub) {
-          const uint32_t a_tm = tmem_base + ACOL0 + (uint32_t)t * 128 + sub * 32;
-          const size_t box = stream ? (size_t)(i % a.xs) * 4 + sub : (size_t)i * 4 + sub;
-          const uint32_t b_addr = nvb::smem_u32(xres + box * X_BOX);
-#pragma unroll
-          for (int kk = 0; kk < QBK / 16; ++kk)
-            tc_mma_f16_tmem_a(tmem_base, a_tm + kk * 8, nvb::sdesc_kmajor_sw128(b_addr + kk * 32), IDESC,
-                              (i > 0 || sub > 0 || kk > 0) ? 1u : 0u);
-        }
-        nvb::tc_commit(&aempty[t]);
-        if (stream) nvb::tc_commit(&xempty[i % a.xs]);
+        if (ok) nvb::tc_commit(&tfull[b]);
       }
-      if (ok) nvb::tc_commit(tfull);
     }
-  } else if (warp >= 4) {
+  } else if (warp == 2) {
+    // ------------------------------------------------------------------ MMA waiter (narrow token tiles)
+    // every wait of the MMA issuer, in its order; each step ends with the named-barrier hand-off
     nvb::pdl_wait();
-    const int dt = threadIdx.x - 128;       // 0 .. 32 * kQDequantWarps - 1
-    bool ok = stream || nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
-    if (ok && !stream) {
-      // the resident activation slice becomes f16 in place (saturating; the layout is elementwise)
-      const uint32_t xbytes = (uint32_t)nks * 4 * X_BOX;
-      for (uint32_t off = (uint32_t)dt * 16; off < xbytes; off += 32 * kQDequantWarps * 16) {
-        uint4 v = *reinterpret_cast<const uint4*>(xres + off);
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = f2_to_h2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
-        *reinterpret_cast<uint4*>(xres + off) = v;
+    if constexpr (WAITER) {
+      int okl = 1;
+      if (lane == 0 && !stream) okl = nvb::mbar_wait(xready, 0, a.err, &abort_flag) ? 1 : 0;
+      bool ok = mma_handoff(__shfl_sync(0xffffffffu, okl, 0));
+      QCursor c;
+      c.start(a);
+      uint32_t it = 0;
+      for (uint32_t unit = 0; ok && c.ok; ++unit, c.next_unit(a)) {
+        const uint32_t b = unit % NACC, use = unit / NACC;
+        for (int j = 0; j < c.nks; ++j, ++it) {
+          okl = 1;
+          if (lane == 0) {
+            if (j == 0) okl = nvb::mbar_wait(&tempty[b], (use & 1u) ^ 1u, a.err, &abort_flag) ? 1 : 0;
+            if (okl && stream) okl = nvb::mbar_wait(&xfull[it % a.xs], (it / a.xs) & 1u, a.err, &abort_flag) ? 1 : 0;
+            if (okl) okl = nvb::mbar_wait(&afull[it % AS], (it / AS) & 1u, a.err, &abort_flag) ? 1 : 0;
+            QTRACE(1, it, 0);
+          }
+          ok = mma_handoff(__shfl_sync(0xffffffffu, okl, 0));
+          QTRACE(1, it, 1);
+          if (!ok) break;
+        }
       }
-      nvb::fence_proxy_async();
     }
-    __syncwarp();
-    if (lane == 0 && !stream) nvb::mbar_arrive(xready);
-    // dequant: two groups of 4 warps take alternate 256-wide row steps; thread = weight row (its TMEM lane);
-    // the f16 sub-tiles go straight from registers into a TMEM slot that the MMA reads as its A operand
+  } else if (warp >= 4 && warp < 4 + kQDequantWarps) {
+    // ------------------------------------------------------------------ dequant
+    // reads only the packed weights (never written by earlier kernels) and writes TMEM: no dependency wait
+    QCursor c;
+    c.start(a);
+    bool ok = true;
+    // two groups of 4 warps take alternate 256-wide row steps; thread = weight row (its TMEM lane); the f16
+    // sub-tiles go straight from registers into a TMEM slot that the MMA reads as its A operand
     const int quarter = warp & 3, r = quarter * 32 + lane, g = (warp - 4) >> 2;
     const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-    for (int i = g; ok && i < nks; i += 2) {
-      const int s = i % a.ws, t = i % AS;
-      if (!nvb::mbar_wait(&wfull[s], (i / a.ws) & 1u, a.err, &abort_flag)) break;
-      if (i >= AS && !nvb::mbar_wait(&aempty[t], ((i / AS) & 1u) ^ 1u, a.err, &abort_flag)) break;
+    for (uint32_t it = 0; ok && c.ok; ++it, c.next_step(a)) {
+      if ((int)(it & 1u) != g) continue;
+      const int s = it % a.ws, t = it % AS;
+      if (!nvb::mbar_wait(&wfull[s], (it / a.ws) & 1u, a.err, &abort_flag)) break;
+      if (quarter == 0) QTRACE(2 + g, it, 0);
+      if (it >= (uint32_t)AS && !nvb::mbar_wait(&aempty[t], ((it / AS) & 1u) ^ 1u, a.err, &abort_flag)) break;
+      if (quarter == 0) QTRACE(2 + g, it, 1);
       nvb::tc_fence_after();
       const uint8_t* p = wring + (size_t)s * stage_bytes + (size_t)r * a.bprs;
 #pragma unroll 1
@@ -719,6 +963,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
         tmem_st_32x32b_x32(lane_base + ACOL0 + (uint32_t)t * 128 + sub * 32, v);
       }
       tmem_st_wait();
+      if (quarter == 0) QTRACE(2 + g, it, 2);
       nvb::tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -727,39 +972,75 @@ __global__ void __launch_bounds__(kQThreads, 1) qgemm_decode_kernel(const __grid
       }
     }
   } else {
-    nvb::pdl_wait();  // warps 2, 3: epilogue only
-  }
-
-  if (warp < 4) {
-    __syncwarp();
-    int ok = 0;
-    if (lane == 0) ok = nvb::mbar_wait(tfull, 0, a.err, &abort_flag) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, ok, 0);
-    nvb::tc_fence_after();
-    if (ok) {
-      const int f = row0 + threadIdx.x;  // TMEM lane = weight row
-      const uint32_t t_row = tmem_base + ((uint32_t)(warp * 32) << 16);
-      constexpr int CH = BN < 64 ? BN : 64;
+    // ------------------------------------------------------------------ epilogue (warps 3, 12, 13, 14)
+    nvb::pdl_wait();
+    const int quarter = warp & 3;
+    const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    constexpr int CH = BN < 64 ? BN : 64;
+    QCursor c;
+    c.start(a);
+    if (!stream) {
+      // resident mode: the activation slice becomes f16 in place first (saturating; elementwise layout)
+      bool okx = !c.ok || nvb::mbar_wait(xbar, 0, a.err, &abort_flag);
+      if (okx && c.ok) {
+        const uint32_t xbytes = (uint32_t)c.nks * 4 * X_BOX;
+        for (uint32_t off = (uint32_t)(quarter * 32 + lane) * 16; off < xbytes; off += 128 * 16) {
+          uint4 v = *reinterpret_cast<const uint4*>(xres + off);
+          uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) w[j] = f2_to_h2(__uint_as_float(w[j] << 16), __uint_as_float(w[j] & 0xFFFF0000u));
+          *reinterpret_cast<uint4*>(xres + off) = v;
+        }
+        nvb::fence_proxy_async();
+      }
+      __syncwarp();
+      if (lane == 0) nvb::mbar_arrive(xready);
+    }
+    for (uint32_t unit = 0; c.ok; ++unit, c.next_unit(a)) {
+      const uint32_t b = unit % NACC, use = unit / NACC;
+      int ok = 0;
+      if (lane == 0) ok = nvb::mbar_wait(&tfull[b], use & 1u, a.err, &abort_flag) ? 1 : 0;
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      if (quarter == 0) QTRACE(4, unit, 0);
+      nvb::tc_fence_after();
+      const int f = c.group * QBM + quarter * 32 + lane;  // TMEM lane = weight row
 #pragma unroll 1
-      for (int c = 0; c < BN; c += CH) {
+      for (int col = 0; col < BN; col += CH) {
         uint32_t v[CH];
 #pragma unroll
-        for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_row + c + q, v + q);
+        for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_lane + b * (NCH * BN) + col + q, v + q);
         nvb::tmem_ld_wait();
         nvb::reg_fence<CH>(v);
+        if constexpr (NCH > 1) {
+#pragma unroll
+          for (int ch = 1; ch < NCH; ++ch) {
+            uint32_t u[CH];
+#pragma unroll
+            for (int q = 0; q < CH; q += 16) nvb::tmem_ld_32x32b_x16(t_lane + b * (NCH * BN) + ch * BN + col + q, u + q);
+            nvb::tmem_ld_wait();
+            nvb::reg_fence<CH>(u);
+#pragma unroll
+            for (int q = 0; q < CH; ++q) v[q] = __float_as_uint(__uint_as_float(v[q]) + __uint_as_float(u[q]));
+          }
+        }
         if (f < a.N) {
           if (a.S == 1) {
 #pragma unroll
             for (int j = 0; j < CH; ++j)
-              if (c + j < a.M) a.out[(long)(c + j) * a.out_ld + f] = __float2bfloat16(__uint_as_float(v[j]));
+              if (col + j < a.M) a.out[(long)(col + j) * a.out_ld + f] = __float2bfloat16(__uint_as_float(v[j]));
           } else {
-            float* dst = a.partial + (long)split * a.M * a.N + f;
+            float* dst = a.partial + (long)c.split * a.M * a.N + f;
 #pragma unroll
             for (int j = 0; j < CH; ++j)
-              if (c + j < a.M) dst[(long)(c + j) * a.N] = __uint_as_float(v[j]);
+              if (col + j < a.M) dst[(long)(col + j) * a.N] = __uint_as_float(v[j]);
           }
         }
       }
+      if (quarter == 0) QTRACE(4, unit, 1);
+      nvb::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) nvb::mbar_arrive(&tempty[b]);
     }
   }
   nvb::tc_fence_before();
@@ -796,7 +1077,7 @@ __global__ void qdequant_kernel(const uint8_t* __restrict__ w, int N, int K, int
 }
 
 struct QPlan {
-  int bn, kper, S, ws, xs, bprs;
+  int bn, kper, S, ws, xs, bprs, grid, per_split;
   size_t smem;
 };
 
@@ -831,61 +1112,67 @@ bool q_type_supported(int t) {
          t == T_TQ2_0 || t == T_MXFP4 || t == T_NVFP4;
 }
 
-// K split: the resident activation slice (BN x kper*256 bf16) must fit kQXBytes, the splits should give every SM
-// a CTA, and the packed ring must keep at least two row steps.
+// Persistent grid of at most one CTA per SM.  The K split S is chosen by a cost model in bytes: the busiest CTA's
+// packed row steps times the SM count (time at a fixed per-SM stream rate), plus the fp32 split partials written
+// and read back; near ties go to fewer splits.  Resident mode also needs the split's activation slice
+// (BN x kper*256) within kQXBytes and at least two packed ring stages beside it.
 QPlan q_plan(int M, int N, int K, int type, int sms) {
   QPlan p{};
   p.bn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   p.bprs = row_step_bytes(type);
   const int ksteps = K / QSTEP, groups = (N + QBM - 1) / QBM;
   const int x_step = p.bn * QSTEP * 2;
+  const int stage = QBM * p.bprs;
   // token tiles of 64 and more stream their activations (an f16 copy) through a ring of row steps: a resident
   // slice would cap the K range at 512 and multiply the splits and their fp32 partials
   p.xs = p.bn >= 64 ? (p.bn >= 256 ? 1 : p.bn >= 128 ? 2 : 3) : 0;
-  int kper = p.xs ? ksteps : kQXBytes / x_step;
-  if (kper < 1) kper = 1;
-  if (kper > ksteps) kper = ksteps;
-  // with few waves of CTAs, take the K split (within the activation budget) whose CTAs fill the last wave best
-  // (fewer splits on a tie: fewer fp32 partials); with many waves the tail matters little and every extra
-  // split costs partial traffic, so keep the fewest
-  if (groups < 2 * sms) {
-    const int kmax = kper;
-    double best = -1.0;
-    for (int kp = kmax; kp >= 1; --kp) {
-      const int S = (ksteps + kp - 1) / kp;
-      if (kp < kmax && (ksteps + kp) / (kp + 1) == S) continue;  // same split count as a larger kper
-      const long ctas = (long)groups * S;
-      const long waves = (ctas + sms - 1) / sms;
-      const double eff = (double)ctas / (double)(waves * sms);
-      if (eff > best + 0.04) {
-        best = eff;
-        kper = kp;
-      }
-      if (S >= 16) break;
+  const int kres = std::max(1, std::min(ksteps, kQXBytes / x_step));
+  const int smax = std::max(16, (ksteps + kres - 1) / kres);
+  double best = -1.0;
+  for (int S = 1; S <= std::min(ksteps, smax); ++S) {
+    const int kper = (ksteps + S - 1) / S;
+    if ((ksteps + kper - 1) / kper != S) continue;  // the same split as a smaller S
+    if (!p.xs && kper > kres) continue;
+    const int ring = (kQRingBytes - (p.xs ? p.xs : kper) * x_step) / stage;
+    if (ring < 2) continue;
+    long per_cta;
+    int grid, per_split = 0;
+    if (p.xs) {
+      const long units = (long)groups * S;
+      grid = (int)std::min<long>(units, sms);
+      per_cta = (units + grid - 1) / grid * kper;
+    } else {
+      per_split = std::min(groups, std::max(1, sms / S));
+      grid = per_split * S;
+      per_cta = (long)((groups + per_split - 1) / per_split) * kper;
+    }
+    const double cost = (double)per_cta * stage * sms + (S > 1 ? (double)S * M * N * 8.0 : 0.0);
+    if (best < 0 || cost < best * 0.97) {
+      best = cost;
+      p.S = S;
+      p.kper = kper;
+      p.grid = grid;
+      p.per_split = per_split;
+      p.ws = std::min(12, ring);
     }
   }
-  const int stage = QBM * p.bprs;
-  int ws = 0;
-  for (;;) {
-    ws = (kQRingBytes - (p.xs ? p.xs : kper) * x_step) / stage;
-    if (ws >= 2 || kper == 1 || p.xs) break;
-    kper = (kper + 1) / 2;
-  }
-  if (ws > 12) ws = 12;
-  p.kper = kper;
-  p.S = (ksteps + kper - 1) / kper;
-  p.ws = ws;
-  p.smem = 1024 + (size_t)(p.xs ? p.xs : kper) * x_step + (size_t)ws * stage +
-           (size_t)(2 + 2 * ws + 2 * kQAStages + 1 + 2 * kQMaxXS) * 8 + 64;
+  TORCH_CHECK(best >= 0, "packed GEMM: no K split fits shared memory");
+  p.smem = 1024 + (size_t)(p.xs ? p.xs : p.kper) * x_step + (size_t)p.ws * stage +
+           (size_t)(2 + 2 * p.ws + 2 * kQAStages + 4 + 2 * kQMaxXS) * 8 + 64;
   return p;
 }
 
 template <int TYPE, int BN>
 void q_launch(const CUtensorMap& xm, const QArgs& a, const QPlan& p, cudaStream_t st) {
   auto kern = qgemm_decode_kernel<TYPE, BN>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem);
-  const int groups = (a.N + QBM - 1) / QBM;
-  C10_CUDA_CHECK(nvb::launch(kern, dim3(groups * a.S), dim3(kQThreads), p.smem, st, xm, a));
+  static int attr_bytes[64] = {0};  // per device: the dynamic shared-memory limit raised so far
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || attr_bytes[dev] < (int)p.smem) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)p.smem));
+    if (dev < 64) attr_bytes[dev] = (int)p.smem;
+  }
+  C10_CUDA_CHECK(nvb::launch(kern, dim3(p.grid), dim3(kQThreads), p.smem, st, xm, a));
 }
 
 template <int TYPE>
@@ -949,6 +1236,20 @@ int64_t qgemm_splits_cuda(int64_t M, int64_t N, int64_t K, int64_t type) {
 
 int64_t qgemm_row_step_bytes(int64_t type) { return row_step_bytes((int)type); }
 
+// Optional clock64 trace of CTA 0 of every following qgemm launch (int64 [6][64][4], see QTRACE); None turns it
+// off.  A profiling aid: the per-role timeline of one CTA shows which hand-off paces the pipeline.
+namespace {
+long long* g_qtrace = nullptr;
+}
+void qgemm_set_trace(c10::optional<torch::Tensor> t) {
+  if (t.has_value()) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kLong && t->numel() >= 6 * 64 * 4, "trace: int64 [6, 64, 4]");
+    g_qtrace = reinterpret_cast<long long*>(t->data_ptr<int64_t>());
+  } else {
+    g_qtrace = nullptr;
+  }
+}
+
 // y[M, N] = x[M, K] @ dequant(w)^T for decode-sized M (<= 256).  With more than one split the fp32 partials go
 // to ``parts`` [S, M, N] (S from qgemm_splits) and, unless ``partial_out``, are summed into ``out``.
 int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, int64_t K, torch::Tensor out,
@@ -971,6 +1272,8 @@ int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, in
   a.ksteps = (int)(K / QSTEP);
   a.kper = p.kper;
   a.S = p.S;
+  a.groups = (int)((N + QBM - 1) / QBM);
+  a.per_split = p.per_split;
   a.ws = p.ws;
   a.xs = p.xs;
   a.bprs = p.bprs;
@@ -978,6 +1281,7 @@ int64_t qgemm_cuda(torch::Tensor x, torch::Tensor w, int64_t type, int64_t N, in
   a.out = reinterpret_cast<bf16*>(out.data_ptr());
   a.out_ld = out.stride(0);
   a.err = err.has_value() ? err->data_ptr<int>() : nullptr;
+  a.trace = g_qtrace;
   if (p.S > 1) {
     TORCH_CHECK(parts.has_value() && parts->is_cuda() && parts->scalar_type() == at::kFloat && parts->is_contiguous() &&
                     parts->numel() >= (long)p.S * M * N,

@@ -113,6 +113,48 @@ def bench_qgemm(ggml_type, M, N, K, iters):
             "TBps": round(byts / ours_p / 1e6, 3)}
 
 
+def trace_qgemm(ggml_type, M, N, K):
+    """Per-role clock64 timeline of CTA 0 of one dequant-fused GEMM launch (cycles from the end of set-up):
+    for every row step the producer's ring slot free time, each dequant group's (packed data ready, TMEM slot
+    free, decoded) times and the MMA waiter's (operands seen, handed to the issuer) times; then the per-unit
+    epilogue."""
+    import numpy as np
+    from ..loaders.gguf import pack_random_blocks
+    from .quant import GgufPacked
+    C = ops._cuda_ext()
+    raw = torch.from_numpy(np.frombuffer(pack_random_blocks(ggml_type, (N, K), 0), dtype=np.uint8).copy()).cuda()
+    w = GgufPacked(raw, ggml_type, N, K)
+    x = torch.randn(M, K, device="cuda").bfloat16()
+    for _ in range(3):
+        w.linear(x)
+    torch.cuda.synchronize()
+    tr = torch.zeros(6, 64, 4, dtype=torch.int64, device="cuda")
+    torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda").fill_(1)  # the weights come from DRAM
+    C.qgemm_set_trace(tr)
+    try:
+        w.linear(x)
+        torch.cuda.synchronize()
+    finally:
+        C.qgemm_set_trace(None)
+    t = tr.cpu()
+    t0 = int(t[5, 0, 0])
+    rel = lambda v: int(v) - t0 if int(v) else -1
+    lines = []
+    for it in range(64):
+        mma_ready, mma_done = rel(t[1, it, 0]), rel(t[1, it, 1])
+        if mma_ready < 0 and mma_done < 0:
+            break
+        g = it & 1
+        lines.append(f"step {it:2d}: producer slot {rel(t[0, it, 0]):7d} | dequant g{g} data {rel(t[2 + g, it, 0]):7d} "
+                     f"slot {rel(t[2 + g, it, 1]):7d} decoded {rel(t[2 + g, it, 2]):7d} | operands seen {mma_ready:7d} "
+                     f"handed to MMA {mma_done:7d}")
+    for u in range(64):
+        if int(t[4, u, 0]) == 0:
+            break
+        lines.append(f"unit {u:2d}: epilogue start {rel(t[4, u, 0]):7d} end {rel(t[4, u, 1]):7d}")
+    return lines
+
+
 def bench_decode(B, ctx, nq, nkv, hd, iters):
     dev = "cuda"
     BS = 256
@@ -194,10 +236,16 @@ def main():
     ap.add_argument("--gemm", default=None, help="GEMM cases M,N,K[,act[,splits]] separated by ';' (e.g. for an ncu capture)")
     ap.add_argument("--decode", default=None, help="single decode-attention case B,ctx,nq,nkv,hd")
     ap.add_argument("--qgemm", default=None, help="packed GGUF GEMM cases TYPE,M,N,K separated by ';' (TYPE e.g. Q4_K)")
+    ap.add_argument("--qtrace", default=None, help="per-role timeline of one packed GEMM launch TYPE,M,N,K")
     a = ap.parse_args()
     hbm, tflops, src = peaks()
     only = set(a.only.split(","))
     rows = []
+    if a.qtrace:
+        from ..loaders.dequant import TYPE_BY_NAME
+        f = a.qtrace.split(",")
+        print("\n".join(trace_qgemm(TYPE_BY_NAME[f[0]], int(f[1]), int(f[2]), int(f[3]))))
+        return
     if a.qgemm:
         from ..loaders.dequant import TYPE_BY_NAME
         for case in a.qgemm.split(";"):
