@@ -888,8 +888,8 @@ int64_t gemm_cuda(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t a
 // addresses as integers; per-rank arrays padded to 8).
 nvb::sp::Args sp_args_from(const std::vector<int64_t>& v, double eps) {
   // layout: mode, rank, R, T, per, per_max, H, n_prod, has_res, norm_mode, wait_ns, epoch, split_flag, my_recv,
-  //         my_rs_flag, residual, norm_w, recv[8], rs_flag[8], gather[8], ag_flag[8], trace, oneshot
-  TORCH_CHECK(v.size() == 19 + 4 * nvb::sp::kMaxRanks, "bad SP plan");
+  //         my_rs_flag, residual, norm_w, recv[8], rs_flag[8], gather[8], ag_flag[8], trace
+  TORCH_CHECK(v.size() == 18 + 4 * nvb::sp::kMaxRanks, "bad SP plan");
   nvb::sp::Args a{};
   a.mode = (int)v[0];
   a.rank = (int)v[1];
@@ -916,10 +916,8 @@ nvb::sp::Args sp_args_from(const std::vector<int64_t>& v, double eps) {
     a.ag_flag[p] = reinterpret_cast<uint32_t*>(v[41 + p]);
   }
   a.trace = reinterpret_cast<unsigned long long*>(v[49]);
-  a.oneshot = (int)v[50];
   TORCH_CHECK(a.R >= 1 && a.R <= nvb::sp::kMaxRanks && a.rank >= 0 && a.rank < a.R, "bad SP rank / size");
   TORCH_CHECK(a.T >= 1 && a.T <= nvb::sp::kMaxRows && a.per >= 1 && a.per <= a.per_max, "bad SP rows");
-  TORCH_CHECK(!a.oneshot || a.T <= a.per_max, "one-shot SP: every rank holds all T rows of every source");
   TORCH_CHECK(a.H % 8 == 0 && a.H <= 128 * 8 * nvb::sp::kMaxChunks, "SP rows need H % 8 == 0 and H <= 8192");
   return a;
 }

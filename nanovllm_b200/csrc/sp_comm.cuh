@@ -38,7 +38,6 @@ constexpr int kRowCtas = 128;     // CTAs that reduce rows: always co-resident (
 
 struct Args {
   int mode;        // 0 off, 1 AG + RMSNorm prologue (consumer), 2 RS epilogue (producer)
-  int oneshot;     // 1: producers push every row to every rank and each rank reduces all rows itself
   int rank, R, T, per, per_max, H;
   int n_prod;      // consumer: producer CTAs per rank of the slot it consumes
   int has_res, norm_mode;
@@ -126,12 +125,10 @@ NV_DEVICE float block_sum(float v, float* red) {
   return s;
 }
 
-// Rows this rank reduces: its SP slice [rank*per, ...) -- or, one-shot, all T rows (every rank holds every
-// partial and computes the same rounded sums in rank order, so the replicated results agree bit for bit).
-// CTA ``cta`` of ``ncta`` handles local rows cta, cta + ncta, ...
-__host__ __device__ __forceinline__ int row0_of(const Args& a) { return a.oneshot ? 0 : a.rank * a.per; }
+// Rows this rank reduces: its SP slice [rank*per, ...).  CTA ``cta`` of ``ncta`` handles local rows cta,
+// cta + ncta, ...
+__host__ __device__ __forceinline__ int row0_of(const Args& a) { return a.rank * a.per; }
 __host__ __device__ __forceinline__ int owned_rows(const Args& a) {
-  if (a.oneshot) return a.T;
   const int r0 = a.rank * a.per;
   const int r1 = a.T < r0 + a.per ? a.T : r0 + a.per;
   return r1 > r0 ? r1 - r0 : 0;
@@ -222,20 +219,13 @@ NV_DEVICE void ag_norm_rows(const Args& a, int cta, int ncta, float* red) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = v[j][e] * inv * g[e];
       const uint4 packed = pack8(o);
-      if (a.oneshot) {
-        *reinterpret_cast<uint4*>(a.gather[a.rank] + (size_t)t * H + c) = packed;  // local rows only
-      } else {
 #pragma unroll
-        for (int p = 0; p < kMaxRanks; ++p)
-          if (p < a.R) *reinterpret_cast<uint4*>(a.gather[p] + (size_t)t * H + c) = packed;
-      }
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < a.R) *reinterpret_cast<uint4*>(a.gather[p] + (size_t)t * H + c) = packed;
     }
   }
   __syncthreads();  // every thread's stores precede the flags below (release is cumulative)
-  if (a.oneshot) {
-    if (tid == 0)
-      for (int i = cta; i < n_own; i += ncta) st_release_gpu(a.ag_flag[a.rank] + r0 + i, ep);
-  } else if (tid < a.R) {
+  if (tid < a.R) {
     for (int i = cta; i < n_own; i += ncta) st_release_sys(a.ag_flag[tid] + r0 + i, ep);
   }
 }
@@ -249,7 +239,7 @@ NV_DEVICE bool wait_ag_rows_warp(const Args& a, int* err) {
   int ok = 1;
   const uint32_t* flags = a.ag_flag[a.rank];
   for (int t = lane; t < a.T && ok; t += 32)
-    if (!(a.oneshot ? wait_eq_gpu(flags + t, ep, t0, a.wait_ns, err) : wait_eq_sys(flags + t, ep, t0, a.wait_ns, err))) {
+    if (!wait_eq_sys(flags + t, ep, t0, a.wait_ns, err)) {
       record_error(err, kErrFlagTimeout);
       ok = 0;
     }
@@ -266,7 +256,7 @@ NV_DEVICE void rs_publish(const Args& a, int cta) {
 }
 
 // Push a bf16 tile held in shared memory -- rows = tokens [t0, t1), 128 features starting at feature f0,
-// row stride ``ld`` elements -- to the owners' receive buffers (16-byte peer stores); one-shot: to every rank.
+// row stride ``ld`` elements -- to the owners' receive buffers (16-byte peer stores).
 NV_DEVICE void rs_push_tile(const Args& a, const __nv_bfloat16* tile, int ld, int t0, int t1, int f0) {
   const int chunks = 16;  // 128 features = 16 x 8
   const int n = (t1 - t0) * chunks;
@@ -274,15 +264,8 @@ NV_DEVICE void rs_push_tile(const Args& a, const __nv_bfloat16* tile, int ld, in
     const int t = t0 + idx / chunks, ch = idx % chunks;
     if (f0 + ch * 8 >= a.H) continue;  // the last 128-row weight tile may overhang H
     const uint4 v = *reinterpret_cast<const uint4*>(tile + (size_t)(t - t0) * ld + ch * 8);
-    if (a.oneshot) {
-#pragma unroll
-      for (int p = 0; p < kMaxRanks; ++p)
-        if (p < a.R)
-          *reinterpret_cast<uint4*>(a.recv[p] + ((size_t)a.rank * a.per_max + t) * a.H + f0 + ch * 8) = v;
-    } else {
-      const int owner = t / a.per, local = t - owner * a.per;
-      *reinterpret_cast<uint4*>(a.recv[owner] + ((size_t)a.rank * a.per_max + local) * a.H + f0 + ch * 8) = v;
-    }
+    const int owner = t / a.per, local = t - owner * a.per;
+    *reinterpret_cast<uint4*>(a.recv[owner] + ((size_t)a.rank * a.per_max + local) * a.H + f0 + ch * 8) = v;
   }
 }
 

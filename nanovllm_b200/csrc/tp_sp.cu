@@ -49,12 +49,7 @@ __global__ void __launch_bounds__(128) sp_embed_rs_kernel(const __grid_constant_
           v = nvb::sp::pack8(f);
         }
       }
-      if (sp.oneshot) {
-        for (int p = 0; p < sp.R; ++p)
-          *reinterpret_cast<uint4*>(sp.recv[p] + ((size_t)sp.rank * sp.per_max + t) * H + c) = v;
-      } else {
-        *reinterpret_cast<uint4*>(sp.recv[owner] + ((size_t)sp.rank * sp.per_max + local) * H + c) = v;
-      }
+      *reinterpret_cast<uint4*>(sp.recv[owner] + ((size_t)sp.rank * sp.per_max + local) * H + c) = v;
     }
   }
   nvb::sp::rs_publish(sp, blockIdx.x);
@@ -69,12 +64,7 @@ __global__ void __launch_bounds__(128) sp_rs_push_kernel(const __grid_constant__
     const int owner = t / sp.per, local = t - owner * sp.per;
     for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
       const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)t * ld + c);
-      if (sp.oneshot) {
-        for (int p = 0; p < sp.R; ++p)
-          *reinterpret_cast<uint4*>(sp.recv[p] + ((size_t)sp.rank * sp.per_max + t) * H + c) = v;
-      } else {
-        *reinterpret_cast<uint4*>(sp.recv[owner] + ((size_t)sp.rank * sp.per_max + local) * H + c) = v;
-      }
+      *reinterpret_cast<uint4*>(sp.recv[owner] + ((size_t)sp.rank * sp.per_max + local) * H + c) = v;
     }
   }
   nvb::sp::rs_publish(sp, blockIdx.x);

@@ -86,8 +86,7 @@ def main() -> None:
     wqkv, wo = rnd(QKV // R, H), rnd(H, H // R)
     wgu, wd = rnd(2 * I // R, H), rnd(H, I // R)
     nw = torch.ones(H, dtype=torch.bfloat16, device=dev)
-    ws_os = spmod.SPWorkspace(256, H, dev, oneshot=True)
-    ws_rs = spmod.SPWorkspace(256, H, dev, oneshot=False)
+    ws_rs = spmod.SPWorkspace(256, H, dev)
     ws_ar = symm.init_workspace(256, H, dev)
     peak = _peak_hbm()
     rows = []
@@ -128,19 +127,18 @@ def main() -> None:
             dist.all_reduce(y)
             ops.rms_norm(y, nw, 1e-6, residual=res2)
 
-        t_sp = _time(lambda: sp_layer(ws_os), args.iters)
         t_rs = _time(lambda: sp_layer(ws_rs), args.iters)
         t_ar = _time(ar_layer, args.iters)
         t_nc = _time(nccl_layer, args.iters)
         wbytes = (wqkv.numel() + wo.numel() + wgu.numel() + wd.numel()) * 2
         link = 4 * (R - 1) / R * T * H * 2
-        roof = max(wbytes / (peak * 1e3), link / (LINK_GBS * 1e3))  # rsag bytes; one-shot moves (R/2)x more
-        rows.append({"tokens": T, "sp_oneshot_us": round(t_sp, 2), "sp_rsag_us": round(t_rs, 2),
+        roof = max(wbytes / (peak * 1e3), link / (LINK_GBS * 1e3))
+        rows.append({"tokens": T, "sp_rsag_us": round(t_rs, 2),
                      "ar_us": round(t_ar, 2), "nccl_cublas_us": round(t_nc, 2),
-                     "roofline_us": round(roof, 2), "sp_frac_of_roofline": round(roof / min(t_sp, t_rs), 3),
+                     "roofline_us": round(roof, 2), "sp_frac_of_roofline": round(roof / t_rs, 3),
                      "weights_MB": round(wbytes / 1e6, 1), "nvlink_MB": round(link / 1e6, 3)})
         if args.trace:
-            for name, w_ in (("oneshot", ws_os), ("rsag", ws_rs)):
+            for name, w_ in (("rsag", ws_rs),):
                 for _ in range(3):  # a few traced layers back to back; the last one is reported
                     dist.barrier()
                     sp_layer(w_)

@@ -77,19 +77,16 @@ class SPPartial:
 
 
 class SPWorkspace:
-    def __init__(self, max_tokens: int, hidden: int, device: torch.device, wait_ns: int = 0,
-                 oneshot: Optional[bool] = None):
+    def __init__(self, max_tokens: int, hidden: int, device: torch.device, wait_ns: int = 0):
         from .. import ops
         self.C = ops._cuda_ext()
         self.R, self.rank = ps.tp_size(), ps.tp_rank()
         assert self.R <= MAX_RANKS, "at most 8 ranks"
         self.max_tokens = min(int(max_tokens), MAX_ROWS)
         self.hidden = int(hidden)
-        # one-shot mode: every rank receives every source's partial of every row (sized for it in both modes)
+        # reduce-scatter to the row owner, then all-gather of the normalised rows (two hand-offs, 2 (R-1)/R x the
+        # bytes); every source's slot holds up to max_tokens rows
         self.per_max = self.max_tokens
-        # one-shot (default): one NVLink hand-off per junction, (R-1) x the bytes; rsag: reduce-scatter to the row
-        # owner, then all-gather of the normalised rows (two hand-offs, 2 (R-1)/R x the bytes)
-        self.oneshot = (os.environ.get("NVB_SP_MODE", "rsag") == "oneshot") if oneshot is None else bool(oneshot)
         self.wait_ns = int(wait_ns)
         H = self.hidden
         self.off_rs = 256
@@ -137,15 +134,13 @@ class SPWorkspace:
     def begin(self, T: int) -> None:
         """Start an SP forward of T tokens: bump the epoch (one tiny kernel) and restart the slot sequence."""
         self.T = int(T)
-        self.per = self.T if self.oneshot else (self.T + self.R - 1) // self.R
+        self.per = (self.T + self.R - 1) // self.R
         self.slot = 0
         self.C.sp_begin(self.epoch_ptr)
         from .. import ops
         ops.add_launches(1)
 
     def owned_rows(self) -> int:
-        if self.oneshot:
-            return self.T
         r0 = self.rank * self.per
         return max(0, min(self.T, r0 + self.per) - r0)
 
@@ -153,13 +148,12 @@ class SPWorkspace:
         return self.gather_buf[:(T or self.T)]
 
     def residual_view(self) -> torch.Tensor:
-        """This rank's residual rows (valid after the last consumer of the forward ran): its SP slice, or all T
-        rows in one-shot mode."""
+        """This rank's residual rows (valid after the last consumer of the forward ran): its SP slice."""
         return self.res_buf[:self.owned_rows()]
 
     def owned_range(self):
         """Global rows [r0, r1) of ``residual_view``."""
-        r0 = 0 if self.oneshot else self.rank * self.per
+        r0 = self.rank * self.per
         return r0, r0 + self.owned_rows()
 
     def _plan(self, mode: int, slot: int, n_prod: int = 0, has_res: int = 0, norm_mode: int = 2,
@@ -178,7 +172,7 @@ class SPWorkspace:
                  int(norm_mode), self.wait_ns, self.epoch_ptr, me + self.off_split + slot * MAX_PROD * 4,
                  me + self.off_recv, rs[self.rank], me + self.off_res,
                  norm_w.data_ptr() if norm_w is not None else 0]
-                + recv + pad + rs + pad + gather + pad + ag + pad + [trace, 1 if self.oneshot else 0])
+                + recv + pad + rs + pad + gather + pad + ag + pad + [trace])
 
     def producer_plan(self):
         """(slot, plan) for the next reduce-scatter producer of this forward."""
