@@ -25,6 +25,7 @@
 #include "tma_host.h"
 
 #include "attention_kernels.cuh"
+#include "attention_tc.cuh"
 
 namespace {
 
@@ -149,6 +150,48 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
         reinterpret_cast<const bf16*>(q.data_ptr()), q_stride, reinterpret_cast<bf16*>(out.data_ptr()), o_stride, kc,
         vc, kvs, cu_q.data_ptr<int>(), cu_k.data_ptr<int>(), bt, bt_stride, paged ? 1 : 0, nseq, nq, nkv, hd,
         block_size, (float)scale, (float)softcap, (int)window, causal ? 1 : 0, total_q));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  // tcgen05 kernel (attention_tc.cuh) whenever its tiles fit: 128 query rows hold whole GQA groups and a paged
+  // key tile never straddles a cache block; the mma.sync kernel below covers the rest (NVB_PREFILL_TC=0 forces it)
+  const int tc_bn = hd == 256 ? 64 : 128;
+  static const bool tc_on = [] {
+    const char* v = getenv("NVB_PREFILL_TC");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (tc_on && 128 % G == 0 && (!paged || block_size % tc_bn == 0)) {
+    CUtensorMap tk, tv;
+    if (paged) {
+      const uint64_t rows = (uint64_t)k_cache->size(0) * nkv * block_size;
+      tk = nvb::make_tmap_2d_bf16(k_cache->data_ptr(), rows, hd, hd, tc_bn);
+      tv = nvb::make_tmap_2d_bf16(v_cache->data_ptr(), rows, hd, hd, tc_bn);
+    } else {
+      const uint64_t T = kv_src->size(0);
+      const uint64_t heads = nq + 2 * nkv;
+      uint64_t dims[3] = {(uint64_t)hd, heads, T};
+      uint64_t strides[2] = {(uint64_t)hd * 2, (uint64_t)kv_src->stride(0) * 2};
+      uint32_t box[3] = {64, 1, (uint32_t)tc_bn};
+      tk = nvb::make_tmap(kv_src->data_ptr(), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, dims, strides, box);
+      tv = tk;
+    }
+    const int TPT = 128 / G;
+    dim3 grid((unsigned)((max_q + TPT - 1) / TPT), nkv, nseq);
+    auto* qp = reinterpret_cast<const bf16*>(q.data_ptr());
+    auto* op = reinterpret_cast<bf16*>(out.data_ptr());
+#define LAUNCH_TC(HD_)                                                                                           \
+  {                                                                                                              \
+    auto kern = prefill_tc_kernel<HD_>;                                                                          \
+    const size_t sm = TcAttnCfg<HD_>::smem();                                                                    \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));            \
+    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(256), sm, stream, tk, tv, qp, q_stride, op, o_stride,            \
+                               cu_q.data_ptr<int>(), cu_k.data_ptr<int>(), bt, bt_stride, paged ? 1 : 0, (int)nq, \
+                               (int)nkv, block_size, (float)scale, (float)softcap, (int)window, causal ? 1 : 0, e)); \
+  }
+    if (hd == 64) LAUNCH_TC(64)
+    else if (hd == 128) LAUNCH_TC(128)
+    else LAUNCH_TC(256)
+#undef LAUNCH_TC
     C10_CUDA_KERNEL_LAUNCH_CHECK();
     return;
   }
