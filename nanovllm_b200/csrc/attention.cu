@@ -139,6 +139,23 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
   } else {
     TORCH_CHECK(kv_src.has_value() && kv_src->stride(-1) == 1, "kv_src required for contiguous prefill");
   }
+  if (hd == 32 && !paged && (128 % G == 0)) {
+    // BERT-small head dim on the tcgen05 kernel in 64-wide tiles (attention_tc.cuh, HDR = 32)
+    const uint64_t T = kv_src->size(0);
+    const uint64_t row = (uint64_t)(nq + 2 * nkv) * hd;
+    CUtensorMap tk = nvb::make_tmap_2d_bf16(kv_src->data_ptr(), T, row, kv_src->stride(0), 128);
+    const int TPT = 128 / G;
+    dim3 grid((unsigned)((max_q + TPT - 1) / TPT), nkv, nseq);
+    auto kern = prefill_tc_kernel<64, 32>;
+    const size_t sm = TcAttnCfg<64>::smem();
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(256), sm, stream, tk, tk, reinterpret_cast<const bf16*>(q.data_ptr()),
+                               q_stride, reinterpret_cast<bf16*>(out.data_ptr()), o_stride, cu_q.data_ptr<int>(),
+                               cu_k.data_ptr<int>(), bt, bt_stride, 0, (int)nq, (int)nkv, block_size, (float)scale,
+                               (float)softcap, (int)window, causal ? 1 : 0, e));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   if (hd != 64 && hd != 128 && hd != 256) {
     const int total_q = q.size(0);
     const bf16* kc = paged ? reinterpret_cast<const bf16*>(k_cache->data_ptr())

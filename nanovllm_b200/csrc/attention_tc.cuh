@@ -98,7 +98,10 @@ __device__ __forceinline__ bool tca_handoff(int ok) {
   return r != 0;
 }
 
-template <int HD>
+// HD: the head dim the tiles are laid out for; HDR (<= HD): the model's head dim.  HDR 32 (BERT-small shapes)
+// runs in 64-wide tiles: Q's upper 32 dims are zero, so the neighbouring head's K dims that the 64-wide K box
+// brings along add nothing to S, and the matching upper half of O is never written out (contiguous K/V only).
+template <int HD, int HDR = HD>
 __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
     long q_tok_stride, bf16* __restrict__ out, long o_tok_stride, const int* __restrict__ cu_q,
@@ -199,9 +202,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
           const int row = (bt[tok / block_size] * nkv + kvh) * block_size + (tok % block_size);
 #pragma unroll
           for (int j = 0; j < HD / 64; ++j) nvb::tma_load_2d(dst + j * C::KBOX, map, &full[s], j * 64, row);
-        } else {
+        } else if constexpr (HDR == HD) {
 #pragma unroll
           for (int j = 0; j < HD / 64; ++j) nvb::tma_load_3d(dst + j * C::KBOX, map, &full[s], j * 64, head, k0 + tok);
+        } else {
+          // 2-D map over packed qkv rows: one 64-wide box from this head's first dim (zero fill past the row end)
+          nvb::tma_load_2d(dst, map, &full[s], head * HDR, k0 + tok);
         }
       }
       if (!ok)  // bounded drain of copies that may still be landing
@@ -297,11 +303,11 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
     const int st4 = tid - 128;
     // Q tile -> shared memory in the 128-byte swizzle the MMA reads (rows past the sequence are zero)
     for (int idx = st4; idx < 128 * (HD / 8); idx += 128) {
-      const int rr = idx / (HD / 8), c = idx % (HD / 8);
+      const int rr = idx / (HD / 8), c = idx % (HD / 8);  // c: 16-byte chunk of the (padded) row
       const int jt = tok_begin + rr / G;
       uint4 v = make_uint4(0, 0, 0, 0);
-      if (jt < qlen)
-        v = *reinterpret_cast<const uint4*>(q + (long)(q0 + jt) * q_tok_stride + (kvh * G + rr % G) * HD + c * 8);
+      if (jt < qlen && c * 8 < HDR)
+        v = *reinterpret_cast<const uint4*>(q + (long)(q0 + jt) * q_tok_stride + (kvh * G + rr % G) * HDR + c * 8);
       *reinterpret_cast<uint4*>(qs + (c >> 3) * C::QBOX + nvb::swz128(rr, c & 7)) = v;
     }
     nvb::fence_proxy_async();
@@ -419,9 +425,9 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
     if (ok) {
       nvb::tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* dst = out + (long)(q0 + jt) * o_tok_stride + (kvh * G + r % G) * HD;
+      bf16* dst = out + (long)(q0 + jt) * o_tok_stride + (kvh * G + r % G) * HDR;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = 0; c < HDR; c += 32) {
         uint32_t u[32];
         if (nt > 0) {
           tca_ld32(lane_base + C::O_COL + c, u);
