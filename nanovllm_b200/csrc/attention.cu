@@ -149,7 +149,7 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
     auto kern = prefill_tc_kernel<64, 32>;
     const size_t sm = TcAttnCfg<64>::smem();
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(256), sm, stream, tk, tk, reinterpret_cast<const bf16*>(q.data_ptr()),
+    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(384), sm, stream, tk, tk, reinterpret_cast<const bf16*>(q.data_ptr()),
                                q_stride, reinterpret_cast<bf16*>(out.data_ptr()), o_stride, cu_q.data_ptr<int>(),
                                cu_k.data_ptr<int>(), bt, bt_stride, 0, (int)nq, (int)nkv, block_size, (float)scale,
                                (float)softcap, (int)window, causal ? 1 : 0, e));
@@ -201,7 +201,7 @@ void prefill_attention_cuda(torch::Tensor q, torch::Tensor out, torch::Tensor cu
     auto kern = prefill_tc_kernel<HD_>;                                                                          \
     const size_t sm = TcAttnCfg<HD_>::smem();                                                                    \
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));            \
-    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(256), sm, stream, tk, tv, qp, q_stride, op, o_stride,            \
+    C10_CUDA_CHECK(nvb::launch(kern, grid, dim3(384), sm, stream, tk, tv, qp, q_stride, op, o_stride,            \
                                cu_q.data_ptr<int>(), cu_k.data_ptr<int>(), bt, bt_stride, paged ? 1 : 0, (int)nq, \
                                (int)nkv, block_size, (float)scale, (float)softcap, (int)window, causal ? 1 : 0, e)); \
   }

@@ -9,8 +9,9 @@
 // pair: the G heads that share a KV head are packed into the MMA's 128 rows, so one K/V tile serves all of
 // them.  Per KV tile of BN keys:
 //   S  = Q K^T        tcgen05.mma, A = Q (shared memory, K-major), B = K tile (shared memory, K-major), D in TMEM
-//   P  = softmax(S)   128 softmax threads, thread = query row = TMEM lane: tcgen05.ld the row, mask, online max,
-//                     exp2, row sum; P goes back as bf16 into the first BN/2 columns of the same TMEM buffer
+//   P  = softmax(S)   256 softmax threads, two per query row (TMEM lane), each on half of the tile's keys:
+//                     tcgen05.ld, mask, online max (exchanged between the halves), exp2, row sum; P goes back
+//                     as bf16 into the first BN/2 columns of the same TMEM buffer
 //   O += P V          tcgen05.mma with A = P read from TMEM and B = V tile (shared memory, MN-major: the cache
 //                     stores keys as rows with head_dim contiguous), fp32 O accumulator in TMEM
 // S is double-buffered in TMEM (S of tile j+1 is computed while the softmax threads work on tile j).  The max
@@ -19,7 +20,7 @@
 // and the final O / l exact.
 // Warps: 0 / 3 TMA producers (K ring / V ring), 1 MMA issuer (lane 0), 2 MMA waiter (does every mbarrier wait of the issuer
 // and hands over through a named barrier: an mbarrier wait in the issuing thread right after a batch of
-// tcgen05.mma stalls until the batch drains), 4-7 softmax + epilogue.  Every wait is bounded.
+// tcgen05.mma stalls until the batch drains), 4-11 softmax + epilogue.  Every wait is bounded.
 #pragma once
 #include "common.cuh"
 
@@ -30,7 +31,7 @@ struct TcAttnCfg {
   static constexpr int BN = HD == 256 ? 64 : 128;     // keys per tile
   // separate K and V rings: a K tile is free once its S MMA is done (so K runs KS tiles ahead of the MMAs),
   // a V tile once its PV MMA is done
-  static constexpr int KS = HD == 64 ? 4 : 3;
+  static constexpr int KS = HD == 64 ? 4 : HD == 256 ? 2 : 3;
   static constexpr int VS = HD == 64 ? 4 : 2;
   static constexpr int KBOX = BN * 128;               // one 64-dim box of a K or V tile, bytes
   static constexpr int KTILE = (HD / 64) * KBOX;      // K (or V) tile, bytes
@@ -38,7 +39,7 @@ struct TcAttnCfg {
   static constexpr int QTILE = (HD / 64) * QBOX;
   static constexpr uint32_t O_COL = 2 * BN;           // TMEM: S buffers [0, 2 BN), O [2 BN, 2 BN + HD)
   static_assert(O_COL + HD <= 512, "TMEM plan");
-  static constexpr size_t smem() { return 1024 + QTILE + (size_t)(KS + VS) * KTILE + 256; }
+  static constexpr size_t smem() { return 1024 + QTILE + (size_t)(KS + VS) * KTILE + 256 + 6 * 128 * 4; }
 };
 
 __device__ __forceinline__ void tca_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -60,6 +61,23 @@ __device__ __forceinline__ void tca_st32(uint32_t taddr, const uint32_t (&r)[32]
       "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
+}
+__device__ __forceinline__ void tca_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// Named barrier 3 over the 256 softmax threads; returns how many passed a non-zero flag.
+__device__ __forceinline__ int __syncthreads_count_named(int flag) {
+  int n;
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.popc.u32 %0, 3, 256, p;\n\t}"
+               : "=r"(n)
+               : "r"(flag)
+               : "memory");
+  return n;
 }
 __device__ __forceinline__ void tca_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -102,7 +120,7 @@ __device__ __forceinline__ bool tca_handoff(int ok) {
 // runs in 64-wide tiles: Q's upper 32 dims are zero, so the neighbouring head's K dims that the 64-wide K box
 // brings along add nothing to S, and the matching upper half of O is never written out (contiguous K/V only).
 template <int HD, int HDR = HD>
-__global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
+__global__ void __launch_bounds__(384, 1) prefill_tc_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q,
     long q_tok_stride, bf16* __restrict__ out, long o_tok_stride, const int* __restrict__ cu_q,
     const int* __restrict__ cu_k, const int* __restrict__ block_tables, int bt_stride, int paged, int nq, int nkv,
@@ -143,6 +161,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
   uint64_t* o_done = s_free + 2;    // one phase per PV
   uint64_t* o_final = o_done + 1;
   uint64_t* q_full = o_final + 1;
+  uint8_t* smem_extra = reinterpret_cast<uint8_t*>(bars) + 256;  // row-max exchange and row sums (4 KB)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -158,12 +177,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       nvb::mbar_init(&s_full[b], 1);
-      nvb::mbar_init(&p_full[b], 4);
+      nvb::mbar_init(&p_full[b], 8);
       nvb::mbar_init(&s_free[b], 1);
     }
     nvb::mbar_init(o_done, 1);
     nvb::mbar_init(o_final, 1);
-    nvb::mbar_init(q_full, 4);
+    nvb::mbar_init(q_full, 8);
     nvb::fence_mbar_init();
   }
   if (warp == 1) {
@@ -298,11 +317,19 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
       }
     }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax + epilogue
-    const int quarter = warp & 3, r = quarter * 32 + lane;  // query row = TMEM lane
-    const int st4 = tid - 128;
+    // ------------------------------------------------------------------ softmax + epilogue (warps 4-11)
+    // warps w and w + 4 share the TMEM lane quarter w & 3 (query rows) and split each S tile's columns: half 0
+    // takes keys [0, BN/2), half 1 [BN/2, BN); the halves exchange row maxima through shared memory once per
+    // tile, rescale their own half of O, and sum their row sums at the end
+    constexpr int HB = BN / 2;          // S columns per half
+    constexpr int PC = BN / 4;          // packed P columns per half
+    constexpr int OH = HD / 2;          // O columns per half
+    const int quarter = warp & 3, half = (warp - 4) >> 2, r = quarter * 32 + lane;
+    const int st8 = tid - 128;
+    float* xmax = reinterpret_cast<float*>(smem_extra);        // [2 tile parities][2 halves][128 rows]
+    float* lsum = xmax + 2 * 2 * 128;                            // [2 halves][128 rows]
     // Q tile -> shared memory in the 128-byte swizzle the MMA reads (rows past the sequence are zero)
-    for (int idx = st4; idx < 128 * (HD / 8); idx += 128) {
+    for (int idx = st8; idx < 128 * (HD / 8); idx += 256) {
       const int rr = idx / (HD / 8), c = idx % (HD / 8);  // c: 16-byte chunk of the (padded) row
       const int jt = tok_begin + rr / G;
       uint4 v = make_uint4(0, 0, 0, 0);
@@ -325,35 +352,37 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
       const int b = j & 1;
       int okw = 1;
       if (lane == 0) okw = nvb::mbar_wait(&s_full[b], (j >> 1) & 1, err, &abort_flag) ? 1 : 0;
-      if (!__shfl_sync(0xffffffffu, okw, 0)) {
-        ok = false;
-        break;
-      }
+      okw = __shfl_sync(0xffffffffu, okw, 0);
+      // every softmax warp reaches the exchange barrier below, ok or not, so none waits there for ever
       nvb::tc_fence_after();
-      float s[BN];
-      {
-        uint32_t u[BN];
+      float s[HB];
+      if (okw) {
+        uint32_t u[HB];
 #pragma unroll
-        for (int c = 0; c < BN; c += 32) tca_ld32(lane_base + (uint32_t)b * BN + c, *reinterpret_cast<uint32_t(*)[32]>(u + c));
+        for (int c = 0; c < HB; c += 32)
+          tca_ld32(lane_base + (uint32_t)b * BN + half * HB + c, *reinterpret_cast<uint32_t(*)[32]>(u + c));
         nvb::tmem_ld_wait();
-        nvb::reg_fence<BN>(u);
+        nvb::reg_fence<HB>(u);
 #pragma unroll
-        for (int e = 0; e < BN; ++e) s[e] = __uint_as_float(u[e]);
+        for (int e = 0; e < HB; ++e) s[e] = __uint_as_float(u[e]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < HB; ++e) s[e] = 0.f;
       }
-      const int key0 = (t_begin + j) * BN;
-      // a tile every key of which this row may see skips the per-key mask
-      const bool whole = rvalid && key0 + BN <= klen &&
-                         (!causal || (key0 + BN - 1 <= rpos && (window <= 0 || key0 > rpos - window)));
+      const int key0 = (t_begin + j) * BN + half * HB;
+      // a half-tile every key of which this row may see skips the per-key mask
+      const bool whole = rvalid && key0 + HB <= klen &&
+                         (!causal || (key0 + HB - 1 <= rpos && (window <= 0 || key0 > rpos - window)));
       float mt = -INFINITY;
       if (whole && softcap <= 0.f) {
 #pragma unroll
-        for (int e = 0; e < BN; ++e) {
+        for (int e = 0; e < HB; ++e) {
           s[e] *= sl2;
           mt = fmaxf(mt, s[e]);
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < BN; ++e) {
+        for (int e = 0; e < HB; ++e) {
           const int key = key0 + e;
           float x = softcap > 0.f ? apply_cap(s[e] * scale, softcap) * kLog2e : s[e] * sl2;
           bool valid = rvalid && key < klen;
@@ -363,6 +392,13 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
           mt = fmaxf(mt, x);
         }
       }
+      xmax[(b * 2 + half) * 128 + r] = mt;
+      const int all_ok = __syncthreads_count_named(okw && ok);
+      if (all_ok != 256) {
+        ok = false;
+        break;
+      }
+      mt = fmaxf(mt, xmax[(b * 2 + (half ^ 1)) * 128 + r]);
       float new_m = m_used;
       bool need = false;
       if (mt > -INFINITY) {
@@ -375,43 +411,38 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
       }
       if (__any_sync(0xffffffffu, need)) {
         // O must hold P_{j-1} V_{j-1} before it is rescaled (j >= 1 here: some earlier tile set m_used)
+        // a failed wait is reported at the next exchange barrier, which every softmax warp still reaches
         okw = 1;
         if (lane == 0) okw = nvb::mbar_wait(o_done, (j - 1) & 1, err, &abort_flag) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, okw, 0)) {
-          ok = false;
-          break;
-        }
+        if (!__shfl_sync(0xffffffffu, okw, 0)) ok = false;
         nvb::tc_fence_after();
         const float f = need ? exp2f(m_used - new_m) : 1.f;
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; ok && c < OH; c += 32) {
           uint32_t u[32];
-          tca_ld32(lane_base + C::O_COL + c, u);
+          tca_ld32(lane_base + C::O_COL + half * OH + c, u);
           nvb::tmem_ld_wait();
           nvb::reg_fence<32>(u);
 #pragma unroll
           for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * f);
-          tca_st32(lane_base + C::O_COL + c, u);
+          tca_st32(lane_base + C::O_COL + half * OH + c, u);
         }
         tca_st_wait();
       }
       if (need) l *= exp2f(m_used - new_m);
       m_used = new_m;
-      // P (bf16 pairs) over the first BN / 2 columns of this S buffer
+      // P (bf16 pairs) of this half over packed columns [half * PC, half * PC + PC) of the S buffer
       float rs = 0.f;
+      uint32_t u[PC];
 #pragma unroll
-      for (int c = 0; c < BN / 2; c += 32) {
-        uint32_t u[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int k = 2 * (c + e);
-          const float p0 = m_used == -INFINITY ? 0.f : exp2f(s[k] - m_used);
-          const float p1 = m_used == -INFINITY ? 0.f : exp2f(s[k + 1] - m_used);
-          rs += p0 + p1;
-          u[e] = nvb::pack_bf16x2(p0, p1);
-        }
-        tca_st32(lane_base + (uint32_t)b * BN + c, u);
+      for (int e = 0; e < PC; ++e) {
+        const float p0 = m_used == -INFINITY ? 0.f : exp2f(s[2 * e] - m_used);
+        const float p1 = m_used == -INFINITY ? 0.f : exp2f(s[2 * e + 1] - m_used);
+        rs += p0 + p1;
+        u[e] = nvb::pack_bf16x2(p0, p1);
       }
+#pragma unroll
+      for (int c = 0; c < PC; c += 16) tca_st16(lane_base + (uint32_t)b * BN + half * PC + c, *reinterpret_cast<uint32_t(*)[16]>(u + c));
       l += rs;
       tca_st_wait();
       nvb::tc_fence_before();
@@ -421,13 +452,17 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(
     // epilogue: O / l, bf16 rows (rows past the sequence are not written)
     int okw = ok ? 1 : 0;
     if (okw && nt > 0 && lane == 0) okw = nvb::mbar_wait(o_final, 0, err, &abort_flag) ? 1 : 0;
-    ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
-    if (ok) {
+    okw = __shfl_sync(0xffffffffu, okw, 0);
+    lsum[half * 128 + r] = l;
+    const int all_ok = __syncthreads_count_named(okw);
+    if (all_ok == 256) {
       nvb::tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const float lt = l + lsum[(half ^ 1) * 128 + r];
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
       bf16* dst = out + (long)(q0 + jt) * o_tok_stride + (kvh * G + r % G) * HDR;
 #pragma unroll 1
-      for (int c = 0; c < HDR; c += 32) {
+      for (int c = half * OH; c < half * OH + OH; c += 32) {
+        if (c >= HDR) break;  // the zero-padded upper dims of a narrow head are not output
         uint32_t u[32];
         if (nt > 0) {
           tca_ld32(lane_base + C::O_COL + c, u);

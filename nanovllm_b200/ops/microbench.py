@@ -235,6 +235,7 @@ def main():
     ap.add_argument("--out", default=None)
     ap.add_argument("--gemm", default=None, help="GEMM cases M,N,K[,act[,splits]] separated by ';' (e.g. for an ncu capture)")
     ap.add_argument("--decode", default=None, help="single decode-attention case B,ctx,nq,nkv,hd")
+    ap.add_argument("--prefill", default=None, help="single causal prefill attention case T,nq,nkv,hd")
     ap.add_argument("--qgemm", default=None, help="packed GGUF GEMM cases TYPE,M,N,K separated by ';' (TYPE e.g. Q4_K)")
     ap.add_argument("--qtrace", default=None, help="per-role timeline of one packed GEMM launch TYPE,M,N,K")
     a = ap.parse_args()
@@ -251,6 +252,10 @@ def main():
         for case in a.qgemm.split(";"):
             f = case.split(",")
             rows.append(bench_qgemm(TYPE_BY_NAME[f[0]], int(f[1]), int(f[2]), int(f[3]), a.iters))
+        only = set()
+    if a.prefill:
+        v = [int(x) for x in a.prefill.split(",")]
+        rows.append(bench_prefill(v[0], v[1], v[2], v[3], a.iters))
         only = set()
     if a.gemm or a.decode:
         only = set()
