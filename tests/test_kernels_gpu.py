@@ -128,14 +128,17 @@ def test_paged_decode_reports_context_beyond_max_len():
 
 @pytest.mark.parametrize("hd,nq,nkv", [(128, 32, 8), (64, 8, 8), (256, 4, 1), (128, 16, 8)])
 @pytest.mark.parametrize("window", [0, 100])
-def test_paged_prefill_with_prefix(hd, nq, nkv, window):
+@pytest.mark.parametrize("amp", [1.0, 12.0])
+def test_paged_prefill_with_prefix(hd, nq, nkv, window, amp):
+    """amp 12: scores spread over tens of units, so the running max moves by more than 2^8 between key tiles and
+    the kernel's lazy O / l rescale runs."""
     # three sequences: fresh prompt, prompt with cached prefix, single-token chunk
     qlens = [77, 130, 1]
     klens = [77, 530, 300]
     B = 3
     kc, vc, bt = _paged_setup(B, nq, nkv, hd, klens, seed=7 + hd)
     T = sum(qlens)
-    q = torch.randn(T, nq, hd, generator=torch.Generator().manual_seed(2)).bfloat16()
+    q = (torch.randn(T, nq, hd, generator=torch.Generator().manual_seed(2)) * amp).bfloat16()
     cu_q = torch.tensor([0, 77, 207, 208], dtype=torch.int32)
     cu_k = torch.tensor([0, 77, 607, 907], dtype=torch.int32)
     scale = hd ** -0.5
