@@ -195,23 +195,6 @@ def all_gather_last(x: torch.Tensor) -> torch.Tensor:
     return torch.cat(chunks, dim=-1)
 
 
-def reduce_scatter_rows(x: torch.Tensor) -> torch.Tensor:
-    """Sum over ranks, each rank keeps its contiguous 1/TP slice of rows (Megatron SP layout)."""
-    if _TP_SIZE == 1:
-        return x
-    out = torch.empty((x.shape[0] // _TP_SIZE,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
-    dist.reduce_scatter_tensor(out, x.contiguous(), group=_GROUP)
-    return out
-
-
-def all_gather_rows(x: torch.Tensor) -> torch.Tensor:
-    if _TP_SIZE == 1:
-        return x
-    out = torch.empty((x.shape[0] * _TP_SIZE,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
-    dist.all_gather_into_tensor(out, x.contiguous(), group=_GROUP)
-    return out
-
-
 def barrier() -> None:
     if _TP_SIZE > 1:
         dist.barrier(group=_GROUP)
