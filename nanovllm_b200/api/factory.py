@@ -117,6 +117,11 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
     # on the CPU too (there they are dequantized per multiply -- for tests)
     mode = os.environ.get("NVB_GGUF_PACKED", "1")
     keep_packed = mode == "force" or (device.type == "cuda" and mode not in ("0", "false", "no"))
+    # under tensor parallelism the tensors stay in host memory until the model is built: each layer then moves
+    # one tensor at a time to the GPU and keeps only its shard, so a rank's device memory peaks near its share
+    # of the weights plus one full tensor (safetensors checkpoints are memory-mapped and behave the same way)
+    from ..parallel import state as ps
+    store = torch.device("cpu") if ps.tp_size() > 1 else device
     from ..utils.progress import LoadProgress
     prog = LoadProgress(f"GGUF {os.path.basename(path)}", len(g.tensors), (options or {}).get(OPTION_LISTENER))
     for name, info in g.tensors.items():
@@ -131,10 +136,10 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
         if keep_packed and _PROJECTION.search(target) and fused_supported(info.ggml_type, info.shape):
             # projection weights stay in GGUF block format on the GPU (dequant-fused GEMM); the bytes are
             # copied out of the file mapping, which closes after loading
-            raw = g.packed(name).to(device)
+            raw = g.packed(name).to(store)
             weights[target] = GgufPacked(raw, info.ggml_type, info.shape[0], info.shape[1])
             continue
-        weights[target] = g.get(name, dtype=torch.float32, device=device).to(dtype)
+        weights[target] = g.get(name, dtype=torch.float32, device=store).to(dtype)
     if sel.architecture == MS.QWEN3 and "lm_head.weight" not in weights:
         hf.tie_word_embeddings = True
     g.close()
