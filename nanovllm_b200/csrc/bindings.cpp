@@ -41,7 +41,8 @@ void mean_pool_l2_cuda(torch::Tensor out, torch::Tensor x, torch::Tensor cu);
 void shortconv_cuda(torch::Tensor proj, torch::Tensor weight, torch::Tensor cu, torch::Tensor rows, torch::Tensor fresh,
                     torch::Tensor state, int64_t state_off, torch::Tensor out);
 void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
-                 torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out);
+                 torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out,
+                 c10::optional<torch::Tensor> ids);
 void rms_norm_post_add_cuda(torch::Tensor x, torch::Tensor residual, c10::optional<torch::Tensor> weight, double eps,
                             int64_t mode, double post_scale);
 void ple_combine_cuda(torch::Tensor out, torch::Tensor proj, torch::Tensor tok, torch::Tensor weight, double eps,

@@ -439,7 +439,10 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
                                                                const int64_t* __restrict__ seeds,
                                                                const int64_t* __restrict__ seq_ids,
                                                                const int* __restrict__ steps, float softcap,
-                                                               int64_t* __restrict__ out) {
+                                                               int64_t* __restrict__ out,
+                                                               const int* __restrict__ ids) {
+  // ids (optional, [B][V]): the row holds candidate logits, column c standing for vocabulary id ids[c] (ids
+  // ascending along the row, so position order is id order); uniforms are keyed and the result reported by id
   nvb::pdl_wait();
   nvb::pdl_trigger();
   __shared__ ArgMax sh_am[32];
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
       for (int j = 0; j < 8; ++j) a = better(a, ArgMax{capped(__bfloat162float(e[j]), softcap), i * 8 + j});
     }
     a = block_argmax(a, sh_am);
-    if (tid == 0) out[row] = a.i == 0x7fffffff ? 0 : a.i;
+    if (tid == 0) out[row] = a.i == 0x7fffffff ? 0 : (ids != nullptr ? ids[(long)row * V + a.i] : a.i);
     return;
   }
   const float invT = 1.f / temps[row];
@@ -664,7 +667,8 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
         }
         if (!keep) continue;
         const int i = b0 + lane * 8 + j;
-        const uint4 r4 = Philox::gen(make_uint4((uint32_t)i, step, sid, 0x6e76u), key2);
+        const uint32_t gi = ids != nullptr ? (uint32_t)ids[(long)row * V + i] : (uint32_t)i;
+        const uint4 r4 = Philox::gen(make_uint4(gi, step, sid, 0x6e76u), key2);
         const float u = (float)(r4.x >> 8) * (1.0f / 16777216.0f);
         const float g = -__logf(fmaxf(1e-10f, u));
         const float pr = __expf(r.v[j] * invT - mx);
@@ -673,12 +677,13 @@ __global__ void __launch_bounds__(kThreads) sample_fast_kernel(const bf16* __res
     }
   }
   best = block_argmax(best, sh_am);
-  if (tid == 0) out[row] = best.i == 0x7fffffff ? 0 : best.i;
+  if (tid == 0) out[row] = best.i == 0x7fffffff ? 0 : (ids != nullptr ? ids[(long)row * V + best.i] : best.i);
 }
 }  // namespace
 
 void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, torch::Tensor topp, torch::Tensor seeds,
-                 torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out) {
+                 torch::Tensor seq_ids, torch::Tensor steps, double softcap, torch::Tensor out,
+                 c10::optional<torch::Tensor> ids) {
   const int B = logits.size(0), V = logits.size(1);
   TORCH_CHECK(logits.stride(1) == 1, "logits rows must be contiguous");
   if (B == 0) return;
@@ -687,13 +692,28 @@ void sample_cuda(torch::Tensor logits, torch::Tensor temps, torch::Tensor topk, 
   logits.stride(0), V, temps.data_ptr<float>(), topk.data_ptr<int>(), topp.data_ptr<float>(),                   \
       seeds.data_ptr<int64_t>(), seq_ids.data_ptr<int64_t>(), steps.data_ptr<int>(), (float)softcap,            \
       out.data_ptr<int64_t>()
-  const bool fast = logits.scalar_type() == at::kBFloat16 && V % 8 == 0 && logits.stride(0) % 8 == 0 &&
-                    (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 15) == 0 && std::getenv("NVB_SAMPLER_SLOW") == nullptr;
+  const bool aligned = logits.scalar_type() == at::kBFloat16 && V % 8 == 0 && logits.stride(0) % 8 == 0 &&
+                       (reinterpret_cast<uintptr_t>(logits.data_ptr()) & 15) == 0;
+  if (ids.has_value()) {
+    // candidate rows (distributed sampling under tensor parallelism): bf16, padded to a multiple of 8 columns
+    TORCH_CHECK(aligned, "candidate sampling needs 16-byte aligned bf16 rows with a multiple of 8 columns");
+    TORCH_CHECK(ids->is_cuda() && ids->scalar_type() == at::kInt && ids->is_contiguous() && ids->size(0) == B &&
+                    ids->size(1) == V,
+                "candidate ids must be contiguous int32 [B, V]");
+    C10_CUDA_CHECK(nvb::launch(sample_fast_kernel, dim3(B), dim3(kThreads), 0, stream,
+                               reinterpret_cast<const bf16*>(logits.data_ptr()), logits.stride(0), V,
+                               temps.data_ptr<float>(), topk.data_ptr<int>(), topp.data_ptr<float>(),
+                               seeds.data_ptr<int64_t>(), seq_ids.data_ptr<int64_t>(), steps.data_ptr<int>(),
+                               (float)softcap, out.data_ptr<int64_t>(), (const int*)ids->data_ptr<int>()));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
+  const bool fast = aligned && std::getenv("NVB_SAMPLER_SLOW") == nullptr;
   if (logits.scalar_type() == at::kFloat)
     C10_CUDA_CHECK(nvb::launch(sample_kernel<float>, dim3(B), dim3(kThreads), 0, stream, logits.data_ptr<float>(), ARGS));
   else if (fast)
     C10_CUDA_CHECK(nvb::launch(sample_fast_kernel, dim3(B), dim3(kThreads), 0, stream,
-                               reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS));
+                               reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS, (const int*)nullptr));
   else
     C10_CUDA_CHECK(nvb::launch(sample_kernel<bf16>, dim3(B), dim3(kThreads), 0, stream, reinterpret_cast<const bf16*>(logits.data_ptr()), ARGS));
 #undef ARGS

@@ -302,6 +302,11 @@ class ModelRunner:
             # vocab-parallel logits: greedy rows need only the distributed argmax (exact, no logit gather)
             if all(s.top_k == 1 for s in seqs):
                 return head.argmax(logits[:n], self.final_softcap)
+            if all(1 <= s.top_k <= head.CANDIDATE_K for s in seqs):
+                # top-k rows: exchange each rank's top-k candidates instead of the [n, V] logits
+                t = self._sampling_tensors(seqs)
+                return head.sample_candidates(logits[:n], *t, kmax=max(s.top_k for s in seqs),
+                                              softcap=self.final_softcap)
             logits = head.gather_full(logits[:n])
         t = self._sampling_tensors(seqs)
         return ops.sample(logits[:n], *t, softcap=self.final_softcap)

@@ -94,6 +94,41 @@ class ParallelLMHead:
             return logits
         return ps.all_gather_last(ops.materialize(logits))[:, :self.vocab]
 
+    # rows whose top_k is at most this sample from exchanged candidates instead of gathered logits
+    CANDIDATE_K = 64
+
+    def sample_candidates(self, logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, kmax: int,
+                          softcap: float = 0.0) -> torch.Tensor:
+        """Seeded sampling of rows with 1 <= top_k <= kmax <= CANDIDATE_K without gathering the logits.  The
+        global top-k set lies inside the union of the ranks' own top-k (value descending, id ascending), and the
+        sampler's masses, cut-offs and Philox draws depend only on the kept tokens' values and ids, so each rank
+        exchanges kmax (value, id) pairs per row and every rank runs the same sampler over the id-sorted union:
+        the tokens equal the single-GPU sampler's (Sampler.java:69-134 semantics)."""
+        logits = ops.materialize(logits)
+        x = logits[:, :self.ncols]
+        K = max(1, min(int(kmax), self.ncols))
+        # exact order: 64-bit keys from the order-preserving float bits, then the inverted local index
+        b = x.float().contiguous().view(torch.int32)
+        okey = torch.where(b < 0, b ^ 0x7FFFFFFF, b).to(torch.int64)
+        idx = torch.arange(x.shape[1], device=x.device, dtype=torch.int64)
+        key = (okey << 32) | (0xFFFFFFFF - idx)
+        top = torch.topk(key, K, dim=1, sorted=False).indices
+        vals = x.gather(1, top).float()
+        gids = (top + self.vstart).to(torch.int32)
+        allv = ps.all_gather_last(vals)
+        allg = ps.all_gather_last(gids)
+        order = torch.argsort(allg, dim=1)
+        allg = allg.gather(1, order)
+        allv = allv.gather(1, order)
+        C = allg.shape[1]
+        Cp = (C + 7) // 8 * 8  # the sampler streams 8 bf16 per load
+        if Cp != C:
+            allv = torch.cat([allv, torch.full((allv.shape[0], Cp - C), float("-inf"), device=allv.device)], 1)
+            allg = torch.cat([allg, torch.full((allg.shape[0], Cp - C), self.vocab, dtype=torch.int32,
+                                               device=allg.device)], 1)
+        return ops.sample(allv.to(torch.bfloat16).contiguous(), temps, top_ks, top_ps, seeds, seq_ids, steps,
+                          softcap=softcap, ids=allg.contiguous())
+
     def argmax(self, logits: torch.Tensor, softcap: float = 0.0) -> torch.Tensor:
         """Greedy tokens [T] (ties to the lowest id) without gathering the logits: each rank reduces its slice and
         only (value, id) pairs are exchanged -- over peer memory with the SP workspace, else an all-gather."""

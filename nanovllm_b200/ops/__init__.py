@@ -491,12 +491,15 @@ def mean_pool_l2(x: torch.Tensor, cu: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float = 0.0, out=None) -> torch.Tensor:
+def sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float = 0.0, out=None,
+           ids: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Seeded sampling per row.  ``ids`` (optional int32 [B, C]): the rows hold candidate logits, column c
+    standing for vocabulary id ids[b, c] (ascending along the row); the draw is keyed and reported by id."""
     if not logits.is_cuda:
-        return ref.sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap)
+        return ref.sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap, ids=ids)
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.long, device=logits.device)
-    _cuda_ext().sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, float(softcap), out)
+    _cuda_ext().sample(logits, temps, top_ks, top_ps, seeds, seq_ids, steps, float(softcap), out, ids)
     add_launches(1)
     return out
 

@@ -271,9 +271,11 @@ def philox_uniform(idx: np.ndarray, step: int, seq_id: int, seed: int) -> np.nda
     return (c0 >> np.uint64(8)).astype(np.float64) * (1.0 / 16777216.0)
 
 
-def sample(logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float = 0.0) -> torch.Tensor:
+def sample(logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, softcap: float = 0.0,
+           ids=None) -> torch.Tensor:
     """Per row: top_k == 1 -> argmax; else softmax(x/T) -> top-k -> top-p (keep while cum < p, first always)
-    -> argmax p / -log(u) (Sampler.java:69-134) with Philox uniforms instead of ThreadLocalRandom."""
+    -> argmax p / -log(u) (Sampler.java:69-134) with Philox uniforms instead of ThreadLocalRandom.  ``ids``
+    (optional [B, C]): the rows are candidates, column c standing for vocabulary id ids[b, c] (ascending)."""
     out = torch.empty(logits.shape[0], dtype=torch.long)
     x_all = logits.float()
     if softcap and softcap > 0:
@@ -281,8 +283,10 @@ def sample(logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, s
     for r in range(logits.shape[0]):
         x = x_all[r]
         k = int(top_ks[r])
+        idmap = None if ids is None else ids[r].long().cpu().numpy()
         if k == 1:
-            out[r] = int(torch.argmax(x))  # first maximal index
+            j = int(torch.argmax(x))  # first maximal index
+            out[r] = j if idmap is None else int(idmap[j])
             continue
         t = float(temps[r])
         xs = x / t
@@ -300,10 +304,11 @@ def sample(logits: torch.Tensor, temps, top_ks, top_ps, seeds, seq_ids, steps, s
             keep = torch.zeros_like(keep)
             keep[kept_order[:n_keep]] = True
         idxs = torch.nonzero(keep).flatten().numpy()
-        u = philox_uniform(idxs, int(steps[r]), int(seq_ids[r]), int(seeds[r]) & 0xFFFFFFFFFFFFFFFF)
+        gidx = idxs if idmap is None else idmap[idxs]
+        u = philox_uniform(gidx, int(steps[r]), int(seq_ids[r]), int(seeds[r]) & 0xFFFFFFFFFFFFFFFF)
         g = -np.log(np.maximum(1e-10, u))
         score = p[idxs].double().numpy() / np.maximum(1e-10, g)
-        out[r] = int(idxs[int(np.argmax(score))])
+        out[r] = int(gidx[int(np.argmax(score))])
     return out
 
 

@@ -299,6 +299,30 @@ def test_act_mul_bias_meanpool():
     close(ops.mean_pool_l2(x.to(DEV), cu.to(DEV)), ref.mean_pool_l2(x, cu), 1e-3)
 
 
+@pytest.mark.parametrize("softcap", [0.0, 5.0])
+def test_candidate_sampling_kernel_matches_full_rows(softcap):
+    """Top-k rows sampled from a candidate row with an id map (the tensor-parallel exchange, here one rank) give
+    the tokens of the sampler over the whole row: masses, cut-offs, ties and Philox draws keyed by vocabulary id."""
+    from nanovllm_b200.layers.embedding import ParallelLMHead
+    B, V = 16, 5003
+    g = torch.Generator().manual_seed(4)
+    full = (torch.randn(B, V, generator=g) * 3).bfloat16()
+    full[3, 17] = full[3, 4000] = full[3, 18] = 11.0
+    dev = torch.device(DEV)
+    head = ParallelLMHead(torch.zeros(V, 8, dtype=torch.bfloat16, device=dev), V)
+    temps = torch.full((B,), 0.9, device=dev)
+    topk = torch.tensor([1, 2, 5, 20, 64, 7, 3, 40] * 2, dtype=torch.int32, device=dev)
+    topp = torch.tensor([1.0, 0.9, 0.5, 0.95, 0.8, 1.0, 0.3, 0.99] * 2, device=dev)
+    seeds = torch.arange(B, dtype=torch.int64, device=dev) + 11
+    sids = torch.arange(B, dtype=torch.int64, device=dev)
+    steps = torch.full((B,), 4, dtype=torch.int32, device=dev)
+    x = full.to(dev)
+    got = head.sample_candidates(x, temps, topk, topp, seeds, sids, steps, kmax=64, softcap=softcap)
+    want = ops.sample(x, temps, topk, topp, seeds, sids, steps, softcap=softcap)
+    torch.cuda.synchronize()
+    assert got.tolist() == want.tolist()
+
+
 def test_sampler_matches_oracle():
     g = torch.Generator().manual_seed(6)
     B, V = 6, 5000

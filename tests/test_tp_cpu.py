@@ -23,6 +23,15 @@ def _tiny():
                     tie_word_embeddings=False)
 
 
+def _params(mode):
+    from nanovllm_b200.sampling_params import SamplingParams
+    if mode == "greedy":
+        return SamplingParams(max_tokens=6, ignore_eos=True).deterministic()
+    if mode == "topk":  # top-k rows exchange candidates instead of the logits
+        return SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, top_k=20, top_p=0.9, seed=5)
+    return SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5)
+
+
 def _run(rank, world, port, q, greedy=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -35,17 +44,17 @@ def _run(rank, world, port, q, greedy=False):
     hf = _tiny()
     llm = LLM((hf, init_random_weights(hf, 0)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
                                                              max_num_batched_tokens=256), device="cpu")
-    sp_ = (SamplingParams(max_tokens=6, ignore_eos=True).deterministic() if greedy else
-           SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))
+    sp_ = _params(greedy)
     outs = llm.generate_token_ids([[1, 2, 3, 4, 5], list(range(20, 90))], sp_)
     q.put((rank, [o.token_ids for o in outs]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("greedy", [False])
+@pytest.mark.parametrize("greedy", ["sampled", "topk"])
 def test_tp2_matches_tp1_on_cpu(greedy):
-    """Sampled rows gather the full logits and must reproduce the TP=1 tokens (greedy rows take the distributed
+    """Sampled rows (no top-k) gather the full logits, top-k rows exchange candidates; both must reproduce the
+    TP=1 tokens exactly (greedy rows take the distributed
     argmax, checked exactly by test_distributed_argmax_is_exact: on random-init models bf16 logits tie often
     enough that a different summation order legitimately flips a greedy token)."""
     from nanovllm_b200.config import EngineConfig
@@ -55,8 +64,7 @@ def test_tp2_matches_tp1_on_cpu(greedy):
     hf = _tiny()
     ref = LLM((hf, init_random_weights(hf, 0)), EngineConfig(max_num_seqs=4, max_model_len=512, num_kvcache_blocks=8,
                                                              max_num_batched_tokens=256), device="cpu")
-    sp_ = (SamplingParams(max_tokens=6, ignore_eos=True).deterministic() if greedy else
-           SamplingParams(max_tokens=6, ignore_eos=True, temperature=0.8, seed=5))
+    sp_ = _params(greedy)
     want = [o.token_ids for o in ref.generate_token_ids([[1, 2, 3, 4, 5], list(range(20, 90))], sp_)]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -71,6 +79,56 @@ def test_tp2_matches_tp1_on_cpu(greedy):
     assert got[0] == got[1], "ranks diverged"
     # fp32 math on CPU: sharded reductions change summation order only
     assert got[0] == want
+
+
+def _cand_run(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nanovllm_b200.layers.embedding import ParallelLMHead
+    from nanovllm_b200.ops import reference_cpu as ref
+    from nanovllm_b200.parallel import state as ps
+    ps.init_tp("gloo")
+    V, T = 301, 8
+    head = ParallelLMHead(torch.zeros(V, 8), V)
+    g = torch.Generator().manual_seed(3)
+    full = (torch.randn(T, V, generator=g) * 3).bfloat16()
+    full[2, 10] = full[2, 250] = full[2, 11] = 9.0   # ties inside and across slices
+    per = head.weight.shape[0]
+    mine = torch.full((T, per), 1e4).bfloat16()
+    mine[:, :head.ncols] = full[:, head.vstart:head.vstart + head.ncols]
+    temps = torch.full((T,), 0.9)
+    topk = torch.tensor([1, 2, 5, 20, 64, 7, 3, 40], dtype=torch.int32)
+    topp = torch.tensor([1.0, 0.9, 0.5, 0.95, 0.8, 1.0, 0.3, 0.99])
+    seeds = torch.arange(T, dtype=torch.int64) + 11
+    sids = torch.arange(T, dtype=torch.int64)
+    steps = torch.full((T,), 4, dtype=torch.int32)
+    res = []
+    for cap in (0.0, 5.0):
+        got = head.sample_candidates(mine, temps, topk, topp, seeds, sids, steps, kmax=64, softcap=cap).tolist()
+        want = ref.sample(full, temps, topk, topp, seeds, sids, steps, cap).tolist()
+        res.append((got, want))
+    q.put((rank, res))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_candidate_sampling_matches_full_vocabulary(world):
+    """Top-k rows sampled from the exchanged per-rank candidates give exactly the tokens of the sampler over the
+    whole vocabulary (ties, top-p cuts, soft-cap included)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cand_run, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        for cand, want in got[r]:
+            assert cand == want, (r, cand, want)
 
 
 def _argmax_run(rank, world, port, q):
