@@ -144,6 +144,7 @@ class BlockManager:
                 self._deallocate_block(bid)
         seq.num_cached_tokens = 0
         seq.block_table.clear()
+        seq.bt_gen += 1
 
     # ------------------------------------------------------------------ decode growth
     def can_append(self, seq: Sequence) -> bool:

@@ -31,6 +31,23 @@ from .context import StepContext, set_context
 from .sequence import Sequence
 
 
+def write_block_rows(btn, rows: List[Optional[tuple]], seqs: List[Sequence]) -> None:
+    """Decode block-table rows in place (numpy view of pinned memory).  The rows persist across steps: a row
+    whose sequence and block-table generation are unchanged only gets its newly appended blocks, any other row
+    is rewritten; entries past a row's context are never read by the attention kernel, so nothing is cleared
+    (padding rows have context 0).  ``rows[i]`` records (seq id, generation, blocks written) for row i."""
+    for i, s in enumerate(seqs):
+        bt_list = s.block_table
+        nb = len(bt_list)
+        st = rows[i]
+        if st is not None and st[0] == s.seq_id and st[1] == s.bt_gen and st[2] <= nb:
+            if st[2] < nb:
+                btn[i, st[2]:nb] = bt_list[st[2]:]
+        elif nb:
+            btn[i, :nb] = bt_list
+        rows[i] = (s.seq_id, s.bt_gen, nb)
+
+
 def _bucket_sizes(max_bs: int) -> List[int]:
     out = [b for b in (1, 2, 4, 8) if b <= max_bs]
     out += list(range(16, max_bs + 1, 16))
@@ -174,6 +191,7 @@ class ModelRunner:
         self.h_sids = buf(S, torch.int64)
         self.h_steps = buf(S, torch.int32)
         self._err_host = buf(1, torch.int32)
+        self._bt_rows: List[Optional[tuple]] = [None] * S  # (seq id, block-table generation, blocks written)
         # numpy views share the pinned memory: element writes from Python stay cheap
         for name in ("ids", "pos", "slots", "cu_q", "cu_k", "ctx", "last", "bt", "rows", "fresh", "temps", "topk",
                      "topp", "seeds", "sids", "steps"):
@@ -190,6 +208,7 @@ class ModelRunner:
         return host[:n].to(self.device, non_blocking=True)
 
     def _fill_block_tables(self, seqs: List[Sequence]) -> int:
+        self._bt_rows = [None] * len(self._bt_rows)  # h_bt is rewritten here with another row width
         width = max(1, max(len(s.block_table) for s in seqs))
         bt = self.n_bt[:len(seqs) * width].reshape(len(seqs), width)
         bt.fill(0)
@@ -417,10 +436,7 @@ class ModelRunner:
         self._fill_decode_rows(seqs, bs)
         width = self.max_blocks_per_seq
         btn = self.n_bt[:bs * width].reshape(bs, width)
-        btn.fill(0)
-        for i, s in enumerate(seqs):
-            if s.block_table:
-                btn[i, :len(s.block_table)] = s.block_table
+        write_block_rows(btn, self._bt_rows, seqs)
         bt = self.h_bt[:bs * width].view(bs, width)
         self._begin_gpu()
         self.last_h2d_bytes += bs * (8 + 8 + 4 + 4 + 4 * width)

@@ -35,7 +35,7 @@ class Sequence:
     __slots__ = ("seq_id", "token_ids", "num_tokens", "num_prompt_tokens", "last_token", "block_size",
                  "block_table", "num_cached_tokens", "num_scheduled_tokens", "status", "is_prefill",
                  "temperature", "top_k", "top_p", "max_tokens", "ignore_eos", "seed", "t_arrival",
-                 "t_first_token", "t_finish", "user_tag")
+                 "t_first_token", "t_finish", "user_tag", "bt_gen")
 
     def __init__(self, token_ids: List[int], sampling: Optional[SamplingParams] = None, block_size: int = 256,
                  user_tag=None):
@@ -49,6 +49,7 @@ class Sequence:
         self.last_token = self.token_ids[-1]
         self.block_size = block_size
         self.block_table: List[int] = []
+        self.bt_gen = 0  # bumped whenever the block table is released (preemption, finish)
         self.num_cached_tokens = 0
         self.num_scheduled_tokens = 0
         self.status = SequenceStatus.WAITING

@@ -219,3 +219,29 @@ def test_nvtx_ranges_are_off_by_default_and_harmless_on_cpu():
             pass
     finally:
         trace.set_enabled(False)
+
+
+def test_decode_block_rows_are_written_incrementally():
+    """The graph-replay block-table rows keep their contents across steps: unchanged sequences only append new
+    blocks, a reordered batch or a released-and-reallocated table rewrites the row."""
+    import numpy as np
+    from nanovllm_b200.engine.model_runner import write_block_rows
+    from nanovllm_b200.engine.sequence import Sequence
+    a, b = Sequence([1, 2, 3]), Sequence([4, 5])
+    a.block_table[:] = [7, 8]
+    b.block_table[:] = [3]
+    btn = np.full((4, 6), -1, dtype=np.int32)
+    rows = [None] * 4
+    write_block_rows(btn, rows, [a, b])
+    assert btn[0, :2].tolist() == [7, 8] and btn[1, :1].tolist() == [3]
+    a.block_table.append(9)
+    btn[0, :2] = -5  # untouched prefix must not be rewritten
+    write_block_rows(btn, rows, [a, b])
+    assert btn[0, :3].tolist() == [-5, -5, 9]
+    write_block_rows(btn, rows, [b, a])  # reordered: both rows rewritten
+    assert btn[0, :1].tolist() == [3] and btn[1, :3].tolist() == [7, 8, 9]
+    b.block_table.clear()
+    b.bt_gen += 1  # what the block manager does on release
+    b.block_table[:] = [11, 12]
+    write_block_rows(btn, rows, [b, a])
+    assert btn[0, :2].tolist() == [11, 12]
