@@ -284,12 +284,13 @@ class ModelRunner:
     def _fill_decode_rows(self, seqs: List[Sequence], pad_to: int) -> None:
         blk = self.block_size
         n = len(seqs)
-        for i, s in enumerate(seqs):
-            p = len(s) - 1
-            self.n_ids[i] = s.last_token
-            self.n_pos[i] = p
-            self.n_slots[i] = s.block_table[p // blk] * blk + p % blk
-            self.n_ctx[i] = p + 1
+        # one list per field and one slice store each: element-wise stores into numpy cost ~0.1 us apiece
+        lens = [s.num_tokens for s in seqs]
+        self.n_ids[:n] = [s.last_token for s in seqs]
+        self.n_ctx[:n] = lens
+        self.n_pos[:n] = self.n_ctx[:n]
+        self.n_pos[:n] -= 1
+        self.n_slots[:n] = [s.block_table[(m - 1) // blk] * blk + (m - 1) % blk for s, m in zip(seqs, lens)]
         if pad_to > n:
             self.n_ids[n:pad_to] = 0
             self.n_pos[n:pad_to] = 0
@@ -299,18 +300,14 @@ class ModelRunner:
     # ------------------------------------------------------------------ sampling
     def _sampling_tensors(self, seqs: List[Sequence]):
         n = len(seqs)
-        base_seed = self.cfg.seed
-        for i, s in enumerate(seqs):
-            self.n_temps[i] = s.temperature
-            self.n_topk[i] = s.top_k
-            self.n_topp[i] = s.top_p
-            if s.seed is not None:
-                self.n_seeds[i] = int(s.seed) & 0x7FFFFFFFFFFFFFFF
-                self.n_sids[i] = 0
-            else:
-                self.n_seeds[i] = (base_seed * 1000003 + s.seq_id) & 0x7FFFFFFFFFFFFFFF
-                self.n_sids[i] = s.seq_id
-            self.n_steps[i] = len(s)
+        base = self.cfg.seed * 1000003
+        self.n_temps[:n] = [s.temperature for s in seqs]
+        self.n_topk[:n] = [s.top_k for s in seqs]
+        self.n_topp[:n] = [s.top_p for s in seqs]
+        self.n_seeds[:n] = [(int(s.seed) if s.seed is not None else base + s.seq_id) & 0x7FFFFFFFFFFFFFFF
+                            for s in seqs]
+        self.n_sids[:n] = [0 if s.seed is not None else s.seq_id for s in seqs]
+        self.n_steps[:n] = [s.num_tokens for s in seqs]
         return tuple(self._h2d(h, n) for h in (self.h_temps, self.h_topk, self.h_topp, self.h_seeds, self.h_sids,
                                                 self.h_steps))
 

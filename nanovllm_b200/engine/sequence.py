@@ -35,7 +35,7 @@ class Sequence:
     __slots__ = ("seq_id", "token_ids", "num_tokens", "num_prompt_tokens", "last_token", "block_size",
                  "block_table", "num_cached_tokens", "num_scheduled_tokens", "status", "is_prefill",
                  "temperature", "top_k", "top_p", "max_tokens", "ignore_eos", "seed", "t_arrival",
-                 "t_first_token", "t_finish", "user_tag", "bt_gen")
+                 "t_first_token", "t_finish", "user_tag", "bt_gen", "_ngrams")
 
     def __init__(self, token_ids: List[int], sampling: Optional[SamplingParams] = None, block_size: int = 256,
                  user_tag=None):
@@ -64,6 +64,7 @@ class Sequence:
         self.t_first_token: Optional[float] = None
         self.t_finish: Optional[float] = None
         self.user_tag = user_tag
+        self._ngrams: Optional[_NgramWindow] = None  # created by the first n-gram check
 
     def __len__(self):
         return self.num_tokens
@@ -115,9 +116,12 @@ class Sequence:
             return False
         if self._same_token_streak() >= 32:
             return True
+        ids = self.token_ids
+        last = self.num_tokens - 1
         max_period = min(64, completion // 2)
         for period in range(16, max_period + 1, 8):
-            if self._ends_with_two_identical_blocks(period):
+            # two equal trailing halves must at least end in equal tokens: one compare rejects almost every period
+            if ids[last] == ids[last - period] and self._ends_with_two_identical_blocks(period):
                 return True
         return completion >= 48 and self._has_overused_ngram()
 
@@ -138,16 +142,54 @@ class Sequence:
         return ids[start:start + period] == ids[start + period:start + 2 * period]
 
     def _has_overused_ngram(self, ngram: int = 12, min_hits: int = 3) -> bool:
+        """True when some ``ngram``-gram lying inside the last min(completion, 128) tokens occurs ``min_hits``
+        times there.  The counts are kept across calls and slid by the tokens appended since the previous call
+        (one n-gram added at the front, one dropped at the back per token) instead of recounting the window."""
         window = min(self.num_completion_tokens, 128)
         if window < ngram * min_hits:
             return False
         start0 = self.num_tokens - window
-        counts = {}
-        ids = self.token_ids
-        for s in range(start0, self.num_tokens - ngram + 1):
-            key = tuple(ids[s:s + ngram])
+        w = self._ngrams
+        if w is None or w.ngram != ngram or w.min_hits != min_hits:
+            w = self._ngrams = _NgramWindow(start0, ngram, min_hits)
+        return w.advance(self.token_ids, self.num_tokens, start0)
+
+
+class _NgramWindow:
+    """Occurrence counts of the n-grams whose starts lie in [lo, hi), with the number of n-grams counted at least
+    ``min_hits`` times; ``advance`` moves both ends forward over a token list that only grows at its end."""
+    __slots__ = ("ngram", "min_hits", "counts", "over", "lo", "hi")
+
+    def __init__(self, start: int, ngram: int, min_hits: int):
+        self.ngram = ngram
+        self.min_hits = min_hits
+        self.counts = {}
+        self.over = 0
+        self.lo = start
+        self.hi = start
+
+    def advance(self, ids: List[int], num_tokens: int, start0: int) -> bool:
+        n, hits, counts = self.ngram, self.min_hits, self.counts
+        end = num_tokens - n + 1
+        hi = self.hi
+        while hi < end:
+            key = tuple(ids[hi:hi + n])
             c = counts.get(key, 0) + 1
-            if c >= min_hits:
-                return True
             counts[key] = c
-        return False
+            if c == hits:
+                self.over += 1
+            hi += 1
+        self.hi = hi
+        lo = self.lo
+        while lo < start0:
+            key = tuple(ids[lo:lo + n])
+            c = counts[key]
+            if c == hits:
+                self.over -= 1
+            if c == 1:
+                del counts[key]
+            else:
+                counts[key] = c - 1
+            lo += 1
+        self.lo = lo
+        return self.over > 0

@@ -167,6 +167,52 @@ def test_degenerate_repetition():
     assert not q.has_degenerate_repetition()
 
 
+def _degenerate_by_definition(ids, prompt):
+    """The stop rule written out directly: recounts every window from scratch."""
+    comp = len(ids) - prompt
+    if comp < 32:
+        return False
+    streak = 0
+    for t in reversed(ids[prompt:]):
+        if t != ids[-1]:
+            break
+        streak += 1
+    if streak >= 32:
+        return True
+    for period in range(16, min(64, comp // 2) + 1, 8):
+        start = len(ids) - 2 * period
+        if start >= prompt and ids[start:start + period] == ids[start + period:]:
+            return True
+    if comp < 48:
+        return False
+    window = min(comp, 128)
+    counts = {}
+    for s in range(len(ids) - window, len(ids) - 12 + 1):
+        key = tuple(ids[s:s + 12])
+        counts[key] = counts.get(key, 0) + 1
+        if counts[key] >= 3:
+            return True
+    return False
+
+
+@pytest.mark.parametrize("alphabet,check_every", [(2, 1), (3, 1), (5, 1), (3, 7), (40, 1), (1000, 3)])
+def test_incremental_repetition_check_matches_definition(alphabet, check_every):
+    """The sliding n-gram counts give the same answer as a full recount after every appended token, also when the
+    check skips steps (the counts then catch up over several tokens at once) and past the 128-token window."""
+    import random
+    rng = random.Random(alphabet * 31 + check_every)
+    for trial in range(6):
+        s = seq(5 + trial)
+        prompt = s.num_prompt_tokens
+        for i in range(400):
+            if rng.random() < 0.3 and s.num_completion_tokens > 12:
+                s.append_token(s.token_ids[-12 + rng.randrange(12)])  # copy a recent token: repeats appear
+            else:
+                s.append_token(1000 + rng.randrange(alphabet))
+            if i % check_every == 0:
+                assert s.has_degenerate_repetition() == _degenerate_by_definition(s.token_ids, prompt), (trial, i)
+
+
 def test_sampling_params_validation():
     with pytest.raises(ValueError):
         SamplingParams(temperature=0.0)
