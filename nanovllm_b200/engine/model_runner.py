@@ -218,28 +218,28 @@ class ModelRunner:
         return width
 
     def prepare_prefill(self, seqs: List[Sequence]):
-        ids, pos, slots = [], [], []
+        ids = []
         cu_q, cu_k = [0], [0]
         max_q = max_k = 0
         counts = []
         bs = self.block_size
+        off = 0
         for s in seqs:
             start = s.num_cached_tokens
             end = start + s.num_scheduled_tokens
             ids.extend(s.token_ids[start:end])
-            pos.extend(range(start, end))
             qlen, klen = end - start, end
+            # positions and KV slots as numpy ranges (a prefill step stages up to max_num_batched_tokens of each)
+            p = np.arange(start, end, dtype=np.int64)
+            self.n_pos[off:off + qlen] = p
+            self.n_slots[off:off + qlen] = np.asarray(s.block_table, dtype=np.int64)[p // bs] * bs + p % bs
+            off += qlen
             cu_q.append(cu_q[-1] + qlen)
             cu_k.append(cu_k[-1] + klen)
             max_q, max_k = max(max_q, qlen), max(max_k, klen)
             counts.append(qlen)
-            bt = s.block_table
-            for p in range(start, end):
-                slots.append(bt[p // bs] * bs + p % bs)
         T, S = len(ids), len(seqs)
         self.n_ids[:T] = ids
-        self.n_pos[:T] = pos
-        self.n_slots[:T] = slots
         self.n_cu_q[:S + 1] = cu_q
         self.n_cu_k[:S + 1] = cu_k
         self.n_last[:S] = cu_q[1:]

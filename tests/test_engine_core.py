@@ -291,3 +291,45 @@ def test_decode_block_rows_are_written_incrementally():
     b.block_table[:] = [11, 12]
     write_block_rows(btn, rows, [b, a])
     assert btn[0, :2].tolist() == [11, 12]
+
+
+def test_prefill_and_decode_staging_match_block_tables():
+    """Step staging: flat ids, positions and KV slots of the scheduled (uncached) tokens of a chunked, partly
+    prefix-cached prefill batch, and the decode rows, agree with a per-token computation from the block tables."""
+    import random
+    import torch
+    from nanovllm_b200.engine import model_runner as mr
+    cfg = EngineConfig(max_num_seqs=8, max_model_len=4096, max_num_batched_tokens=1500)
+    sch = Scheduler(cfg, num_blocks=64)
+    rng = random.Random(3)
+    shared = [rng.randrange(1000) for _ in range(512)]
+    for n in (700, 300, 1100, 40):
+        sch.add(Sequence(shared + [rng.randrange(1000) for _ in range(n)], SamplingParams(max_tokens=4), 256))
+    r = mr.ModelRunner.__new__(mr.ModelRunner)
+    r.cfg, r.is_cuda, r.block_size, r.max_blocks_per_seq = cfg, False, 256, 16
+    r.state_arena, r.device, r.last_h2d_bytes, r.step_events, r._started = None, torch.device("cpu"), 0, None, False
+    r._staging()
+    steps = 0
+    while not sch.is_finished():
+        seqs, pre = sch.schedule()
+        if pre:
+            ids, pos, ctx = r.prepare_prefill(seqs)
+            want_ids, want_pos, want_slots = [], [], []
+            for s in seqs:
+                a = s.num_cached_tokens
+                for p in range(a, a + s.num_scheduled_tokens):
+                    want_ids.append(s.token_ids[p])
+                    want_pos.append(p)
+                    want_slots.append(s.block_table[p // 256] * 256 + p % 256)
+            assert ids.tolist() == want_ids and pos.tolist() == want_pos
+            assert ctx.slot_mapping.tolist() == want_slots
+        else:
+            ids, pos, ctx = r.prepare_decode(seqs)
+            assert ids.tolist() == [s.last_token for s in seqs]
+            assert pos.tolist() == [len(s) - 1 for s in seqs]
+            assert ctx.context_lens.tolist() == [len(s) for s in seqs]
+            assert ctx.slot_mapping.tolist() == [s.block_table[(len(s) - 1) // 256] * 256 + (len(s) - 1) % 256
+                                                 for s in seqs]
+        sch.postprocess(seqs, [rng.randrange(1000) for _ in seqs], pre)
+        steps += 1
+    assert steps > 4
