@@ -332,6 +332,9 @@ class EngineConfig:
     enable_prefix_caching: bool = True
     fused_comm: bool = True
     seed: int = 0
+    # TP request intake: "spmd" = every rank receives the same requests and schedules them itself; "rank0" = only
+    # rank 0 takes requests and broadcasts each step's plan, the other ranks run ``LLM.serve_worker``
+    front_door: str = "spmd"
 
     def __post_init__(self):
         if self.kvcache_block_size % 256 != 0:
@@ -340,6 +343,9 @@ class EngineConfig:
             raise ValueError("gpu_memory_utilization must be in (0, 1]")
         if self.max_num_seqs < 1 or self.max_num_batched_tokens < 1:
             raise ValueError("max_num_seqs and max_num_batched_tokens must be >= 1")
+        self.front_door = os.environ.get("NVB_TP_FRONT_DOOR", self.front_door)
+        if self.front_door not in ("spmd", "rank0"):
+            raise ValueError("front_door must be 'spmd' or 'rank0'")
         env = os.environ.get("NANOVLLM_ENFORCE_EAGER")
         if env is not None:
             self.enforce_eager = env not in ("0", "false", "False")

@@ -66,6 +66,28 @@ class Sequence:
         self.user_tag = user_tag
         self._ngrams: Optional[_NgramWindow] = None  # created by the first n-gram check
 
+    @classmethod
+    def mirror(cls, seq_id: int, token_ids: List[int], num_prompt_tokens: int, block_size: int) -> "Sequence":
+        """A copy of another rank's sequence, kept up to date from step plans (no id drawn, no validation)."""
+        s = cls.__new__(cls)
+        s.seq_id = seq_id
+        s.token_ids = list(token_ids)
+        s.num_tokens = len(s.token_ids)
+        s.num_prompt_tokens = num_prompt_tokens
+        s.last_token = s.token_ids[-1]
+        s.block_size = block_size
+        s.block_table = []
+        s.bt_gen = 0
+        s.num_cached_tokens = 0
+        s.num_scheduled_tokens = 0
+        s.status = SequenceStatus.RUNNING
+        s.is_prefill = True
+        s.temperature, s.top_k, s.top_p, s.max_tokens, s.ignore_eos, s.seed = 1.0, 0, 1.0, 0, True, None
+        s.t_arrival, s.t_first_token, s.t_finish = time.perf_counter(), None, None
+        s.user_tag = None
+        s._ngrams = None
+        return s
+
     def __len__(self):
         return self.num_tokens
 

@@ -10,7 +10,9 @@ Reference: nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/llm/LLM.java:
   an error (865-874);
 * warmup = one synthetic 64-token prefill + 16 decode steps (277-301).
 New here: per-request TTFT / TPOT (``GenerationStats``), an online request API (``add_request`` / ``step`` /
-``abort``) for Poisson serving, and TP=1/2/4/8 through torch.distributed (SPMD: every rank runs this engine).
+``abort``) for Poisson serving, and TP=1/2/4/8 through torch.distributed: SPMD (every rank runs this engine on the
+same requests) or one front door (rank 0 takes the requests and broadcasts step plans, ``serve_worker`` on the
+other ranks follows them; ``engine/plan.py``).
 """
 from __future__ import annotations
 
@@ -110,6 +112,16 @@ class LLM:
         self.runner = ModelRunner(self.model, hf, self.cfg, self.device)
         self.scheduler = Scheduler(self.cfg, self.runner.num_blocks, stop, on_release=self.runner.release_state,
                                    max_live_seqs=self.runner.state_capacity)
+        # TP with one front door: rank 0 schedules and broadcasts step plans, the other ranks follow them
+        self._plan_tx = self._plan_rx = None
+        if ps.tp_size() > 1 and self.cfg.front_door == "rank0":
+            from .engine.plan import PlanReceiver, PlanSender
+            group = ps.control_group()
+            if ps.tp_rank() == 0:
+                self._plan_tx = PlanSender(group)
+                self.scheduler.on_release = self._release_and_note
+            else:
+                self._plan_rx = PlanReceiver(group, self.cfg.kvcache_block_size, release=self.runner.release_state)
         self._lock = threading.Lock()
         self._cancel = threading.Event()
         self._closed = False
@@ -119,7 +131,7 @@ class LLM:
         self.advisors: List = []      # LlmAdvisor list run before every chat turn
         self.advisor_mixer = None
         self.think_tags = None
-        if warmup:
+        if warmup and self._plan_rx is None:  # a front-door worker follows rank 0's warm-up through the plans
             self.warmup()
 
     # ------------------------------------------------------------------ builder
@@ -139,6 +151,7 @@ class LLM:
         def num_kvcache_blocks(self, v): self._cfg["num_kvcache_blocks"] = int(v); return self
         def gpu_memory_utilization(self, v): self._cfg["gpu_memory_utilization"] = float(v); return self
         def tensor_parallel_size(self, v): self._cfg["tensor_parallel_size"] = int(v); return self
+        def front_door(self, v): self._cfg["front_door"] = str(v); return self
         def enforce_eager(self, v=True): self._cfg["enforce_eager"] = bool(v); return self
         def cuda_graph_max_bs(self, v): self._cfg["cuda_graph_max_bs"] = int(v); return self
         def stop_token_ids(self, ids): self._cfg["stop_token_ids"] = tuple(int(i) for i in ids); return self
@@ -177,8 +190,48 @@ class LLM:
     def close(self) -> None:
         if not self._closed:
             self.scheduler.clear()
+            if self._plan_tx is not None and not ps.abort_requested():
+                self._plan_tx.send_shutdown()  # ends every worker's serve_worker loop
             self.runner.close()
             self._closed = True
+
+    def _release_and_note(self, seq: Sequence) -> None:
+        self.runner.release_state(seq)
+        self._plan_tx.note_release(seq)
+
+    @property
+    def is_worker(self) -> bool:
+        """True on ranks > 0 of a front-door TP engine: they take no requests and run ``serve_worker``."""
+        return self._plan_rx is not None
+
+    def serve_worker(self) -> int:
+        """Follow rank 0's step plans until it closes its engine (front-door TP, ranks > 0); returns the number of
+        steps run.  Raises TensorParallelAbort when a peer failed or this rank's tokens diverged from rank 0's."""
+        if self._plan_rx is None:
+            raise NanoLlvmException("serve_worker runs on ranks > 0 of an engine built with front_door='rank0'")
+        from .engine.plan import KIND_SHUTDOWN
+        rx = self._plan_rx
+        steps = 0
+        try:
+            while True:
+                ps.check_abort()
+                kind, is_prefill, seqs = rx.apply(rx.recv())
+                if kind == KIND_SHUTDOWN:
+                    return steps
+                with nvtx("step:prefill" if is_prefill else "step:decode"):
+                    toks = self.runner.run(seqs, is_prefill)
+                rx.note_sampled(seqs, toks)
+                steps += 1
+        except BaseException as e:
+            if ps.abort_requested() or ps.peer_aborted(wait_s=2.0 if isinstance(e, torch.distributed.DistError) else 0.0):
+                if isinstance(e, TensorParallelAbort):
+                    raise
+                raise TensorParallelAbort(ps.abort_reason()) from e
+            ps.signal_abort(f"{type(e).__name__}: {e}")
+            raise
+        finally:
+            self._closed = True
+            self.runner.close()
 
     def __enter__(self):
         return self
@@ -189,6 +242,9 @@ class LLM:
     # ------------------------------------------------------------------ online API
     def add_request(self, prompt_token_ids: List[int], sampling: Optional[SamplingParams] = None,
                     tag=None) -> Sequence:
+        if self._plan_rx is not None:
+            raise NanoLlvmException(f"rank {ps.tp_rank()} is a front-door worker: requests go to rank 0, this rank "
+                                    "runs serve_worker()")
         sp = self._fit_sampling(len(prompt_token_ids), sampling or self.default_sampling)
         seq = Sequence(prompt_token_ids, sp, self.cfg.kvcache_block_size, user_tag=tag)
         self.scheduler.add(seq)
@@ -205,6 +261,9 @@ class LLM:
         with nvtx("schedule"):
             seqs, is_prefill = self.scheduler.schedule()
         try:
+            if self._plan_tx is not None:
+                with nvtx("plan"):
+                    self._plan_tx.send_step(seqs, is_prefill)
             with nvtx("step:prefill" if is_prefill else "step:decode"):
                 toks = self.runner.run(seqs, is_prefill)
         except BaseException as e:

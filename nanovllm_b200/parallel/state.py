@@ -157,6 +157,19 @@ def init_tp(backend: Optional[str] = None, timeout_s: float = 120.0) -> None:
     _start_watcher()
 
 
+_CTRL = None
+
+
+def control_group():
+    """A Gloo group over all ranks for host-side control messages (step plans).  Created on first use, which must
+    happen at the same point on every rank; its timeout is long because a serving worker waits for the next
+    plan for as long as the server is idle (a failed peer is noticed through the abort flag instead)."""
+    global _CTRL
+    if _CTRL is None:
+        _CTRL = dist.new_group(backend="gloo", timeout=datetime.timedelta(days=7))
+    return _CTRL
+
+
 def set_tp_for_testing(rank: int, size: int, group=None) -> None:
     global _TP_SIZE, _TP_RANK, _GROUP
     _TP_RANK, _TP_SIZE, _GROUP = rank, size, group
@@ -201,9 +214,10 @@ def barrier() -> None:
 
 
 def destroy() -> None:
-    global _TP_SIZE, _TP_RANK, _GROUP, _STORE
+    global _TP_SIZE, _TP_RANK, _GROUP, _STORE, _CTRL
     _stop_watcher()
     _STORE = None
+    _CTRL = None
     if dist.is_initialized():
         dist.destroy_process_group()
     _TP_SIZE, _TP_RANK, _GROUP = 1, 0, None
