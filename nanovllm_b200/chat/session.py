@@ -253,7 +253,7 @@ class ChatSession:
         t0 = time.perf_counter()
         if self.advisors:
             enr = AdvisorRunner.enrich(self.llm, self.advisors, model_user, self._prior_users(), sp,
-                                       self.mixer, self.tags)
+                                       self.mixer, self.tags, getattr(self.llm, "advisor_note_filter", None))
             for r in enr.responses:
                 if r.text:
                     emit(self.listener, self, LlmTextKind.TEXT_ADVISOR_NOTE, f"[{r.advisor_name}] {r.text}\n")

@@ -16,6 +16,7 @@ other ranks follows them; ``engine/plan.py``).
 """
 from __future__ import annotations
 
+import os
 import threading
 import time
 from dataclasses import dataclass, field
@@ -78,8 +79,11 @@ class GenerationOutput:
 
 class LLM:
     def __init__(self, model, cfg: Optional[EngineConfig] = None, sampling: Optional[SamplingParams] = None,
-                 device: Optional[Union[str, torch.device]] = None, warmup: bool = False):
-        """``model``: an ``LlmModel`` (from LlmModelFactory) or a (HfConfig, weights-dict) tuple."""
+                 device: Optional[Union[str, torch.device]] = None, warmup: bool = False,
+                 unpack_parameters: bool = False, cpu_threads: Optional[int] = None):
+        """``model``: an ``LlmModel`` (from LlmModelFactory) or a (HfConfig, weights-dict) tuple.
+        ``unpack_parameters``: expand packed GGUF projections to bf16 for this engine (the shared model keeps its
+        packed tensors).  ``cpu_threads``: intra-op threads when the engine runs on the CPU device."""
         from .api.model import LlmModel
         if isinstance(model, LlmModel):
             if model.is_embedding():
@@ -99,9 +103,17 @@ class LLM:
         if device is None:
             device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
         self.device = torch.device(device)
+        if cpu_threads is not None and self.device.type == "cpu":
+            torch.set_num_threads(int(cpu_threads))
+        if unpack_parameters:
+            from .ops.quant import GgufPacked
+            weights = {k: (v.dequantize(torch.bfloat16).to(self.device) if isinstance(v, GgufPacked) else v)
+                       for k, v in weights.items()}
+        from .models.base import unpacked_parameters
         from .models.registry import causal_model_class
         cls = causal_model_class(hf)
-        self.model = cls(hf, weights, self.device, max_pos=self.cfg.max_model_len + 1)
+        with unpacked_parameters(unpack_parameters):  # QAT integer weights expand at graph build
+            self.model = cls(hf, weights, self.device, max_pos=self.cfg.max_model_len + 1)
         stop = list(self.cfg.stop_token_ids)
         if not stop and tokenizer is not None:
             stop = list(tokenizer.stop_token_ids())
@@ -130,6 +142,7 @@ class LLM:
         self.system_prompt = ""       # default system prompt for chat sessions (empty, as in the reference)
         self.advisors: List = []      # LlmAdvisor list run before every chat turn
         self.advisor_mixer = None
+        self.advisor_note_filter = None  # keep-test for advisor notes (default: non-blank)
         self.think_tags = None
         if warmup and self._plan_rx is None:  # a front-door worker follows rank 0's warm-up through the plans
             self.warmup()
@@ -142,6 +155,8 @@ class LLM:
             self._sampling = SamplingParams()
             self._device = None
             self._warmup = False
+            self._unpack = False
+            self._cpu_threads = None
             self._extra = {}
 
         def max_num_batched_tokens(self, v): self._cfg["max_num_batched_tokens"] = int(v); return self
@@ -150,6 +165,26 @@ class LLM:
         def kvcache_block_size(self, v): self._cfg["kvcache_block_size"] = int(v); return self
         def num_kvcache_blocks(self, v): self._cfg["num_kvcache_blocks"] = int(v); return self
         def gpu_memory_utilization(self, v): self._cfg["gpu_memory_utilization"] = float(v); return self
+
+        def kv_heap_fraction(self, v):
+            """The reference's share of the heap for the KV cache: here the share of device memory the engine may
+            fill (weights, activations and KV pages), in (0, 1]."""
+            return self.gpu_memory_utilization(v)
+
+        def cpu_threads(self, v):
+            """Intra-op threads when the engine runs on the CPU device (>= 1); CUDA engines run on streams."""
+            if int(v) < 1:
+                raise ValueError(f"cpu_threads must be >= 1, got {v}")
+            self._cpu_threads = int(v)
+            return self
+
+        def all_cpu_threads(self): return self.cpu_threads(os.cpu_count() or 1)
+        def disable_multi_cpu(self): return self.cpu_threads(1)
+
+        def allow_unpack_parameters(self, v=True):
+            """Expand packed GGUF projections to bf16 for this engine (more memory, the dense GEMM path)."""
+            self._unpack = bool(v)
+            return self
         def tensor_parallel_size(self, v): self._cfg["tensor_parallel_size"] = int(v); return self
         def front_door(self, v): self._cfg["front_door"] = str(v); return self
         def enforce_eager(self, v=True): self._cfg["enforce_eager"] = bool(v); return self
@@ -161,15 +196,27 @@ class LLM:
         def deterministic(self): self._sampling = self._sampling.deterministic(); return self
         def device(self, d): self._device = d; return self
         def warmup(self, v=True): self._warmup = bool(v); return self
+        def skip_warmup(self): return self.warmup(False)
         # chat-level defaults picked up by ChatSession / RagSession (LLM.java builder knobs)
         def listen(self, listener): self._extra["listener"] = listener; return self
         def system_prompt(self, text: str): self._extra["system_prompt"] = text or ""; return self
+        def no_system_prompt(self): return self.system_prompt("")
+        def default_system_prompt(self): self._extra.pop("system_prompt", None); return self
         def advisors(self, *advisors): self._extra["advisors"] = list(advisors); return self
+        def no_advisors(self): self._extra["advisors"] = []; self._extra["advisor_mixer"] = None; return self
+
+        def advisor_note_filter(self, keep: Callable[[str], bool]):
+            """Keep-test applied to each advisor's decoded note before mixing (default: non-blank)."""
+            if not callable(keep):
+                raise TypeError("advisor_note_filter needs a callable")
+            self._extra["advisor_note_filter"] = keep
+            return self
         def advisor_mixer(self, mixer): self._extra["advisor_mixer"] = mixer; return self
         def think_tags(self, tags): self._extra["think_tags"] = tags; return self
 
         def build(self) -> "LLM":
-            llm = LLM(self._model, EngineConfig(**self._cfg), self._sampling, self._device, self._warmup)
+            llm = LLM(self._model, EngineConfig(**self._cfg), self._sampling, self._device, self._warmup,
+                      unpack_parameters=self._unpack, cpu_threads=self._cpu_threads)
             for k, v in self._extra.items():
                 setattr(llm, k, v)
             return llm
@@ -407,7 +454,8 @@ class LLM:
         from .chat.session import AdvisorRunner
         return AdvisorRunner.enrich(self, list(self.advisors or []), model_user_text, list(prior_dialog or []),
                                     sampling or self.default_sampling, mixer=self.advisor_mixer,
-                                    tags=self.think_tags or ThinkTags())
+                                    tags=self.think_tags or ThinkTags(),
+                                    note_filter=getattr(self, "advisor_note_filter", None))
 
     def new_conversation(self):
         """Fresh dialog history: the engine's system prompt as a system turn when it is not blank."""

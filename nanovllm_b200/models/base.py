@@ -7,6 +7,8 @@ Interface mirrors nano-vllm-java/src/main/java/com/igormaznitsa/nanollvm/models/
 """
 from __future__ import annotations
 
+import contextlib
+import contextvars
 import math
 from typing import Callable, Dict, Iterable, List, Optional, Tuple
 
@@ -14,6 +16,23 @@ import torch
 
 from ..config import HfConfig
 from ..exceptions import ModelLoadException
+
+# set while an engine that unpacks its parameters builds its model graph: packed sources (GGUF blocks, QAT
+# integer weights) are expanded to dense bf16 instead of taking the dequant-fused GEMM
+_UNPACK = contextvars.ContextVar("nvb_unpack_parameters", default=False)
+
+
+@contextlib.contextmanager
+def unpacked_parameters(on: bool = True):
+    token = _UNPACK.set(bool(on))
+    try:
+        yield
+    finally:
+        _UNPACK.reset(token)
+
+
+def unpacking() -> bool:
+    return _UNPACK.get()
 
 
 class WeightBag:

@@ -34,7 +34,7 @@ from ..layers.embedding import ParallelLMHead, VocabParallelEmbedding
 from ..layers.norms import RMSNorm, RotaryTables
 from ..ops.quant import cat_rows
 from ..parallel import state as tp
-from .base import CausalLMBase, WeightBag, random_weights
+from .base import CausalLMBase, WeightBag, random_weights, unpacking
 
 
 def _dims(hf: HfConfig, i: int):
@@ -92,7 +92,7 @@ def qat_group_weights(bag, names: Sequence[str], device) -> list:
     CPU), else dense bf16 for all members -- one GEMM never mixes the two."""
     mode = os.environ.get("NVB_GGUF_PACKED", "1")
     on = mode == "force" or (torch.device(device).type == "cuda" and mode not in ("0", "false", "no"))
-    if on:
+    if on and not unpacking():
         raws = [bag.tensors.get(n) for n in names]
         blocks = [r.to_gguf_blocks() if hasattr(r, "to_gguf_blocks") else None for r in raws]
         if all(b is not None for b in blocks):

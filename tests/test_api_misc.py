@@ -49,3 +49,44 @@ def test_sources_bytes_and_path_load_the_same_model(tmp_path):
     assert a.hf_config.hidden_size == b.hf_config.hidden_size
     assert set(a.weights) == set(b.weights)
     assert mem._dir is None  # spooled folder removed after the load
+
+
+def _tiny_qwen():
+    from nanovllm_b200.config import HfConfig
+    from nanovllm_b200.models.registry import init_random_weights
+    hf = HfConfig(vocab_size=300, hidden_size=128, intermediate_size=256, num_hidden_layers=1, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=32, max_position_embeddings=512, model_type="qwen3")
+    return hf, init_random_weights(hf, 1)
+
+
+def test_builder_knobs_of_the_reference_builder(monkeypatch):
+    """LLM.java:1499-1870 builder knobs: system prompt / advisors overrides, KV memory share, CPU workers,
+    unpacking, warm-up switches."""
+    import torch
+    from nanovllm_b200.chat import session
+    from nanovllm_b200.llm import LLM
+    threads = torch.get_num_threads()
+    try:
+        b = (LLM.builder(_tiny_qwen()).device("cpu").num_kvcache_blocks(8).max_model_len(256).kv_heap_fraction(0.5)
+             .disable_multi_cpu().system_prompt("be brief").no_system_prompt().advisors(object()).no_advisors()
+             .warmup().skip_warmup().advisor_note_filter(lambda s: "keep" in s))
+        llm = b.build()
+        assert llm.cfg.gpu_memory_utilization == 0.5
+        assert torch.get_num_threads() == 1
+        assert llm.system_prompt == "" and llm.advisors == [] and llm.advisor_mixer is None
+        seen = {}
+        monkeypatch.setattr(session.AdvisorRunner, "enrich",
+                            staticmethod(lambda *a, **kw: seen.update(kw) or "enriched"))
+        assert llm.run_advisors("hello") == "enriched"
+        assert seen["note_filter"]("keep this") and not seen["note_filter"]("drop")
+        llm2 = LLM.builder(_tiny_qwen()).device("cpu").num_kvcache_blocks(8).max_model_len(256) \
+            .system_prompt("x").default_system_prompt().build()
+        assert llm2.system_prompt == ""
+    finally:
+        torch.set_num_threads(threads)
+    with pytest.raises(ValueError):
+        LLM.builder(_tiny_qwen()).cpu_threads(0)
+    with pytest.raises(ValueError):
+        LLM.builder(_tiny_qwen()).device("cpu").kv_heap_fraction(0.0).build()
+    with pytest.raises(TypeError):
+        LLM.builder(_tiny_qwen()).advisor_note_filter("not callable")

@@ -224,6 +224,28 @@ def test_gemma4_qat_projections_run_packed(tmp_path, monkeypatch):
     assert (got - want).abs().max() < 0.05
 
 
+def test_allow_unpack_parameters_expands_packed_projections(tmp_path, monkeypatch):
+    """``allow_unpack_parameters`` (LLM.java:1819-1835): an engine over a packed model expands its projections to
+    bf16 (the shared model keeps its packed tensors) and gives the packed engine's logits within bf16 rounding."""
+    from nanovllm_b200.api.factory import LlmModelFactory
+    from nanovllm_b200.models.writers import byte_level_tokenizer_json
+    hf = gemma4_tiny(hidden_size=256, intermediate_size=256)
+    d = write_gemma4_qat_folder(str(tmp_path / "g4u"), hf, init_random_weights(hf, 8), scale_cols=4,
+                                tokenizer_json=byte_level_tokenizer_json(300))
+    ids = list(range(5, 37))
+    monkeypatch.setenv("NVB_GGUF_PACKED", "force")
+    model = LlmModelFactory.make(d, device="cpu")
+    packed = LLM(model, _cfg(), device="cpu")
+    groups = [g for L in packed.model.layers for g in (L.qkv, L.o_proj, L.gate_up, L.down)]
+    assert any(not isinstance(w, torch.Tensor) for g in groups for w in (getattr(g, "ws", None) or [g.w]))
+    want = _engine_logits(packed, ids).float()
+    llm = LLM.builder(model).device("cpu").max_model_len(_cfg().max_model_len).allow_unpack_parameters().build()
+    groups = [g for L in llm.model.layers for g in (L.qkv, L.o_proj, L.gate_up, L.down)]
+    assert all(isinstance(w, torch.Tensor) for g in groups for w in (getattr(g, "ws", None) or [g.w]))
+    got = _engine_logits(llm, ids).float()
+    assert torch.nn.functional.cosine_similarity(got, want, dim=0) > 0.999
+
+
 @pytest.mark.gpu
 def test_gemma4_qat_packed_gemm_on_gpu(tmp_path, monkeypatch):
     """On the GPU the converted QAT projections run the dequant-fused tcgen05 GEMM (decode) and the dequant +

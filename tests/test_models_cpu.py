@@ -155,6 +155,29 @@ def test_factory_gguf_qwen3_q8_0_close_to_dense(tmp_path):
     assert torch.nn.functional.cosine_similarity(a, b, dim=0) > 0.99
 
 
+def test_unpacked_engine_over_packed_gguf_model(tmp_path, monkeypatch):
+    """An engine built with unpack_parameters over a model whose GGUF projections stay packed gets dense bf16
+    copies (the model keeps its blocks) and the packed engine's logits within bf16 rounding."""
+    from nanovllm_b200.ops.quant import GgufPacked
+    hf = HfConfig(vocab_size=300, hidden_size=128, intermediate_size=256, num_hidden_layers=2, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=32, max_position_embeddings=2048, model_type="qwen3",
+                  architectures=["Qwen3ForCausalLM"], tie_word_embeddings=False)
+    p = write_gguf_model(str(tmp_path / "q3p.gguf"), hf, init_random_weights(hf, 0), "Q8_0")
+    monkeypatch.setenv("NVB_GGUF_PACKED", "force")
+    m = LlmModelFactory.make(p, device="cpu")
+    n_packed = sum(isinstance(v, GgufPacked) for v in m.weights.values())
+    assert n_packed > 0
+    ids = list(range(3, 60))
+    packed = LLM(m, _cfg(), device="cpu")
+    assert all(isinstance(L.down.weight, GgufPacked) for L in packed.model.layers)
+    a = _prefill_logits(packed, ids)
+    llm = LLM(m, _cfg(), device="cpu", unpack_parameters=True)
+    assert sum(isinstance(v, GgufPacked) for v in m.weights.values()) == n_packed
+    assert all(isinstance(L.down.weight, torch.Tensor) for L in llm.model.layers)
+    b = _prefill_logits(llm, ids)
+    assert torch.nn.functional.cosine_similarity(a, b, dim=0) > 0.999
+
+
 def test_factory_gguf_lfm2_q4_k_m(tmp_path):
     hf = lfm2_tiny()
     w = init_random_weights(hf, 3)
