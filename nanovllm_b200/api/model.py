@@ -64,6 +64,15 @@ class LlmModel:
         from ..chat.markup import ThinkTags
         return self.options.get("think_tags") or ThinkTags.default()
 
+    def chat_specials(self):
+        """Chat-markup markers that end a visible answer (checkpoint option ``chat_specials``, else the default
+        ChatML / Gemma / Llama set)."""
+        from ..chat.markup import ChatSpecials
+        sp = self.options.get("chat_specials")
+        if sp is None:
+            return ChatSpecials.default()
+        return sp if isinstance(sp, ChatSpecials) else ChatSpecials(tuple(sp))
+
     def __repr__(self) -> str:
         hf = self.hf_config
         return (f"LlmModel(arch={self.architecture_name}, layers={hf.num_hidden_layers}, hidden={hf.hidden_size}, "

@@ -26,7 +26,7 @@ from ..sampling_params import SamplingParams
 from ..utils.limits import ResourceLimits
 from . import prompts
 from .listeners import LlmListener, LlmTextKind, emit
-from .markup import ChatReply, ThinkTags, parse, salvage_from_thinking
+from .markup import ChatReply, ChatSpecials, ReplyScanner, ThinkTags, parse, salvage_from_thinking
 from .messages import ChatMessage, truncate_history
 
 MAX_ADVISOR_TOKENS = 256
@@ -186,6 +186,8 @@ class ChatSession:
         self.tok = llm.tokenizer
         self.sampling = sampling or llm.default_sampling
         self.tags = think_tags or getattr(llm, "think_tags", None) or _engine_think_tags(llm)
+        specials = getattr(llm, "chat_specials", None)
+        self.specials = (specials() if callable(specials) else None) or ChatSpecials.default()
         self.enable_thinking = enable_thinking
         self.max_history = max_history_messages
         self.timeout_s = timeout_s
@@ -306,20 +308,20 @@ class ChatSession:
         dec = self.tok.stream_decoder(skip_special=True)
         stream = self._stream = _TurnStream()
         raw: List[str] = []
+        scanner = ReplyScanner(self.tags, self.specials)  # fed one decoded delta per token, never rescanned
 
         def on_token(_i, _sid, token):
             delta = dec.push(token)
             if not delta:
                 return
             raw.append(delta)
-            text = "".join(raw)
-            p = parse(text, self.tags)
-            stream.push(self.listener, self, text, p.thinking, p.answer, p.think_open)
+            p = scanner.feed(delta).snapshot()
+            stream.push(self.listener, self, "".join(raw), p.thinking, p.answer, p.think_open)
 
         out = self.llm.generate_token_ids([ids], sp, on_token=on_token if self.listener else None,
                                           timeout_s=self.timeout_s)[0]
         full = self.tok.decode(out.token_ids, skip_special=True)
-        p = parse(full, self.tags)
+        p = parse(full, self.tags, self.specials)
         return ChatReply(p.answer, p.thinking, full, getattr(self.llm, "last_stats", None), think_open=p.think_open)
 
     def _finish(self, reply: ChatReply) -> ChatReply:

@@ -242,6 +242,14 @@ class LLM:
             self.runner.close()
             self._closed = True
 
+    def is_closed(self) -> bool:
+        return self._closed
+
+    def chat_specials(self):
+        """The model's chat-markup markers (stripped from visible answers)."""
+        from .chat.markup import ChatSpecials
+        return self.model_handle.chat_specials() if self.model_handle is not None else ChatSpecials.default()
+
     def _release_and_note(self, seq: Sequence) -> None:
         self.runner.release_state(seq)
         self._plan_tx.note_release(seq)

@@ -90,3 +90,17 @@ def test_builder_knobs_of_the_reference_builder(monkeypatch):
         LLM.builder(_tiny_qwen()).device("cpu").kv_heap_fraction(0.0).build()
     with pytest.raises(TypeError):
         LLM.builder(_tiny_qwen()).advisor_note_filter("not callable")
+
+
+def test_model_chat_specials_option_and_engine_accessors():
+    from nanovllm_b200.api.model import LlmModel
+    from nanovllm_b200.chat.markup import ChatSpecials
+    from nanovllm_b200.llm import LLM
+    hf, w = _tiny_qwen()
+    m = LlmModel(hf, w, options={"chat_specials": ["<|x|>"]})
+    assert m.chat_specials().markers == ("<|x|>",)
+    assert LlmModel(hf, w).chat_specials() == ChatSpecials.default()
+    llm = LLM.builder(m).device("cpu").num_kvcache_blocks(8).max_model_len(256).build()
+    assert llm.chat_specials().markers == ("<|x|>",) and not llm.is_closed()
+    llm.close()
+    assert llm.is_closed()

@@ -206,6 +206,19 @@ def test_chat_session_on_tiny_model_cpu():
     assert [m.role for m in s.history] == ["system", "user", "assistant", "user", "assistant"]
 
 
+def test_session_uses_the_models_chat_specials():
+    """A checkpoint's own end-of-answer marker (LlmModel option ``chat_specials``) ends the visible answer, both
+    in the streamed events and in the final reply."""
+    from nanovllm_b200.chat.markup import ChatSpecials
+    llm = ScriptedLLM(["Six. [[stop]] trailing junk"])
+    llm.chat_specials = lambda: ChatSpecials(("[[stop]]",))
+    listener, events = LlmListeners.collecting()
+    r = ChatSession(llm, listener=listener).send("3+3?")
+    assert r.answer == "Six."
+    shown = "".join(e.text for e in events if e.kind == LlmTextKind.TEXT_ASSISTANT and not e.snapshot)
+    assert shown.strip() == "Six."
+
+
 def test_reply_scanner_streams_token_by_token_like_a_single_parse():
     from nanovllm_b200.chat.markup import ReplyScanner
     raw = "<think>plan: add\nthe numbers</think>The answer is 4.<|im_end|>tail"
