@@ -230,24 +230,36 @@ def _is_cjk(cp: int) -> bool:
             0x2F800 <= cp <= 0x2FA1F)
 
 
+# ASCII fast path of the BERT basic tokeniser: runs of ASCII are cleaned by one str.translate (control characters
+# are category Cc and dropped; tab / newline / CR stay as whitespace) and split into words and single punctuation
+# characters by one regex, at C speed; the other characters take the per-character path below.
+_ASCII_CLEAN = {c: None for c in list(range(0, 9)) + [11, 12] + list(range(14, 32)) + [127]}
+_ASCII_PUNCT = r"!-/:-@\[-`{-~"
+_ASCII_WORDS = regex.compile(rf"[{_ASCII_PUNCT}]|[^\s{_ASCII_PUNCT}]+")
+_ASCII_RUN = regex.compile(r"([\x00-\x7f]+)")
+
+
 def bert_basic_tokenize(text: str, lowercase: bool = True, strip_accents: Optional[bool] = None) -> List[str]:
-    out = []
-    for ch in text:
-        cp = ord(ch)
-        if cp == 0 or cp == 0xFFFD or (unicodedata.category(ch).startswith("C") and ch not in "\t\n\r"):
-            continue
-        if _is_cjk(cp):
-            out.append(f" {ch} ")
-        elif ch in "\t\n\r" or unicodedata.category(ch) == "Zs":
-            out.append(" ")
-        else:
-            out.append(ch)
-    text = "".join(out)
+    """BERT basic tokenisation: drop control characters, space out CJK ideographs, split on whitespace, optional
+    lower-case and accent strip, then split off every punctuation character."""
+    if text.isascii():
+        t = text.translate(_ASCII_CLEAN)
+        return _ASCII_WORDS.findall(t.lower() if lowercase else t)
+    parts = _ASCII_RUN.split(text)  # non-ASCII runs at even indices, ASCII runs at odd ones
+    for i in range(1, len(parts), 2):
+        parts[i] = parts[i].translate(_ASCII_CLEAN)
+    for i in range(0, len(parts), 2):
+        if parts[i]:
+            parts[i] = _clean_chars(parts[i])
     words = []
-    for w in text.split():
+    strip = strip_accents or (strip_accents is None and lowercase)
+    for w in "".join(parts).split():
+        if w.isascii():
+            words.extend(_ASCII_WORDS.findall(w.lower() if lowercase else w))
+            continue
         if lowercase:
             w = w.lower()
-        if strip_accents or (strip_accents is None and lowercase):
+        if strip:
             w = "".join(c for c in unicodedata.normalize("NFD", w) if unicodedata.category(c) != "Mn")
         cur = ""
         for ch in w:
@@ -263,6 +275,21 @@ def bert_basic_tokenize(text: str, lowercase: bool = True, strip_accents: Option
     return words
 
 
+def _clean_chars(text: str) -> str:
+    out = []
+    for ch in text:
+        cp = ord(ch)
+        if cp == 0 or cp == 0xFFFD or (unicodedata.category(ch).startswith("C") and ch not in "\t\n\r"):
+            continue
+        if _is_cjk(cp):
+            out.append(f" {ch} ")
+        elif ch in "\t\n\r" or unicodedata.category(ch) == "Zs":
+            out.append(" ")
+        else:
+            out.append(ch)
+    return "".join(out)
+
+
 class WordPiece(Codec):
     def __init__(self, vocab: Dict[str, int], unk_token: str = "[UNK]", prefix: str = "##",
                  lowercase: bool = True, strip_accents: Optional[bool] = None, max_chars: int = 100):
@@ -272,8 +299,18 @@ class WordPiece(Codec):
         self.lowercase = lowercase
         self.strip_accents = strip_accents
         self.max_chars = max_chars
+        self._cache: Dict[str, List[int]] = {}
 
     def _word(self, w: str) -> List[int]:
+        hit = self._cache.get(w)
+        if hit is not None:
+            return hit
+        ids = self._match(w)
+        if len(self._cache) < 200_000:
+            self._cache[w] = ids
+        return ids
+
+    def _match(self, w: str) -> List[int]:
         if len(w) > self.max_chars:
             return [self.unk_id]
         out = []

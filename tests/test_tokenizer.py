@@ -144,3 +144,50 @@ def test_stream_decoder_emits_complete_characters(tmp_path):
     out = "".join(sd.push(i) for i in ids) + sd.flush()
     assert out == text
     assert "�" not in out
+
+
+def _basic_by_definition(text, lowercase=True, strip_accents=None):
+    """BERT basic tokenisation written per character (the definition the fast path must reproduce)."""
+    import unicodedata
+    from nanovllm_b200.tokenizer.codecs import _is_cjk, _is_punct
+    out = []
+    for ch in text:
+        cp = ord(ch)
+        if cp == 0 or cp == 0xFFFD or (unicodedata.category(ch).startswith("C") and ch not in "\t\n\r"):
+            continue
+        out.append(f" {ch} " if _is_cjk(cp) else " " if ch in "\t\n\r" or unicodedata.category(ch) == "Zs" else ch)
+    words = []
+    for w in "".join(out).split():
+        if lowercase:
+            w = w.lower()
+        if strip_accents or (strip_accents is None and lowercase):
+            w = "".join(c for c in unicodedata.normalize("NFD", w) if unicodedata.category(c) != "Mn")
+        cur = ""
+        for ch in w:
+            if _is_punct(ch):
+                if cur:
+                    words.append(cur)
+                    cur = ""
+                words.append(ch)
+            else:
+                cur += ch
+        if cur:
+            words.append(cur)
+    return words
+
+
+@pytest.mark.parametrize("lowercase,strip", [(True, None), (False, None), (True, False), (False, True)])
+def test_bert_basic_tokenize_fast_path_matches_definition(lowercase, strip):
+    import random
+    from nanovllm_b200.tokenizer.codecs import bert_basic_tokenize
+    alphabet = (list("abcXYZ019 ,.;!?-_'\"()[]{}@#$%^&*+=~`|\\/<>:") +
+                ["\t", "\n", "\r", "\x00", "\x01", "\x0b", "\x0c", "\x1c", "\x1f", "\x7f",  # ASCII controls
+                 "\x85", "\u00a0", "\u3000", "\u2028", "\u200b", "\ufffd",  # NEL, Zs, Zs, Zl, Cf, replacement
+                 "\u00e9", "\u00c4", "\u00f1", "e\u0301", "\u0301",  # accents, combining acute
+                 "\u4e2d", "\u6587", "\uff0c", "\u3002", "\u201c", "\u201d", "\u2014",  # CJK, CJK / other punct
+                 "\u212a", "\u0130", "\u00df", "\u03a9", "\U0001f600", "\U00020001"])  # Kelvin, dotted I, ...
+    rng = random.Random(11)
+    for n in range(600):
+        pool = alphabet[:52] if n % 3 == 0 else alphabet  # a third of the cases are pure ASCII
+        text = "".join(rng.choice(pool) for _ in range(rng.randint(0, 40)))
+        assert bert_basic_tokenize(text, lowercase, strip) == _basic_by_definition(text, lowercase, strip), repr(text)
