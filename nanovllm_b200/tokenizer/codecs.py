@@ -51,7 +51,8 @@ BYTE_DECODER = {v: k for k, v in BYTE_ENCODER.items()}
 
 
 def bpe_merge(symbols: List[str], ranks: Dict[Tuple[str, str], int]) -> List[str]:
-    """Apply merges lowest rank first until no adjacent pair is mergeable."""
+    """Apply merges lowest rank first until no adjacent pair is mergeable (the pure-Python path; byte-level
+    vocabularies use the C++ core in csrc/host/bpe.cpp when it is built)."""
     if len(symbols) < 2:
         return symbols
     while True:
@@ -85,19 +86,65 @@ class Codec:
         raise NotImplementedError
 
 
+def _native_core():
+    try:
+        import torch  # noqa: F401  (loads the libraries the extension links against)
+        from .. import _host
+        return _host
+    except ImportError:  # the host helpers were not built: the pure-Python merge below runs instead
+        return None
+
+
 class ByteBpe(Codec):
     def __init__(self, vocab: Dict[str, int], merges: List[Tuple[str, str]], pattern: Optional[str] = GPT2_PATTERN,
-                 unk_id: Optional[int] = None):
+                 unk_id: Optional[int] = None, native: Optional[bool] = None):
         self.vocab = vocab
         self.ranks = {m: i for i, m in enumerate(merges)}
         self.split = regex.compile(pattern) if pattern else None
         self.unk_id = unk_id
         self._cache: Dict[str, List[int]] = {}
+        host = _native_core() if native is not False else None
+        if native and host is None:
+            raise ImportError("nanovllm_b200._host is not built (python setup.py build_ext --inplace)")
+        self._core = self._build_core(host) if host is not None else None
+
+    def _build_core(self, host):
+        """Intern every symbol a merge can produce and hand the merge table to the C++ core (csrc/host/bpe.cpp)."""
+        ids: Dict[str, int] = {}
+        syms: List[str] = []
+
+        def sid(x: str) -> int:
+            i = ids.get(x)
+            if i is None:
+                i = ids[x] = len(syms)
+                syms.append(x)
+            return i
+
+        byte_sym = [sid(BYTE_ENCODER[b]) for b in range(256)]
+        left, right, rank, merged = [], [], [], []
+        for (a, b), r in self.ranks.items():
+            left.append(sid(a))
+            right.append(sid(b))
+            rank.append(r)
+            merged.append(sid(a + b))
+        vocab, unk = self.vocab, self.unk_id
+        sym_vocab = [vocab.get(x, -1) for x in syms]
+        fb_off, fb_ids = [0], []
+        for x, v in zip(syms, sym_vocab):
+            if v < 0:  # unknown merged piece: its single byte symbols (as the Python path does)
+                fb_ids.extend(j for j in (vocab.get(ch, unk) for ch in x) if j is not None)
+            fb_off.append(len(fb_ids))
+        return host.ByteBpeCore(byte_sym, left, right, rank, merged, sym_vocab, fb_off, fb_ids)
 
     def _word(self, word: str) -> List[int]:
         hit = self._cache.get(word)
         if hit is not None:
             return hit
+        if self._core is not None:
+            ids = self._core.encode_word(word.encode("utf-8"))
+            if len(self._cache) < 100_000:
+                self._cache[word] = ids
+            return ids
         mapped = "".join(BYTE_ENCODER[b] for b in word.encode("utf-8"))
         pieces = bpe_merge(list(mapped), self.ranks)
         ids = []

@@ -191,3 +191,31 @@ def test_bert_basic_tokenize_fast_path_matches_definition(lowercase, strip):
         pool = alphabet[:52] if n % 3 == 0 else alphabet  # a third of the cases are pure ASCII
         text = "".join(rng.choice(pool) for _ in range(rng.randint(0, 40)))
         assert bert_basic_tokenize(text, lowercase, strip) == _basic_by_definition(text, lowercase, strip), repr(text)
+
+
+def test_native_byte_bpe_core_matches_python_merge(tmp_path):
+    """The C++ merge core (csrc/host/bpe.cpp) gives the pure-Python merge's ids: trained merges, random byte
+    strings (multi-byte UTF-8, rare bytes) and a merged piece missing from the vocabulary (byte fallback)."""
+    import random
+    from nanovllm_b200.tokenizer import codecs as C
+    if C._native_core() is None:
+        pytest.skip("host extension not built")
+    t = _train_bytelevel(tmp_path)
+    j = json.loads(t.to_str())
+    vocab = dict(j["model"]["vocab"])
+    merges = [tuple(m.split(" ")) if isinstance(m, str) else tuple(m) for m in j["model"]["merges"]]
+    # drop one merged piece from the vocabulary: both paths must fall back to its byte symbols
+    gone = next(m for m in reversed(merges) if (m[0] + m[1]).isascii() and (m[0] + m[1]).isalpha())
+    vocab.pop(gone[0] + gone[1])
+    py = C.ByteBpe(vocab, merges, C.GPT2_PATTERN, native=False)
+    nat = C.ByteBpe(vocab, merges, C.GPT2_PATTERN, native=True)
+    assert py._core is None and nat._core is not None
+    rng = random.Random(5)
+    texts = SAMPLES + CORPUS[:3] + [gone[0] + gone[1] + " " + gone[0] + gone[1]]
+    for _ in range(300):
+        texts.append("".join(chr(rng.choice([rng.randrange(32, 127), rng.randrange(0xa0, 0x800),
+                                              rng.randrange(0x3000, 0x9fff), rng.randrange(0x1f300, 0x1f64f)]))
+                             for _ in range(rng.randint(1, 30))))
+    for s in texts:
+        assert nat.encode(s) == py.encode(s), s
+    assert len(nat.encode(gone[0] + gone[1])) == len(gone[0] + gone[1])  # the fallback ran: one id per byte
