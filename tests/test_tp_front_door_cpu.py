@@ -196,3 +196,36 @@ def test_idle_worker_learns_of_rank0_failure():
     assert state == "aborted"
     reason, elapsed = info
     assert "injected failure" in reason and elapsed < 30
+
+
+def _example_run(rank, world, port, q):
+    import io
+    import contextlib
+    import sys as _sys
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      CUDA_VISIBLE_DEVICES="")
+    examples = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "examples")
+    _sys.path.insert(0, examples)
+    import tp_serve
+    buf = io.StringIO()
+    with contextlib.redirect_stdout(buf):
+        rc = tp_serve.main([])
+    q.put((rank, rc, buf.getvalue()))
+
+
+def test_tp_serve_example_runs_on_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_example_run, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    for _ in procs:
+        r, rc, out = q.get(timeout=240)
+        got[r] = (rc, out)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0][0] == 0 and "3 answers" in got[0][1] and "Time taken" in got[0][1]
+    assert got[1][0] == 0 and "followed" in got[1][1]
