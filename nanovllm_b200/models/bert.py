@@ -9,8 +9,10 @@ data-parallel over GPUs (one replica per rank, token-balanced shares, one all-ga
 """
 from __future__ import annotations
 
+import itertools
 from typing import Dict, List, Tuple
 
+import numpy as np
 import torch
 
 from .. import ops
@@ -113,13 +115,17 @@ class BertEncoder:
                 tokens += len(batch[j])
                 j += 1
             chunk = batch[i:j]
-            ids = torch.tensor([t for s in chunk for t in s], dtype=torch.long, device=self.device)
-            pos = torch.tensor([p for s in chunk for p in range(len(s))], dtype=torch.long, device=self.device)
-            cu_l = [0]
-            for s in chunk:
-                cu_l.append(cu_l[-1] + len(s))
-            cu = torch.tensor(cu_l, dtype=torch.int32, device=self.device)
-            e = self.encode_packed(ids, pos, cu, max(len(s) for s in chunk)).float()
+            # flat ids, positions and cu_seqlens built in numpy (a Python list per token cost ~5x more host time
+            # than the encoder pass leaves per chunk)
+            lens = np.fromiter((len(s) for s in chunk), dtype=np.int64, count=len(chunk))
+            cu_np = np.zeros(len(chunk) + 1, dtype=np.int64)
+            np.cumsum(lens, out=cu_np[1:])
+            T = int(cu_np[-1])
+            ids = torch.from_numpy(np.fromiter(itertools.chain.from_iterable(chunk), dtype=np.int64, count=T))
+            pos = torch.from_numpy(np.arange(T, dtype=np.int64) - np.repeat(cu_np[:-1], lens))
+            cu = torch.from_numpy(cu_np.astype(np.int32))
+            ids, pos, cu = (t.to(self.device) for t in (ids, pos, cu))
+            e = self.encode_packed(ids, pos, cu, int(lens.max())).float()
             outs.append(e if keep_device else e.cpu())
             i = j
         return torch.cat(outs, 0)
