@@ -192,6 +192,8 @@ class ModelRunner:
         self.h_steps = buf(S, torch.int32)
         self._err_host = buf(1, torch.int32)
         self._bt_rows: List[Optional[tuple]] = [None] * S  # (seq id, block-table generation, blocks written)
+        self._samp_key: Optional[List[int]] = None  # seq ids whose sampling knobs are on the device, in row order
+        self._samp_dev: tuple = ()
         # numpy views share the pinned memory: element writes from Python stay cheap
         for name in ("ids", "pos", "slots", "cu_q", "cu_k", "ctx", "last", "bt", "rows", "fresh", "temps", "topk",
                      "topp", "seeds", "sids", "steps"):
@@ -299,17 +301,25 @@ class ModelRunner:
 
     # ------------------------------------------------------------------ sampling
     def _sampling_tensors(self, seqs: List[Sequence]):
+        """(temperature, top_k, top_p, seed, seed id, step) per row on the device.  Only the step changes while
+        the batch keeps its sequences in the same order (every decode step between admissions and finishes):
+        the other five stay on the device from the step that staged them."""
         n = len(seqs)
-        base = self.cfg.seed * 1000003
-        self.n_temps[:n] = [s.temperature for s in seqs]
-        self.n_topk[:n] = [s.top_k for s in seqs]
-        self.n_topp[:n] = [s.top_p for s in seqs]
-        self.n_seeds[:n] = [(int(s.seed) if s.seed is not None else base + s.seq_id) & 0x7FFFFFFFFFFFFFFF
-                            for s in seqs]
-        self.n_sids[:n] = [0 if s.seed is not None else s.seq_id for s in seqs]
         self.n_steps[:n] = [s.num_tokens for s in seqs]
-        return tuple(self._h2d(h, n) for h in (self.h_temps, self.h_topk, self.h_topp, self.h_seeds, self.h_sids,
-                                                self.h_steps))
+        steps = self._h2d(self.h_steps, n)
+        key = [s.seq_id for s in seqs]
+        if key != self._samp_key:
+            base = self.cfg.seed * 1000003
+            self.n_temps[:n] = [s.temperature for s in seqs]
+            self.n_topk[:n] = [s.top_k for s in seqs]
+            self.n_topp[:n] = [s.top_p for s in seqs]
+            self.n_seeds[:n] = [(int(s.seed) if s.seed is not None else base + s.seq_id) & 0x7FFFFFFFFFFFFFFF
+                                for s in seqs]
+            self.n_sids[:n] = [0 if s.seed is not None else s.seq_id for s in seqs]
+            self._samp_dev = tuple(self._h2d(h, n) for h in (self.h_temps, self.h_topk, self.h_topp, self.h_seeds,
+                                                             self.h_sids))
+            self._samp_key = key
+        return self._samp_dev + (steps,)
 
     def sample(self, logits: torch.Tensor, seqs: List[Sequence]) -> torch.Tensor:
         n = len(seqs)

@@ -333,3 +333,23 @@ def test_prefill_and_decode_staging_match_block_tables():
         sch.postprocess(seqs, [rng.randrange(1000) for _ in seqs], pre)
         steps += 1
     assert steps > 4
+
+
+def test_sampling_knobs_stay_on_device_while_the_batch_is_unchanged():
+    import torch
+    from nanovllm_b200.engine import model_runner as mr
+    cfg = EngineConfig(max_num_seqs=8, max_model_len=512)
+    r = mr.ModelRunner.__new__(mr.ModelRunner)
+    r.cfg, r.is_cuda, r.block_size, r.max_blocks_per_seq = cfg, False, 256, 2
+    r.device, r.last_h2d_bytes, r.step_events, r._started = torch.device("cpu"), 0, None, False
+    r._staging()
+    a = Sequence([1, 2, 3], SamplingParams(temperature=0.5, top_k=3, top_p=0.9, seed=11))
+    b = Sequence([4, 5], SamplingParams(temperature=0.9, top_k=0, top_p=0.5))
+    t1 = r._sampling_tensors([a, b])
+    a.append_token(7)
+    t2 = r._sampling_tensors([a, b])
+    assert all(x is y for x, y in zip(t1[:5], t2[:5]))  # knobs not staged again
+    assert t2[5].tolist() == [4, 2]
+    t3 = r._sampling_tensors([b, a])  # another order: restaged
+    assert t3[0].tolist() == pytest.approx([0.9, 0.5]) and t3[1].tolist() == [0, 3]
+    assert t3[3].tolist()[1] == 11 and t3[4].tolist() == [b.seq_id, 0] and t3[5].tolist() == [2, 4]
