@@ -335,6 +335,9 @@ class EngineConfig:
     # TP request intake: "spmd" = every rank receives the same requests and schedules them itself; "rank0" = only
     # rank 0 takes requests and broadcasts each step's plan, the other ranks run ``LLM.serve_worker``
     front_door: str = "spmd"
+    # debug: check every step's ids / positions / slots / block tables / state rows on the host before the kernels
+    # use them as addresses, and that no KV slot or shared page is written twice (engine/checks.py)
+    check_inputs: bool = False
 
     def __post_init__(self):
         if self.kvcache_block_size % 256 != 0:
@@ -343,6 +346,8 @@ class EngineConfig:
             raise ValueError("gpu_memory_utilization must be in (0, 1]")
         if self.max_num_seqs < 1 or self.max_num_batched_tokens < 1:
             raise ValueError("max_num_seqs and max_num_batched_tokens must be >= 1")
+        if os.environ.get("NVB_CHECK_INPUTS") not in (None, "", "0"):
+            self.check_inputs = True
         self.front_door = os.environ.get("NVB_TP_FRONT_DOOR", self.front_door)
         if self.front_door not in ("spmd", "rank0"):
             raise ValueError("front_door must be 'spmd' or 'rank0'")

@@ -247,6 +247,9 @@ class ModelRunner:
         self.n_last[:S] = cu_q[1:]
         self.n_last[:S] -= 1
         width = self._fill_block_tables(seqs)
+        if self.cfg.check_inputs:
+            self._check(seqs, T, S, self.n_bt[:S * width].reshape(S, width),
+                        np.diff(np.asarray(cu_k, dtype=np.int64)), np.repeat(np.arange(S), counts))
         ctx = StepContext(is_prefill=True, num_seqs=S, num_tokens=T,
                           slot_mapping=self._h2d(self.h_slots, T),
                           block_tables=self._h2d(self.h_bt, S * width).view(S, width),
@@ -276,6 +279,9 @@ class ModelRunner:
         bs = self.block_size
         self._fill_decode_rows(seqs, S)
         width = self._fill_block_tables(seqs)
+        if self.cfg.check_inputs:
+            self._check(seqs, S, S, self.n_bt[:S * width].reshape(S, width), self.n_ctx[:S].astype(np.int64),
+                        np.arange(S))
         ctx = StepContext(is_prefill=False, num_seqs=S, num_tokens=S,
                           slot_mapping=self._h2d(self.h_slots, S), context_lens=self._h2d(self.h_ctx, S),
                           block_tables=self._h2d(self.h_bt, S * width).view(S, width),
@@ -298,6 +304,17 @@ class ModelRunner:
             self.n_pos[n:pad_to] = 0
             self.n_slots[n:pad_to] = -1
             self.n_ctx[n:pad_to] = 0
+
+    def _check(self, seqs: List[Sequence], T: int, S: int, bt, ctx_lens, seq_of_token) -> None:
+        """Debug-mode range / consistency / race check of the staged step (engine/checks.py)."""
+        from .checks import check_step
+        rows = None
+        if self.state_arena is not None:
+            rows = np.asarray([self.state_rows.get(s.seq_id, 0) for s in seqs], dtype=np.int64)
+        check_step(ids=self.n_ids[:T], pos=self.n_pos[:T], slots=self.n_slots[:T].astype(np.int64), block_tables=bt,
+                   context_lens=ctx_lens, seq_of_token=seq_of_token, vocab=self.hf.vocab_size,
+                   max_pos=self.cfg.max_model_len, num_blocks=self.num_blocks, block_size=self.block_size,
+                   state_rows=rows, state_capacity=0 if self.state_arena is None else self.state_arena.shape[0])
 
     # ------------------------------------------------------------------ sampling
     def _sampling_tensors(self, seqs: List[Sequence]):
@@ -444,6 +461,8 @@ class ModelRunner:
         width = self.max_blocks_per_seq
         btn = self.n_bt[:bs * width].reshape(bs, width)
         write_block_rows(btn, self._bt_rows, seqs)
+        if self.cfg.check_inputs:
+            self._check(seqs, n, n, btn[:n], self.n_ctx[:n].astype(np.int64), np.arange(n))
         bt = self.h_bt[:bs * width].view(bs, width)
         self._begin_gpu()
         self.last_h2d_bytes += bs * (8 + 8 + 4 + 4 + 4 * width)

@@ -38,3 +38,8 @@ class DeviceWaitTimeout(NanoLlvmException):
 
 class TensorParallelAbort(NanoLlvmException):
     """Another tensor-parallel rank failed; this rank stops before launching its next step."""
+
+
+class StepInputError(NanoLlvmException):
+    """Debug-mode step check: an index the kernels would use as an address is out of range, or two sequences of
+    one step would write the same KV page (a data race) -- caught on the host before any kernel runs."""

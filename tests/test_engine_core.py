@@ -353,3 +353,41 @@ def test_sampling_knobs_stay_on_device_while_the_batch_is_unchanged():
     t3 = r._sampling_tensors([b, a])  # another order: restaged
     assert t3[0].tolist() == pytest.approx([0.9, 0.5]) and t3[1].tolist() == [0, 3]
     assert t3[3].tolist()[1] == 11 and t3[4].tolist() == [b.seq_id, 0] and t3[5].tolist() == [2, 4]
+
+
+def test_step_input_checks_pass_a_real_run_and_catch_violations():
+    """Debug-mode step checks (engine/checks.py): a full engine run with chunked prefill, prefix sharing and
+    preemption passes them; bad ids, slots, block-table entries and page races are reported, not executed."""
+    import numpy as np
+    from nanovllm_b200.config import HfConfig
+    from nanovllm_b200.engine.checks import check_step
+    from nanovllm_b200.exceptions import StepInputError
+    from nanovllm_b200.llm import LLM
+    from nanovllm_b200.models.registry import init_random_weights
+    hf = HfConfig(vocab_size=300, hidden_size=64, intermediate_size=128, num_hidden_layers=1, num_attention_heads=2,
+                  num_key_value_heads=1, head_dim=32, max_position_embeddings=1024, model_type="qwen3")
+    cfg = EngineConfig(max_num_seqs=4, max_model_len=1024, num_kvcache_blocks=5, max_num_batched_tokens=300,
+                       check_inputs=True)
+    llm = LLM((hf, init_random_weights(hf, 0)), cfg, device="cpu")
+    shared = list(range(1, 257))
+    prompts = [shared + [7] * 30, shared + [8] * 200, list(range(40, 290)), [3] * 20]
+    outs = llm.generate_token_ids(prompts, SamplingParams(max_tokens=40, ignore_eos=True, seed=1))
+    assert all(len(o.token_ids) == 40 for o in outs) and llm.scheduler.num_preemptions > 0
+
+    base = dict(ids=np.array([5, 6]), pos=np.array([256, 3]), slots=np.array([256 * 2 + 0, 256 * 3 + 3]),
+                block_tables=np.array([[1, 2], [3, 0]]), context_lens=np.array([257, 4]),
+                seq_of_token=np.array([0, 1]), vocab=300, max_pos=1024, num_blocks=5, block_size=256)
+    check_step(**base)
+    cases = [("ids", np.array([5, 300]), "token id"), ("slots", np.array([256 * 2, 256 * 5]), "slot"),
+             ("block_tables", np.array([[1, 7], [3, 0]]), "block-table entry"),
+             ("slots", np.array([256 * 2 + 1, 256 * 3 + 3]), "not the block table's slot"),
+             ("context_lens", np.array([600, 4]), "pages")]
+    for key, val, msg in cases:
+        with pytest.raises(StepInputError, match=msg):
+            check_step(**{**base, key: val})
+    # two tokens of one step on one slot, and a page written by one sequence while another's table holds it
+    with pytest.raises(StepInputError, match="more than one token"):
+        check_step(**{**base, "pos": np.array([3, 3]), "slots": np.array([256 * 3 + 3, 256 * 3 + 3]),
+                      "block_tables": np.array([[3, 0], [3, 0]]), "context_lens": np.array([4, 4])})
+    with pytest.raises(StepInputError, match="copy-on-write"):
+        check_step(**{**base, "block_tables": np.array([[1, 2], [3, 2]]), "context_lens": np.array([257, 300])})
