@@ -9,7 +9,9 @@ B200 design:
 * the KV arena is one zero-initialised bf16 allocation per (kv heads, head dim) class, laid out
   [layers, 2, num_blocks, kv_heads, block_size, head_dim] so a 64-token tile of one head is one contiguous
   TMA box; the block count comes from free device memory (``gpu_memory_utilization``) instead of the JVM heap;
-* step metadata is written into pinned host staging buffers and copied with one async H2D per field;
+* step metadata is written into pinned host staging buffers and copied with one async H2D per field; the
+  sampling knobs stay on the device while a decode batch keeps its sequences, and graph-replay block-table rows
+  are only appended to;
 * decode runs as a replay of a CUDA graph captured per batch bucket (1, 2, 4, 8, 16, 32, ...); padded rows get
   slot -1 (no KV write) and context length 0 (no attention work);
 * the sampler keys Philox by (request seed, position) when the request has a seed, else by

@@ -314,7 +314,12 @@ class LLM:
     def step(self, appended_out: Optional[list] = None):
         ps.check_abort()  # a peer rank failed: stop before launching anything that would wait for it
         with nvtx("schedule"):
-            seqs, is_prefill = self.scheduler.schedule()
+            try:
+                seqs, is_prefill = self.scheduler.schedule()
+            except BaseException as e:
+                if self._plan_tx is not None:  # front door: the workers wait for a plan that will not come
+                    ps.signal_abort(f"rank 0 could not schedule: {type(e).__name__}: {e}")
+                raise
         try:
             if self._plan_tx is not None:
                 with nvtx("plan"):
