@@ -15,6 +15,7 @@ token pieces back to text:
 """
 from __future__ import annotations
 
+import heapq
 import unicodedata
 from functools import lru_cache
 from typing import Dict, List, Optional, Sequence, Tuple
@@ -200,8 +201,61 @@ class MetaspaceBpe(Codec):
         self.byte_fallback = byte_fallback
         self.unk_id = unk_id
         self.split_on_space = split_on_space
+        # Merges never cross a boundary "x|▁" (x not ▁) when no piece holds a non-▁ character followed by ▁: the
+        # text can then be cut there and each piece merged alone with the same result (and cached), instead of
+        # running the merge over the whole text, whose cost grows with the square of its length.
+        inner = regex.compile(f"[^{SPIECE}]{SPIECE}")
+        self._chunk_safe = not any(inner.search(p) for p in vocab) and \
+            not any(inner.search(a + b) for a, b in (self.ranks or ()))
+        self._cut = regex.compile(f"(?<=[^{SPIECE}])(?={SPIECE})")
+        self._cache: Dict[str, List[int]] = {}
 
     def _merge_by_score(self, symbols: List[str]) -> List[str]:
+        """Highest-scoring adjacent merge first (leftmost among equal scores), one merge at a time, with a heap
+        of candidate pairs over a linked list of symbols: O(n log n) for a whole unsplit text."""
+        n = len(symbols)
+        if n < 2:
+            return symbols
+        sym = list(symbols)
+        nxt = list(range(1, n + 1))
+        nxt[-1] = -1
+        prv = list(range(-1, n - 1))
+        alive = [True] * n
+        vocab, scores = self.vocab, self.scores
+        heap: List[Tuple[float, int, int, str]] = []
+
+        def push(i: int) -> None:
+            j = nxt[i]
+            if j < 0:
+                return
+            cand = sym[i] + sym[j]
+            k = vocab.get(cand)
+            if k is not None:
+                sc = scores[k] if scores is not None and k < len(scores) else 0.0
+                heapq.heappush(heap, (-sc, i, j, cand))
+
+        for i in range(n - 1):
+            push(i)
+        while heap:
+            _, i, j, cand = heapq.heappop(heap)
+            if not (alive[i] and alive[j] and nxt[i] == j and sym[i] + sym[j] == cand):
+                continue  # stale: a neighbour merged since this pair was queued
+            sym[i] = cand
+            alive[j] = False
+            nxt[i] = nxt[j]
+            if nxt[j] >= 0:
+                prv[nxt[j]] = i
+            if prv[i] >= 0:
+                push(prv[i])
+            push(i)
+        out, i = [], 0
+        while i >= 0:
+            out.append(sym[i])
+            i = nxt[i]
+        return out
+
+    def _merge_by_score_rounds(self, symbols: List[str]) -> List[str]:
+        """Reference form of ``_merge_by_score``: rescan every adjacent pair per merge (quadratic; for tests)."""
         while len(symbols) > 1:
             best = None
             best_score = None
@@ -243,11 +297,19 @@ class MetaspaceBpe(Codec):
         chunks = [t]
         if self.split_on_space:
             chunks = [c for c in regex.split(f"(?={SPIECE})", t) if c]
+        elif self._chunk_safe:
+            chunks = [c for c in self._cut.split(t) if c]
         out: List[int] = []
+        cache = self._cache
         for c in chunks:
-            syms = list(c)
-            syms = bpe_merge(syms, self.ranks) if self.ranks is not None else self._merge_by_score(syms)
-            out.extend(self._pieces_to_ids(syms))
+            ids = cache.get(c)
+            if ids is None:
+                syms = list(c)
+                syms = bpe_merge(syms, self.ranks) if self.ranks is not None else self._merge_by_score(syms)
+                ids = self._pieces_to_ids(syms)
+                if len(cache) < 100_000 and len(c) <= 256:
+                    cache[c] = ids
+            out.extend(ids)
         return out
 
     def decode(self, pieces: Sequence[str]) -> str:

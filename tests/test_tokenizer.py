@@ -219,3 +219,42 @@ def test_native_byte_bpe_core_matches_python_merge(tmp_path):
     for s in texts:
         assert nat.encode(s) == py.encode(s), s
     assert len(nat.encode(gone[0] + gone[1])) == len(gone[0] + gone[1])  # the fallback ran: one id per byte
+
+
+def _spm_vocab(rng, inner_space: bool):
+    import string
+    letters = "abcde"
+    vocab = {"<unk>": 0}
+    for i in range(256):
+        vocab[f"<0x{i:02X}>"] = len(vocab)
+    for c in letters + "▁":
+        vocab.setdefault(c, len(vocab))
+    for _ in range(120):
+        p = "".join(rng.choice(letters) for _ in range(rng.randint(2, 4)))
+        vocab.setdefault(p, len(vocab))
+        vocab.setdefault("▁" + p[:rng.randint(1, len(p))], len(vocab))
+    vocab.setdefault("▁▁", len(vocab))
+    if inner_space:  # pieces across a word boundary: the text may not be cut
+        vocab.setdefault("a▁b", len(vocab))
+        vocab.setdefault("e▁", len(vocab))
+    return vocab
+
+
+@pytest.mark.parametrize("inner_space", [False, True])
+def test_sentencepiece_bpe_heap_merge_and_word_cuts_match_full_rescans(inner_space):
+    """Score-ordered SentencePiece merging: the heap form equals the rescan-every-pair form (ties: leftmost),
+    and cutting the text before each word (only when no piece spans a word boundary) changes no id."""
+    import random
+    from nanovllm_b200.tokenizer import codecs as C
+    rng = random.Random(3 + inner_space)
+    vocab = _spm_vocab(rng, inner_space)
+    scores = [float(rng.randint(0, 6)) for _ in range(len(vocab))]  # many ties
+    cod = C.MetaspaceBpe(vocab, None, scores, add_prefix=True, byte_fallback=True, unk_id=0)
+    assert cod._chunk_safe == (not inner_space)
+    for _ in range(300):
+        text = "".join(rng.choice("abcde  é") for _ in range(rng.randint(1, 60)))
+        t = text.replace(" ", C.SPIECE)
+        t = t if t.startswith(C.SPIECE) else C.SPIECE + t  # the codec's prefix rule
+        want = cod._pieces_to_ids(cod._merge_by_score_rounds(list(t)))
+        assert cod._merge_by_score(list(t)) == cod._merge_by_score_rounds(list(t)), t
+        assert cod.encode(text) == want, text
