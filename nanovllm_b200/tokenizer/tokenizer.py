@@ -258,30 +258,36 @@ class Tokenizer:
 
 
 class StreamDecoder:
-    """Incremental detokeniser that only emits text once the bytes form complete UTF-8 characters."""
+    """Incremental detokeniser that only emits text once the bytes form complete UTF-8 characters.
+
+    A push decodes only the tokens since the previous emission plus the ones before it back to the emission
+    before that (``prefix`` .. end), and emits what that window decodes to beyond its already-emitted part
+    (``prefix`` .. ``read``).  Both decodes start at the same token, so word joins, leading-space rules and
+    multi-byte characters come out as in a decode of the whole reply, at a cost that does not grow with the
+    reply's length."""
 
     def __init__(self, tok: Tokenizer, skip_special: bool = True):
         self.tok = tok
         self.skip = skip_special
         self.ids: List[int] = []
-        self.emitted = 0
+        self.prefix = 0  # window start: a token boundary whose preceding text is emitted
+        self.read = 0    # tokens whose text is emitted
 
     def push(self, token_id: int) -> str:
         self.ids.append(int(token_id))
-        text = self.tok.decode(self.ids, self.skip)
+        head = self.tok.decode(self.ids[self.prefix:self.read], self.skip)
+        full = self.tok.decode(self.ids[self.prefix:], self.skip)
         # hold back a trailing replacement character: it is usually an incomplete multi-byte sequence
-        safe = text[:-1] if text.endswith("�") else text
-        if len(safe) <= self.emitted:
+        if len(full) <= len(head) or full.endswith("\ufffd"):
             return ""
-        out = safe[self.emitted:]
-        self.emitted = len(safe)
-        return out
+        self.prefix, self.read = self.read, len(self.ids)
+        return full[len(head):]
 
     def flush(self) -> str:
-        text = self.tok.decode(self.ids, self.skip)
-        out = text[self.emitted:]
-        self.emitted = len(text)
-        return out
+        head = self.tok.decode(self.ids[self.prefix:self.read], self.skip)
+        full = self.tok.decode(self.ids[self.prefix:], self.skip)
+        self.prefix = self.read = len(self.ids)
+        return full[len(head):]
 
 
 def utf8_complete_prefix(data: bytes) -> Tuple[str, bytes]:

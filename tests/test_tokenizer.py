@@ -258,3 +258,33 @@ def test_sentencepiece_bpe_heap_merge_and_word_cuts_match_full_rescans(inner_spa
         want = cod._pieces_to_ids(cod._merge_by_score_rounds(list(t)))
         assert cod._merge_by_score(list(t)) == cod._merge_by_score_rounds(list(t)), t
         assert cod.encode(text) == want, text
+
+
+def test_stream_decoder_windows_concatenate_to_the_full_decode(tmp_path):
+    """Pushing a reply token by token (random ids: partial UTF-8 bytes, special tokens, word joins) emits text
+    whose concatenation with the flush is the decode of the whole reply, for byte-level BPE, SentencePiece BPE
+    and WordPiece vocabularies."""
+    import random
+    from tokenizers import Tokenizer as T, decoders, models, pre_tokenizers, trainers
+    toks = [Tokenizer.from_pretrained(_save(_train_bytelevel(tmp_path), tmp_path, "bl.json"))]
+    b = T(models.BPE(byte_fallback=True, unk_token="<unk>"))
+    b.pre_tokenizer = pre_tokenizers.Metaspace()
+    b.decoder = decoders.Metaspace()
+    b.train_from_iterator(CORPUS, trainers.BpeTrainer(vocab_size=300, special_tokens=["<unk>"] +
+                                                      [f"<0x{i:02X}>" for i in range(256)]))
+    toks.append(Tokenizer.from_pretrained(_save(b, tmp_path, "msp.json")))
+    w = T(models.WordPiece(unk_token="[UNK]"))
+    w.pre_tokenizer = pre_tokenizers.BertPreTokenizer()
+    w.decoder = decoders.WordPiece()
+    w.train_from_iterator(CORPUS, trainers.WordPieceTrainer(vocab_size=300, special_tokens=["[UNK]", "[CLS]", "[SEP]"]))
+    toks.append(Tokenizer.from_pretrained(_save(w, tmp_path, "wp.json")))
+    rng = random.Random(9)
+    for tok in toks:
+        for _ in range(40):
+            ids = tok.encode(rng.choice(CORPUS)[:rng.randint(5, 120)]) + [rng.randrange(tok.vocab_size)
+                                                                         for _ in range(rng.randint(0, 12))]
+            for skip in (True, False):
+                sd = tok.stream_decoder(skip_special=skip)
+                parts = [sd.push(i) for i in ids]
+                assert "".join(parts) + sd.flush() == tok.decode(ids, skip_special=skip)
+                assert not any(p.endswith("�") for p in parts)
