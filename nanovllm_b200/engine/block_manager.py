@@ -17,7 +17,7 @@ from __future__ import annotations
 
 import hashlib
 from array import array
-from collections import deque
+from collections import OrderedDict
 from typing import Dict, List
 
 from .sequence import Sequence
@@ -58,7 +58,9 @@ class BlockManager:
         self.prefix_caching = prefix_caching
         self.blocks = [Block(i) for i in range(num_blocks)]
         self.hash_to_block_id: Dict[int, int] = {}
-        self.free_block_ids = deque(range(num_blocks))
+        # FIFO free list as an ordered set: pop the oldest, append freed pages, and take a cached page out of
+        # the middle in O(1) (a prefix-cache hit on a free page)
+        self.free_block_ids: "OrderedDict[int, None]" = OrderedDict.fromkeys(range(num_blocks))
         self.used_block_ids = set()
         # counters for observability
         self.prefix_hit_blocks = 0
@@ -79,7 +81,7 @@ class BlockManager:
     def _allocate_block(self) -> int:
         if not self.free_block_ids:
             raise RuntimeError("no free KV blocks")
-        bid = self.free_block_ids.popleft()
+        bid, _ = self.free_block_ids.popitem(last=False)
         block = self.blocks[bid]
         if block.ref_count != 0:
             raise RuntimeError("free block has ref_count != 0")
@@ -93,7 +95,7 @@ class BlockManager:
         if self.blocks[bid].ref_count != 0:
             raise RuntimeError("cannot free block with refs")
         self.used_block_ids.discard(bid)
-        self.free_block_ids.append(bid)
+        self.free_block_ids[bid] = None
 
     # ------------------------------------------------------------------ prefill admission
     def can_allocate(self, seq: Sequence) -> int:
@@ -127,7 +129,7 @@ class BlockManager:
                 block.ref_count += 1
             else:
                 block.ref_count = 1
-                self.free_block_ids.remove(bid)
+                del self.free_block_ids[bid]
                 self.used_block_ids.add(bid)
             seq.block_table.append(bid)
         for _ in range(num_cached_blocks, seq.num_blocks):
