@@ -28,6 +28,7 @@ from .model import LlmModel
 OPTION_THINK_TAGS = "think_tags"
 OPTION_CHAT_SPECIALS = "chat_specials"
 OPTION_LISTENER = "listener"  # an LlmListener that receives load progress events
+OPTION_UNPACK = "unpack_parameters"  # expand packed weights (GGUF blocks, QAT integers) to bf16 at load
 
 
 def _is_gguf(path: str) -> bool:
@@ -86,6 +87,27 @@ class LlmModelFactory:
             self._options[OPTION_THINK_TAGS] = tags
             return self
 
+        def chat_specials(self, specials):
+            """Chat-markup markers that end a visible answer (a ChatSpecials or a list of strings)."""
+            self._options[OPTION_CHAT_SPECIALS] = specials
+            return self
+
+        def listen(self, listener):
+            """LlmListener for load progress (None: silent)."""
+            self._options[OPTION_LISTENER] = listener
+            return self
+
+        def unpack_parameters(self, v: bool = True):
+            """Expand packed weights to bf16 during this load (more device memory, the dense GEMM path); engines
+            built on the model then never see packed tensors."""
+            self._options[OPTION_UNPACK] = bool(v)
+            return self
+
+        def options(self, opts: dict):
+            """Replace the load options map."""
+            self._options = dict(opts or {})
+            return self
+
         def device(self, d):
             self._device = d
             return self
@@ -98,6 +120,11 @@ class LlmModelFactory:
     @staticmethod
     def builder() -> "LlmModelFactory.Builder":
         return LlmModelFactory.Builder()
+
+    @staticmethod
+    def open(path) -> "LlmModelFactory.Builder":
+        """``LlmModelFactory.open(path)...build()``: a builder bound to ``path``."""
+        return LlmModelFactory.Builder().path(path)
 
 
 # linear projections built by the layer classes (layers/linear.py), HF and GGUF tensor names
@@ -117,6 +144,8 @@ def _load_gguf(path: str, options, device, dtype) -> LlmModel:
     # on the CPU too (there they are dequantized per multiply -- for tests)
     mode = os.environ.get("NVB_GGUF_PACKED", "1")
     keep_packed = mode == "force" or (device.type == "cuda" and mode not in ("0", "false", "no"))
+    if (options or {}).get(OPTION_UNPACK):
+        keep_packed = False
     # under tensor parallelism the tensors stay in host memory until the model is built: each layer then moves
     # one tensor at a time to the GPU and keeps only its shard, so a rank's device memory peaks near its share
     # of the weights plus one full tensor (safetensors checkpoints are memory-mapped and behave the same way)

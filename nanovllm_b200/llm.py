@@ -105,6 +105,8 @@ class LLM:
         self.device = torch.device(device)
         if cpu_threads is not None and self.device.type == "cpu":
             torch.set_num_threads(int(cpu_threads))
+        if isinstance(model, LlmModel) and model.options.get("unpack_parameters"):
+            unpack_parameters = True  # the model was opened with unpack_parameters
         if unpack_parameters:
             from .ops.quant import GgufPacked
             weights = {k: (v.dequantize(torch.bfloat16).to(self.device) if isinstance(v, GgufPacked) else v)

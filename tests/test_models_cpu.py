@@ -178,6 +178,30 @@ def test_unpacked_engine_over_packed_gguf_model(tmp_path, monkeypatch):
     assert torch.nn.functional.cosine_similarity(a, b, dim=0) > 0.999
 
 
+def test_factory_open_builder_unpacks_at_load(tmp_path, monkeypatch):
+    """LlmModelFactory.open(path) builder knobs (LlmModelFactory.java:817-870): unpack_parameters expands the GGUF
+    blocks during the load, listen / chat_specials / think_tags land in the model options."""
+    from nanovllm_b200.chat.listeners import LlmListeners
+    from nanovllm_b200.chat.markup import ChatSpecials, ThinkTags
+    from nanovllm_b200.ops.quant import GgufPacked
+    hf = HfConfig(vocab_size=300, hidden_size=128, intermediate_size=256, num_hidden_layers=2, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=32, max_position_embeddings=2048, model_type="qwen3",
+                  architectures=["Qwen3ForCausalLM"], tie_word_embeddings=False)
+    p = write_gguf_model(str(tmp_path / "q3o.gguf"), hf, init_random_weights(hf, 0), "Q8_0")
+    monkeypatch.setenv("NVB_GGUF_PACKED", "force")
+    listener, events = LlmListeners.collecting()
+    packed = LlmModelFactory.open(p).device("cpu").build()
+    assert any(isinstance(v, GgufPacked) for v in packed.weights.values())
+    m = (LlmModelFactory.open(p).device("cpu").unpack_parameters().listen(listener)
+         .chat_specials(ChatSpecials(("<x>",))).think_tags(ThinkTags("<t>", "</t>")).build())
+    assert not any(isinstance(v, GgufPacked) for v in m.weights.values())
+    assert m.chat_specials().markers == ("<x>",) and m.think_tags().open == "<t>" and events
+    ids = list(range(3, 40))
+    a = _prefill_logits(LLM(packed, _cfg(), device="cpu"), ids)
+    b = _prefill_logits(LLM(m, _cfg(), device="cpu"), ids)
+    assert torch.nn.functional.cosine_similarity(a, b, dim=0) > 0.999
+
+
 def test_factory_gguf_lfm2_q4_k_m(tmp_path):
     hf = lfm2_tiny()
     w = init_random_weights(hf, 3)
