@@ -184,11 +184,11 @@ class ChatSession:
             raise ValueError("max_history_messages must be >= 2")
         self.llm = llm
         self.tok = llm.tokenizer
-        self.sampling = sampling or llm.default_sampling
+        self._sp = sampling or llm.default_sampling
         self.tags = think_tags or getattr(llm, "think_tags", None) or _engine_think_tags(llm)
         specials = getattr(llm, "chat_specials", None)
         self.specials = (specials() if callable(specials) else None) or ChatSpecials.default()
-        self.enable_thinking = enable_thinking
+        self._thinking = enable_thinking
         self.max_history = max_history_messages
         self.timeout_s = timeout_s
         self.advisors = list(advisors if advisors is not None else (getattr(llm, "advisors", None) or []))
@@ -210,15 +210,109 @@ class ChatSession:
         self._stream: Optional[_TurnStream] = None
 
     # -------------------------------------------------------------------------------------- knobs
+    # fluent setters of the reference session (ChatSession.java:99-405); each returns the session
+    @staticmethod
+    def open(llm, max_tokens: int) -> "ChatSession":
+        """A session with the engine's default sampling and ``max_tokens`` new tokens per turn."""
+        return ChatSession(llm, sampling=llm.default_sampling.with_(max_tokens=int(max_tokens)))
+
     def listen(self, listener: Optional[LlmListener]) -> "ChatSession":
         self.listener = listener
         return self
+
+    def sampling(self, sp: SamplingParams) -> "ChatSession":
+        if sp is None:
+            raise ValueError("sampling must not be None")
+        self._sp = sp
+        return self
+
+    def sampling_params(self) -> SamplingParams:
+        return self._sp
+
+    def deterministic(self) -> "ChatSession":
+        return self.sampling(self._sp.deterministic())
+
+    def max_tokens(self, n: int) -> "ChatSession":
+        return self.sampling(self._sp.with_(max_tokens=int(n)))
+
+    def seed(self, *messages: ChatMessage) -> "ChatSession":
+        """Append prior turns (e.g. a few-shot dialog) to the history."""
+        for m in messages:
+            self.history.extend(m if isinstance(m, (list, tuple)) else [m])
+        self._cap()
+        return self
+
+    def timeout(self, seconds: Optional[float]) -> "ChatSession":
+        self.timeout_s = None if seconds is None else float(seconds)
+        return self
+
+    def enable_thinking(self, on: bool = True) -> "ChatSession":
+        self._thinking = bool(on)
+        return self
+
+    def thinking_enabled(self) -> bool:
+        return self._thinking
+
+    def think_tags(self, tags: Optional[ThinkTags] = None):
+        """With ``tags``: set them and return the session; without: the session's think tags."""
+        if tags is None:
+            return self.tags
+        self.tags = tags
+        return self
+
+    def recover_unusable_answers(self, on: bool = True) -> "ChatSession":
+        self.recover = bool(on)
+        return self
+
+    def unusable_answer(self, predicate: Callable[[str], bool]) -> "ChatSession":
+        if not callable(predicate):
+            raise TypeError("unusable_answer needs a callable")
+        self.unusable = predicate
+        return self
+
+    def unusable_answer_fallback(self, text: str) -> "ChatSession":
+        self.fallback_reply = text or DEFAULT_FALLBACK_REPLY
+        return self
+
+    def max_history_messages(self, n: int) -> "ChatSession":
+        if n < 2:
+            raise ValueError("max_history_messages must be >= 2")
+        self.max_history = int(n)
+        self._cap()
+        return self
+
+    def emit_debug_prompts(self, on: bool = True) -> "ChatSession":
+        self.debug = bool(on)
+        return self
+
+    def diagnostics(self, consumer: Optional[Callable[[str], None]]) -> "ChatSession":
+        """Send the session's diagnostic lines (retries, salvage) to ``consumer`` besides the listener."""
+        self._diag_sink = consumer
+        return self
+
+    def stream_to(self, think_out=None, answer_out=None) -> "ChatSession":
+        """Write streamed thinking / answer text to file-like objects (e.g. sys.stdout) as it arrives."""
+        def listener(_source, event):
+            out = think_out if event.kind == LlmTextKind.TEXT_THINKING else \
+                answer_out if event.kind == LlmTextKind.TEXT_ASSISTANT else None
+            if out is not None and not event.snapshot:
+                out.write(event.text)
+                if hasattr(out, "flush"):
+                    out.flush()
+        self.listener = listener
+        return self
+
+    def last_generate_stats(self):
+        return getattr(self.llm, "last_stats", None)
 
     def clear(self) -> None:
         self.history = [m for m in self.history[:1] if m.role == "system"]
 
     def _diag(self, text: str) -> None:
         emit(self.listener, self, LlmTextKind.TEXT_DIAGNOSTICS, text)
+        sink = getattr(self, "_diag_sink", None)
+        if sink is not None:
+            sink(text)
 
     def _cap(self) -> None:
         while len(self.history) > self.max_history:
@@ -247,11 +341,11 @@ class ChatSession:
         hist_user, model_user = (history_user_text or "").strip(), (model_user_text or "").strip()
         if not hist_user or not model_user:
             raise ValueError("user text must not be blank")
-        sp = sampling or self.sampling
+        sp = sampling or self._sp
         self.history.append(ChatMessage.user(hist_user))
         self._cap()
         truncate_history(self.history, self.tok, self.llm.cfg.max_model_len, sp.max_tokens,
-                         self.enable_thinking, self.tags)
+                         self._thinking, self.tags)
         t0 = time.perf_counter()
         if self.advisors:
             enr = AdvisorRunner.enrich(self.llm, self.advisors, model_user, self._prior_users(), sp,
@@ -295,13 +389,13 @@ class ChatSession:
             msgs = list(self.history)
             if msgs and msgs[-1].role == "user" and msgs[-1].content != model_user_text:
                 msgs[-1] = ChatMessage.user(model_user_text)
-        truncate_history(msgs, self.tok, self.llm.cfg.max_model_len, sp.max_tokens, self.enable_thinking,
+        truncate_history(msgs, self.tok, self.llm.cfg.max_model_len, sp.max_tokens, self._thinking,
                          self.tags)
         return msgs
 
     def _generate(self, model_user_text: str, isolate: bool, sp: SamplingParams) -> ChatReply:
         msgs = self._turn_messages(model_user_text, isolate, sp)
-        prompt = self.tok.apply_chat_template(msgs, True, self.enable_thinking, self.tags.open, self.tags.close)
+        prompt = self.tok.apply_chat_template(msgs, True, self._thinking, self.tags.open, self.tags.close)
         if self.debug:
             emit(self.listener, self, LlmTextKind.TEXT_DEBUG, prompt)
         ids = self.tok.encode(prompt, allow_special=True)

@@ -87,8 +87,8 @@ class RagSession:
         self.llm = llm
         self.index = index
         self.chat = chat or ChatSession(llm)
-        self.chat.enable_thinking = False
-        self.base_sampling = sampling or self.chat.sampling
+        self.chat.enable_thinking(False)
+        self.base_sampling = sampling or self.chat.sampling_params()
         self.top_k(top_k).max_context(max_context_chars)
         if max_tokens_when_no_hits < 1:
             raise ValueError("max_tokens_when_no_hits must be >= 1")

@@ -257,7 +257,7 @@ def test_llm_front_door_chat_rag_and_advisors():
     from nanovllm_b200.rag import RagFactory
     llm = FrontDoorLLM(["Four.", "Paris lies on the Seine.", "note A", "note B"], system_prompt="Be brief.")
     s = llm.chat(7)  # int: max new tokens per turn, engine defaults otherwise
-    assert s.sampling.max_tokens == 7 and s.sampling.temperature == llm.default_sampling.temperature
+    assert s.sampling_params().max_tokens == 7 and s.sampling_params().temperature == llm.default_sampling.temperature
     assert s.send("2+2?").answer == "Four."
     ix = RagFactory.of("Paris is the capital of France. It lies on the Seine river.")
     r = llm.rag(ix, max_tokens=32)
@@ -273,3 +273,25 @@ def test_llm_front_door_chat_rag_and_advisors():
     llm._closed = True
     with pytest.raises(Exception):
         llm.chat()
+
+
+def test_chat_session_fluent_knobs():
+    """ChatSession setters of the reference (ChatSession.java:99-405) return the session and take effect."""
+    import io
+    llm = ScriptedLLM(["<think>hmm</think>Ten.", "x", "Eleven.", "", ""])
+    think, answer, diag = io.StringIO(), io.StringIO(), []
+    s = (ChatSession.open(llm, 9).deterministic().max_tokens(5).timeout(3.0).enable_thinking(True)
+         .max_history_messages(4).emit_debug_prompts(False).recover_unusable_answers(True)
+         .unusable_answer(lambda a: a.strip() in ("", "x")).unusable_answer_fallback("n/a")
+         .diagnostics(diag.append).stream_to(think, answer)
+         .seed(ChatMessage.user("5+5?"), ChatMessage.assistant("Ten.")))
+    assert s.sampling_params().max_tokens == 5 and s.sampling_params().top_k == 1  # deterministic kept
+    assert s.thinking_enabled() and s.timeout_s == 3.0 and s.think_tags() is s.tags
+    assert [m.role for m in s.history] == ["user", "assistant"]
+    r = s.send("5+5 again?")
+    assert r.answer == "Ten." and think.getvalue() == "hmm" and answer.getvalue() == "Ten."
+    assert s.send("6+5?").answer == "Eleven." and any("retrying" in d for d in diag)  # "x" is unusable
+    assert s.send("and?").answer == "n/a"  # still unusable after the retry: the fallback reply
+    assert len(s.history) <= 4
+    with pytest.raises(ValueError):
+        s.max_history_messages(1)
