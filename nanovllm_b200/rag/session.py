@@ -92,8 +92,8 @@ class RagSession:
         self.top_k(top_k).max_context(max_context_chars)
         if max_tokens_when_no_hits < 1:
             raise ValueError("max_tokens_when_no_hits must be >= 1")
-        self.max_tokens_when_no_hits = max_tokens_when_no_hits
-        self.isolate_generation = isolate_generation
+        self._no_hit_tokens = max_tokens_when_no_hits
+        self._isolate = isolate_generation
         self.last_hits: List[RagHit] = []
         self.anchor_query = ""
         self.last_source = ""
@@ -127,6 +127,64 @@ class RagSession:
         self.chat.listen(listener)
         return self
 
+    # the reference session's other knobs (RagSession.java:96-400): RAG ones here, chat ones forwarded
+    @staticmethod
+    def open(llm_or_chat, index: RagIndex, max_tokens: Optional[int] = None) -> "RagSession":
+        """``open(llm, index[, max_tokens])`` or ``open(chat_session, index)`` (reuses its dialog and knobs)."""
+        if isinstance(llm_or_chat, ChatSession):
+            return RagSession(llm_or_chat.llm, index, chat=llm_or_chat)
+        chat = ChatSession.open(llm_or_chat, max_tokens) if max_tokens is not None else None
+        return RagSession(llm_or_chat, index, chat=chat)
+
+    @staticmethod
+    def format_user_message(hits: List[RagHit], question: str, max_context_chars: Optional[int] = None) -> str:
+        """The model-facing grounded turn: retrieved passages, then the question."""
+        return format_user_message(hits, question, max_context_chars if max_context_chars is not None else 1 << 30)
+
+    def max_tokens_when_no_hits(self, n: int) -> "RagSession":
+        if n < 1:
+            raise ValueError("max_tokens_when_no_hits must be >= 1")
+        self._no_hit_tokens = int(n)
+        return self
+
+    def isolate_generation(self, on: bool = True) -> "RagSession":
+        self._isolate = bool(on)
+        return self
+
+    def _forward(self, name: str, *args) -> "RagSession":
+        getattr(self.chat, name)(*args)
+        return self
+
+    def timeout(self, seconds: Optional[float]) -> "RagSession":
+        return self._forward("timeout", seconds)
+
+    def enable_thinking(self, on: bool = True) -> "RagSession":
+        return self._forward("enable_thinking", on)
+
+    def think_tags(self, tags: ThinkTags) -> "RagSession":
+        return self._forward("think_tags", tags)
+
+    def max_history_messages(self, n: int) -> "RagSession":
+        return self._forward("max_history_messages", n)
+
+    def recover_unusable_answers(self, on: bool = True) -> "RagSession":
+        return self._forward("recover_unusable_answers", on)
+
+    def unusable_answer(self, predicate) -> "RagSession":
+        return self._forward("unusable_answer", predicate)
+
+    def unusable_answer_fallback(self, text: str) -> "RagSession":
+        return self._forward("unusable_answer_fallback", text)
+
+    def emit_debug_prompts(self, on: bool = True) -> "RagSession":
+        return self._forward("emit_debug_prompts", on)
+
+    def diagnostics(self, consumer) -> "RagSession":
+        return self._forward("diagnostics", consumer)
+
+    def stream_to(self, think_out=None, answer_out=None) -> "RagSession":
+        return self._forward("stream_to", think_out, answer_out)
+
     def clear(self) -> None:
         self.chat.clear()
         self.last_hits, self.anchor_query, self.last_source, self.last_retrieval_query = [], "", "", ""
@@ -153,10 +211,10 @@ class RagSession:
         prompt = format_user_message(self.last_hits, q, self.max_context_chars)
         base = self.base_sampling
         if not self.last_hits:
-            sp = base.with_(max_tokens=max(base.max_tokens, self.max_tokens_when_no_hits))
+            sp = base.with_(max_tokens=max(base.max_tokens, self._no_hit_tokens))
         else:
             sp = base.with_(temperature=min(base.temperature, GROUNDED_TEMPERATURE_CAP))
-        isolate = not self.last_hits or self.isolate_generation
+        isolate = not self.last_hits or self._isolate
         return self.chat.send_prepared(q, prompt, isolate=isolate, sampling=sp)
 
     def _retrieve(self, q: str) -> List[RagHit]:

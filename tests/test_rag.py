@@ -146,3 +146,26 @@ def test_rag_session_turns_with_scripted_engine():
     assert llm.calls[1][1].max_tokens == 48 and llm.calls[1][1].temperature == pytest.approx(0.1)
     r = rag.send("Tell me about quantum chromodynamics lattice simulations")
     assert rag.last_hits == [] and llm.calls[-1][1].max_tokens >= 384
+
+
+def test_rag_session_fluent_knobs():
+    """RagSession.open and its knobs (RagSession.java:96-400): RAG knobs act on the turn, chat knobs reach the
+    underlying ChatSession, format_user_message builds the grounded turn."""
+    from test_chat import ScriptedLLM
+    from nanovllm_b200.chat import ChatSession
+    llm = ScriptedLLM(["I do not know.", "Philipp."])
+    diag = []
+    rag = (RagSession.open(llm, _grimm_index(), 16).max_tokens_when_no_hits(99).isolate_generation(True)
+           .timeout(2.0).max_history_messages(6).diagnostics(diag.append).emit_debug_prompts(False))
+    assert rag.chat.timeout_s == 2.0 and rag.chat.max_history == 6 and not rag.chat.thinking_enabled()
+    rag.send("Tell me about quantum chromodynamics lattice simulations")
+    assert llm.calls[-1][1].max_tokens == 99
+    chat = ChatSession(llm)
+    rag2 = RagSession.open(chat, _grimm_index())
+    assert rag2.chat is chat
+    rag2.send("Who was the father of the Grimm brothers?")
+    hits = _grimm_index().retrieve("father Grimm brothers", 2)
+    msg = RagSession.format_user_message(hits, "Who was the father?")
+    assert "Who was the father?" in msg and "Philipp" in msg
+    with pytest.raises(ValueError):
+        rag.max_tokens_when_no_hits(0)
