@@ -60,6 +60,18 @@ class LlmModel:
     def usable_modalities(self) -> List[str]:
         return ["text->embedding"] if self.is_embedding() else ["text->text"]
 
+    def input_modalities(self) -> List[str]:
+        """Inputs the checkpoint declares (text, plus image / audio / video towers it carries)."""
+        return self.modalities()
+
+    def output_modalities(self) -> List[str]:
+        return ["embedding"] if self.is_embedding() else ["text"]
+
+    @property
+    def path(self) -> str:
+        """Where the model was loaded from (folder or .gguf file)."""
+        return self.source
+
     def think_tags(self):
         from ..chat.markup import ThinkTags
         return self.options.get("think_tags") or ThinkTags.default()

@@ -102,5 +102,6 @@ def test_model_chat_specials_option_and_engine_accessors():
     assert LlmModel(hf, w).chat_specials() == ChatSpecials.default()
     llm = LLM.builder(m).device("cpu").num_kvcache_blocks(8).max_model_len(256).build()
     assert llm.chat_specials().markers == ("<|x|>",) and not llm.is_closed()
+    assert m.input_modalities() == ["text"] and m.output_modalities() == ["text"] and m.path == ""
     llm.close()
     assert llm.is_closed()
