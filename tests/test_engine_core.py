@@ -391,3 +391,9 @@ def test_step_input_checks_pass_a_real_run_and_catch_violations():
                       "block_tables": np.array([[3, 0], [3, 0]]), "context_lens": np.array([4, 4])})
     with pytest.raises(StepInputError, match="copy-on-write"):
         check_step(**{**base, "block_tables": np.array([[1, 2], [3, 2]]), "context_lens": np.array([257, 300])})
+
+
+def test_host_bench_runs():
+    from nanovllm_b200.utils.host_bench import run
+    res = run(batch=8, steps=5, warmup=60)
+    assert res["total"] > 0 and set(res) >= {"schedule", "postprocess"}
