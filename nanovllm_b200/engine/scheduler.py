@@ -19,6 +19,7 @@ can free per-sequence recurrent state (LFM2 conv state), as Scheduler.java:92-10
 """
 from __future__ import annotations
 
+import itertools
 from collections import deque
 from typing import Callable, List, Optional, Sequence as Seq, Tuple
 
@@ -126,6 +127,17 @@ class Scheduler:
     def _schedule_decode(self) -> List[Sequence]:
         scheduled: List[Sequence] = []
         bm = self.block_manager
+        # common case: the free pages cover every sequence that opens a new page this step, so nobody is
+        # preempted and the batch is the running head in order (what the loop below produces, without the churn)
+        head = list(itertools.islice(self.running, self.max_num_seqs))
+        bs = self.block_size
+        opening = sum(1 for s in head if s.num_tokens % bs == 1)
+        if head and opening <= bm.num_free_blocks:
+            for s in head:
+                s.num_scheduled_tokens = 1
+                s.is_prefill = False
+                bm.may_append(s)
+            return head
         while self.running and len(scheduled) < self.max_num_seqs:
             seq = self.running.popleft()
             ok = True
