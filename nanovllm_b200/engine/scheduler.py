@@ -46,6 +46,7 @@ class Scheduler:
         self.running: deque = deque()
         self.on_release = on_release
         self.num_preemptions = 0
+        self.decode_fast_path = True  # one-pass decode batch when no page is short (tests compare both forms)
 
     def is_finished(self) -> bool:
         return not self.waiting and not self.running
@@ -129,7 +130,7 @@ class Scheduler:
         bm = self.block_manager
         # common case: the free pages cover every sequence that opens a new page this step, so nobody is
         # preempted and the batch is the running head in order (what the loop below produces, without the churn)
-        head = list(itertools.islice(self.running, self.max_num_seqs))
+        head = list(itertools.islice(self.running, self.max_num_seqs)) if self.decode_fast_path else []
         bs = self.block_size
         opening = sum(1 for s in head if s.num_tokens % bs == 1)
         if head and opening <= bm.num_free_blocks:

@@ -397,3 +397,31 @@ def test_host_bench_runs():
     from nanovllm_b200.utils.host_bench import run
     res = run(batch=8, steps=5, warmup=60)
     assert res["total"] > 0 and set(res) >= {"schedule", "postprocess"}
+
+
+def test_decode_fast_path_schedules_like_the_preempting_loop():
+    """The one-pass decode batch and the pop / re-push loop give the same batches, pages and preemptions over a
+    random request stream with a pool small enough to preempt."""
+    import random
+
+    def trace(fast):
+        rng = random.Random(21)
+        cfg = EngineConfig(max_num_seqs=5, max_model_len=2048, max_num_batched_tokens=600)
+        sch = Scheduler(cfg, num_blocks=8)
+        sch.decode_fast_path = fast
+        for i in range(9):
+            sch.add(Sequence([rng.randrange(100) for _ in range(rng.randint(5, 500))],
+                             SamplingParams(max_tokens=rng.randint(5, 400), ignore_eos=True), 256))
+        out = []
+        while not sch.is_finished():
+            seqs, pre = sch.schedule()
+            out.append((pre, [(s.seq_id - base, tuple(s.block_table)) for s in seqs]))
+            sch.postprocess(seqs, [rng.randrange(100) for _ in seqs], pre)
+        return out, sch.num_preemptions
+
+    from nanovllm_b200.engine import sequence as _sq
+    base = next(_sq._SEQ_COUNTER) + 1
+    slow = trace(False)
+    base = next(_sq._SEQ_COUNTER) + 1
+    fast = trace(True)
+    assert slow[1] > 0 and fast == slow
