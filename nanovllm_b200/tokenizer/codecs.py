@@ -49,6 +49,8 @@ def bytes_to_unicode() -> Dict[int, str]:
 
 BYTE_ENCODER = bytes_to_unicode()
 BYTE_DECODER = {v: k for k, v in BYTE_ENCODER.items()}
+_BYTE_CHARS = frozenset(BYTE_DECODER)
+_TO_LATIN1 = {ord(ch): b for ch, b in BYTE_DECODER.items()}  # str.translate: byte symbol -> the byte as a char
 
 
 def bpe_merge(symbols: List[str], ranks: Dict[Tuple[str, str], int]) -> List[str]:
@@ -171,6 +173,9 @@ class ByteBpe(Codec):
         return out
 
     def decode(self, pieces: Sequence[str]) -> str:
+        text = "".join(pieces)
+        if _BYTE_CHARS.issuperset(text):  # every character is a byte symbol: translate and re-read as UTF-8
+            return text.translate(_TO_LATIN1).encode("latin-1").decode("utf-8", errors="replace")
         data = bytearray()
         for p in pieces:
             for ch in p:

@@ -288,3 +288,27 @@ def test_stream_decoder_windows_concatenate_to_the_full_decode(tmp_path):
                 parts = [sd.push(i) for i in ids]
                 assert "".join(parts) + sd.flush() == tok.decode(ids, skip_special=skip)
                 assert not any(p.endswith("�") for p in parts)
+
+
+def test_byte_level_decode_fast_path_matches_per_symbol_decode():
+    """Pieces made only of byte symbols decode through one translate; mixed pieces (added tokens with other
+    characters) through the per-symbol loop; both give the per-symbol loop's text."""
+    import random
+    from nanovllm_b200.tokenizer import codecs as C
+
+    def slow(pieces):
+        data = bytearray()
+        for p in pieces:
+            for ch in p:
+                b = C.BYTE_DECODER.get(ch)
+                data.extend(ch.encode("utf-8") if b is None else bytes([b]))
+        return data.decode("utf-8", errors="replace")
+
+    cod = C.ByteBpe({}, [], C.GPT2_PATTERN, native=False)
+    rng = random.Random(4)
+    syms = list(C.BYTE_DECODER)
+    for _ in range(300):
+        pieces = ["".join(rng.choice(syms) for _ in range(rng.randint(1, 4))) for _ in range(rng.randint(0, 12))]
+        if rng.random() < 0.3:
+            pieces.insert(rng.randrange(len(pieces) + 1), rng.choice(["<|im_end|>", "\n", "é", "中"]))
+        assert cod.decode(pieces) == slow(pieces)
